@@ -1,0 +1,872 @@
+/*
+ * mimoracle.c -- CPU restatement of mimir-model's quantized decode path.
+ *
+ * TEST INFRASTRUCTURE, NOT PRODUCT: the checker for the GPU library and the
+ * timed CPU baseline.  See mimoracle.h for the contract and the rule that
+ * only tests, smoke() and bench.py's CPU legs may use it.
+ *
+ * Compile with -ffp-contract=off (the Makefile does): every a*b+c below is
+ * two roundings unless written as fmaf().
+ */
+#include "mimoracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ */
+/* small helpers                                                        */
+/* ------------------------------------------------------------------ */
+
+static inline uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint16_t le16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static inline void put16(uint8_t *p, uint16_t v) { p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); }
+
+typedef void (*range_fn)(void *ctx, int64_t lo, int64_t hi);
+typedef struct { range_fn fn; void *ctx; int64_t lo, hi; } range_job;
+
+static void *range_thread(void *p) {
+    range_job *j = (range_job *)p;
+    j->fn(j->ctx, j->lo, j->hi);
+    return NULL;
+}
+
+/* Runs fn over [0, n) split into nthreads contiguous pieces, like the
+ * reference's parallel() over output rows (interp/pool.go:33-66). */
+static void parallel_for(int64_t n, int nthreads, range_fn fn, void *ctx) {
+    if (nthreads > 256) nthreads = 256;
+    if (nthreads > n) nthreads = (int)n;
+    if (nthreads <= 1) { fn(ctx, 0, n); return; }
+    pthread_t th[256];
+    range_job jobs[256];
+    int ok[256];
+    int64_t per = (n + nthreads - 1) / nthreads;
+    for (int t = 0; t < nthreads; t++) {
+        int64_t lo = t * per, hi = lo + per < n ? lo + per : n;
+        jobs[t] = (range_job){fn, ctx, lo < n ? lo : n, hi};
+        ok[t] = 0;
+        if (t > 0 && jobs[t].lo < jobs[t].hi) ok[t] = pthread_create(&th[t], NULL, range_thread, &jobs[t]) == 0;
+    }
+    fn(ctx, jobs[0].lo, jobs[0].hi);
+    for (int t = 1; t < nthreads; t++) {
+        if (ok[t]) pthread_join(th[t], NULL);
+        else if (jobs[t].lo < jobs[t].hi) fn(ctx, jobs[t].lo, jobs[t].hi);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* f16 <-> f32, float.go:24-88                                          */
+/* ------------------------------------------------------------------ */
+
+float mo_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000) << 16;
+    uint32_t exp = (h >> 10) & 0x1F, mant = h & 0x3FF;
+    if (exp == 0) {
+        if (mant == 0) return bits_f32(sign);
+        /* subnormal: mant * 2^-24, renormalised */
+        uint32_t e = 127 - 15 + 1;
+        while ((mant & 0x400) == 0) { mant <<= 1; e--; }
+        return bits_f32(sign | (e << 23) | ((mant & 0x3FF) << 13));
+    }
+    if (exp == 0x1F) return bits_f32(sign | 0x7F800000u | (mant << 13));
+    return bits_f32(sign | ((exp + 127 - 15) << 23) | (mant << 13));
+}
+
+uint16_t mo_f32_to_f16(float f) {
+    uint32_t b = f32_bits(f);
+    uint16_t sign = (uint16_t)((b >> 16) & 0x8000);
+    int32_t exp = (int32_t)((b >> 23) & 0xFF);
+    uint32_t mant = b & 0x7FFFFF;
+    if (exp == 0xFF) {
+        if (mant == 0) return sign | 0x7C00;
+        return (uint16_t)(sign | 0x7E00 | (mant >> 13)); /* quiet NaN, top payload kept */
+    }
+    int32_t e = exp - 127 + 15;
+    if (e >= 0x1F) return sign | 0x7C00;
+    if (e <= 0) {
+        if (e < -11) return sign;
+        mant |= 0x800000;
+        uint32_t shift = (uint32_t)(14 - e);
+        uint32_t half = 1u << (shift - 1);
+        uint32_t rem = mant & ((half << 1) - 1);
+        uint32_t q = mant >> shift;
+        if (rem > half || (rem == half && (q & 1))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)e << 10) | (mant >> 13);
+    uint32_t rem = mant & 0x1FFF;
+    if (rem > 0x1000 || (rem == 0x1000 && (q & 1))) q++;
+    return (uint16_t)(sign | q);
+}
+
+void mo_cast_f16(const float *x, uint16_t *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = mo_f32_to_f16(x[i]);
+}
+
+/* ------------------------------------------------------------------ */
+/* sizes, dtype.go:48-129                                               */
+/* ------------------------------------------------------------------ */
+
+int64_t mo_row_bytes(int dt, int64_t k) {
+    switch (dt) {
+    case MO_F32: return 4 * k;
+    case MO_F16: return 2 * k;
+    case MO_Q8_0: return k % 32 ? 0 : k / 32 * 34;
+    case MO_Q4_K: return k % 256 ? 0 : k / 256 * 144;
+    case MO_Q6_K: return k % 256 ? 0 : k / 256 * 210;
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* decoders, quant.go:197-344                                           */
+/* ------------------------------------------------------------------ */
+
+/* Q8_0: y = d*q, quant.go:197-206 */
+static void deq_q8_0(const uint8_t *src, float *dst, int64_t nb) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = src + 34 * b;
+        float d = mo_f16_to_f32(le16(blk));
+        for (int j = 0; j < 32; j++) dst[32 * b + j] = d * (float)(int8_t)blk[2 + j];
+    }
+}
+
+/* getScaleMinK4, quant.go:246-254 */
+static inline void scale_min_k4(int j, const uint8_t *q, uint8_t *sc, uint8_t *m) {
+    if (j < 4) { *sc = q[j] & 63; *m = q[j + 4] & 63; return; }
+    *sc = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+    *m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+}
+
+/* Q4_K: y = (d*sc)*n - dmin*m, each product rounded, quant.go:260-289 */
+static void deq_q4_k(const uint8_t *src, float *dst, int64_t nb) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = src + 144 * b;
+        float d = mo_f16_to_f32(le16(blk)), dmin = mo_f16_to_f32(le16(blk + 2));
+        const uint8_t *scales = blk + 4, *q = blk + 16;
+        float *y = dst + 256 * b;
+        for (int c = 0; c < 4; c++) {
+            uint8_t sc, m;
+            scale_min_k4(2 * c, scales, &sc, &m);
+            float d1 = d * (float)sc, m1 = dmin * (float)m;
+            scale_min_k4(2 * c + 1, scales, &sc, &m);
+            float d2 = d * (float)sc, m2 = dmin * (float)m;
+            for (int l = 0; l < 32; l++) y[64 * c + l] = d1 * (float)(q[32 * c + l] & 0xF) - m1;
+            for (int l = 0; l < 32; l++) y[64 * c + 32 + l] = d2 * (float)(q[32 * c + l] >> 4) - m2;
+        }
+    }
+}
+
+/* Q6_K: y = (d*sc)*(q-32), quant.go:294-321 */
+static void deq_q6_k(const uint8_t *src, float *dst, int64_t nb) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = src + 210 * b;
+        float d = mo_f16_to_f32(le16(blk + 208));
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+            const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);
+            float *y = dst + 256 * b + 128 * h;
+            for (int l = 0; l < 32; l++) {
+                int is = l / 16;
+                int q1 = (int)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                y[l] = (d * (float)sc[is + 0]) * (float)q1;
+                y[l + 32] = (d * (float)sc[is + 2]) * (float)q2;
+                y[l + 64] = (d * (float)sc[is + 4]) * (float)q3;
+                y[l + 96] = (d * (float)sc[is + 6]) * (float)q4;
+            }
+        }
+    }
+}
+
+int mo_dequantize(int dt, const uint8_t *src, float *dst, int64_t n) {
+    switch (dt) {
+    case MO_F32: memcpy(dst, src, 4 * (size_t)n); return 0;
+    case MO_F16:
+        for (int64_t i = 0; i < n; i++) dst[i] = mo_f16_to_f32(le16(src + 2 * i));
+        return 0;
+    case MO_Q8_0: if (n % 32) return -1; deq_q8_0(src, dst, n / 32); return 0;
+    case MO_Q4_K: if (n % 256) return -1; deq_q4_k(src, dst, n / 256); return 0;
+    case MO_Q6_K: if (n % 256) return -1; deq_q6_k(src, dst, n / 256); return 0;
+    }
+    return -1;
+}
+
+/* ------------------------------------------------------------------ */
+/* encoders                                                             */
+/* ------------------------------------------------------------------ */
+
+/* quantizeQ8_0, quant.go:208-228 (roundf: half away from zero) */
+void mo_quantize_q8_0(const float *x, uint8_t *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 32; b++) {
+        const float *xb = x + 32 * b;
+        float amax = 0;
+        for (int j = 0; j < 32; j++) { float a = fabsf(xb[j]); if (a > amax) amax = a; }
+        float d = amax / 127.0f, id = d != 0 ? 1.0f / d : 0.0f;
+        uint8_t *blk = dst + 34 * b;
+        put16(blk, mo_f32_to_f16(d));
+        for (int j = 0; j < 32; j++) blk[2 + j] = (uint8_t)(int8_t)roundf(xb[j] * id);
+    }
+}
+
+static inline float f16_round(float f) { return mo_f16_to_f32(mo_f32_to_f16(f)); }
+static inline int clampi(int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; }
+
+/* Q4_K encoder (this project's own; min/max fit per sub-block of 32).
+ * Sub-block j covers [-dmin*m_j, d*sc_j*15 - dmin*m_j]; d and dmin are the
+ * largest sub-block step and offset over 63, rounded to f16; sc, m are
+ * 6-bit; quants are the nearest of 0..15 under the decoded step. */
+static void enc_q4_k_block(const float *x, uint8_t *blk) {
+    float step[8], off[8], maxstep = 0, maxoff = 0;
+    for (int j = 0; j < 8; j++) {
+        float lo = 0, hi = 0;
+        for (int i = 0; i < 32; i++) {
+            float v = x[32 * j + i];
+            if (v < lo) lo = v;
+            if (v > hi) hi = v;
+        }
+        step[j] = (hi - lo) / 15.0f;
+        off[j] = -lo;
+        if (step[j] > maxstep) maxstep = step[j];
+        if (off[j] > maxoff) maxoff = off[j];
+    }
+    float d = f16_round(maxstep / 63.0f), dmin = f16_round(maxoff / 63.0f);
+    uint8_t sc[8], m[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = (uint8_t)(d > 0 ? clampi((int)lrintf(step[j] / d), 0, 63) : 0);
+        m[j] = (uint8_t)(dmin > 0 ? clampi((int)lrintf(off[j] / dmin), 0, 63) : 0);
+    }
+    memset(blk, 0, 144);
+    put16(blk, mo_f32_to_f16(d));
+    put16(blk + 2, mo_f32_to_f16(dmin));
+    uint8_t *s = blk + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    uint8_t q[256];
+    for (int j = 0; j < 8; j++) {
+        float ds = d * (float)sc[j], dm = dmin * (float)m[j];
+        for (int i = 0; i < 32; i++)
+            q[32 * j + i] = (uint8_t)(ds > 0 ? clampi((int)lrintf((x[32 * j + i] + dm) / ds), 0, 15) : 0);
+    }
+    for (int c = 0; c < 4; c++)
+        for (int l = 0; l < 32; l++)
+            blk[16 + 32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
+}
+
+void mo_quantize_q4_k(const float *x, uint8_t *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) enc_q4_k_block(x + 256 * b, dst + 144 * b);
+}
+
+/* Q6_K encoder (this project's own).  Group g of 16 elements uses scale
+ * sc[g]: the element of largest magnitude maps to -32, the scales are
+ * 8-bit signed under one f16 d. */
+static void enc_q6_k_block(const float *x, uint8_t *blk) {
+    float gs[16], maxs = 0;
+    for (int g = 0; g < 16; g++) {
+        float vmax = 0, amax = 0;
+        for (int i = 0; i < 16; i++) {
+            float v = x[16 * g + i];
+            if (fabsf(v) > amax) { amax = fabsf(v); vmax = v; }
+        }
+        gs[g] = vmax / -32.0f;
+        if (fabsf(gs[g]) > maxs) maxs = fabsf(gs[g]);
+    }
+    float d = f16_round(maxs / 127.0f);
+    int8_t sc[16];
+    for (int g = 0; g < 16; g++) sc[g] = (int8_t)(d > 0 ? clampi((int)lrintf(gs[g] / d), -128, 127) : 0);
+    uint8_t q[256];
+    for (int g = 0; g < 16; g++) {
+        float ds = d * (float)sc[g];
+        for (int i = 0; i < 16; i++)
+            q[16 * g + i] = (uint8_t)(ds != 0 ? clampi((int)lrintf(x[16 * g + i] / ds), -32, 31) + 32 : 32);
+    }
+    memset(blk, 0, 210);
+    for (int h = 0; h < 2; h++) {
+        uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+        const uint8_t *y = q + 128 * h;
+        for (int l = 0; l < 32; l++) {
+            uint8_t q1 = y[l], q2 = y[l + 32], q3 = y[l + 64], q4 = y[l + 96];
+            ql[l] = (uint8_t)((q1 & 0xF) | ((q3 & 0xF) << 4));
+            ql[l + 32] = (uint8_t)((q2 & 0xF) | ((q4 & 0xF) << 4));
+            qh[l] = (uint8_t)((q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6));
+        }
+    }
+    memcpy(blk + 192, sc, 16);
+    put16(blk + 208, mo_f32_to_f16(d));
+}
+
+void mo_quantize_q6_k(const float *x, uint8_t *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) enc_q6_k_block(x + 256 * b, dst + 210 * b);
+}
+
+int mo_quantize(int dt, const float *x, uint8_t *dst, int64_t n) {
+    switch (dt) {
+    case MO_Q8_0: if (n % 32) return -1; mo_quantize_q8_0(x, dst, n); return 0;
+    case MO_Q4_K: if (n % 256) return -1; mo_quantize_q4_k(x, dst, n); return 0;
+    case MO_Q6_K: if (n % 256) return -1; mo_quantize_q6_k(x, dst, n); return 0;
+    case MO_F32: memcpy(dst, x, 4 * (size_t)n); return 0;
+    case MO_F16: for (int64_t i = 0; i < n; i++) put16(dst + 2 * i, mo_f32_to_f16(x[i])); return 0;
+    }
+    return -1;
+}
+
+/* ---- seeded synthetic values ---- */
+
+static inline uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+/* Element i of stream `seed`: Box-Muller on two 53-bit uniforms. */
+static inline double normal_at(uint64_t seed, uint64_t i) {
+    uint64_t a = mix64(seed ^ mix64(2 * i)), b = mix64(seed ^ mix64(2 * i + 1));
+    double u1 = ((double)(a >> 11) + 1.0) * 0x1p-53; /* (0, 1] */
+    double u2 = (double)(b >> 11) * 0x1p-53;         /* [0, 1) */
+    return sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+}
+
+void mo_gen_normal(uint64_t seed, int64_t n, float mean, float sigma, float *x) {
+    for (int64_t i = 0; i < n; i++) x[i] = (float)(mean + sigma * normal_at(seed, (uint64_t)i));
+}
+
+typedef struct { int dt; uint64_t seed; int64_t k; float sigma; uint8_t *dst; } gen_ctx;
+
+static void gen_rows(void *p, int64_t lo, int64_t hi) {
+    gen_ctx *c = (gen_ctx *)p;
+    float *row = (float *)malloc(sizeof(float) * (size_t)c->k);
+    int64_t rb = mo_row_bytes(c->dt, c->k);
+    for (int64_t r = lo; r < hi; r++) {
+        for (int64_t i = 0; i < c->k; i++) row[i] = (float)(c->sigma * normal_at(c->seed, (uint64_t)(r * c->k + i)));
+        mo_quantize(c->dt, row, c->dst + r * rb, c->k);
+    }
+    free(row);
+}
+
+int mo_gen_weight(int dt, uint64_t seed, int64_t n, int64_t k, float sigma, uint8_t *dst, int nthreads) {
+    if (mo_row_bytes(dt, k) == 0) return -1;
+    gen_ctx c = {dt, seed, k, sigma, dst};
+    parallel_for(n, nthreads, gen_rows, &c);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* 8-bit activations, internal/kernels/q8.go:50-97, 237-273             */
+/* ------------------------------------------------------------------ */
+
+int mo_q8_quantize(const float *x, int64_t k, int block, int8_t *q, float *d32, int16_t *xs, int16_t *m32) {
+    if (k == 0 || (block != 32 && block != 256) || k % block) return 0;
+    for (int64_t b = 0; b < k / block; b++) {
+        const float *xb = x + block * b;
+        int8_t *qb = q + block * b;
+        /* amaxQ8Go: refuse NaN and |x| > 2^60 */
+        float amax = 0;
+        for (int i = 0; i < block; i++) {
+            float a = bits_f32(f32_bits(xb[i]) & 0x7FFFFFFFu);
+            if (!(a <= 0x1p60f)) return 0;
+            if (a > amax) amax = a;
+        }
+        if (amax == 0) memset(qb, 0, (size_t)block);
+        else
+            for (int i = 0; i < block; i++) /* quantQ8Go: RoundToEven in float64 */
+                qb[i] = (int8_t)rint(127.0 * (double)xb[i] / (double)amax);
+        for (int r = 0; r < block / 32; r++) {
+            int16_t s = 0;
+            for (int i = 0; i < 32; i++) s = (int16_t)(s + qb[32 * r + i]);
+            if (xs) xs[block * b / 32 + r] = s;
+        }
+        if (m32)
+            for (int i = 0; i < block / 2; i++)
+                m32[block * b / 2 + i] = (int16_t)(32 * ((int16_t)qb[2 * i] + (int16_t)qb[2 * i + 1]));
+        float d = amax / 127.0f;
+        for (int r = 0; r < block / 32; r++) d32[block * b / 32 + r] = d;
+    }
+    return 1;
+}
+
+static inline int f16_finite(const uint8_t *p) { return (le16(p) & 0x7C00) != 0x7C00; }
+
+int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k,
+                   float *out) {
+    float tot = 0, off = 0;
+    for (int64_t b = 0; b < k / 256; b++) {
+        const int8_t *y = q + 256 * b;
+        float dx = d32[8 * b];
+        if (dt == MO_Q4_K) {
+            const uint8_t *blk = row + 144 * b;
+            if (!f16_finite(blk) || !f16_finite(blk + 2)) return 0;
+            float d = mo_f16_to_f32(le16(blk)), dmin = mo_f16_to_f32(le16(blk + 2));
+            int32_t sc[8], m[8];
+            const uint8_t *s = blk + 4;
+            for (int j = 0; j < 4; j++) {
+                sc[j] = s[j] & 63;
+                m[j] = s[j + 4] & 63;
+                sc[4 + j] = (s[j + 8] & 0xF) | ((s[j] >> 6) << 4);
+                m[4 + j] = (s[j + 8] >> 4) | ((s[j + 4] >> 6) << 4);
+            }
+            int32_t S = 0, M = 0;
+            for (int c = 0; c < 4; c++) {
+                int32_t lo = 0, hi = 0;
+                for (int i = 0; i < 32; i++) {
+                    uint8_t v = blk[16 + 32 * c + i];
+                    lo += (int32_t)(v & 15) * y[64 * c + i];
+                    hi += (int32_t)(v >> 4) * y[64 * c + 32 + i];
+                }
+                S += sc[2 * c] * lo + sc[2 * c + 1] * hi;
+            }
+            for (int j = 0; j < 8; j++) M += m[j] * (int32_t)xs[8 * b + j];
+            tot = fmaf((float)S, d * dx, tot);
+            off = fmaf((float)M, dmin * dx, off);
+            continue;
+        }
+        const uint8_t *blk = row + 210 * b;
+        if (!f16_finite(blk + 208)) return 0;
+        float d = mo_f16_to_f32(le16(blk + 208));
+        int32_t S = 0;
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+            const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);
+            const int8_t *yh = y + 128 * h;
+            for (int l = 0; l < 32; l++) {
+                int is = l / 16;
+                int32_t q1 = (int32_t)((ql[l] & 0xF) | ((qh[l] & 3) << 4)) - 32;
+                int32_t q2 = (int32_t)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                int32_t q3 = (int32_t)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                int32_t q4 = (int32_t)((ql[l + 32] >> 4) | ((qh[l] >> 6) << 4)) - 32;
+                S += sc[is] * q1 * yh[l] + sc[is + 2] * q2 * yh[l + 32] + sc[is + 4] * q3 * yh[l + 64] +
+                     sc[is + 6] * q4 * yh[l + 96];
+            }
+        }
+        tot = fmaf((float)S, d * dx, tot);
+    }
+    *out = tot - off;
+    return 1;
+}
+
+float mo_dot_f32(const float *a, const float *b, int64_t n) {
+    float s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    int64_t i = 0;
+    for (; i + 4 <= n; i += 4) {
+        s0 += a[i] * b[i];
+        s1 += a[i + 1] * b[i + 1];
+        s2 += a[i + 2] * b[i + 2];
+        s3 += a[i + 3] * b[i + 3];
+    }
+    for (; i < n; i++) s0 += a[i] * b[i];
+    return (s0 + s1) + (s2 + s3);
+}
+
+/* ------------------------------------------------------------------ */
+/* matrix products                                                      */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    const float *x; int64_t rows, k; int dt; const uint8_t *w; int64_t n; const float *bias; float *y;
+    int block;
+    /* a8 state */
+    const int8_t *q; const float *d32; const int16_t *xs; const uint8_t *quantized;
+} mm_ctx;
+
+/* linearCols, interp/fast.go:180-196 (purego RowDot: decode, then dotF32Go) */
+static void mm_f32_cols(void *p, int64_t lo, int64_t hi) {
+    mm_ctx *c = (mm_ctx *)p;
+    int64_t rb = mo_row_bytes(c->dt, c->k);
+    float *buf = (float *)malloc(sizeof(float) * (size_t)(c->k ? c->k : 1));
+    for (int64_t j = lo; j < hi; j++) {
+        mo_dequantize(c->dt, c->w + j * rb, buf, c->k);
+        for (int64_t i = 0; i < c->rows; i++) {
+            float s = mo_dot_f32(c->x + i * c->k, buf, c->k);
+            if (c->bias) s += c->bias[j];
+            c->y[i * c->n + j] = s;
+        }
+    }
+    free(buf);
+}
+
+int mo_dequant_matmul(const float *x, int64_t rows, int64_t k, int dt, const uint8_t *w, int64_t n,
+                      const float *bias, float *y, int nthreads) {
+    if (mo_row_bytes(dt, k) == 0 && k != 0) return -1;
+    mm_ctx c = {x, rows, k, dt, w, n, bias, y, 0, NULL, NULL, NULL, NULL};
+    parallel_for(n, nthreads, mm_f32_cols, &c);
+    return 0;
+}
+
+/* linearA8's loop over weight rows, interp/fast.go:324-377: the 8-bit
+ * kernel for quantized rows, the f32 kernel for rows it refuses and for the
+ * whole weight row once a block scale is found not finite. */
+static void mm_a8_cols(void *p, int64_t lo, int64_t hi) {
+    mm_ctx *c = (mm_ctx *)p;
+    int64_t rb = mo_row_bytes(c->dt, c->k);
+    float *buf = (float *)malloc(sizeof(float) * (size_t)c->k);
+    for (int64_t j = lo; j < hi; j++) {
+        const uint8_t *row = c->w + j * rb;
+        int q8 = 1, loaded = 0;
+        for (int64_t i = 0; i < c->rows; i++) {
+            float s = 0;
+            if (q8 && c->quantized[i])
+                q8 = mo_dot_q8k_ref(c->dt, row, c->q + i * c->k, c->d32 + i * (c->k / 32), c->xs + i * (c->k / 32), c->k, &s);
+            if (!q8 || !c->quantized[i]) {
+                if (!loaded) { mo_dequantize(c->dt, row, buf, c->k); loaded = 1; }
+                s = mo_dot_f32(c->x + i * c->k, buf, c->k);
+            }
+            if (c->bias) s += c->bias[j];
+            c->y[i * c->n + j] = s;
+        }
+    }
+    free(buf);
+}
+
+typedef struct { const float *x; int64_t k; int block; int8_t *q; float *d32; int16_t *xs; uint8_t *ok; } q8_ctx;
+
+static void q8_rows(void *p, int64_t lo, int64_t hi) {
+    q8_ctx *c = (q8_ctx *)p;
+    for (int64_t i = lo; i < hi; i++)
+        c->ok[i] = (uint8_t)mo_q8_quantize(c->x + i * c->k, c->k, c->block, c->q + i * c->k, c->d32 + i * (c->k / 32),
+                                           c->xs + i * (c->k / 32), NULL);
+}
+
+int mo_dequant_matmul_a8(const float *x, int64_t rows, int64_t k, int dt, const uint8_t *w, int64_t n,
+                         const float *bias, int block, float *y, int nthreads) {
+    if (block != 32 && block != 256) return -1;
+    /* FusedQ8Blocks(dt, 256) holds for Q4_K and Q6_K only (q8.go:104-115);
+     * everything else is the exact f32 product. */
+    if (block != 256 || (dt != MO_Q4_K && dt != MO_Q6_K) || k == 0)
+        return mo_dequant_matmul(x, rows, k, dt, w, n, bias, y, nthreads);
+    if (k % 256) return -1;
+    int8_t *q = (int8_t *)malloc((size_t)(rows * k));
+    float *d32 = (float *)malloc(sizeof(float) * (size_t)(rows * k / 32));
+    int16_t *xs = (int16_t *)malloc(sizeof(int16_t) * (size_t)(rows * k / 32));
+    uint8_t *ok = (uint8_t *)malloc((size_t)rows + 1);
+    q8_ctx qc = {x, k, block, q, d32, xs, ok};
+    parallel_for(rows, nthreads, q8_rows, &qc);
+    mm_ctx c = {x, rows, k, dt, w, n, bias, y, block, q, d32, xs, ok};
+    parallel_for(n, nthreads, mm_a8_cols, &c);
+    free(q); free(d32); free(xs); free(ok);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* per-token operators                                                  */
+/* ------------------------------------------------------------------ */
+
+void mo_rms_norm(const float *x, int64_t rows, int64_t n, const float *scale, double eps, float *y) {
+    if (n == 0) return;
+    float epsf = (float)eps;
+    for (int64_t r = 0; r < rows; r++) {
+        const float *src = x + r * n;
+        float *row = y + r * n;
+        double ss = 0;
+        for (int64_t j = 0; j < n; j++) ss += (double)src[j] * (double)src[j];
+        float inv = (float)(1.0 / sqrt((double)(float)(ss / (double)n) + (double)epsf));
+        for (int64_t j = 0; j < n; j++) {
+            float v = src[j] * inv;
+            if (scale) v = v * scale[j];
+            row[j] = v;
+        }
+    }
+}
+
+int mo_rope(const float *x, int B, int H, int T, int D, const int64_t *pos, int pos_rows, double theta,
+            int rotary, int interleaved, float *y) {
+    if (rotary <= 0 || rotary % 2 || rotary > D) return -1;
+    int h = rotary / 2;
+    double *inv = (double *)malloc(sizeof(double) * (size_t)h);
+    float *cs = (float *)malloc(sizeof(float) * 2 * (size_t)h);
+    for (int i = 0; i < h; i++) inv[i] = pow(theta, -2.0 * (double)i / (double)rotary);
+    for (int b = 0; b < B; b++)
+        for (int t = 0; t < T; t++) {
+            int pb = pos_rows != 1 ? b : 0;
+            double pp = (double)pos[pb * T + t];
+            for (int i = 0; i < h; i++) {
+                double ang = pp * inv[i];
+                cs[2 * i] = (float)(cos(ang) * 1.0);
+                cs[2 * i + 1] = (float)(sin(ang) * 1.0);
+            }
+            for (int hd = 0; hd < H; hd++) {
+                int64_t at = (((int64_t)b * H + hd) * T + t) * D;
+                const float *src = x + at;
+                float *row = y + at;
+                memcpy(row, src, sizeof(float) * (size_t)D);
+                for (int i = 0; i < h; i++) {
+                    int i1 = interleaved ? 2 * i : i, i2 = interleaved ? 2 * i + 1 : i + h;
+                    float x1 = src[i1], x2 = src[i2], c = cs[2 * i], s = cs[2 * i + 1];
+                    row[i1] = x1 * c - x2 * s;
+                    row[i2] = x2 * c + x1 * s;
+                }
+            }
+        }
+    free(inv); free(cs);
+    return 0;
+}
+
+/* one key/value row as f32 (f16 converts exactly) */
+static const float *kv_row(const void *base, int dt, int64_t j, int d, float *buf) {
+    if (dt == MO_F32) return (const float *)base + j * d;
+    const uint8_t *p = (const uint8_t *)base + 2 * j * d;
+    for (int i = 0; i < d; i++) buf[i] = mo_f16_to_f32(le16(p + 2 * i));
+    return buf;
+}
+
+/* attendRow, interp/fast.go:728-751, with the plain-Go kernels of attn.go.
+ * Returns 0 (caller takes the scalar path) when the largest score is not finite. */
+static int attend_row(const float *q, const void *kb, const void *vb, int dt, int64_t st, int64_t n, int d,
+                      float scale, float *sc, float *acc, float *o, float *buf) {
+    for (int64_t j = 0; j < n; j++) sc[j] = mo_dot_f32(q, kv_row(kb, dt, st + j, d, buf), d) * scale;
+    float mx = -INFINITY;
+    for (int64_t j = 0; j < n; j++) if (sc[j] > mx || sc[j] != sc[j]) mx = sc[j];
+    if (isinf(mx) || mx != mx) return 0;
+    float sum = 0;
+    for (int64_t j = 0; j < n; j++) { float e = (float)exp((double)(sc[j] - mx)); sc[j] = e; sum += e; }
+    for (int i = 0; i < d; i++) acc[i] = 0;
+    for (int64_t j = 0; j < n; j++) {
+        const float *vr = kv_row(vb, dt, st + j, d, buf);
+        for (int i = 0; i < d; i++) acc[i] += sc[j] * vr[i];
+    }
+    for (int i = 0; i < d; i++) o[i] = acc[i] / sum;
+    return 1;
+}
+
+int mo_attention(const float *q, int B, int Hq, int Tq, int D, const void *k, const void *v, int kv_dtype,
+                 int Hkv, int Tk, const uint8_t *mask, const int *mask_shape, double scale_d, int causal,
+                 float *out) {
+    if (Hkv <= 0 || Hq % Hkv) return -1;
+    if (kv_dtype != MO_F32 && kv_dtype != MO_F16) return -1;
+    int G = Hq / Hkv;
+    float scale = (float)scale_d;
+    int64_t mst[4] = {0, 0, 0, 0};
+    if (mask) {
+        int64_t acc = 1;
+        for (int i = 3; i >= 0; i--) { if (mask_shape[i] != 1) mst[i] = acc; acc *= mask_shape[i]; }
+    }
+    int esz = kv_dtype == MO_F32 ? 4 : 2;
+    float *sc = (float *)malloc(sizeof(float) * (size_t)(Tk ? Tk : 1));
+    float *acc = (float *)malloc(sizeof(float) * (size_t)D);
+    float *buf = (float *)malloc(sizeof(float) * (size_t)D);
+    int rows_in_order = !mask || mst[3] == 1;
+    for (int b = 0; b < B; b++)
+        for (int h = 0; h < Hq; h++) {
+            int kvh = b * Hkv + h / G;
+            const uint8_t *kb = (const uint8_t *)k + (int64_t)kvh * Tk * D * esz;
+            const uint8_t *vb = (const uint8_t *)v + (int64_t)kvh * Tk * D * esz;
+            for (int i = 0; i < Tq; i++) {
+                const float *qi = q + (((int64_t)b * Hq + h) * Tq + i) * D;
+                float *o = out + (((int64_t)b * Hq + h) * Tq + i) * D;
+                const uint8_t *mrow = mask ? mask + b * mst[0] + h * mst[1] + i * mst[2] : NULL;
+                int64_t end = Tk, st = 0;
+                if (mask && rows_in_order) {
+                    /* ends/starts of a boolean mask row, interp/fast.go:606-636 */
+                    end = Tk;
+                    while (end > 0 && mrow[end - 1] == 0) end--;
+                    while (st < end && mrow[st] == 0) st++;
+                }
+                if (causal) { int64_t lim = i + (Tk - Tq) + 1; if (lim < end) end = lim; if (end < 0) end = 0; }
+                if (rows_in_order && st < end) {
+                    int hole = 0;
+                    if (mask) for (int64_t j = st; j < end; j++) if (mrow[j] == 0) { hole = 1; break; }
+                    if (!hole && attend_row(qi, kb, vb, kv_dtype, st, end - st, D, scale, sc, acc, o, buf)) continue;
+                }
+                /* scalar path, interp/fast.go:661-716 */
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < end; j++) {
+                    float s = -INFINITY;
+                    int allowed = !causal || j <= i + (Tk - Tq);
+                    if (mask) allowed = allowed && mrow[j * mst[3]] != 0;
+                    if (allowed) s = mo_dot_f32(qi, kv_row(kb, kv_dtype, j, D, buf), D) * scale + 0.0f;
+                    sc[j] = s;
+                    if (s > mx || s != s) mx = s;
+                }
+                float sum = 0;
+                for (int64_t j = 0; j < end; j++) {
+                    if (isinf(sc[j]) && sc[j] < 0 && !(isinf(mx) && mx < 0)) { sc[j] = 0; continue; }
+                    float e = (float)exp((double)(sc[j] - mx));
+                    sc[j] = e;
+                    sum += e;
+                }
+                for (int d = 0; d < D; d++) acc[d] = 0;
+                for (int64_t j = 0; j < end; j++) {
+                    if (sc[j] == 0) continue;
+                    const float *vr = kv_row(vb, kv_dtype, j, D, buf);
+                    for (int d = 0; d < D; d++) acc[d] += sc[j] * vr[d];
+                }
+                for (int d = 0; d < D; d++) o[d] = acc[d] / sum;
+            }
+        }
+    free(sc); free(acc); free(buf);
+    return 0;
+}
+
+void mo_swiglu(const float *a, const float *b, int64_t n, float *y) {
+    for (int64_t i = 0; i < n; i++) y[i] = (float)((double)a[i] / (1.0 + exp(-(double)a[i])) * (double)b[i]);
+}
+
+int mo_embedding(int dt, const uint8_t *table, int64_t V, int64_t E, const int32_t *ids, int64_t n, float *y) {
+    int64_t rb = mo_row_bytes(dt, E);
+    if (rb == 0) return -1;
+    for (int64_t i = 0; i < n; i++) {
+        int64_t id = ids[i];
+        if (id >= 0 && id < V) mo_dequantize(dt, table + id * rb, y + i * E, E);
+        else memset(y + i * E, 0, sizeof(float) * (size_t)E);
+    }
+    return 0;
+}
+
+int32_t mo_argmax(const float *v, int64_t n) {
+    int64_t best = 0;
+    for (int64_t i = 0; i < n; i++) if (v[i] > v[best]) best = i;
+    return (int32_t)best;
+}
+
+/* ------------------------------------------------------------------ */
+/* llama graph, importer/llama.go:400-534                               */
+/* ------------------------------------------------------------------ */
+
+typedef struct { int dt; const uint8_t *p; } wref;
+typedef struct { wref attn_norm, q, k, v, o, ffn_norm, gate, up, down; void *ck, *cv; } layer_w;
+
+struct mo_llama {
+    mo_llama_config c;
+    wref embd, out_norm, out;
+    layer_w *L;
+};
+
+mo_llama *mo_llama_new(const mo_llama_config *c) {
+    if (c->layers <= 0 || c->heads <= 0 || c->kv_heads <= 0 || c->heads % c->kv_heads) return NULL;
+    mo_llama *m = (mo_llama *)calloc(1, sizeof(mo_llama));
+    m->c = *c;
+    if (m->c.nthreads <= 0) m->c.nthreads = 1;
+    m->L = (layer_w *)calloc((size_t)c->layers, sizeof(layer_w));
+    size_t cache = (size_t)c->kv_heads * c->context * c->head_dim * (c->cache_f16 ? 2 : 4);
+    for (int l = 0; l < c->layers; l++) { m->L[l].ck = calloc(1, cache); m->L[l].cv = calloc(1, cache); }
+    return m;
+}
+
+void mo_llama_free(mo_llama *m) {
+    if (!m) return;
+    for (int l = 0; l < m->c.layers; l++) { free(m->L[l].ck); free(m->L[l].cv); }
+    free(m->L);
+    free(m);
+}
+
+void mo_llama_reset(mo_llama *m) {
+    size_t cache = (size_t)m->c.kv_heads * m->c.context * m->c.head_dim * (m->c.cache_f16 ? 2 : 4);
+    for (int l = 0; l < m->c.layers; l++) { memset(m->L[l].ck, 0, cache); memset(m->L[l].cv, 0, cache); }
+}
+
+int mo_llama_set_weight(mo_llama *m, const char *name, int dt, const void *data) {
+    wref w = {dt, (const uint8_t *)data};
+    if (!strcmp(name, "token_embd.weight")) { m->embd = w; return 0; }
+    if (!strcmp(name, "output_norm.weight")) { m->out_norm = w; return 0; }
+    if (!strcmp(name, "output.weight")) { m->out = w; return 0; }
+    int l = 0, used = 0;
+    char rest[64];
+    if (sscanf(name, "blk.%d.%63s%n", &l, rest, &used) != 2 || l < 0 || l >= m->c.layers) return -1;
+    layer_w *L = &m->L[l];
+    if (!strcmp(rest, "attn_norm.weight")) L->attn_norm = w;
+    else if (!strcmp(rest, "attn_q.weight")) L->q = w;
+    else if (!strcmp(rest, "attn_k.weight")) L->k = w;
+    else if (!strcmp(rest, "attn_v.weight")) L->v = w;
+    else if (!strcmp(rest, "attn_output.weight")) L->o = w;
+    else if (!strcmp(rest, "ffn_norm.weight")) L->ffn_norm = w;
+    else if (!strcmp(rest, "ffn_gate.weight")) L->gate = w;
+    else if (!strcmp(rest, "ffn_up.weight")) L->up = w;
+    else if (!strcmp(rest, "ffn_down.weight")) L->down = w;
+    else return -1;
+    return 0;
+}
+
+/* matmulBias, importer/llama.go:264-280: a8.v2 block 256 for K-quants when a8 */
+static int mm(mo_llama *m, const float *x, int64_t rows, int64_t k, wref w, int64_t n, float *y) {
+    if (!w.p) return -1;
+    if (m->c.a8) return mo_dequant_matmul_a8(x, rows, k, w.dt, w.p, n, NULL, 256, y, m->c.nthreads);
+    return mo_dequant_matmul(x, rows, k, w.dt, w.p, n, NULL, y, m->c.nthreads);
+}
+
+int mo_llama_forward(mo_llama *m, const int32_t *tokens, const int64_t *positions, int T, float *logits, int all_rows) {
+    const mo_llama_config *c = &m->c;
+    int E = c->embed, H = c->heads, Hkv = c->kv_heads, D = c->head_dim, F = c->ffn, C = c->context;
+    int64_t KV = (int64_t)Hkv * D;
+    if (!m->embd.p || !m->out_norm.p) return -1;
+    for (int t = 0; t < T; t++) if (positions[t] < 0 || positions[t] >= C) return -1;
+    float *x = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *h = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *q = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *kk = (float *)malloc(sizeof(float) * (size_t)T * KV);
+    float *vv = (float *)malloc(sizeof(float) * (size_t)T * KV);
+    float *qh = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *kh = (float *)malloc(sizeof(float) * (size_t)T * KV);
+    float *vh = (float *)malloc(sizeof(float) * (size_t)T * KV);
+    float *att = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *o = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *g = (float *)malloc(sizeof(float) * (size_t)T * F);
+    float *u = (float *)malloc(sizeof(float) * (size_t)T * F);
+    float *a = (float *)malloc(sizeof(float) * (size_t)T * F);
+    uint8_t *mask = (uint8_t *)malloc((size_t)T * C);
+    int rc = 0;
+    mo_embedding(m->embd.dt, m->embd.p, c->vocab, E, tokens, T, x);
+    for (int t = 0; t < T; t++)
+        for (int j = 0; j < C; j++) mask[(int64_t)t * C + j] = (uint8_t)(j <= positions[t]);
+    int mshape[4] = {1, 1, T, C};
+    int esz = c->cache_f16 ? 2 : 4;
+    for (int l = 0; l < c->layers && rc == 0; l++) {
+        layer_w *L = &m->L[l];
+        mo_rms_norm(x, T, E, (const float *)L->attn_norm.p, c->norm_eps, h);
+        rc |= mm(m, h, T, E, L->q, E, q);
+        rc |= mm(m, h, T, E, L->k, KV, kk);
+        rc |= mm(m, h, T, E, L->v, KV, vv);
+        /* [1,T,n,D] -> [1,n,T,D] */
+        for (int t = 0; t < T; t++)
+            for (int hd = 0; hd < H; hd++)
+                memcpy(qh + ((int64_t)hd * T + t) * D, q + (int64_t)t * E + (int64_t)hd * D, sizeof(float) * D);
+        for (int t = 0; t < T; t++)
+            for (int hd = 0; hd < Hkv; hd++) {
+                memcpy(kh + ((int64_t)hd * T + t) * D, kk + (int64_t)t * KV + (int64_t)hd * D, sizeof(float) * D);
+                memcpy(vh + ((int64_t)hd * T + t) * D, vv + (int64_t)t * KV + (int64_t)hd * D, sizeof(float) * D);
+            }
+        mo_rope(qh, 1, H, T, D, positions, 1, c->rope_theta, c->rope_dims, c->interleaved, q);
+        mo_rope(kh, 1, Hkv, T, D, positions, 1, c->rope_theta, c->rope_dims, c->interleaved, kk);
+        /* cast (f16 cache) and scatter at the positions, interp/prim.go:76-96, 278 */
+        for (int hd = 0; hd < Hkv; hd++)
+            for (int t = 0; t < T; t++) {
+                const float *kr = kk + ((int64_t)hd * T + t) * D, *vr = vh + ((int64_t)hd * T + t) * D;
+                int64_t at = ((int64_t)hd * C + positions[t]) * D;
+                if (esz == 2) {
+                    mo_cast_f16(kr, (uint16_t *)L->ck + at, D);
+                    mo_cast_f16(vr, (uint16_t *)L->cv + at, D);
+                } else {
+                    memcpy((float *)L->ck + at, kr, sizeof(float) * D);
+                    memcpy((float *)L->cv + at, vr, sizeof(float) * D);
+                }
+            }
+        mo_attention(q, 1, H, T, D, L->ck, L->cv, c->cache_f16 ? MO_F16 : MO_F32, Hkv, C, mask, mshape,
+                     1.0 / sqrt((double)D), 0, att);
+        for (int t = 0; t < T; t++)
+            for (int hd = 0; hd < H; hd++)
+                memcpy(o + (int64_t)t * E + (int64_t)hd * D, att + ((int64_t)hd * T + t) * D, sizeof(float) * D);
+        rc |= mm(m, o, T, E, L->o, E, h);
+        for (int64_t i = 0; i < (int64_t)T * E; i++) x[i] = x[i] + h[i];
+        mo_rms_norm(x, T, E, (const float *)L->ffn_norm.p, c->norm_eps, h);
+        rc |= mm(m, h, T, E, L->gate, F, g);
+        rc |= mm(m, h, T, E, L->up, F, u);
+        mo_swiglu(g, u, (int64_t)T * F, a);
+        rc |= mm(m, a, T, F, L->down, E, h);
+        for (int64_t i = 0; i < (int64_t)T * E; i++) x[i] = x[i] + h[i];
+    }
+    if (rc == 0) {
+        wref head = m->out.p ? m->out : m->embd; /* tied embeddings when output.weight is absent */
+        int first = all_rows ? 0 : T - 1;
+        mo_rms_norm(x + (int64_t)first * E, T - first, E, (const float *)m->out_norm.p, c->norm_eps, h);
+        rc |= mm(m, h, T - first, E, head, c->vocab, logits);
+    }
+    free(x); free(h); free(q); free(kk); free(vv); free(qh); free(kh); free(vh); free(att); free(o);
+    free(g); free(u); free(a); free(mask);
+    return rc ? -1 : 0;
+}
