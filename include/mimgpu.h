@@ -1,0 +1,208 @@
+/*
+ * mimgpu.h -- C ABI of the B200 (sm_100a) backend for mimir-model's
+ * quantized decode hot path.
+ *
+ * The Go interpreter of gsoultan/mimir-model runs each `call` op through
+ * fastPaths[key](attrs, in, dts, shapes) (interp/fast.go:40-59), and those
+ * fast paths send the work to internal/kernels.  This library is what a cgo
+ * adapter with that signature calls instead.  The entry points below take
+ * plain pointers and sizes only; tensors keep the reference's layouts:
+ *
+ *   - weights: the byte-exact block layouts of spec/dtypes.md (Q8_0 = 64,
+ *     Q4_K = 66, Q6_K = 67; F32 = 1, F16 = 2), rows of K elements along the
+ *     last axis, W is [N, K] (spec/stdlib.md:216-228);
+ *   - activations: f32, row-major, last axis innermost;
+ *   - positions: int64; token ids: int32; masks: one byte per bool.
+ *
+ * Error convention (interp/fast.go:40, interp/interp.go:429-436): every
+ * function returns a status code and never aborts or throws across the ABI.
+ * MIMGPU_ENOTHANDLED is the fast path's handled=false (a dtype or shape this
+ * backend does not serve; the caller runs the canonical body); every other
+ * non-zero code is the fast path's err.  mimgpu_last_error() gives the text.
+ *
+ * Threading: a context may be used from several threads; calls on one
+ * context are serialised on its stream.  Weight handles are read-only and
+ * may be shared by sessions.  A session is used by one thread at a time.
+ */
+#ifndef MIMGPU_H
+#define MIMGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MIMGPU_ABI_VERSION 1
+
+enum {
+    MIMGPU_OK = 0,
+    MIMGPU_ENOTHANDLED = 1, /* not this backend's case: run the canonical body */
+    MIMGPU_EINVAL = 2,      /* malformed call (shapes, dtypes, attributes)   */
+    MIMGPU_ENOMEM = 3,      /* device memory exhausted                        */
+    MIMGPU_ECUDA = 4,       /* CUDA runtime error                             */
+    MIMGPU_ENCCL = 5,       /* NCCL error (tensor-parallel sessions)          */
+    MIMGPU_ETIMEOUT = 6     /* a bounded wait on the device expired           */
+};
+
+enum { MIMGPU_F32 = 1, MIMGPU_F16 = 2, MIMGPU_Q8_0 = 64, MIMGPU_Q4_K = 66, MIMGPU_Q6_K = 67 };
+
+typedef struct mimgpu_ctx mimgpu_ctx;
+typedef struct mimgpu_tensor mimgpu_tensor;
+typedef struct mimgpu_model mimgpu_model;
+typedef struct mimgpu_session mimgpu_session;
+
+/* ------------------------------------------------------------ context */
+
+/* ABI version of the loaded library (MIMGPU_ABI_VERSION). */
+int mimgpu_abi_version(void);
+
+/* Opens a context on CUDA device `device` with its own stream.  Replaces
+ * nothing in the reference (which has no device); the Go side opens one per
+ * Program (interp/interp.go:52-67). */
+int mimgpu_open(int device, mimgpu_ctx **out);
+void mimgpu_close(mimgpu_ctx *ctx);
+/* Text of the last error on this context ("" if none).  Valid until the
+ * next call on the context. */
+const char *mimgpu_last_error(mimgpu_ctx *ctx);
+/* Upper bound, in milliseconds, of every wait on the device (default 60000). */
+int mimgpu_set_timeout_ms(mimgpu_ctx *ctx, int64_t ms);
+
+/* ------------------------------------------------------------ weights */
+
+/* Uploads one weight tensor, byte for byte, into device memory.  Called at
+ * Open for each weight whose ref.Tensor.Data is a slice of the read-only
+ * mapping (interp/interp.go:101-121, file.go:394-399); `bytes` must be
+ * exactly the size shape x dtype implies (ref/tensor.go:51-70).  The caller
+ * keeps its mapping; the handle owns the device copy. */
+int mimgpu_upload(mimgpu_ctx *ctx, int dtype, int ndim, const int64_t *shape, const void *bytes, size_t nbytes,
+                  mimgpu_tensor **out);
+void mimgpu_tensor_free(mimgpu_tensor *t);
+/* Device address of the uploaded bytes (for callers that keep activations
+ * on the device). */
+const void *mimgpu_tensor_device_ptr(const mimgpu_tensor *t);
+
+/* ------------------------------------------- per-op fast paths (host I/O)
+ * Each mirrors one fastPaths entry of interp/fast.go:42-59: inputs and
+ * outputs are host buffers; outputs are written by the call. */
+
+/* Dequantize (quant.go:37-69): n elements of dtype from `src` (exactly the
+ * bytes they occupy) to f32, bit-exact. */
+int mimgpu_dequantize(mimgpu_ctx *ctx, int dtype, const void *src, size_t nbytes, float *dst, int64_t n);
+
+/* dequant_matmul.v1 (fastDequantMatmul, interp/fast.go:222-230):
+ * y[rows, N] = x[rows, K] W^T + bias, W decoded exactly; tolerance of
+ * spec/stdlib.md section 3.3.  bias may be NULL. */
+int mimgpu_dequant_matmul(mimgpu_ctx *ctx, const float *x, int64_t rows, int64_t k, const mimgpu_tensor *w,
+                          const float *bias, float *y);
+
+/* dequant_matmul_a8.v2 (fastDequantMatmulA8V2, interp/fast.go:232-244) with
+ * its `block` attribute (32 or 256; anything else is EINVAL as in
+ * a8Block, interp/transformer.go:201-214).  With block 256 and Q4_K/Q6_K
+ * weights the result is bit-identical to the reference's 8-bit kernels
+ * (internal/kernels/q8k_test.go:35-117), rows it refuses taking the f32
+ * product (interp/fast.go:282-379); other cases are the exact v1 product. */
+int mimgpu_dequant_matmul_a8(mimgpu_ctx *ctx, int block, const float *x, int64_t rows, int64_t k,
+                             const mimgpu_tensor *w, const float *bias, float *y);
+
+/* rms_norm.v1 over the last axis (fastRMSNorm, interp/fast.go:434-485). */
+int mimgpu_rms_norm(mimgpu_ctx *ctx, const float *x, int64_t rows, int64_t n, const float *scale, double eps,
+                    float *y);
+
+/* rope.v1 (fastRope, interp/fast.go:507-557) on x [B,H,T,D] with positions
+ * [pos_rows, T] (pos_rows 1 or B); YaRN attributes are not served
+ * (ENOTHANDLED). */
+int mimgpu_rope(mimgpu_ctx *ctx, const float *x, int b, int h, int t, int d, const int64_t *pos, int pos_rows,
+                double theta, int rotary_dims, int interleaved, float *y);
+
+/* attention.v1 / v2 (attentionFast, interp/fast.go:569-751): q f32
+ * [B,Hq,Tq,D]; k, v [B,Hkv,Tk,D] of kv_dtype F32 or F16; optional boolean
+ * mask (one byte per element) of shape mask_shape[4], each axis 1 or full.
+ * scale <= 0 means 1/sqrt(D).  Float masks and softcap are ENOTHANDLED. */
+int mimgpu_attention(mimgpu_ctx *ctx, const float *q, int b, int hq, int tq, int d, const void *k, const void *v,
+                     int kv_dtype, int hkv, int tk, const uint8_t *mask, const int *mask_shape, double scale,
+                     int causal, float *out);
+
+/* swiglu.v1 (fastSwiglu, interp/fast.go:487-498): y = silu(a) * b. */
+int mimgpu_swiglu(mimgpu_ctx *ctx, const float *a, const float *b, int64_t n, float *y);
+
+/* embedding.v1 (fastEmbedding, interp/fast.go:818-842): decoded rows of
+ * `table` for n int32 ids; out-of-range ids give zero rows. */
+int mimgpu_embedding(mimgpu_ctx *ctx, const mimgpu_tensor *table, const int32_t *ids, int64_t n, float *y);
+
+/* ------------------------------- device-resident products (no host copies)
+ * Same arithmetic as the host-buffer calls; all pointers are device memory
+ * and the work is queued on `stream` (a cudaStream_t, NULL = the context's
+ * stream) without waiting.  Used by callers that keep activations in HBM. */
+int mimgpu_dequant_matmul_a8_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
+                                 const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
+int mimgpu_dequant_matmul_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
+                              const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
+
+/* ------------------------------------------ 8-bit activations on the device
+ * Rows of activations quantized once and multiplied by several weights, as
+ * linearA8 does with a Q8Batch (interp/fast.go:282-379, internal/kernels/
+ * q8.go:154-201).  Blocks of 256 (dequant_matmul_a8.v2, block = 256). */
+typedef struct mimgpu_q8 mimgpu_q8;
+int mimgpu_q8_new(mimgpu_ctx *ctx, int64_t rows, int64_t k, mimgpu_q8 **out);
+void mimgpu_q8_free(mimgpu_q8 *q);
+/* QuantizeBlocks (q8.go:50-97) of rows x k f32 device values; rows the
+ * reference refuses are flagged and later take the f32 product. */
+int mimgpu_q8_quantize_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, mimgpu_q8 *q);
+/* y = x W^T (+ bias) from activations quantized by mimgpu_q8_quantize_dev
+ * (DotQ8 / DotQ8x4, q8.go:119-235); x_dev is the same f32 input, read only
+ * for refused rows.  W must be Q4_K or Q6_K. */
+int mimgpu_gemv_q8_dev(mimgpu_ctx *ctx, void *stream, const mimgpu_q8 *q, const float *x_dev,
+                       const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
+
+/* ------------------------------------------------ synthetic weights, bytes
+ * Not part of the reference interface: seeded random-init weights for the
+ * benchmark configurations, made on the device (values from N(mean, sigma)
+ * by a counter-based generator, encoded as dtype), and a copy of a tensor's
+ * bytes back to the host. */
+int mimgpu_synth_tensor(mimgpu_ctx *ctx, int dtype, uint64_t seed, int ndim, const int64_t *shape, float mean,
+                        float sigma, mimgpu_tensor **out);
+int mimgpu_tensor_download(const mimgpu_tensor *t, void *bytes, size_t nbytes);
+size_t mimgpu_tensor_nbytes(const mimgpu_tensor *t);
+
+/* ----------------------------------------- whole-step decoder (sessions)
+ * The llama graph of importer/llama.go:317-547 run as one device-resident
+ * step per Session.Run (interp/interp.go:409-526): activations and the
+ * key-value cache stay in HBM; only token ids, positions and the logits (or
+ * the greedy id) cross the bus. */
+typedef struct {
+    int layers, embed, ffn, heads, kv_heads, head_dim, rope_dims, vocab;
+    int context;      /* key-value cache length C per sequence */
+    double rope_theta, norm_eps;
+    int a8;           /* 1: dequant_matmul_a8.v2 block 256 for Q4_K/Q6_K weights */
+    int cache_f16;    /* 1: f16 cache (attention.v2); 0: f32 cache (attention.v1) */
+    int interleaved;  /* rope pairs: 1 adjacent (llama), 0 halves (qwen2) */
+    int max_tokens;   /* largest T of one run (prompt length) */
+} mimgpu_llama_config;
+
+int mimgpu_model_new(mimgpu_ctx *ctx, const mimgpu_llama_config *cfg, mimgpu_model **out);
+/* Binds an uploaded weight by its GGUF name (token_embd.weight,
+ * blk.N.attn_q.weight, ..., output_norm.weight, output.weight).  The
+ * model keeps the handle; it must outlive the model. */
+int mimgpu_model_set_weight(mimgpu_model *m, const char *name, const mimgpu_tensor *w);
+void mimgpu_model_free(mimgpu_model *m);
+
+int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out);
+void mimgpu_session_free(mimgpu_session *s);
+/* Zeroes the key-value cache (a fresh Session). */
+int mimgpu_session_reset(mimgpu_session *s);
+/* One run of the graph: T tokens at the given positions, logits [T, vocab]
+ * (all_rows) or the last row's [vocab] into host memory, as
+ * cmd/mim-run/main.go:133-174 reads them. */
+int mimgpu_session_run(mimgpu_session *s, const int32_t *tokens, const int64_t *positions, int t, float *logits,
+                       int all_rows);
+/* Greedy decode (cmd/mim-run/main.go:219-257): feeds `token` at `pos`, picks
+ * the first maximum of the logits, feeds it back, `steps` times; writes the
+ * picked ids.  One step is one device-resident graph launch. */
+int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int steps, int32_t *ids_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MIMGPU_H */

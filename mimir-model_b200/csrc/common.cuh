@@ -1,0 +1,200 @@
+// common.cuh -- device helpers shared by the sm_100a kernels of libmimgpu.
+//
+// Bit-exact scalar conversions (float.go:24-88 of gsoultan/mimir-model),
+// block-format constants (spec/dtypes.md:124-135), the mbarrier / bulk-copy
+// PTX used by the staged GEMV, and bounded waits that report a timeout
+// instead of spinning forever.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mimgpu {
+
+enum DType : int { F32 = 1, F16 = 2, Q8_0 = 64, Q4_K = 66, Q6_K = 67 };
+
+// Error bits a kernel may set in the context's device status word.
+enum DevStatus : unsigned { DEV_TIMEOUT = 1u, DEV_BADARG = 2u };
+
+__host__ __device__ inline int block_elems(int dt) {
+    return dt == Q4_K || dt == Q6_K ? 256 : dt == Q8_0 ? 32 : 1;
+}
+__host__ __device__ inline int block_bytes(int dt) {
+    return dt == Q4_K ? 144 : dt == Q6_K ? 210 : dt == Q8_0 ? 34 : dt == F16 ? 2 : 4;
+}
+__host__ __device__ inline long long row_bytes(int dt, long long k) {
+    int be = block_elems(dt);
+    if (k % be) return 0;
+    return k / be * block_bytes(dt);
+}
+
+// ---------------------------------------------------------------- f16 bits
+// f16 -> f32 exactly, including subnormals, infinities and NaN payloads
+// (F16ToF32, float.go:24-43).  Written with integer ops so the NaN payload
+// is kept bit for bit.
+__device__ __forceinline__ float f16_to_f32(uint32_t h) {
+    uint32_t sign = (h & 0x8000u) << 16, exp = (h >> 10) & 0x1Fu, mant = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0x1F) {
+        bits = sign | 0x7F800000u | (mant << 13);
+    } else if (exp != 0) {
+        bits = sign | ((exp + 112u) << 23) | (mant << 13);
+    } else if (mant == 0) {
+        bits = sign;
+    } else {
+        // subnormal: mant * 2^-24; normalise with a count of leading zeros
+        int lz = __clz(mant) - 21;  // leading zeros within the 11-bit field
+        mant = (mant << lz) & 0x3FFu;
+        bits = sign | ((uint32_t)(113 - lz) << 23) | (mant << 13);
+    }
+    return __uint_as_float(bits);
+}
+
+// f32 -> f16 with round to nearest even; NaN stays a quiet NaN with the top
+// payload bits (F32ToF16, float.go:49-82).
+__device__ __forceinline__ uint16_t f32_to_f16(float f) {
+    uint32_t b = __float_as_uint(f);
+    uint32_t sign = (b >> 16) & 0x8000u;
+    int exp = (int)((b >> 23) & 0xFF);
+    uint32_t mant = b & 0x7FFFFFu;
+    if (exp == 0xFF) return (uint16_t)(mant ? (sign | 0x7E00u | (mant >> 13)) : (sign | 0x7C00u));
+    int e = exp - 127 + 15;
+    if (e >= 0x1F) return (uint16_t)(sign | 0x7C00u);
+    if (e <= 0) {
+        if (e < -11) return (uint16_t)sign;
+        mant |= 0x800000u;
+        uint32_t shift = (uint32_t)(14 - e);
+        uint32_t half = 1u << (shift - 1);
+        uint32_t rem = mant & ((half << 1) - 1);
+        uint32_t q = mant >> shift;
+        if (rem > half || (rem == half && (q & 1u))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)e << 10) | (mant >> 13);
+    uint32_t rem = mant & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+}
+
+__device__ __forceinline__ bool f16_finite(uint32_t h) { return (h & 0x7C00u) != 0x7C00u; }
+
+// Q4_K sub-block scale and min j (0..7) from the 12 packed bytes
+// (getScaleMinK4, quant.go:246-254).  `s` holds the 12 bytes as 3 words.
+__device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &m) {
+    auto byte = [&](int i) -> int { return (int)((s[i >> 2] >> ((i & 3) * 8)) & 0xFFu); };
+    if (j < 4) {
+        sc = byte(j) & 63;
+        m = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
+        m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+}
+
+// ------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with the given parity to complete.  Gives up after
+// `limit_ns` nanoseconds of wall time (2 s by default), sets DEV_TIMEOUT in
+// *status and returns false, so a lost arrival ends the kernel with an error
+// the host reads instead of a hang.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *status,
+                                                  uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0 && global_ns() - t0 > limit_ns) break;
+    }
+    if (status) atomicOr(status, (unsigned)DEV_TIMEOUT);
+    return false;
+}
+
+// One-dimensional bulk copy global -> shared, completing on `bar`.  Both
+// addresses must be 16-byte aligned and `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Streaming 128-bit global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Four bytes starting at a byte address that may be unaligned, read from
+// shared memory as two aligned words.
+__device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t *p) {
+    uintptr_t a = (uintptr_t)p;
+    const uint32_t *w = (const uint32_t *)(a & ~(uintptr_t)3);
+    uint32_t sh = (uint32_t)(a & 3) * 8;
+    uint32_t lo = w[0];
+    if (sh == 0) return lo;
+    return __funnelshift_r(lo, w[1], sh);
+}
+
+// Programmatic dependent launch: wait for the grid this one depends on, and
+// signal that dependents may start their prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace mimgpu

@@ -1,0 +1,333 @@
+// k_ops.cu -- per-token operators of the llama decode step on sm_100a.
+//
+// References (gsoultan/mimir-model):
+//   rms_norm   interp/fast.go:434-485   float64 sum of squares, mean rounded
+//              to f32, inv = f32(1/sqrt(mean + eps)), y = (x*inv)*scale with
+//              two f32 roundings.
+//   rope       interp/fast.go:507-557   cos/sin of pos*inv_freq in float64,
+//              rounded to f32; y1 = x1*c - x2*s, y2 = x2*c + x1*s unfused.
+//   swiglu     internal/kernels/attn.go:63-73 (plain Go): float64 silu times
+//              b, rounded once.
+//   attention  interp/fast.go:569-751, internal/kernels/attn.go:26-121:
+//              visible keys from the boolean mask, softmax with exp of
+//              (s - max) in float64 rounded to f32, f16 keys and values
+//              converted exactly.
+//   argmax     cmd/mim-run/main.go:184-193: first index of the maximum.
+#include <cfloat>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mimgpu {
+
+namespace {
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, cudaLaunchAttribute *attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, int n, const float *__restrict__ scale,
+                                                      float eps, float *__restrict__ y) {
+    __shared__ double dred[8];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int row = blockIdx.x, t = threadIdx.x;
+    const float *xr = x + (long long)row * n;
+    double ss = 0;
+    for (int i = t; i < n; i += 256) {
+        const double e = (double)xr[i];
+        ss = __fma_rn(e, e, ss);
+    }
+    ss = warp_sum_d(ss);
+    if ((t & 31) == 0) dred[t >> 5] = ss;
+    __syncthreads();
+    double tot = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot += dred[i];
+    const float ms = (float)__ddiv_rn(tot, (double)n);
+    const float inv = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)ms, (double)eps)));
+    for (int i = t; i < n; i += 256) {
+        float v = __fmul_rn(xr[i], inv);
+        if (scale) v = __fmul_rn(v, scale[i]);
+        y[(long long)row * n + i] = v;
+    }
+}
+
+// One block per (b, t); threads over heads x pairs.
+__global__ void rope_kernel(const float *__restrict__ x, int H, int T, int D, const int64_t *__restrict__ pos,
+                            int pos_rows, const double *__restrict__ inv_freq, int rotary, int interleaved,
+                            float *__restrict__ y) {
+    extern __shared__ float cs[];  // 2 * rotary/2
+    pdl_launch_dependents();
+    pdl_wait();
+    const int bt = blockIdx.x, b = bt / T, t = bt % T, h = rotary / 2;
+    const double pp = (double)pos[(pos_rows != 1 ? b : 0) * T + t];
+    for (int i = threadIdx.x; i < h; i += blockDim.x) {
+        const double ang = __dmul_rn(pp, inv_freq[i]);
+        double s, c;
+        sincos(ang, &s, &c);
+        cs[2 * i] = (float)c;
+        cs[2 * i + 1] = (float)s;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < H * D; idx += blockDim.x) {
+        const int hd = idx / D, e = idx % D;
+        const long long at = (((long long)b * H + hd) * T + t) * D;
+        float out;
+        if (e >= rotary) {
+            out = x[at + e];
+        } else {
+            int i, first;
+            if (interleaved) { i = e >> 1; first = !(e & 1); }
+            else { i = e < h ? e : e - h; first = e < h; }
+            const int i1 = interleaved ? 2 * i : i, i2 = interleaved ? 2 * i + 1 : i + h;
+            const float x1 = x[at + i1], x2 = x[at + i2], c = cs[2 * i], s = cs[2 * i + 1];
+            out = first ? __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)) : __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        }
+        y[at + e] = out;
+    }
+}
+
+__device__ __forceinline__ float silu_mul(float a, float b) {
+    const double ad = (double)a;
+    return (float)__dmul_rn(__ddiv_rn(ad, __dadd_rn(1.0, exp(-ad))), (double)b);
+}
+
+__global__ void swiglu_kernel(const float *__restrict__ a, const float *__restrict__ b, long long n, float *__restrict__ y) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = silu_mul(a[i], b[i]);
+}
+
+__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, long long n, float *__restrict__ y) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void cast_f16_kernel(const float *__restrict__ x, uint16_t *__restrict__ y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = f32_to_f16(x[i]);
+}
+
+__device__ __forceinline__ float kv_at(const void *base, int f16, long long i) {
+    return f16 ? f16_to_f32(((const uint16_t *)base)[i]) : ((const float *)base)[i];
+}
+
+// ---------------------------------------------------------- attention (general)
+// One 256-thread block per query row (b, h, i); scores in dynamic shared memory.
+__global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
+    extern __shared__ float sc[];
+    __shared__ float red[8];
+    __shared__ int ired[8];
+    __shared__ float qsh[512];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    const int row = blockIdx.x;
+    const int i = row % a.Tq, h = (row / a.Tq) % a.Hq, b = row / (a.Tq * a.Hq);
+    const int G = a.Hq / a.Hkv, kvh = b * a.Hkv + h / G;
+    const float *q = a.q + (long long)row * a.D;
+    for (int d = t; d < a.D; d += 256) qsh[d] = q[d];
+    const long long kvoff = (long long)kvh * a.Tk * a.D;
+    const uint8_t *mrow = a.mask ? a.mask + b * a.mst[0] + h * a.mst[1] + i * a.mst[2] : nullptr;
+    const bool in_order = !a.mask || a.mst[3] == 1;
+    // visible range [st, end) of a boolean mask row, interp/fast.go:606-636
+    int end = a.Tk, st = 0;
+    if (a.mask && in_order) {
+        int last = -1, first = a.Tk;
+        for (int j = t; j < a.Tk; j += 256)
+            if (mrow[j]) { last = max(last, j); first = min(first, j); }
+        for (int o = 16; o; o >>= 1) {
+            last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+            first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+        }
+        if (lane == 0) { ired[w] = last; red[w] = __int_as_float(first); }
+        __syncthreads();
+        last = -1; first = a.Tk;
+        for (int k = 0; k < 8; k++) { last = max(last, ired[k]); first = min(first, __float_as_int(red[k])); }
+        __syncthreads();
+        end = last + 1;
+        st = first < end ? first : end;
+    }
+    if (a.causal) end = max(0, min(end, i + (a.Tk - a.Tq) + 1));
+    __syncthreads();
+    bool vector_path = in_order && st < end;
+    if (vector_path && a.mask) {
+        int hole = 0;
+        for (int j = st + t; j < end; j += 256) hole |= mrow[j] == 0;
+        vector_path = !__syncthreads_or(hole);
+    }
+    const int j0 = vector_path ? st : 0;
+    // scores: one warp per key
+    for (int j = j0 + w; j < end; j += 8) {
+        float s = 0.f;
+        for (int d = lane; d < a.D; d += 32) s = __fmaf_rn(qsh[d], kv_at(a.k, a.kv_f16, kvoff + (long long)j * a.D + d), s);
+        s = warp_sum(s);
+        bool allowed = true;
+        if (!vector_path) {
+            allowed = !a.causal || j <= i + (a.Tk - a.Tq);
+            if (a.mask) allowed = allowed && mrow[(long long)j * a.mst[3]] != 0;
+        }
+        if (lane == 0) sc[j - j0] = allowed ? __fmul_rn(s, a.scale) : -INFINITY;
+    }
+    __syncthreads();
+    const int n = end - j0;
+    float mx = -INFINITY;
+    int nan = 0;
+    for (int j = t; j < n; j += 256) {
+        const float s = sc[j];
+        if (s != s) nan = 1; else mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) red[w] = mx;
+    nan = __syncthreads_or(nan);
+    mx = red[0];
+    for (int k = 1; k < 8; k++) mx = fmaxf(mx, red[k]);
+    if (nan) mx = __int_as_float(0x7fc00000);
+    __syncthreads();
+    // the vector path of the reference requires a finite maximum; otherwise
+    // the scalar path, whose only differences are the masked keys' zeros
+    const bool mx_neg_inf = mx == -INFINITY;
+    float psum = 0.f;
+    for (int j = t; j < n; j += 256) {
+        const float s = sc[j];
+        float e;
+        if (s == -INFINITY && !mx_neg_inf) e = 0.f;
+        else e = (float)exp((double)__fsub_rn(s, mx));
+        sc[j] = e;
+        psum += e;
+    }
+    psum = warp_sum(psum);
+    __syncthreads();
+    if (lane == 0) red[w] = psum;
+    __syncthreads();
+    float sum = 0.f;
+    for (int k = 0; k < 8; k++) sum += red[k];
+    for (int d = t; d < a.D; d += 256) {
+        float acc = 0.f;
+        for (int j = 0; j < n; j++) {
+            const float e = sc[j];
+            if (e == 0.f) continue;
+            acc = __fmaf_rn(e, kv_at(a.v, a.kv_f16, kvoff + (long long)(j0 + j) * a.D + d), acc);
+        }
+        a.out[(long long)row * a.D + d] = __fdiv_rn(acc, sum);
+    }
+}
+
+// ------------------------------------------------------------- argmax
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ v, long long n, int *__restrict__ out) {
+    __shared__ float bvs[32];
+    __shared__ long long bis[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    float bv = 0.f;
+    long long bi = -1;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = v[i];
+        if (x == x && (bi < 0 || x > bv)) { bv = x; bi = i; }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const long long oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { bvs[w] = bv; bis[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+            if (bis[k] >= 0 && (bis[0] < 0 || bvs[k] > bvs[0] || (bvs[k] == bvs[0] && bis[k] < bis[0]))) {
+                bvs[0] = bvs[k];
+                bis[0] = bis[k];
+            }
+        const float v0 = n > 0 ? v[0] : 0.f;
+        *out = (n == 0 || v0 != v0 || bis[0] < 0) ? 0 : (int)bis[0];
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm(const float *x, int rows, int n, const float *scale, float eps, float *y, cudaStream_t st,
+                           bool pdl) {
+    if (rows <= 0 || n <= 0) return cudaSuccess;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(rows), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_kernel, x, n, scale, eps, y);
+}
+
+cudaError_t launch_rope(const float *x, int B, int H, int T, int D, const int64_t *pos, int pos_rows,
+                        const double *inv_freq, int rotary, int interleaved, float *y, cudaStream_t st, bool pdl) {
+    if (B * T <= 0) return cudaSuccess;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(B * T), dim3(256), sizeof(float) * rotary, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, rope_kernel, x, H, T, D, pos, pos_rows, inv_freq, rotary, interleaved, y);
+}
+
+static unsigned grid_for(long long n) {
+    long long g = (n + 255) / 256;
+    return (unsigned)(g > 148LL * 16 ? 148LL * 16 : (g < 1 ? 1 : g));
+}
+
+cudaError_t launch_swiglu(const float *a, const float *b, long long n, float *y, cudaStream_t st, bool pdl) {
+    if (n <= 0) return cudaSuccess;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid_for(n)), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, swiglu_kernel, a, b, n, y);
+}
+
+cudaError_t launch_add(const float *a, const float *b, long long n, float *y, cudaStream_t st, bool pdl) {
+    if (n <= 0) return cudaSuccess;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid_for(n)), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, add_kernel, a, b, n, y);
+}
+
+cudaError_t launch_cast_f16(const float *x, uint16_t *y, long long n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    cast_f16_kernel<<<grid_for(n), 256, 0, st>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+constexpr int kMaxAttnKeys = 49152;
+
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
+    const long long rows = (long long)a.B * a.Hq * a.Tq;
+    if (rows <= 0) return cudaSuccess;
+    if (a.Tk > kMaxAttnKeys || a.D > 512) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (size_t)(a.Tk > 0 ? a.Tk : 1);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attention_kernel<<<(unsigned)rows, 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *v, long long n, int *out, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(1024), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, out);
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace mimgpu

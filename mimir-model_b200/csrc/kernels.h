@@ -1,0 +1,93 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal API of
+// libmimgpu; the public C ABI is include/mimgpu.h).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mimgpu {
+
+// 8-bit activations in blocks of 256 (internal/kernels/q8.go:50-97):
+// q [rows,K] int8, dx [rows,K/256] scale amax/127, xs [rows,K/32] sums of
+// each run of 32 quants, ys [rows,K/16] sums of each run of 16, ok [rows]
+// (0 when the reference would refuse the row: NaN, Inf or |x| > 2^60).
+struct ActQ8 {
+    int8_t *q;
+    float *dx;
+    int16_t *xs;
+    int16_t *ys;
+    int *ok;
+};
+size_t act_q8_bytes(int rows, long long K);
+ActQ8 act_q8_carve(void *base, int rows, long long K);
+
+// One weight matrix of a fused GEMV launch: W [n, K] in its block dtype,
+// byte-exact rows of row_bytes(dt, K); y[a*ldy + j] for activation row a.
+struct GemvSeg {
+    const uint8_t *w;
+    int dt;
+    int n;
+    float *y;
+    long long ldy;
+    const float *bias;  // [n] or null
+    const float *res;   // residual added after the product (res[a*ldy + j]), or null
+};
+
+constexpr int kMaxSegs = 4;
+
+cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st, bool pdl);
+// y = rms_norm(x) * scale, and its 8-bit blocks (fast.go:434-485 then q8.go:50-97);
+// act may have a null q (no quantization)
+cudaError_t launch_rmsnorm_quant(const float *x, int rows, int n, const float *scale, float eps, float *y,
+                                 ActQ8 act, cudaStream_t st, bool pdl);
+// y = silu(gate)*up (attn.go:63-73, float64) and its 8-bit blocks; act.q may be null
+cudaError_t launch_swiglu_quant(const float *gate, const float *up, long long ldg, int rows, int n, float *y,
+                                ActQ8 act, cudaStream_t st, bool pdl);
+// dequant_matmul_a8.v2 block 256 over up to kMaxSegs Q4_K/Q6_K matrices
+// sharing the activations.  x is the f32 input, used for refused rows.
+// Sets the kernel attributes the GEMV launches need (call outside stream capture).
+cudaError_t gemv_a8_prepare();
+cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
+                           unsigned *status, cudaStream_t st, bool pdl);
+// dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
+cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
+                            cudaStream_t st, bool pdl);
+
+// dequantize n elements (quant.go Dequantize) and embedding rows (fast.go:818-842)
+cudaError_t launch_dequantize(int dt, const uint8_t *src, float *dst, long long n, cudaStream_t st);
+cudaError_t launch_embedding(int dt, const uint8_t *table, long long V, int E, const int32_t *ids, int n,
+                             float *y, cudaStream_t st, bool pdl);
+
+cudaError_t launch_rmsnorm(const float *x, int rows, int n, const float *scale, float eps, float *y,
+                           cudaStream_t st, bool pdl);
+// rope.v1 on x [B,H,T,D]; pos [pos_rows, T]; inv_freq [rotary/2] (float64)
+cudaError_t launch_rope(const float *x, int B, int H, int T, int D, const int64_t *pos, int pos_rows,
+                        const double *inv_freq, int rotary, int interleaved, float *y, cudaStream_t st,
+                        bool pdl);
+cudaError_t launch_swiglu(const float *a, const float *b, long long n, float *y, cudaStream_t st, bool pdl);
+cudaError_t launch_add(const float *a, const float *b, long long n, float *y, cudaStream_t st, bool pdl);
+cudaError_t launch_cast_f16(const float *x, uint16_t *y, long long n, cudaStream_t st);
+// general attention.v1/v2 (per-op path): q [B,Hq,Tq,D] f32, k/v [B,Hkv,Tk,D] f32 or f16,
+// mask bool with broadcast strides (elements) or null
+struct AttnArgs {
+    const float *q;
+    const void *k, *v;
+    int kv_f16;
+    int B, Hq, Tq, D, Hkv, Tk;
+    const uint8_t *mask;
+    long long mst[4];
+    float scale;
+    int causal;
+    float *out;
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+cudaError_t launch_argmax(const float *v, long long n, int *out, cudaStream_t st, bool pdl);
+
+// seeded synthetic weights (k_synth.cu)
+cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,
+                         cudaStream_t st);
+
+int num_sms();
+
+}  // namespace mimgpu

@@ -1,0 +1,407 @@
+// model.cu -- the llama graph of importer/llama.go:317-547 (gsoultan/mimir-model)
+// as a device-resident step: mimgpu_model / mimgpu_session of include/mimgpu.h.
+//
+// One Session.Run (interp/interp.go:409-526) of the graph becomes one
+// enqueue of ~10 kernels per layer on the session's stream, chained with
+// programmatic dependent launch so each GEMV streams its weights while the
+// previous kernel finishes.  The T = 1 step is captured once as a CUDA
+// graph (positions and token ids are read from device memory, so the same
+// graph serves every step); greedy generation replays it with the argmax and
+// the position update inside, so nothing crosses the bus between steps.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "kernels.h"
+#include "model_kernels.h"
+
+using namespace mimgpu;
+
+namespace {
+
+struct LayerW {
+    const mimgpu_tensor *attn_norm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+    const mimgpu_tensor *ffn_norm = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+};
+
+constexpr int kChunkDecode = 64;  // keys per attention split when T = 1
+
+}  // namespace
+
+struct mimgpu_model {
+    mimgpu_ctx *ctx = nullptr;
+    mimgpu_llama_config c{};
+    const mimgpu_tensor *embd = nullptr, *out_norm = nullptr, *out = nullptr;
+    std::vector<LayerW> L;
+    double *inv_freq = nullptr;  // device [rope_dims/2]
+};
+
+struct mimgpu_session {
+    mimgpu_model *m = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<void *> kc, vc;
+    size_t cache_bytes = 0;
+    void *arena = nullptr;
+    float *x = nullptr, *h = nullptr, *qkv = nullptr, *qh = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr;
+    float *logits = nullptr, *po = nullptr, *pml = nullptr;
+    ActQ8 actE{}, actF{};
+    int32_t *tok = nullptr, *ids = nullptr;
+    int64_t *pos = nullptr;
+    int *amax = nullptr, *step = nullptr;
+    int S_decode = 0, S_prefill = 0, chunk_prefill = 0;
+    cudaGraphExec_t g_step = nullptr;    // T=1 forward, logits of the row
+    cudaGraphExec_t g_greedy = nullptr;  // T=1 forward + argmax + advance
+};
+
+namespace {
+
+int check_shape(mimgpu_ctx *c, const char *name, const mimgpu_tensor *w, long long d0, long long d1) {
+    if (!w) return fail(c, MIMGPU_EINVAL, "weight %s is missing", name);
+    const bool ok = d1 < 0 ? (w->ndim == 1 && w->shape[0] == d0) : (w->ndim == 2 && w->shape[0] == d0 && w->shape[1] == d1);
+    if (!ok) return fail(c, MIMGPU_EINVAL, "weight %s has the wrong shape", name);
+    return MIMGPU_OK;
+}
+
+bool matrix_dtype(int dt, bool a8) { return dt == Q4_K || dt == Q6_K || (!a8 && (dt == Q8_0 || dt == F16 || dt == F32)); }
+
+int validate(mimgpu_model *m) {
+    const auto &c = m->c;
+    mimgpu_ctx *x = m->ctx;
+    const long long E = c.embed, F = c.ffn, V = c.vocab, KV = (long long)c.kv_heads * c.head_dim;
+    int rc;
+    if ((rc = check_shape(x, "token_embd.weight", m->embd, V, E))) return rc;
+    if ((rc = check_shape(x, "output_norm.weight", m->out_norm, E, -1))) return rc;
+    if (m->out && (rc = check_shape(x, "output.weight", m->out, V, E))) return rc;
+    if (m->out_norm->dtype != F32) return fail(x, MIMGPU_ENOTHANDLED, "norm weights must be f32");
+    for (int l = 0; l < c.layers; l++) {
+        const LayerW &w = m->L[l];
+        const struct { const char *n; const mimgpu_tensor *t; long long d0, d1; } list[] = {
+            {"attn_norm", w.attn_norm, E, -1}, {"attn_q", w.q, E, E},       {"attn_k", w.k, KV, E},
+            {"attn_v", w.v, KV, E},           {"attn_output", w.o, E, E},  {"ffn_norm", w.ffn_norm, E, -1},
+            {"ffn_gate", w.gate, F, E},       {"ffn_up", w.up, F, E},      {"ffn_down", w.down, E, F}};
+        for (auto &e : list) {
+            std::string n = "blk." + std::to_string(l) + "." + e.n + ".weight";
+            if ((rc = check_shape(x, n.c_str(), e.t, e.d0, e.d1))) return rc;
+            if (e.d1 < 0 && e.t->dtype != F32) return fail(x, MIMGPU_ENOTHANDLED, "%s must be f32", n.c_str());
+            if (e.d1 >= 0 && !matrix_dtype(e.t->dtype, c.a8))
+                return fail(x, MIMGPU_ENOTHANDLED, "%s: dtype %d is not served", n.c_str(), e.t->dtype);
+        }
+    }
+    const mimgpu_tensor *head = m->out ? m->out : m->embd;
+    if (!matrix_dtype(head->dtype, c.a8)) return fail(x, MIMGPU_ENOTHANDLED, "output head dtype %d", head->dtype);
+    return MIMGPU_OK;
+}
+
+// Enqueues one run of the graph for T tokens whose ids and positions are
+// already in s->tok / s->pos.  Logits of every row (all_rows) or of the
+// last row go to s->logits; with greedy, the argmax and step update follow.
+cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy, unsigned *status) {
+    mimgpu_model *m = s->m;
+    const auto &c = m->c;
+    const int E = c.embed, F = c.ffn, H = c.heads, Hkv = c.kv_heads, D = c.head_dim, KV = Hkv * D;
+    const long long ldq = E + 2LL * KV;
+    const bool a8 = c.a8 != 0;
+    cudaStream_t st = s->st;
+    const bool pdl = true;
+    cudaError_t e;
+#define CK(x)                              \
+    do {                                   \
+        if ((e = (x)) != cudaSuccess) return e; \
+    } while (0)
+    const ActQ8 none{};
+    CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl));
+    const int S = T == 1 ? s->S_decode : s->S_prefill;
+    const int chunk = T == 1 ? kChunkDecode : s->chunk_prefill;
+    for (int l = 0; l < c.layers; l++) {
+        const LayerW &w = m->L[l];
+        CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
+                                a8 ? s->actE : none, st, pdl));
+        GemvSeg qkv[3] = {{w.q->dev, w.q->dtype, E, s->qkv, ldq, nullptr, nullptr},
+                          {w.k->dev, w.k->dtype, KV, s->qkv + E, ldq, nullptr, nullptr},
+                          {w.v->dev, w.v->dtype, KV, s->qkv + E + KV, ldq, nullptr, nullptr}};
+        if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
+        else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
+        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
+                           c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
+        CK(launch_rope_scatter(ra, st, pdl));
+        AttnSplitArgs sa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16, chunk, S,
+                         (float)(1.0 / std::sqrt((double)D)), s->po, s->pml};
+        CK(launch_attn_split(sa, st, pdl));
+        AttnCombineArgs ca{s->po, s->pml, s->pos, T, H, D, S, chunk, s->att, a8 ? s->actE : none};
+        CK(launch_attn_combine(ca, st, pdl));
+        GemvSeg o{w.o->dev, w.o->dtype, E, s->x, E, nullptr, s->x};
+        if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
+        else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
+        CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
+                                a8 ? s->actE : none, st, pdl));
+        GemvSeg gu[2] = {{w.gate->dev, w.gate->dtype, F, s->gu, 2LL * F, nullptr, nullptr},
+                         {w.up->dev, w.up->dtype, F, s->gu + F, 2LL * F, nullptr, nullptr}};
+        if (a8) CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl));
+        else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
+        CK(launch_swiglu_quant(s->gu, s->gu + F, 2LL * F, T, F, s->a, a8 ? s->actF : none, st, pdl));
+        GemvSeg dn{w.down->dev, w.down->dtype, E, s->x, E, nullptr, s->x};
+        if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl));
+        else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
+    }
+    const int first = all_rows ? 0 : T - 1, rows = T - first;
+    CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
+                            (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl));
+    const mimgpu_tensor *head = m->out ? m->out : m->embd;
+    GemvSeg hs{head->dev, head->dtype, c.vocab, s->logits, c.vocab, nullptr, nullptr};
+    if (a8) CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl));
+    else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
+    if (greedy) {
+        CK(launch_argmax(s->logits, c.vocab, s->amax, st, pdl));
+        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl));
+    }
+#undef CK
+    return cudaSuccess;
+}
+
+int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out) {
+    mimgpu_ctx *c = s->m->ctx;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(c, e, "begin capture");
+    cudaError_t fe = enqueue_forward(s, 1, false, greedy, c->status);
+    e = cudaStreamEndCapture(s->st, &g);
+    if (fe != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return cuda_fail(c, fe, "capture forward");
+    }
+    if (e != cudaSuccess) return cuda_fail(c, e, "end capture");
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return cuda_fail(c, e, "instantiate");
+}
+
+void free_session(mimgpu_session *s) {
+    if (!s) return;
+    cudaSetDevice(s->m->ctx->device);
+    if (s->st) cudaStreamSynchronize(s->st);
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    for (void *p : s->kc) cudaFree(p);
+    for (void *p : s->vc) cudaFree(p);
+    if (s->arena) cudaFree(s->arena);
+    if (s->st) cudaStreamDestroy(s->st);
+    delete s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mimgpu_model_new(mimgpu_ctx *ctx, const mimgpu_llama_config *cfg, mimgpu_model **out) {
+    if (!ctx || !cfg || !out) return MIMGPU_EINVAL;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    *out = nullptr;
+    const auto &c = *cfg;
+    if (c.layers <= 0 || c.embed <= 0 || c.ffn <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+        c.head_dim <= 0 || c.heads * c.head_dim != c.embed || c.vocab <= 0 || c.context <= 0 || c.max_tokens <= 0 ||
+        c.max_tokens > c.context)
+        return fail(ctx, MIMGPU_EINVAL, "llama config is inconsistent");
+    if (c.rope_dims <= 0 || c.rope_dims % 2 || c.rope_dims > c.head_dim)
+        return fail(ctx, MIMGPU_EINVAL, "rope dimension count %d for head size %d", c.rope_dims, c.head_dim);
+    if (c.head_dim % 32 || c.head_dim > 128 || c.heads / c.kv_heads > 8)
+        return fail(ctx, MIMGPU_ENOTHANDLED, "head size %d / group %d not served", c.head_dim, c.heads / c.kv_heads);
+    if (c.a8 && (c.embed % 256 || c.ffn % 256))
+        return fail(ctx, MIMGPU_ENOTHANDLED, "8-bit activations need E and F multiples of 256");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    auto *m = new mimgpu_model;
+    m->ctx = ctx;
+    m->c = c;
+    m->L.resize(c.layers);
+    std::vector<double> inv(c.rope_dims / 2);
+    for (int i = 0; i < c.rope_dims / 2; i++) inv[i] = std::pow(c.rope_theta, -2.0 * (double)i / (double)c.rope_dims);
+    cudaError_t e = cudaMalloc(&m->inv_freq, inv.size() * sizeof(double));
+    if (e == cudaSuccess) e = cudaMemcpy(m->inv_freq, inv.data(), inv.size() * sizeof(double), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        if (m->inv_freq) cudaFree(m->inv_freq);
+        delete m;
+        return cuda_fail(ctx, e, "model");
+    }
+    *out = m;
+    return MIMGPU_OK;
+}
+
+int mimgpu_model_set_weight(mimgpu_model *m, const char *name, const mimgpu_tensor *w) {
+    if (!m || !name || !w) return MIMGPU_EINVAL;
+    if (w->ctx != m->ctx) return fail(m->ctx, MIMGPU_EINVAL, "weight %s belongs to another context", name);
+    if (!strcmp(name, "token_embd.weight")) { m->embd = w; return MIMGPU_OK; }
+    if (!strcmp(name, "output_norm.weight")) { m->out_norm = w; return MIMGPU_OK; }
+    if (!strcmp(name, "output.weight")) { m->out = w; return MIMGPU_OK; }
+    int l = -1, used = 0;
+    char rest[64] = {0};
+    if (sscanf(name, "blk.%d.%63s%n", &l, rest, &used) != 2 || l < 0 || l >= m->c.layers)
+        return fail(m->ctx, MIMGPU_EINVAL, "unknown weight %s", name);
+    LayerW &L = m->L[l];
+    const struct { const char *n; const mimgpu_tensor **slot; } names[] = {
+        {"attn_norm.weight", &L.attn_norm}, {"attn_q.weight", &L.q},       {"attn_k.weight", &L.k},
+        {"attn_v.weight", &L.v},           {"attn_output.weight", &L.o},  {"ffn_norm.weight", &L.ffn_norm},
+        {"ffn_gate.weight", &L.gate},      {"ffn_up.weight", &L.up},      {"ffn_down.weight", &L.down}};
+    for (auto &e : names)
+        if (!strcmp(rest, e.n)) {
+            *e.slot = w;
+            return MIMGPU_OK;
+        }
+    return fail(m->ctx, MIMGPU_EINVAL, "unknown weight %s", name);
+}
+
+void mimgpu_model_free(mimgpu_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    if (m->inv_freq) cudaFree(m->inv_freq);
+    delete m;
+}
+
+int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
+    if (!m || !out) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    *out = nullptr;
+    int rc = validate(m);
+    if (rc || (rc = use_device(c))) return rc;
+    if ((rc = cuda_fail(c, gemv_a8_prepare(), "gemv setup"))) return rc;
+    const auto &k = m->c;
+    auto *s = new mimgpu_session;
+    s->m = m;
+    const long long T = k.max_tokens, E = k.embed, F = k.ffn, V = k.vocab, H = k.heads, D = k.head_dim;
+    const long long KV = (long long)k.kv_heads * D;
+    s->S_decode = (k.context + kChunkDecode - 1) / kChunkDecode;
+    // prompts: at most 8 splits per query row, chunks a multiple of 64
+    s->chunk_prefill = (int)(((k.context + 7) / 8 + 63) / 64 * 64);
+    s->S_prefill = (k.context + s->chunk_prefill - 1) / s->chunk_prefill;
+    const long long split_rows = std::max((long long)s->S_decode, T * s->S_prefill);
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    size_t bytes = 0;
+    const size_t sz[] = {al(T * E * 4), al(T * E * 4), al(T * (E + 2 * KV) * 4), al(T * E * 4), al(T * E * 4),
+                         al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), al(split_rows * H * D * 4),
+                         al(split_rows * H * 2 * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
+                         al(T * 4), al(T * 8), al(65536 * 4), al(256)};
+    for (size_t b : sz) bytes += b;
+    cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&s->arena, bytes);
+    if (e != cudaSuccess) {
+        free_session(s);
+        return cuda_fail(c, e, "session memory");
+    }
+    uint8_t *p = (uint8_t *)s->arena;
+    int i = 0;
+    auto take = [&]() { uint8_t *r = p; p += sz[i++]; return r; };
+    s->x = (float *)take();
+    s->h = (float *)take();
+    s->qkv = (float *)take();
+    s->qh = (float *)take();
+    s->att = (float *)take();
+    s->gu = (float *)take();
+    s->a = (float *)take();
+    s->logits = (float *)take();
+    s->po = (float *)take();
+    s->pml = (float *)take();
+    s->actE = act_q8_carve(take(), (int)T, E);
+    s->actF = act_q8_carve(take(), (int)T, F);
+    s->tok = (int32_t *)take();
+    s->pos = (int64_t *)take();
+    s->ids = (int32_t *)take();
+    uint8_t *misc = take();
+    s->amax = (int *)misc;
+    s->step = (int *)(misc + 16);
+    s->cache_bytes = (size_t)k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
+    s->kc.resize(k.layers, nullptr);
+    s->vc.resize(k.layers, nullptr);
+    for (int l = 0; l < k.layers && e == cudaSuccess; l++) {
+        e = cudaMalloc(&s->kc[l], s->cache_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&s->vc[l], s->cache_bytes);
+    }
+    if (e != cudaSuccess) {
+        free_session(s);
+        return cuda_fail(c, e, "key-value cache");
+    }
+    if ((rc = mimgpu_session_reset(s))) {
+        free_session(s);
+        return rc;
+    }
+    *out = s;
+    return MIMGPU_OK;
+}
+
+void mimgpu_session_free(mimgpu_session *s) { free_session(s); }
+
+int mimgpu_session_reset(mimgpu_session *s) {
+    if (!s) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaError_t e = cudaSuccess;
+    for (size_t l = 0; l < s->kc.size() && e == cudaSuccess; l++) {
+        e = cudaMemsetAsync(s->kc[l], 0, s->cache_bytes, s->st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(s->vc[l], 0, s->cache_bytes, s->st);
+    }
+    if (e != cudaSuccess) return cuda_fail(c, e, "reset");
+    return sync_bounded(c, s->st);
+}
+
+int mimgpu_session_run(mimgpu_session *s, const int32_t *tokens, const int64_t *positions, int T, float *logits,
+                       int all_rows) {
+    if (!s || !tokens || !positions || !logits) return MIMGPU_EINVAL;
+    mimgpu_model *m = s->m;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (T <= 0 || T > m->c.max_tokens) return fail(c, MIMGPU_EINVAL, "%d tokens; the session takes 1..%d", T, m->c.max_tokens);
+    for (int i = 0; i < T; i++)
+        if (positions[i] < 0 || positions[i] >= m->c.context)
+            return fail(c, MIMGPU_EINVAL, "position %lld outside the cache of %d", (long long)positions[i], m->c.context);
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(s->tok, tokens, T * 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, positions, T * 8, cudaMemcpyHostToDevice, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    if (T == 1) {
+        if (!s->g_step && (rc = capture(s, false, &s->g_step))) return rc;
+        e = cudaGraphLaunch(s->g_step, s->st);
+    } else {
+        e = enqueue_forward(s, T, all_rows != 0, false, c->status);
+    }
+    if (e != cudaSuccess) return cuda_fail(c, e, "forward");
+    const long long rows = all_rows ? T : 1;
+    e = cudaMemcpyAsync(logits, s->logits, rows * m->c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
+    return sync_bounded(c, s->st);
+}
+
+int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int steps, int32_t *ids_out) {
+    if (!s || !ids_out || steps < 0) return MIMGPU_EINVAL;
+    mimgpu_model *m = s->m;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (steps > 65536 || pos < 0 || pos + steps > m->c.context)
+        return fail(c, MIMGPU_EINVAL, "%d steps from position %lld exceed the cache of %d", steps, (long long)pos,
+                    m->c.context);
+    if (steps == 0) return MIMGPU_OK;
+    int rc = use_device(c);
+    if (rc) return rc;
+    const int zero = 0;
+    cudaError_t e = cudaMemcpyAsync(s->tok, &token, 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, &pos, 8, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->step, &zero, 4, cudaMemcpyHostToDevice, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    if (!s->g_greedy && (rc = capture(s, true, &s->g_greedy))) return rc;
+    for (int i = 0; i < steps && e == cudaSuccess; i++) e = cudaGraphLaunch(s->g_greedy, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ids_out, s->ids, steps * 4, cudaMemcpyDeviceToHost, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "generate");
+    return sync_bounded(c, s->st);
+}
+
+}  // extern "C"
+
+// Internal hooks for bench.py-style timing through the C ABI live in
+// bench_api.cu.

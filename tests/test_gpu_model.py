@@ -1,0 +1,159 @@
+"""The device-resident llama step (mimgpu_session_*) against the reference's
+tiny-Llama fixture and against the CPU oracle.  Needs a B200.
+
+Bars (gsoultan/mimir-model):
+  cmd/mim-run/main_test.go:179-216  v1 graph, f32 cache: prompt and step
+      logits within 2e-5 of the largest logit of the float64 oracle, and the
+      same 8 greedy ids;
+  cmd/mim-run/main_test.go:218-267  a8 graph, f16 cache: logits within 1.1x
+      llama.cpp's own distance from the float64 oracle;
+  token identity: greedy ids identical to the CPU restatement of the
+      reference (the a8 products are bit-exact; attention is the only
+      tolerance-level step) over 64 steps at 8B layer shapes.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import f32b64
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import mimgpu
+    c = mimgpu.Context(0)
+    yield c
+    c.close()
+
+
+def _model(ctx, e, w, **over):
+    import mimgpu
+    cfg = dict(e["config"], interleaved=1, max_tokens=len(e["prompt_ids"]))
+    cfg.update(over)
+    return mimgpu.Model(ctx, cfg, w)
+
+
+def test_tiny_llama_v1_matches_float64_oracle(ctx, tiny):
+    e, w = tiny
+    V = e["config"]["vocab"]
+    m = _model(ctx, e, w, a8=0, cache_f16=0)
+    s = m.session()
+    ids = e["prompt_ids"]
+    all_ = s.run(ids, np.arange(len(ids)), all_rows=True)
+    want = f32b64(e["prompt_logits"]).reshape(len(ids), V)
+    assert np.abs(all_ - want).max() <= 2e-5 * np.abs(want).max()
+    logits, pos = all_[-1], len(ids)
+    for i, nxt in enumerate(e["greedy"]):
+        w_ = f32b64(e["greedy_logits"][i])
+        assert np.abs(logits - w_).max() <= 2e-5 * np.abs(w_).max()
+        assert int(np.argmax(logits)) == nxt
+        logits = s.run([nxt], [pos])[0]
+        pos += 1
+    s.free()
+    m.free()
+
+
+@pytest.mark.parametrize("cache_f16,bound", [(0, 1.0), (1, 1.1)])
+def test_tiny_llama_a8_within_llama_cpp(ctx, tiny, cache_f16, bound):
+    e, w = tiny
+    V = e["config"]["vocab"]
+    m = _model(ctx, e, w, a8=1, cache_f16=cache_f16)
+    s = m.session()
+    ids = e["prompt_ids"]
+    all_ = s.run(ids, np.arange(len(ids)), all_rows=True)
+    worst = np.abs(all_ - f32b64(e["prompt_logits"]).reshape(len(ids), V)).max()
+    logits, pos = all_[-1], len(ids)
+    for i, nxt in enumerate(e["greedy"]):
+        worst = max(worst, np.abs(logits - f32b64(e["greedy_logits"][i])).max())
+        logits = s.run([nxt], [pos])[0]
+        pos += 1
+    assert worst <= e["llama_cpp_max_diff"] * bound
+    s.free()
+    m.free()
+
+
+def test_tiny_llama_a8_matches_cpu_restatement(ctx, tiny):
+    """Prompt logits and 48 greedy ids against the oracle's a8 + f16 graph."""
+    e, w = tiny
+    m = _model(ctx, e, w, a8=1, cache_f16=1)
+    s = m.session()
+    ref = O.Llama(dict(e["config"], a8=1, cache_f16=1, interleaved=1), w)
+    ids = e["prompt_ids"]
+    got = s.run(ids, np.arange(len(ids)), all_rows=True)
+    want = ref.forward(ids, np.arange(len(ids)), all_rows=True)
+    assert np.abs(got - want).max() <= 1e-3 * np.abs(want).max()
+    tok, pos = int(np.argmax(got[-1])), len(ids)
+    gen = s.generate(tok, pos, 48)
+    cur, want_ids = tok, []
+    for i in range(48):
+        lg = ref.forward([cur], [pos + i])[0]
+        cur = O.argmax(lg)
+        want_ids.append(cur)
+    assert gen.tolist() == want_ids
+    s.free()
+    m.free()
+
+
+def _synthetic(layers, E, H, Hkv, F, V, seed=1):
+    """Random-init llama weights, Q4_K_M layout (Q6_K for attn_v, ffn_down,
+    output), f32 norms 1 + N(0, 0.02)."""
+    D = E // H
+    KV = Hkv * D
+    w = {}
+    sd = seed * 1000
+    def q(name, dt, n, k):
+        nonlocal sd
+        sd += 1
+        w[name] = (dt, O.gen_weight(dt, sd, n, k).ravel())
+    def norm(name, n):
+        nonlocal sd
+        sd += 1
+        w[name] = (O.F32, O.gen_normal(sd, n, 1.0, 0.02))
+    q("token_embd.weight", O.Q4_K, V, E)
+    for l in range(layers):
+        p = f"blk.{l}."
+        norm(p + "attn_norm.weight", E)
+        q(p + "attn_q.weight", O.Q4_K, E, E)
+        q(p + "attn_k.weight", O.Q4_K, KV, E)
+        q(p + "attn_v.weight", O.Q6_K, KV, E)
+        q(p + "attn_output.weight", O.Q4_K, E, E)
+        norm(p + "ffn_norm.weight", E)
+        q(p + "ffn_gate.weight", O.Q4_K, F, E)
+        q(p + "ffn_up.weight", O.Q4_K, F, E)
+        q(p + "ffn_down.weight", O.Q6_K, E, F)
+    norm("output_norm.weight", E)
+    q("output.weight", O.Q6_K, V, E)
+    cfg = dict(layers=layers, embed=E, ffn=F, heads=H, kv_heads=Hkv, head_dim=D, rope_dims=D, vocab=V,
+               rope_theta=500000.0, norm_eps=1e-5)
+    return cfg, w
+
+
+def test_8b_layer_shapes_token_identity(ctx):
+    """Two layers of the 8B shape (E 4096, 32/8 heads, F 14336) with a 32000
+    vocabulary: prompt of 16 ids then 64 greedy steps, token-identical to
+    the CPU restatement; logits of the prompt close."""
+    import mimgpu
+    cfg, w = _synthetic(2, 4096, 32, 8, 14336, 32000)
+    C = 128
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, cfg["vocab"], 16).astype(np.int32)
+    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=16), w)
+    s = m.session()
+    ref = O.Llama(dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1), w)
+    got = s.run(prompt, np.arange(16))[0]
+    want = ref.forward(prompt, np.arange(16))[0]
+    assert np.abs(got - want).max() <= 1e-3 * np.abs(want).max()
+    tok = O.argmax(want)
+    gen = s.generate(tok, 16, 64)
+    cur, want_ids, margins = tok, [], []
+    for i in range(64):
+        lg = ref.forward([cur], [16 + i])[0]
+        top = np.sort(lg)[-2:]
+        margins.append(float(top[1] - top[0]))
+        cur = O.argmax(lg)
+        want_ids.append(cur)
+    assert gen.tolist() == want_ids, (gen.tolist(), want_ids, margins)
+    s.free()
+    m.free()

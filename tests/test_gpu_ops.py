@@ -1,0 +1,294 @@
+"""Per-op parity of the GPU fast paths against the CPU oracle, through the
+C ABI (libmimgpu.so via ctypes).  Needs a B200.
+
+Bars (reference file:line in gsoultan/mimir-model):
+  dequantize           bit-exact (quant.go:197-344, testdata/quant_golden.json)
+  dequant_matmul_a8.v2 bit-exact with dotQ8KRef (internal/kernels/q8k_test.go:35-117),
+                       batch-invariant (interp/transformer_test.go:297-354)
+  dequant_matmul.v1    spec/stdlib.md section 3.3: |err| <= (K+1) u sum|x w| + |bias|,
+                       and max relative error <= 1e-3
+  rms_norm, rope, swiglu, embedding   bit-exact with the oracle except where a
+                       reference float64 step could round differently (noted per test)
+  attention            spec/stdlib.md section 6.2: (4 D S + 2 Tk + 64) u V
+"""
+import base64
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+U = 2.0 ** -24
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import mimgpu
+    c = mimgpu.Context(0)
+    yield c
+    c.close()
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+# ------------------------------------------------------------- dequantize
+
+@pytest.mark.parametrize("name,dt", [("q8_0", O.Q8_0), ("q4_k", O.Q4_K), ("q6_k", O.Q6_K)])
+def test_dequantize_golden(ctx, quant_golden, name, dt):
+    g = quant_golden[name]
+    raw = np.frombuffer(base64.b64decode(g["bytes"]), np.uint8)
+    want = np.array(g["bits"], np.uint32)
+    assert np.array_equal(bits(ctx.dequantize(dt, raw, want.size)), want)
+
+
+@pytest.mark.parametrize("dt", [O.Q8_0, O.Q4_K, O.Q6_K])
+def test_dequantize_random_and_edge_blocks(ctx, dt):
+    be, bb = O.BLOCK[dt]
+    rng = np.random.default_rng(dt)
+    raw = rng.integers(0, 256, 64 * bb, dtype=np.uint8)
+    # finite scales in most blocks; keep a few inf/nan/subnormal ones
+    want = O.dequantize(dt, raw, 64 * be)
+    got = ctx.dequantize(dt, raw, 64 * be)
+    # NaN payloads after arithmetic are not specified by IEEE 754; every
+    # other value (subnormals and infinities included) must match bit for bit
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(bits(got[~nan]), bits(want[~nan]))
+
+
+# -------------------------------------------------- 8-bit activation GEMV
+
+def _weights(dt, n, k, seed):
+    return O.gen_weight(dt, seed, n, k)
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+@pytest.mark.parametrize("n,k,rows", [(8, 256, 1), (37, 2048, 1), (64, 5632, 3), (300, 4096, 1),
+                                      (129, 4096, 5), (96, 11008, 2), (24, 14336, 8), (40, 4096, 16)])
+def test_a8_bit_exact(ctx, dt, n, k, rows):
+    w = _weights(dt, n, k, 1000 + n)
+    x = O.gen_normal(7 + rows, rows * k).reshape(rows, k)
+    bias = O.gen_normal(3, n)
+    t = ctx.upload(dt, (n, k), w)
+    want = O.dequant_matmul_a8(x, dt, w, n, bias)
+    got = ctx.dequant_matmul(x, t, bias, a8_block=256)
+    assert np.array_equal(bits(got), bits(want))
+    t.free()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+def test_a8_edge_cases(ctx, dt):
+    """q8k_test.go:122-187: tiny and huge activations, a zero block, the
+    largest finite scales, subnormal scales; plus refused rows (Inf, NaN)
+    and a weight row with a non-finite scale (fast.go:282-379)."""
+    k, n = 2048, 16
+    bb = 144 if dt == O.Q4_K else 210
+    w = bytearray(_weights(dt, n, k, 77).tobytes())
+    rb = k // 256 * bb
+    for o in range(rb, 2 * rb, bb):  # row 1: largest finite scales, all-ones quants
+        if dt == O.Q4_K:
+            w[o:o + 4] = bytes([0xFF, 0x7B, 0xFF, 0x7B])
+            w[o + 4:o + 144] = b"\xff" * 140
+        else:
+            w[o + 208:o + 210] = bytes([0xFF, 0x7B])
+            w[o:o + 192] = b"\xff" * 192
+            w[o + 192:o + 208] = b"\x80" * 16
+    if dt == O.Q4_K:  # row 2: subnormal scales; row 3: dmin = inf
+        w[2 * rb:2 * rb + 4] = bytes([0x01, 0x00, 0xFF, 0x03])
+        w[3 * rb + 2:3 * rb + 4] = bytes([0x00, 0x7C])
+    else:
+        w[2 * rb + 208:2 * rb + 210] = bytes([0x01, 0x00])
+        w[3 * rb + 208:3 * rb + 210] = bytes([0x00, 0x7E])
+    w = np.frombuffer(bytes(w), np.uint8)
+    x = O.gen_normal(5, 6 * k).reshape(6, k)
+    x[1] *= np.float32(1e-30)
+    x[2] *= np.float32(1e15)
+    x[3, :256] = 0
+    x[4, 9] = np.inf
+    x[5, 100] = np.nan
+    t = ctx.upload(dt, (n, k), w)
+    want = O.dequant_matmul_a8(x, dt, w, n)
+    got = ctx.dequant_matmul(x, t, a8_block=256)
+    exact = np.ones_like(want, bool)
+    exact[4:, :] = False  # refused rows: f32 product, tolerance
+    exact[:, 3] = False   # refused weight row
+    assert np.array_equal(bits(got[exact]), bits(want[exact]))
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(np.isinf(got), np.isinf(want))
+    fin = ~exact & np.isfinite(want)
+    wd = O.dequantize(dt, w, n * k).reshape(n, k).astype(np.float64)
+    scale = np.abs(np.nan_to_num(x.astype(np.float64), posinf=0, neginf=0)) @ np.abs(np.nan_to_num(wd)).T
+    assert np.all(np.abs(got[fin] - want[fin]) <= (k + 1) * U * 4 * scale[fin] + 1e-30)
+    t.free()
+
+
+def test_a8_batch_invariance(ctx):
+    """interp/transformer_test.go:297-354: each row's result is the same bits
+    alone as in any batch."""
+    k, n, rows = 1024, 40, 13
+    for dt in (O.Q4_K, O.Q6_K):
+        w = _weights(dt, n, k, 5)
+        x = O.gen_normal(9, rows * k).reshape(rows, k)
+        x[4, 3] = np.inf
+        t = ctx.upload(dt, (n, k), w)
+        together = ctx.dequant_matmul(x, t, a8_block=256)
+        for i in range(rows):
+            alone = ctx.dequant_matmul(x[i:i + 1], t, a8_block=256)
+            assert np.array_equal(bits(alone[0]), bits(together[i]))
+        t.free()
+
+
+def test_a8_block_attribute(ctx):
+    import mimgpu
+    w = _weights(O.Q4_K, 4, 256, 1)
+    t = ctx.upload(O.Q4_K, (4, 256), w)
+    x = O.gen_normal(1, 256).reshape(1, 256)
+    with pytest.raises(mimgpu.MimGPUError) as e:
+        ctx.dequant_matmul(x, t, a8_block=64)
+    assert e.value.code == mimgpu.EINVAL
+    # block 32 on K-quants is the exact (v1) product
+    y32 = ctx.dequant_matmul(x, t, a8_block=32)
+    yv1 = ctx.dequant_matmul(x, t)
+    assert np.array_equal(bits(y32), bits(yv1))
+    t.free()
+
+
+# ------------------------------------------------------- f32 activations
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+@pytest.mark.parametrize("n,k,rows", [(64, 256, 1), (200, 4096, 1), (33, 11008, 2), (16, 14336, 4)])
+def test_v1_within_spec_tolerance(ctx, dt, n, k, rows):
+    w = _weights(dt, n, k, 300 + n)
+    x = O.gen_normal(11, rows * k).reshape(rows, k)
+    bias = O.gen_normal(12, n)
+    t = ctx.upload(dt, (n, k), w)
+    got = ctx.dequant_matmul(x, t, bias).astype(np.float64)
+    wd = O.dequantize(dt, w, n * k).reshape(n, k).astype(np.float64)
+    exact = x.astype(np.float64) @ wd.T + bias
+    bound = (k + 1) * U * (np.abs(x.astype(np.float64)) @ np.abs(wd).T + np.abs(bias))
+    assert np.all(np.abs(got - exact) <= bound)
+    rel = np.abs(got - exact).max() / np.abs(exact).max()
+    assert rel <= 1e-3
+    t.free()
+
+
+# --------------------------------------------------------- per-token ops
+
+def test_rms_norm_matches_oracle(ctx):
+    """fast.go:434-485.  The float64 sum of squares is a tree sum here and a
+    sequential sum in the reference; the mean is rounded to f32 first, so the
+    results agree bit for bit unless the float64 sums straddle an f32
+    rounding boundary (probability ~1e-5 per row)."""
+    x = O.gen_normal(21, 64 * 4096).reshape(64, 4096)
+    x[3] *= 1e-20
+    scale = O.gen_normal(22, 4096, 1.0, 0.02)
+    got = ctx.rms_norm(x, scale, 1e-5)
+    want = O.rms_norm(x, scale, 1e-5)
+    same_rows = np.all(bits(got) == bits(want), axis=1)
+    assert same_rows.sum() >= 63
+    assert np.allclose(got, want, rtol=(4096 + 24) * U, atol=0)
+
+
+@pytest.mark.parametrize("interleaved", [True, False])
+def test_rope_matches_oracle(ctx, interleaved):
+    """fast.go:507-557: cos/sin in float64 rounded to f32; the rotation is
+    the same f32 operations, so results are bit-exact unless a float64
+    cos/sin differs in its last bit at an f32 rounding boundary."""
+    B, H, T, D = 1, 8, 7, 128
+    x = O.gen_normal(31, B * H * T * D).reshape(B, H, T, D)
+    pos = np.array([[0, 1, 5, 100, 1000, 2303, 131071]], np.int64)
+    got = ctx.rope(x, pos, 500000.0, D, interleaved)
+    want = O.rope(x, pos, 500000.0, D, interleaved)
+    mism = (bits(got) != bits(want)).mean()
+    assert mism < 1e-3
+    A = float(pos.max())
+    assert np.all(np.abs(got - want) <= (16 + 4 * A) * U * np.abs(x).max())
+
+
+def test_rope_partial_rotary(ctx):
+    x = O.gen_normal(32, 2 * 3 * 4 * 64).reshape(2, 3, 4, 64)
+    pos = np.array([[1, 2, 3, 4], [7, 8, 9, 10]], np.int64)
+    got = ctx.rope(x, pos, 10000.0, 32, False)
+    want = O.rope(x, pos, 10000.0, 32, False)
+    assert np.array_equal(got[..., 32:], x[..., 32:])
+    assert np.allclose(got, want, rtol=0, atol=1e-5)
+
+
+def test_swiglu_matches_oracle(ctx):
+    a = O.gen_normal(41, 100000) * 4
+    b = O.gen_normal(42, 100000)
+    a[:4] = [np.inf, -np.inf, np.nan, -100.0]
+    got = ctx.swiglu(a, b)
+    want = O.swiglu(a, b)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert (bits(got[ok]) != bits(want[ok])).sum() <= 2
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+def test_embedding_exact(ctx, dt):
+    V, E = 50, 512
+    table = _weights(dt, V, E, 51)
+    t = ctx.upload(dt, (V, E), table)
+    ids = np.array([0, 49, 7, -1, 50, 7], np.int32)
+    got = ctx.embedding(t, ids)
+    want = O.embedding(dt, table, V, E, ids)
+    assert np.array_equal(bits(got), bits(want))
+    assert not got[3].any() and not got[4].any()
+    t.free()
+
+
+def _attn_bound(q, k, v, scale):
+    qd, kd, vd = (np.asarray(a, np.float64) for a in (q, k, v))
+    G = q.shape[1] // k.shape[1]
+    kf = np.repeat(kd, G, axis=1)
+    vf = np.repeat(vd, G, axis=1)
+    S = scale * np.einsum("bhid,bhjd->bhij", np.abs(qd), np.abs(kf)).max(axis=-1, keepdims=True)
+    V = np.abs(vf).max(axis=(2, 3), keepdims=True)
+    return (4 * q.shape[3] * S + 2 * k.shape[2] + 64) * U * V
+
+
+@pytest.mark.parametrize("kv", [np.float16, np.float32])
+def test_attention_cache_mask(ctx, kv):
+    """The llama graph's call: one query block over a cache with the mask
+    j <= p (importer/llama.go:364-397), GQA 4."""
+    B, Hq, Hkv, D, C = 1, 8, 2, 128, 96
+    pos = np.array([5, 6, 7, 40], np.int64)
+    Tq = pos.size
+    q = O.gen_normal(61, B * Hq * Tq * D).reshape(B, Hq, Tq, D)
+    k = O.gen_normal(62, B * Hkv * C * D).reshape(B, Hkv, C, D).astype(kv)
+    v = O.gen_normal(63, B * Hkv * C * D).reshape(B, Hkv, C, D).astype(kv)
+    mask = (np.arange(C)[None, :] <= pos[:, None]).reshape(1, 1, Tq, C)
+    scale = 1 / np.sqrt(D)
+    got = ctx.attention(q, k, v, mask)
+    want = O.attention(q, k, v, mask)
+    assert np.all(np.abs(got - want) <= 2 * _attn_bound(q, k, v, scale))
+
+
+def test_attention_holes_causal_and_empty(ctx):
+    B, Hq, Hkv, Tq, Tk, D = 2, 4, 4, 3, 20, 64
+    q = O.gen_normal(71, B * Hq * Tq * D).reshape(B, Hq, Tq, D)
+    k = O.gen_normal(72, B * Hkv * Tk * D).reshape(B, Hkv, Tk, D)
+    v = O.gen_normal(73, B * Hkv * Tk * D).reshape(B, Hkv, Tk, D)
+    rng = np.random.default_rng(7)
+    mask = rng.random((B, 1, Tq, Tk)) < 0.6
+    mask[0, 0, 1, :] = False  # a row with every key hidden: NaN
+    got = ctx.attention(q, k, v, mask, causal=True)
+    want = O.attention(q, k, v, mask, causal=True)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    bound = np.broadcast_to(2 * _attn_bound(q, k, v, 1 / 8.0), got.shape)
+    assert np.all(np.abs(got[ok] - want[ok]) <= bound[ok])
+
+
+def test_fast_paths_registry(ctx):
+    """The registry keys of interp/fast.go:42-59 this backend serves."""
+    for key in ("dequant_matmul.v1", "dequant_matmul_a8.v2", "rms_norm.v1", "rope.v1", "attention.v2",
+                "swiglu.v1", "embedding.v1"):
+        assert key in ctx.fast_paths
+    out, handled = ctx.fast_paths["rope.v1"]({"yarn_factor": 2.0}, [np.zeros((1, 1, 1, 2), np.float32),
+                                                                    np.zeros((1, 1), np.int64)])
+    assert handled is False
