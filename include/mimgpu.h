@@ -201,6 +201,9 @@ int mimgpu_session_run(mimgpu_session *s, const int32_t *tokens, const int64_t *
  * the first maximum of the logits, feeds it back, `steps` times; writes the
  * picked ids.  One step is one device-resident graph launch. */
 int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int steps, int32_t *ids_out);
+/* The session's CUDA stream (a cudaStream_t), for callers that time or
+ * order their own device work against the session's. */
+void *mimgpu_session_stream(mimgpu_session *s);
 
 #ifdef __cplusplus
 }

@@ -81,7 +81,11 @@ __device__ __forceinline__ bool f16_finite(uint32_t h) { return (h & 0x7C00u) !=
 // Q4_K sub-block scale and min j (0..7) from the 12 packed bytes
 // (getScaleMinK4, quant.go:246-254).  `s` holds the 12 bytes as 3 words.
 __device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &m) {
-    auto byte = [&](int i) -> int { return (int)((s[i >> 2] >> ((i & 3) * 8)) & 0xFFu); };
+    // byte i of the 12 packed bytes, selected without a runtime-indexed array
+    auto byte = [&](int i) -> int {
+        const uint32_t w = i < 4 ? s[0] : (i < 8 ? s[1] : s[2]);
+        return (int)((w >> ((i & 3) * 8)) & 0xFFu);
+    };
     if (j < 4) {
         sc = byte(j) & 63;
         m = byte(j + 4) & 63;

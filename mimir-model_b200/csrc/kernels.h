@@ -10,8 +10,9 @@ namespace mimgpu {
 
 // 8-bit activations in blocks of 256 (internal/kernels/q8.go:50-97):
 // q [rows,K] int8, dx [rows,K/256] scale amax/127, xs [rows,K/32] sums of
-// each run of 32 quants, ys [rows,K/16] sums of each run of 16, ok [rows]
-// (0 when the reference would refuse the row: NaN, Inf or |x| > 2^60).
+// each run of 32 quants, ys [rows,K/16] sums of each run of 16, and
+// ok [rows,K/256] per block (0 when the block holds NaN, Inf or |x| > 2^60;
+// the reference then refuses the whole row).
 struct ActQ8 {
     int8_t *q;
     float *dx;

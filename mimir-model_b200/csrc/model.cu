@@ -275,10 +275,10 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->m = m;
     const long long T = k.max_tokens, E = k.embed, F = k.ffn, V = k.vocab, H = k.heads, D = k.head_dim;
     const long long KV = (long long)k.kv_heads * D;
+    // attention splits of 64 keys for every query row
     s->S_decode = (k.context + kChunkDecode - 1) / kChunkDecode;
-    // prompts: at most 8 splits per query row, chunks a multiple of 64
-    s->chunk_prefill = (int)(((k.context + 7) / 8 + 63) / 64 * 64);
-    s->S_prefill = (k.context + s->chunk_prefill - 1) / s->chunk_prefill;
+    s->chunk_prefill = kChunkDecode;
+    s->S_prefill = s->S_decode;
     const long long split_rows = std::max((long long)s->S_decode, T * s->S_prefill);
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     size_t bytes = 0;
@@ -401,7 +401,6 @@ int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int s
     return sync_bounded(c, s->st);
 }
 
-}  // extern "C"
+void *mimgpu_session_stream(mimgpu_session *s) { return s ? (void *)s->st : nullptr; }
 
-// Internal hooks for bench.py-style timing through the C ABI live in
-// bench_api.cu.
+}  // extern "C"

@@ -24,7 +24,7 @@ struct AttnSplitArgs {
     const void *kc, *vc;   // [Hkv, C, D]
     const int64_t *pos;    // [T]
     int T, H, Hkv, D, C, cache_f16;
-    int chunk, S;          // keys per split, splits
+    int chunk, S;          // keys per split (64), splits
     float scale;
     float *po;             // [T, H, S, D]
     float *pml;            // [T, H, S, 2]
@@ -39,7 +39,7 @@ struct AttnCombineArgs {
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
-size_t attn_split_smem(int G, int D, int chunk);
+size_t attn_split_smem(int G, int D, int f16);
 cudaError_t launch_attn_split(const AttnSplitArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_combine(const AttnCombineArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_advance(const int *argmax, int32_t *tok, int64_t *pos, int32_t *ids, int *step, cudaStream_t st,

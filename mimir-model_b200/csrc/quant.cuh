@@ -1,0 +1,55 @@
+// quant.cuh -- quantization of one 256-element activation block by a
+// 256-thread CUDA block (QuantizeBlocks, internal/kernels/q8.go:50-97 and
+// 237-273 of gsoultan/mimir-model), shared by every kernel that produces
+// 8-bit activations.
+#pragma once
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mimgpu {
+
+struct QuantScratch {
+    float amax[8];
+    int bad[8];
+};
+
+// Quantizes the block whose element threadIdx.x is v: amax over the block,
+// q = RoundToEven(127*x/amax) in float64, dx = amax/127, the sums of each
+// run of 32 and of 16 quants, and the block's flag (0 when it holds NaN,
+// Inf or |x| > 2^60, which the reference refuses).
+__device__ __forceinline__ void quant_block_256(float v, long long row, long long K, int blk, ActQ8 act,
+                                                QuantScratch &qs) {
+    const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+    const float a = fabsf(v);
+    const bool bad = !(a <= 0x1p60f);
+    const float m = warp_max(bad ? 0.f : a);
+    const unsigned anyb = __ballot_sync(0xffffffffu, bad);
+    if (lane == 0) {
+        qs.amax[w] = m;
+        qs.bad[w] = anyb != 0;
+    }
+    __syncthreads();
+    float amax = qs.amax[0];
+    int anybad = qs.bad[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) {
+        amax = fmaxf(amax, qs.amax[i]);
+        anybad |= qs.bad[i];
+    }
+    int q = 0;
+    if (amax != 0.f && !anybad) q = (int)rint(__ddiv_rn(127.0 * (double)v, (double)amax));
+    act.q[row * K + (long long)blk * 256 + t] = (int8_t)q;
+    int s16 = q;
+    for (int o = 8; o; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
+    const long long kb = row * (K / 256) + blk;
+    if ((lane & 15) == 0) act.ys[kb * 16 + w * 2 + (lane >> 4)] = (int16_t)s16;
+    if (lane == 0) act.xs[kb * 8 + w] = (int16_t)s32;
+    if (t == 0) {
+        act.dx[kb] = __fdiv_rn(amax, 127.f);
+        act.ok[kb] = anybad ? 0 : 1;
+    }
+}
+
+}  // namespace mimgpu

@@ -60,6 +60,7 @@ SIGNATURES = {
     "mimgpu_session_reset": (I32, [P]),
     "mimgpu_session_run": (I32, [P, P, P, I32, P, I32]),
     "mimgpu_session_generate": (I32, [P, I32, I64, I32, P]),
+    "mimgpu_session_stream": (P, [P]),
 }
 
 
@@ -348,6 +349,14 @@ class Session:
         ids = np.empty(steps, np.int32)
         self.m.ctx._check(lib().mimgpu_session_generate(self.h, token, pos, steps, _p(ids)))
         return ids
+
+    @property
+    def stream(self) -> int:
+        return lib().mimgpu_session_stream(self.h)
+
+    def run_ptr(self, tok_ptr: int, pos_ptr: int, t: int, logits_ptr: int, all_rows: bool = False):
+        """session_run on caller-owned host buffers (e.g. pinned memory)."""
+        self.m.ctx._check(lib().mimgpu_session_run(self.h, tok_ptr, pos_ptr, t, logits_ptr, int(all_rows)))
 
     def free(self):
         if self.h:
