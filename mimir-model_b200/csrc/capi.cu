@@ -373,7 +373,7 @@ int mimgpu_attention(mimgpu_ctx *c, const float *q, int b, int hq, int tq, int d
         }
         mbytes = acc;
     }
-    if (tk > 49152 || d > 512) return fail(c, MIMGPU_ENOTHANDLED, "attention: %d keys of %d dims", tk, d);
+    if (tk > 49152 || d > 512 || d % 8) return fail(c, MIMGPU_ENOTHANDLED, "attention: %d keys of %d dims", tk, d);
     const long long nq = (long long)b * hq * tq * d, nkv = (long long)b * hkv * tk * d;
     if (nq == 0) return MIMGPU_OK;
     const int es = kv_dtype == F16 ? 2 : 4;

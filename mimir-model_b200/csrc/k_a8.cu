@@ -15,6 +15,7 @@
 // The products themselves are in k_gemv_a8.cu.
 #include "common.cuh"
 #include "kernels.h"
+#include "amd64_math.cuh"
 #include "quant.cuh"
 
 namespace mimgpu {
@@ -100,13 +101,9 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
     if (act.q) quant_block_256(v, row, n, b, act, qs);
 }
 
-__device__ __forceinline__ float silu_mul_f64(float a, float b) {
-    const double ad = (double)a;
-    return (float)__dmul_rn(__ddiv_rn(ad, __dadd_rn(1.0, exp(-ad))), (double)b);
-}
-
-// swiglu.v1 (plain-Go SiluMulF32, internal/kernels/attn.go:63-73) fused
-// with the quantization of its output for the down projection.
+// swiglu.v1 (SiluMulF32, internal/kernels/attn.go:59-73: siluMulF32AVX2 on
+// the first n&~7 elements, float64 on the rest) fused with the quantization
+// of its output for the down projection.
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *__restrict__ gate, const float *__restrict__ up,
                                                            long long ldg, int n, float *__restrict__ y, ActQ8 act) {
     __shared__ QuantScratch qs;
@@ -116,7 +113,8 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *__restri
     const int b = blockIdx.y, i = b * 256 + threadIdx.x;
     float v = 0.f;
     if (i < n) {
-        v = silu_mul_f64(gate[row * ldg + i], up[row * ldg + i]);
+        v = i < (n & ~7) ? silu_mul_amd64(gate[row * ldg + i], up[row * ldg + i])
+                         : silu_mul_f64(gate[row * ldg + i], up[row * ldg + i]);
         y[row * n + i] = v;
     }
     if (act.q) quant_block_256(v, row, n, b, act, qs);

@@ -1,13 +1,14 @@
 // k_model.cu -- kernels of the device-resident llama step (importer/llama.go:
 // 400-534 of gsoultan/mimir-model): RoPE with the key/value cache write,
-// split-K attention over the cache, its combine fused with the 8-bit
-// quantization of the output, and the greedy-step bookkeeping.
+// attention over the cache with the reference's amd64 arithmetic fused with
+// the 8-bit quantization of its output, and the greedy-step bookkeeping.
 //
 // Layouts in HBM: qkv [T, E + 2*Hkv*D] (the three projections side by side),
 // q heads [H, T, D], cache [Hkv, C, D] per layer (f16 or f32), attention
 // output [T, H*D] (the layout the o projection reads).
 #include "common.cuh"
 #include "model_kernels.h"
+#include "amd64_math.cuh"
 #include "quant.cuh"
 
 namespace mimgpu {
@@ -73,140 +74,120 @@ __global__ void rope_scatter_kernel(RopeScatterArgs a) {
     else ((float *)a.kc)[at] = out;
 }
 
-__device__ __forceinline__ float h2f(uint32_t h) {  // f16 bits -> f32 (exact)
-    float f;
-    asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"((unsigned short)h));
-    return f;
-}
-
-// Split-K attention of the G query heads sharing kv head blockIdx.x, for
-// query row blockIdx.y, over the 64 keys [64 s, 64 s + 64) of its visible
-// range [0, pos + 1) (the mask j <= p of importer/llama.go:364-397).  The
-// key and value rows are staged in shared memory with a 2-word row pad so
-// the row-parallel reads below fall on distinct banks.  Writes the split's
-// max, sum of exp(s - max) and unnormalised output.
+// attention.v2 (attention.v1 for an f32 cache) of HPB = 256/D query heads
+// h0 = HPB*blockIdx.x.. of query row t = blockIdx.y over the keys [0, pos+1)
+// its mask admits (j <= p, importer/llama.go:364-397), computed exactly as
+// attendRow (interp/fast.go:728-751) with the reference's amd64 kernels:
+// scores as scoresF16AVX2 (8 fused lanes, group-of-four / tail orders),
+// ExpSumF32 (Cephes expf on the first n&~7 keys with its lane-sum order,
+// float64 exp on the rest), the fused key-ordered weighted sum of wsumF16AVX2,
+// o = acc/sum.  The 256 outputs of the block (H*D row-major, the layout the o
+// projection reads) are then quantized to 8 bits when act.q is set.
 template <bool F16>
-__global__ void __launch_bounds__(128) attn_split_kernel(AttnSplitArgs a) {
-    extern __shared__ __align__(16) uint32_t sm[];
-    const int G = a.H / a.Hkv, D = a.D;
-    const int P = (F16 ? D / 2 : D) + 2;      // row pitch in 32-bit words
-    float *qs = (float *)sm;                  // [G][D]
-    uint32_t *kt = sm + G * D;                // [64][P]
-    uint32_t *vt = kt + 64 * P;               // [64][P]
-    float *sc = (float *)(vt + 64 * P);       // [G][64]
-    float *ml = sc + G * 64;                  // [G][2]
+__global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
+    extern __shared__ float asmem[];
+    __shared__ QuantScratch qs;
+    __shared__ float red[8][8];
+    __shared__ float hsum[8], hmax[8];
     pdl_launch_dependents();
     pdl_wait();
-    const int hk = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
-    const long long end = a.pos[t] + 1, j0 = (long long)s * 64;
-    const long long pidx = ((long long)t * a.H + hk * G) * a.S + s;  // head g adds g*S
-    if (j0 >= end) {
-        if (tid < G) {
-            a.pml[(pidx + (long long)tid * a.S) * 2] = -INFINITY;
-            a.pml[(pidx + (long long)tid * a.S) * 2 + 1] = 0.f;
-        }
-        return;
-    }
-    const int n = (int)min(64LL, end - j0);
-    // stage q, K and V (all loads issued before any use)
-    for (int i = tid; i < G * D; i += 128) qs[i] = a.qh[((long long)(hk * G + i / D) * a.T + t) * D + i % D];
-    const int wpr = F16 ? D / 2 : D;          // words per key row
-    const int cpr = wpr / 4;                  // 16-byte pieces per key row
-    const uint4 *kg = (const uint4 *)((const uint32_t *)a.kc + ((long long)hk * a.C + j0) * wpr);
-    const uint4 *vg = (const uint4 *)((const uint32_t *)a.vc + ((long long)hk * a.C + j0) * wpr);
-    for (int i = tid; i < n * cpr; i += 128) {
-        const uint4 k4 = kg[i], v4 = vg[i];
-        const int j = i / cpr, c = i % cpr;
-        uint32_t *kd = kt + j * P + 4 * c, *vd = vt + j * P + 4 * c;
-        *(uint2 *)kd = make_uint2(k4.x, k4.y);
-        *(uint2 *)(kd + 2) = make_uint2(k4.z, k4.w);
-        *(uint2 *)vd = make_uint2(v4.x, v4.y);
-        *(uint2 *)(vd + 2) = make_uint2(v4.z, v4.w);
-    }
+    const int D = a.D, HPB = 256 / D, G = a.H / a.Hkv;
+    const int t = blockIdx.y, h0 = blockIdx.x * HPB, tid = threadIdx.x;
+    const int nh = min(HPB, a.H - h0);  // heads of this block (fewer in a last partial block)
+    const int n = (int)(a.pos[t] + 1);
+    float *q = asmem;                   // [HPB][D]
+    float *sc = asmem + 256;            // [HPB][C]
+    if (tid / D < nh) q[tid] = a.qh[((long long)(h0 + tid / D) * a.T + t) * D + tid % D];
     __syncthreads();
-    // scores: thread (key j, parity hh) dots the words 2i + hh of row j
-    {
-        const int j = tid >> 1, hh = tid & 1;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (j < n) {
-            const uint32_t *kr = kt + j * P;
-            for (int i = 0; i < wpr / 2; i++) {
-                const int wi = 2 * i + hh;
-                const uint32_t kw = kr[wi];
-                if (F16) {
-                    const float k0 = h2f(kw & 0xFFFF), k1 = h2f(kw >> 16);
-                    for (int g = 0; g < G; g++) {
-                        acc[g] = __fmaf_rn(qs[g * D + 2 * wi], k0, acc[g]);
-                        acc[g] = __fmaf_rn(qs[g * D + 2 * wi + 1], k1, acc[g]);
-                    }
-                } else {
-                    const float k0 = __uint_as_float(kw);
-                    for (int g = 0; g < G; g++) acc[g] = __fmaf_rn(qs[g * D + wi], k0, acc[g]);
+    // scores: an 8-lane group per (key, head); group g of pass u takes item
+    // base + 32 u + g: key item / nh, head item % nh
+    const int l = tid & 7, grp = tid >> 3;
+    const int n4 = n & ~3, items = n * nh;
+    for (int base = 0; base < items; base += 32 * 4) {
+        float acc[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int item = base + 32 * u + grp;
+            acc[u] = 0.f;
+            if (item < items) {
+                const int j = item / nh, hh = item % nh;
+                const long long kr = ((long long)((h0 + hh) / G) * a.C + j) * D;
+                const float *qr = q + hh * D;
+                for (int c = 0; c < D / 8; c++) {
+                    const float kv = F16 ? h2f_bits(((const uint16_t *)a.kc)[kr + 8 * c + l])
+                                         : ((const float *)a.kc)[kr + 8 * c + l];
+                    acc[u] = __fmaf_rn(qr[8 * c + l], kv, acc[u]);
                 }
             }
         }
-        for (int g = 0; g < G; g++) {
-            const float v = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
-            if (hh == 0 && j < n) sc[g * 64 + j] = __fmul_rn(v, a.scale);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int item = base + 32 * u + grp;
+            const int j = item / nh;
+            const float v = score_combine(acc[u], j >= n4);  // the 8 lanes of a group share j
+            if (item < items && l == 0) sc[(item % nh) * a.C + j] = __fmul_rn(v, a.scale);
         }
     }
     __syncthreads();
+    // max per head (warp hh); exact in any order
     const int lane = tid & 31, w = tid >> 5;
-    for (int g = w; g < G; g += 4) {
+    if (w < nh) {
         float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[g * 64 + j]);
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[w * a.C + j]);
         m = warp_max(m);
-        float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float e = (float)exp((double)__fsub_rn(sc[g * 64 + j], m));
-            sc[g * 64 + j] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) { ml[2 * g] = m; ml[2 * g + 1] = l; }
+        if (lane == 0) hmax[w] = m;
     }
     __syncthreads();
-    for (int d = tid; d < D; d += 128) {
-        float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int j = 0; j < n; j++) {
-            const uint32_t vw = vt[j * P + (F16 ? d >> 1 : d)];
-            const float v = F16 ? h2f((d & 1) ? (vw >> 16) : (vw & 0xFFFF)) : __uint_as_float(vw);
-            for (int g = 0; g < G; g++) o[g] = __fmaf_rn(sc[g * 64 + j], v, o[g]);
-        }
-        for (int g = 0; g < G; g++) a.po[(pidx + (long long)g * a.S) * D + d] = o[g];
+    // exp of the scores: Cephes on the first n&~7 keys (none when n < 8)
+    const int n8 = n >= 8 ? (n & ~7) : 0;
+    for (int i = tid; i < items; i += 256) {
+        const int hh = i / n, j = i % n;
+        const float x = __fsub_rn(sc[hh * a.C + j], hmax[hh]);
+        sc[hh * a.C + j] = j < n8 ? expf_amd64(x) : (float)exp((double)x);
     }
-    if (tid < G) {
-        a.pml[(pidx + (long long)tid * a.S) * 2] = ml[2 * tid];
-        a.pml[(pidx + (long long)tid * a.S) * 2 + 1] = ml[2 * tid + 1];
+    __syncthreads();
+    // ExpSumF32's sum: 8 lane sums in key order, combined, then the tail in order
+    if (tid < 8 * nh) {
+        const int hh = tid >> 3, ll = tid & 7;
+        float sl = 0.f;
+        for (int j = ll; j < n8; j += 8) sl = __fadd_rn(sl, sc[hh * a.C + j]);
+        red[hh][ll] = sl;
     }
-}
-
-// Merges the splits of query row blockIdx.x for output elements
-// [256 b, 256 b + 256) of out [T, H*D], then quantizes that block (act.q).
-__global__ void __launch_bounds__(256) attn_combine_kernel(AttnCombineArgs a) {
-    __shared__ QuantScratch qs;
-    pdl_launch_dependents();
-    pdl_wait();
-    const int t = blockIdx.x, b = blockIdx.y, i = b * 256 + threadIdx.x;
-    const int E = a.H * a.D;
-    const long long end = a.pos[t] + 1;
-    const int S = (int)min((long long)a.S, (end + a.chunk - 1) / a.chunk);
-    float v = 0.f;
-    if (i < E) {
-        const int h = i / a.D, d = i % a.D;
-        const long long base = ((long long)t * a.H + h) * a.S;
-        float M = -INFINITY;
-        for (int s = 0; s < S; s++) M = fmaxf(M, a.pml[(base + s) * 2]);
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < S; s++) {
-            const float f = expf(a.pml[(base + s) * 2] - M);
-            L = __fmaf_rn(a.pml[(base + s) * 2 + 1], f, L);
-            O = __fmaf_rn(a.po[(base + s) * a.D + d], f, O);
-        }
-        v = __fdiv_rn(O, L);
-        a.out[(long long)t * E + i] = v;
+    __syncthreads();
+    if (tid < nh) {
+        const float *r = red[tid];
+        float sum = 0.f;
+        if (n8) sum = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[4]), __fadd_rn(r[1], r[5])),
+                                __fadd_rn(__fadd_rn(r[2], r[6]), __fadd_rn(r[3], r[7])));
+        for (int j = n8; j < n; j++) sum = __fadd_rn(sum, sc[tid * a.C + j]);
+        hsum[tid] = sum;
     }
-    if (a.act.q) quant_block_256(v, t, E, b, a.act, qs);
+    __syncthreads();
+    // weighted sum of the values: one fused multiply-add per key, in key order
+    const int hh = tid / D, d = tid % D;
+    if (hh >= nh) return;  // only in a partial block, which never quantizes (E % 256 != 0)
+    const long long vr = (long long)((h0 + hh) / G) * a.C * D + d;
+    const float *e = sc + hh * a.C;
+    float acc = 0.f;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            v[u] = F16 ? h2f_bits(((const uint16_t *)a.vc)[vr + (long long)(j + u) * D])
+                       : ((const float *)a.vc)[vr + (long long)(j + u) * D];
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc = __fmaf_rn(e[j + u], v[u], acc);
+    }
+    for (; j < n; j++) {
+        const float v = F16 ? h2f_bits(((const uint16_t *)a.vc)[vr + (long long)j * D])
+                            : ((const float *)a.vc)[vr + (long long)j * D];
+        acc = __fmaf_rn(e[j], v, acc);
+    }
+    const float o = __fdiv_rn(acc, hsum[hh]);
+    const int E = a.H * D;
+    a.out[(long long)t * E + (long long)h0 * D + tid] = o;
+    if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 
 // After the argmax of a greedy step: the picked id becomes the next input
@@ -229,38 +210,25 @@ cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool 
     return cudaLaunchKernelEx(&cfg, rope_scatter_kernel, a);
 }
 
-size_t attn_split_smem(int G, int D, int f16) {
-    const int P = (f16 ? D / 2 : D) + 2;
-    return sizeof(float) * ((size_t)G * D + 2 * 64 * (size_t)P + (size_t)G * 64 + 2 * G);
-}
-
-cudaError_t launch_attn_split(const AttnSplitArgs &a, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
     if (a.T <= 0) return cudaSuccess;
-    const int G = a.H / a.Hkv;
-    if (G > 8 || a.D % 32 || a.D > 128 || a.chunk != 64) return cudaErrorInvalidValue;
-    const size_t smem = attn_split_smem(G, a.D, a.cache_f16);
+    // heads of 32..256 elements dividing 256; the fused quantization needs
+    // whole blocks of 256 outputs
+    if (a.D < 32 || 256 % a.D || a.Hkv <= 0 || a.H % a.Hkv || (a.act.q && a.H % (256 / a.D)))
+        return cudaErrorInvalidValue;
+    const int HPB = 256 / a.D;
+    const size_t smem = attn_exact_smem(a.D, a.C);
+    if (smem > kAttnSmemMax) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = mk(dim3(a.Hkv, a.T, a.S), dim3(128), smem, st, pdl, attr);
+    cudaLaunchConfig_t cfg = mk(dim3((a.H + HPB - 1) / HPB, a.T), dim3(256), smem, st, pdl, attr);
     if (a.cache_f16) {
-        if (smem > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(attn_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
-        return cudaLaunchKernelEx(&cfg, attn_split_kernel<true>, a);
-    }
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attn_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(attn_exact_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        return cudaLaunchKernelEx(&cfg, attn_exact_kernel<true>, a);
     }
-    return cudaLaunchKernelEx(&cfg, attn_split_kernel<false>, a);
-}
-
-cudaError_t launch_attn_combine(const AttnCombineArgs &a, cudaStream_t st, bool pdl) {
-    if (a.T <= 0) return cudaSuccess;
-    if (a.act.q && (a.H * a.D) % 256) return cudaErrorInvalidValue;
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = mk(dim3(a.T, (a.H * a.D + 255) / 256), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, attn_combine_kernel, a);
+    cudaError_t e = cudaFuncSetAttribute(attn_exact_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, attn_exact_kernel<false>, a);
 }
 
 cudaError_t launch_advance(const int *argmax, int32_t *tok, int64_t *pos, int32_t *ids, int *step, cudaStream_t st,

@@ -6,15 +6,16 @@
 //              two f32 roundings.
 //   rope       interp/fast.go:507-557   cos/sin of pos*inv_freq in float64,
 //              rounded to f32; y1 = x1*c - x2*s, y2 = x2*c + x1*s unfused.
-//   swiglu     internal/kernels/attn.go:63-73 (plain Go): float64 silu times
-//              b, rounded once.
-//   attention  interp/fast.go:569-751, internal/kernels/attn.go:26-121:
-//              visible keys from the boolean mask, softmax with exp of
-//              (s - max) in float64 rounded to f32, f16 keys and values
-//              converted exactly.
+//   swiglu     internal/kernels/attn.go:59-73: siluMulF32AVX2 on the first
+//              n&~7 elements, float64 on the rest.
+//   attention  interp/fast.go:569-751, internal/kernels/attn.go:26-121 and
+//              attn_amd64.s: the vector path of rows without masked holes,
+//              the scalar path otherwise; f16 keys and values converted
+//              exactly.
 //   argmax     cmd/mim-run/main.go:184-193: first index of the maximum.
 #include <cfloat>
 
+#include "amd64_math.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -97,16 +98,12 @@ __global__ void rope_kernel(const float *__restrict__ x, int H, int T, int D, co
     }
 }
 
-__device__ __forceinline__ float silu_mul(float a, float b) {
-    const double ad = (double)a;
-    return (float)__dmul_rn(__ddiv_rn(ad, __dadd_rn(1.0, exp(-ad))), (double)b);
-}
 
 __global__ void swiglu_kernel(const float *__restrict__ a, const float *__restrict__ b, long long n, float *__restrict__ y) {
     pdl_launch_dependents();
     pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        y[i] = silu_mul(a[i], b[i]);
+        y[i] = i < (n & ~7LL) ? silu_mul_amd64(a[i], b[i]) : silu_mul_f64(a[i], b[i]);
 }
 
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, long long n, float *__restrict__ y) {
@@ -127,18 +124,26 @@ __device__ __forceinline__ float kv_at(const void *base, int f16, long long i) {
 
 // ---------------------------------------------------------- attention (general)
 // One 256-thread block per query row (b, h, i); scores in dynamic shared memory.
+// Rows whose visible keys [st, end) hold no masked key take the reference's
+// vector path (attendRow, interp/fast.go:728-751, with the amd64 kernels:
+// 8 fused lanes per score in the group-of-four / tail orders, Cephes expf on
+// the first n&~7 keys with the lane-sum order, fused key-ordered weighted
+// sum); rows with holes, or whose largest score is not finite, take the
+// scalar path of fast.go:661-716 (dotF32Go scores, masked keys -inf, exp in
+// float64, sequential sum, unfused accumulation skipping zero weights).
 __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
     extern __shared__ float sc[];
     __shared__ float red[8];
     __shared__ int ired[8];
     __shared__ float qsh[512];
+    __shared__ float lsum[8], ssum;
     const int t = threadIdx.x, lane = t & 31, w = t >> 5;
     const int row = blockIdx.x;
     const int i = row % a.Tq, h = (row / a.Tq) % a.Hq, b = row / (a.Tq * a.Hq);
-    const int G = a.Hq / a.Hkv, kvh = b * a.Hkv + h / G;
-    const float *q = a.q + (long long)row * a.D;
-    for (int d = t; d < a.D; d += 256) qsh[d] = q[d];
-    const long long kvoff = (long long)kvh * a.Tk * a.D;
+    const int G = a.Hq / a.Hkv, kvh = b * a.Hkv + h / G, D = a.D;
+    const float *q = a.q + (long long)row * D;
+    for (int d = t; d < D; d += 256) qsh[d] = q[d];
+    const long long kvoff = (long long)kvh * a.Tk * D;
     const uint8_t *mrow = a.mask ? a.mask + b * a.mst[0] + h * a.mst[1] + i * a.mst[2] : nullptr;
     const bool in_order = !a.mask || a.mst[3] == 1;
     // visible range [st, end) of a boolean mask row, interp/fast.go:606-636
@@ -167,60 +172,126 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
         for (int j = st + t; j < end; j += 256) hole |= mrow[j] == 0;
         vector_path = !__syncthreads_or(hole);
     }
-    const int j0 = vector_path ? st : 0;
-    // scores: one warp per key
-    for (int j = j0 + w; j < end; j += 8) {
-        float s = 0.f;
-        for (int d = lane; d < a.D; d += 32) s = __fmaf_rn(qsh[d], kv_at(a.k, a.kv_f16, kvoff + (long long)j * a.D + d), s);
-        s = warp_sum(s);
-        bool allowed = true;
-        if (!vector_path) {
-            allowed = !a.causal || j <= i + (a.Tk - a.Tq);
-            if (a.mask) allowed = allowed && mrow[(long long)j * a.mst[3]] != 0;
+    float mx;
+    int n, j0;
+    if (vector_path) {
+        // scores of keys st.. as scoresF16AVX2 / scoresF32AVX2
+        j0 = st;
+        n = end - st;
+        const int l = t & 7, grp = t >> 3, n4 = n & ~3;
+        for (int base = 0; base < n; base += 32) {
+            const int j = base + grp;
+            float acc = 0.f;
+            if (j < n) {
+                const long long kr = kvoff + (long long)(j0 + j) * D;
+                for (int c = 0; c < D / 8; c++) acc = __fmaf_rn(qsh[8 * c + l], kv_at(a.k, a.kv_f16, kr + 8 * c + l), acc);
+            }
+            const float v = score_combine(acc, j >= n4);
+            if (j < n && l == 0) sc[j] = __fmul_rn(v, a.scale);
         }
-        if (lane == 0) sc[j - j0] = allowed ? __fmul_rn(s, a.scale) : -INFINITY;
+        __syncthreads();
+        float m = -INFINITY;
+        int nan = 0;
+        for (int j = t; j < n; j += 256) {
+            const float s = sc[j];
+            if (s != s) nan = 1; else m = fmaxf(m, s);
+        }
+        m = warp_max(m);
+        if (lane == 0) red[w] = m;
+        nan = __syncthreads_or(nan);
+        mx = red[0];
+        for (int k = 1; k < 8; k++) mx = fmaxf(mx, red[k]);
+        __syncthreads();
+        vector_path = !nan && mx != INFINITY && mx != -INFINITY;
     }
-    __syncthreads();
-    const int n = end - j0;
-    float mx = -INFINITY;
-    int nan = 0;
-    for (int j = t; j < n; j += 256) {
-        const float s = sc[j];
-        if (s != s) nan = 1; else mx = fmaxf(mx, s);
+    if (!vector_path) {
+        // scalar scores of keys 0..end: dotF32Go's four strided lanes, then
+        // times scale plus zero; masked keys -inf
+        j0 = 0;
+        n = end;
+        const int l = t & 3, grp = t >> 2, D4 = D & ~3;
+        for (int base = 0; base < n; base += 64) {
+            const int j = base + grp;
+            float acc = 0.f;
+            if (j < n) {
+                const long long kr = kvoff + (long long)j * D;
+                for (int e = l; e < D4; e += 4) acc = __fadd_rn(acc, __fmul_rn(qsh[e], kv_at(a.k, a.kv_f16, kr + e)));
+                if (l == 0)
+                    for (int e = D4; e < D; e++) acc = __fadd_rn(acc, __fmul_rn(qsh[e], kv_at(a.k, a.kv_f16, kr + e)));
+            }
+            const float a1 = __shfl_xor_sync(0xffffffffu, acc, 1);    // s0+s1 / s2+s3
+            const float p = __fadd_rn((l & 1) ? a1 : acc, (l & 1) ? acc : a1);
+            const float p2 = __shfl_xor_sync(0xffffffffu, p, 2);
+            const float tot = __fadd_rn((l & 2) ? p2 : p, (l & 2) ? p : p2);
+            if (j < n && l == 0) {
+                bool allowed = !a.causal || j <= i + (a.Tk - a.Tq);
+                if (a.mask) allowed = allowed && mrow[(long long)j * a.mst[3]] != 0;
+                sc[j] = allowed ? __fadd_rn(__fmul_rn(tot, a.scale), 0.f) : -INFINITY;
+            }
+        }
+        __syncthreads();
+        float m = -INFINITY;
+        int nan = 0;
+        for (int j = t; j < n; j += 256) {
+            const float s = sc[j];
+            if (s != s) nan = 1; else m = fmaxf(m, s);
+        }
+        m = warp_max(m);
+        if (lane == 0) red[w] = m;
+        nan = __syncthreads_or(nan);
+        mx = red[0];
+        for (int k = 1; k < 8; k++) mx = fmaxf(mx, red[k]);
+        if (nan) mx = __int_as_float(0x7fc00000);
+        __syncthreads();
     }
-    mx = warp_max(mx);
-    if (lane == 0) red[w] = mx;
-    nan = __syncthreads_or(nan);
-    mx = red[0];
-    for (int k = 1; k < 8; k++) mx = fmaxf(mx, red[k]);
-    if (nan) mx = __int_as_float(0x7fc00000);
-    __syncthreads();
-    // the vector path of the reference requires a finite maximum; otherwise
-    // the scalar path, whose only differences are the masked keys' zeros
+    if (vector_path) {
+        const int n8 = n >= 8 ? (n & ~7) : 0;
+        for (int j = t; j < n; j += 256) {
+            const float x = __fsub_rn(sc[j], mx);
+            sc[j] = j < n8 ? expf_amd64(x) : (float)exp((double)x);
+        }
+        __syncthreads();
+        if (t < 8) {
+            float sl = 0.f;
+            for (int j = t; j < n8; j += 8) sl = __fadd_rn(sl, sc[j]);
+            lsum[t] = sl;
+        }
+        __syncthreads();
+        if (t == 0) {
+            float sum = 0.f;
+            if (n8) sum = __fadd_rn(__fadd_rn(__fadd_rn(lsum[0], lsum[4]), __fadd_rn(lsum[1], lsum[5])),
+                                    __fadd_rn(__fadd_rn(lsum[2], lsum[6]), __fadd_rn(lsum[3], lsum[7])));
+            for (int j = n8; j < n; j++) sum = __fadd_rn(sum, sc[j]);
+            ssum = sum;
+        }
+        __syncthreads();
+        for (int d = t; d < D; d += 256) {
+            float acc = 0.f;
+            for (int j = 0; j < n; j++) acc = __fmaf_rn(sc[j], kv_at(a.v, a.kv_f16, kvoff + (long long)(j0 + j) * D + d), acc);
+            a.out[(long long)row * D + d] = __fdiv_rn(acc, ssum);
+        }
+        return;
+    }
     const bool mx_neg_inf = mx == -INFINITY;
-    float psum = 0.f;
     for (int j = t; j < n; j += 256) {
         const float s = sc[j];
-        float e;
-        if (s == -INFINITY && !mx_neg_inf) e = 0.f;
-        else e = (float)exp((double)__fsub_rn(s, mx));
-        sc[j] = e;
-        psum += e;
+        sc[j] = (s == -INFINITY && !mx_neg_inf) ? 0.f : (float)exp((double)__fsub_rn(s, mx));
     }
-    psum = warp_sum(psum);
     __syncthreads();
-    if (lane == 0) red[w] = psum;
+    if (t == 0) {
+        float sum = 0.f;
+        for (int j = 0; j < n; j++) sum = __fadd_rn(sum, sc[j]);  // masked keys add +0
+        ssum = sum;
+    }
     __syncthreads();
-    float sum = 0.f;
-    for (int k = 0; k < 8; k++) sum += red[k];
-    for (int d = t; d < a.D; d += 256) {
+    for (int d = t; d < D; d += 256) {
         float acc = 0.f;
         for (int j = 0; j < n; j++) {
             const float e = sc[j];
             if (e == 0.f) continue;
-            acc = __fmaf_rn(e, kv_at(a.v, a.kv_f16, kvoff + (long long)(j0 + j) * a.D + d), acc);
+            acc = __fadd_rn(acc, __fmul_rn(e, kv_at(a.v, a.kv_f16, kvoff + (long long)j * D + d)));
         }
-        a.out[(long long)row * a.D + d] = __fdiv_rn(acc, sum);
+        a.out[(long long)row * D + d] = __fdiv_rn(acc, ssum);
     }
 }
 
@@ -303,7 +374,7 @@ constexpr int kMaxAttnKeys = 49152;
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     const long long rows = (long long)a.B * a.Hq * a.Tq;
     if (rows <= 0) return cudaSuccess;
-    if (a.Tk > kMaxAttnKeys || a.D > 512) return cudaErrorInvalidValue;
+    if (a.Tk > kMaxAttnKeys || a.D > 512 || a.D % 8) return cudaErrorInvalidValue;
     const size_t smem = sizeof(float) * (size_t)(a.Tk > 0 ? a.Tk : 1);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -30,8 +30,6 @@ struct LayerW {
     const mimgpu_tensor *ffn_norm = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
 };
 
-constexpr int kChunkDecode = 64;  // keys per attention split when T = 1
-
 }  // namespace
 
 struct mimgpu_model {
@@ -49,12 +47,11 @@ struct mimgpu_session {
     size_t cache_bytes = 0;
     void *arena = nullptr;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *qh = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr;
-    float *logits = nullptr, *po = nullptr, *pml = nullptr;
+    float *logits = nullptr;
     ActQ8 actE{}, actF{};
     int32_t *tok = nullptr, *ids = nullptr;
     int64_t *pos = nullptr;
     int *amax = nullptr, *step = nullptr;
-    int S_decode = 0, S_prefill = 0, chunk_prefill = 0;
     cudaGraphExec_t g_step = nullptr;    // T=1 forward, logits of the row
     cudaGraphExec_t g_greedy = nullptr;  // T=1 forward + argmax + advance
 };
@@ -116,8 +113,6 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     } while (0)
     const ActQ8 none{};
     CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl));
-    const int S = T == 1 ? s->S_decode : s->S_prefill;
-    const int chunk = T == 1 ? kChunkDecode : s->chunk_prefill;
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
@@ -130,11 +125,9 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
-        AttnSplitArgs sa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16, chunk, S,
-                         (float)(1.0 / std::sqrt((double)D)), s->po, s->pml};
-        CK(launch_attn_split(sa, st, pdl));
-        AttnCombineArgs ca{s->po, s->pml, s->pos, T, H, D, S, chunk, s->att, a8 ? s->actE : none};
-        CK(launch_attn_combine(ca, st, pdl));
+        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
+                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none};
+        CK(launch_attn_exact(aa, st, pdl));
         GemvSeg o{w.o->dev, w.o->dtype, E, s->x, E, nullptr, s->x};
         if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
@@ -209,8 +202,10 @@ int mimgpu_model_new(mimgpu_ctx *ctx, const mimgpu_llama_config *cfg, mimgpu_mod
         return fail(ctx, MIMGPU_EINVAL, "llama config is inconsistent");
     if (c.rope_dims <= 0 || c.rope_dims % 2 || c.rope_dims > c.head_dim)
         return fail(ctx, MIMGPU_EINVAL, "rope dimension count %d for head size %d", c.rope_dims, c.head_dim);
-    if (c.head_dim % 32 || c.head_dim > 128 || c.heads / c.kv_heads > 8)
-        return fail(ctx, MIMGPU_ENOTHANDLED, "head size %d / group %d not served", c.head_dim, c.heads / c.kv_heads);
+    if (c.head_dim % 32 || 256 % c.head_dim)
+        return fail(ctx, MIMGPU_ENOTHANDLED, "head size %d not served (32, 64, 128 or 256)", c.head_dim);
+    if (attn_exact_smem(c.head_dim, c.context) > kAttnSmemMax)
+        return fail(ctx, MIMGPU_ENOTHANDLED, "context %d too long for the attention scores in shared memory", c.context);
     if (c.a8 && (c.embed % 256 || c.ffn % 256))
         return fail(ctx, MIMGPU_ENOTHANDLED, "8-bit activations need E and F multiples of 256");
     int rc = use_device(ctx);
@@ -275,16 +270,10 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->m = m;
     const long long T = k.max_tokens, E = k.embed, F = k.ffn, V = k.vocab, H = k.heads, D = k.head_dim;
     const long long KV = (long long)k.kv_heads * D;
-    // attention splits of 64 keys for every query row
-    s->S_decode = (k.context + kChunkDecode - 1) / kChunkDecode;
-    s->chunk_prefill = kChunkDecode;
-    s->S_prefill = s->S_decode;
-    const long long split_rows = std::max((long long)s->S_decode, T * s->S_prefill);
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     size_t bytes = 0;
     const size_t sz[] = {al(T * E * 4), al(T * E * 4), al(T * (E + 2 * KV) * 4), al(T * E * 4), al(T * E * 4),
-                         al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), al(split_rows * H * D * 4),
-                         al(split_rows * H * 2 * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
+                         al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
                          al(T * 4), al(T * 8), al(65536 * 4), al(256)};
     for (size_t b : sz) bytes += b;
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
@@ -304,8 +293,6 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->gu = (float *)take();
     s->a = (float *)take();
     s->logits = (float *)take();
-    s->po = (float *)take();
-    s->pml = (float *)take();
     s->actE = act_q8_carve(take(), (int)T, E);
     s->actF = act_q8_carve(take(), (int)T, F);
     s->tok = (int32_t *)take();

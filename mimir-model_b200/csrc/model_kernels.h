@@ -19,29 +19,25 @@ struct RopeScatterArgs {
     void *kc, *vc;         // [Hkv, C, D]
 };
 
-struct AttnSplitArgs {
-    const float *qh;       // [H, T, D]
-    const void *kc, *vc;   // [Hkv, C, D]
-    const int64_t *pos;    // [T]
-    int T, H, Hkv, D, C, cache_f16;
-    int chunk, S;          // keys per split (64), splits
-    float scale;
-    float *po;             // [T, H, S, D]
-    float *pml;            // [T, H, S, 2]
-};
-
-struct AttnCombineArgs {
-    const float *po, *pml;
+// Attention of the model step: q heads [H, T, D] (after RoPE) over the cache
+// [Hkv, C, D], keys [0, pos[t]] for query row t; out [T, H*D] and, when
+// act.q is set, its 8-bit blocks.
+struct AttnArgs2 {
+    const float *qh;
+    const void *kc, *vc;
     const int64_t *pos;
-    int T, H, D, S, chunk;
-    float *out;            // [T, H*D]
-    ActQ8 act;             // q null: no quantization
+    int T, H, Hkv, D, C, cache_f16;
+    float scale;
+    float *out;
+    ActQ8 act;
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
-size_t attn_split_smem(int G, int D, int f16);
-cudaError_t launch_attn_split(const AttnSplitArgs &a, cudaStream_t st, bool pdl);
-cudaError_t launch_attn_combine(const AttnCombineArgs &a, cudaStream_t st, bool pdl);
+// Dynamic shared memory of the attention kernel: q and the scores of the
+// 256/D heads of a block over the whole context.
+constexpr size_t kAttnSmemMax = 200 * 1024;
+inline size_t attn_exact_smem(int D, int C) { return sizeof(float) * (256 + (size_t)(256 / D) * C); }
+cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
 cudaError_t launch_advance(const int *argmax, int32_t *tok, int64_t *pos, int32_t *ids, int *step, cudaStream_t st,
                            bool pdl);
 

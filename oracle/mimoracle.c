@@ -608,6 +608,48 @@ int mo_rope(const float *x, int B, int H, int T, int D, const int64_t *pos, int 
     return 0;
 }
 
+/* ------------------------------------------------------------------ */
+/* the amd64 vector kernels of internal/kernels/attn_amd64.s            */
+/* ------------------------------------------------------------------ */
+
+/* exp(t) as expSumF32AVX2 computes it (attn_amd64.s:82-237): Cephes' expf
+ * in float32 -- t = f*ln2 + r with f = RoundToEven(t*log2e), r by two fused
+ * steps, a degree-5 polynomial in r evaluated with fused multiply-adds,
+ * times 2^f -- and 0 below the limit (where VCMPPS GE_OQ is false; NaN too).
+ * The constants are the kernel's `expc` table. */
+static inline float expf_amd64(float t) {
+    const float lo = bits_f32(0xc2aeac4fu), log2e = bits_f32(0x3fb8aa3bu);
+    const float c1 = bits_f32(0x3f318000u), c2 = bits_f32(0xb95e8083u);
+    const float p0 = bits_f32(0x39506967u), p1 = bits_f32(0x3ab743ceu), p2 = bits_f32(0x3c088908u);
+    const float p3 = bits_f32(0x3d2aa9c1u), p4 = bits_f32(0x3e2aaaaau), p5 = bits_f32(0x3f000000u);
+    const int valid = t >= lo;
+    const float u = t > lo ? t : lo; /* VMAXPS: the second operand on NaN or equality */
+    const float f = rintf(u * log2e);
+    float r = fmaf(-f, c1, u);
+    r = fmaf(-f, c2, r);
+    const float r2 = r * r;
+    float p = p0;
+    p = fmaf(r, p, p1);
+    p = fmaf(r, p, p2);
+    p = fmaf(r, p, p3);
+    p = fmaf(r, p, p4);
+    p = fmaf(r, p, p5);
+    p = fmaf(r2, p, r);
+    p = p + 1.0f;
+    const float y = p * bits_f32((uint32_t)((int)f + 127) << 23);
+    return valid ? y : 0.0f;
+}
+
+/* silu(a)*b as siluMulF32AVX2 computes it (attn_amd64.s:465-527):
+ * h = exp(-|a|/2), silu = a/(1+h*h) for a >= 0, (a*h)*h/(1+h*h) below. */
+static inline float silu_mul_amd64(float a, float b) {
+    const float t = bits_f32(f32_bits(a) | 0x80000000u) * 0.5f;
+    const float h = expf_amd64(t);
+    const float den = h * h + 1.0f;
+    const float num = a >= 0.0f ? a : (a * h) * h;
+    return (num / den) * b;
+}
+
 /* one key/value row as f32 (f16 converts exactly) */
 static const float *kv_row(const void *base, int dt, int64_t j, int d, float *buf) {
     if (dt == MO_F32) return (const float *)base + j * d;
@@ -616,20 +658,55 @@ static const float *kv_row(const void *base, int dt, int64_t j, int d, float *bu
     return buf;
 }
 
-/* attendRow, interp/fast.go:728-751, with the plain-Go kernels of attn.go.
+/* attendRow, interp/fast.go:728-751, with the amd64 kernels of attn.go
+ * (d a multiple of 8, as for every llama head size):
+ *   ScoresF16/F32 -> scoresF16AVX2/scoresF32AVX2 (attn_amd64.s:12-80, 308-385):
+ *     8 fused-multiply-add accumulators a[l] over elements 8c+l; keys in
+ *     groups of four combine ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)), the last
+ *     n%4 keys ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)); then times scale;
+ *   ExpSumF32 (attn.go:41-56): the first n&~7 through expSumF32AVX2 with
+ *     8 lane sums combined ((S0+S4)+(S1+S5))+((S2+S6)+(S3+S7)), the rest
+ *     float32(math.Exp(float64)) added in order (all of them when n < 8);
+ *   WeightedSumF16/F32 -> wsum*AVX2: one fused multiply-add per element and
+ *     key, in key order;
+ *   o = acc / sum.
  * Returns 0 (caller takes the scalar path) when the largest score is not finite. */
 static int attend_row(const float *q, const void *kb, const void *vb, int dt, int64_t st, int64_t n, int d,
                       float scale, float *sc, float *acc, float *o, float *buf) {
-    for (int64_t j = 0; j < n; j++) sc[j] = mo_dot_f32(q, kv_row(kb, dt, st + j, d, buf), d) * scale;
+    const int64_t n4 = n & ~(int64_t)3;
+    for (int64_t j = 0; j < n; j++) {
+        const float *kr = kv_row(kb, dt, st + j, d, buf);
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int c = 0; c < d / 8; c++)
+            for (int l = 0; l < 8; l++) a[l] = fmaf(q[8 * c + l], kr[8 * c + l], a[l]);
+        const float v = j < n4 ? ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]))
+                               : ((a[0] + a[4]) + (a[1] + a[5])) + ((a[2] + a[6]) + (a[3] + a[7]));
+        sc[j] = v * scale;
+    }
     float mx = -INFINITY;
     for (int64_t j = 0; j < n; j++) if (sc[j] > mx || sc[j] != sc[j]) mx = sc[j];
     if (isinf(mx) || mx != mx) return 0;
     float sum = 0;
-    for (int64_t j = 0; j < n; j++) { float e = (float)exp((double)(sc[j] - mx)); sc[j] = e; sum += e; }
+    int64_t j = 0;
+    if (n >= 8) {
+        const int64_t n8 = n & ~(int64_t)7;
+        float S[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (; j < n8; j++) {
+            const float e = expf_amd64(sc[j] - mx);
+            sc[j] = e;
+            S[j & 7] += e;
+        }
+        sum = ((S[0] + S[4]) + (S[1] + S[5])) + ((S[2] + S[6]) + (S[3] + S[7]));
+    }
+    for (; j < n; j++) {
+        const float e = (float)exp((double)(sc[j] - mx));
+        sc[j] = e;
+        sum += e;
+    }
     for (int i = 0; i < d; i++) acc[i] = 0;
-    for (int64_t j = 0; j < n; j++) {
-        const float *vr = kv_row(vb, dt, st + j, d, buf);
-        for (int i = 0; i < d; i++) acc[i] += sc[j] * vr[i];
+    for (int64_t jj = 0; jj < n; jj++) {
+        const float *vr = kv_row(vb, dt, st + jj, d, buf);
+        for (int i = 0; i < d; i++) acc[i] = fmaf(sc[jj], vr[i], acc[i]);
     }
     for (int i = 0; i < d; i++) o[i] = acc[i] / sum;
     return 1;
@@ -704,8 +781,14 @@ int mo_attention(const float *q, int B, int Hq, int Tq, int D, const void *k, co
     return 0;
 }
 
+/* SiluMulF32 (attn.go:59-73): siluMulF32AVX2 on the first n&~7 elements,
+ * float64 on the rest.  fastSwiglu (interp/fast.go:487-498) hands it pieces
+ * of n/(8*GOMAXPROCS) elements; for the llama shapes on the reference's
+ * 4-core benchmark machine every piece is a multiple of 8. */
 void mo_swiglu(const float *a, const float *b, int64_t n, float *y) {
-    for (int64_t i = 0; i < n; i++) y[i] = (float)((double)a[i] / (1.0 + exp(-(double)a[i])) * (double)b[i]);
+    const int64_t n8 = n & ~(int64_t)7;
+    for (int64_t i = 0; i < n8; i++) y[i] = silu_mul_amd64(a[i], b[i]);
+    for (int64_t i = n8; i < n; i++) y[i] = (float)((double)a[i] / (1.0 + exp(-(double)a[i])) * (double)b[i]);
 }
 
 int mo_embedding(int dt, const uint8_t *table, int64_t V, int64_t E, const int32_t *ids, int64_t n, float *y) {

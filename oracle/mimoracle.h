@@ -11,8 +11,9 @@
  *
  * Arithmetic contract: this file is compiled with -ffp-contract=off so that a
  * product followed by a sum is rounded twice, as the Go code computes it on
- * amd64; fused multiply-adds appear only where the reference asks for one
- * (fmaf in mo_dot_q8k_ref, after internal/kernels/q8k_test.go:35-117).
+ * amd64; fused multiply-adds appear only where the reference's kernels use
+ * one (fmaf in mo_dot_q8k_ref after internal/kernels/q8k_test.go:35-117, and
+ * in the restated amd64 attention and SiLU kernels of attn_amd64.s).
  */
 #ifndef MIMORACLE_H
 #define MIMORACLE_H
@@ -91,15 +92,16 @@ void mo_rms_norm(const float *x, int64_t rows, int64_t n, const float *scale, do
  * without YaRN).  pos has pos_rows (1 or B) rows of T positions. */
 int mo_rope(const float *x, int B, int H, int T, int D, const int64_t *pos, int pos_rows, double theta,
             int rotary, int interleaved, float *y);
-/* attention.v1/v2 fast path, interp/fast.go:569-751 with kernels/attn.go:26-121
- * (plain-Go kernels).  k and v are f32 or f16 (kv_dtype) [B,Hkv,Tk,D]; mask is
+/* attention.v1/v2 fast path, interp/fast.go:569-751 with the amd64 kernels of
+ * internal/kernels/attn.go:26-121 / attn_amd64.s (rows with a masked key
+ * inside their visible range take the scalar path of fast.go:661-716).  k and v are f32 or f16 (kv_dtype) [B,Hkv,Tk,D]; mask is
  * NULL or bool bytes broadcast over mask_shape[4] (each 1 or full).  Rows
  * whose keys are all masked give NaN. */
 int mo_attention(const float *q, int B, int Hq, int Tq, int D, const void *k, const void *v, int kv_dtype,
                  int Hkv, int Tk, const uint8_t *mask, const int *mask_shape, double scale, int causal,
                  float *out);
 /* swiglu.v1 fast path, interp/fast.go:487-498 with kernels/attn.go:63-73
- * (plain Go: float64 silu, rounded once). */
+ * (siluMulF32AVX2 for the first n&~7 elements, float64 for the rest). */
 void mo_swiglu(const float *a, const float *b, int64_t n, float *y);
 /* embedding.v1 fast path, interp/fast.go:818-842; out-of-range ids give zeros. */
 int mo_embedding(int dt, const uint8_t *table, int64_t V, int64_t E, const int32_t *ids, int64_t n, float *y);
