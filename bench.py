@@ -149,10 +149,11 @@ def build_model(ctx, cfg, context, max_tokens):
     return mimgpu.Model(ctx, full, weights), weights
 
 
-def gemv_roofline(ctx, cfg, weights, torch, reps=2):
+def gemv_roofline(ctx, cfg, weights, torch, reps=3):
     """The GEMV kernel alone over the decode shapes of every layer (cold L2:
-    each launch reads a different weight), timed per launch with CUDA events
-    on the launching stream.  Returns (bytes per launch, seconds per launch,
+    each launch reads a different weight), the launches captured back to
+    back in one CUDA graph and timed with CUDA events on the launching stream
+    around each replay.  Returns (bytes per launch, seconds per launch,
     launches)."""
     import mimgpu
     lib = mimgpu.lib()
@@ -173,22 +174,35 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=2):
         plan.append((weights[f"blk.{l}.ffn_down.weight"][1], q8f, x_f, F))
     plan.append((weights["output.weight"][1], q8e, x_e, E))
     torch.cuda.synchronize()
-    total_t, total_b, launches = 0.0, 0, 0
-    for rep in range(reps + 1):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in plan]
-        with torch.cuda.stream(st):
-            for (t, q8, x, K), (a, b) in zip(plan, evs):
-                a.record(st)
-                ctx._check(lib.mimgpu_gemv_q8_dev(ctx.h, st.cuda_stream, q8, x.data_ptr(), t.h, None, y.data_ptr()))
-                b.record(st)
-        st.synchronize()
-        if rep == 0:
-            continue  # warm-up pass
-        for (t, q8, x, K), (a, b) in zip(plan, evs):
+
+    def enqueue():
+        for t, q8, x, K in plan:
+            ctx._check(lib.mimgpu_gemv_q8_dev(ctx.h, st.cuda_stream, q8, x.data_ptr(), t.h, None, y.data_ptr()))
+
+    with torch.cuda.stream(st):
+        enqueue()  # warm-up: kernel attributes, tensor maps
+    st.synchronize()
+    # the launches back to back in one CUDA graph, so that host submission
+    # does not gap them; one event pair around each replay
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st, capture_error_mode="thread_local"):
+        enqueue()
+    total_t = 0.0
+    with torch.cuda.stream(st):
+        g.replay()  # warm-up replay
+        for rep in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            g.replay()
+            b.record(st)
+            b.synchronize()
             total_t += a.elapsed_time(b) / 1e3
-            n = t.shape[0]
-            total_b += nbytes(t.dtype, t.shape) + K + K // 256 * 4 + K // 32 * 2 + K // 16 * 2 + 4 * n
-            launches += 1
+    del g
+    total_b, launches = 0, 0
+    for t, q8, x, K in plan:
+        n = t.shape[0]
+        total_b += reps * (nbytes(t.dtype, t.shape) + K + K // 256 * 4 + K // 32 * 2 + K // 16 * 2 + 4 * n)
+        launches += reps
     lib.mimgpu_q8_free(q8e)
     lib.mimgpu_q8_free(q8f)
     return total_b / launches, total_t / launches, launches
