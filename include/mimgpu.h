@@ -140,6 +140,23 @@ int mimgpu_dequant_matmul_a8_dev(mimgpu_ctx *ctx, void *stream, const float *x_d
 int mimgpu_dequant_matmul_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
                               const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
 
+/* Same as mimgpu_dequant_matmul_a8_dev for Q4_K / Q6_K weights with K a
+ * multiple of 256, but the 8-bit activation scratch lives in a fixed 1 MiB
+ * static device array instead of the context's workspace, so the call
+ * allocates no device memory.  No counterpart in the reference: it serves
+ * callers that cannot allocate while they run (a server whose HBM is all
+ * handed to its own pool, a decode loop that cannot afford the device-wide
+ * synchronization of cudaMalloc / cudaFree).
+ * Limit: rows x K must fit the buffer (act bytes <= 1 MiB, e.g. 16 rows of
+ * 14336); larger calls return MIMGPU_EINVAL with the sizes in the message.
+ * Other dtypes return MIMGPU_ENOTHANDLED.  The first call on a device looks
+ * the buffer's address up (cudaGetSymbolAddress), so make it outside stream
+ * capture.  The buffer is shared by every call on a device: two calls whose
+ * work overlaps in time on that device (different streams, or different
+ * contexts, without ordering between them) race on it; order them. */
+int mimgpu_dequant_matmul_a8_static(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
+                                    const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
+
 /* ------------------------------------------ 8-bit activations on the device
  * Rows of activations quantized once and multiplied by several weights, as
  * linearA8 does with a Q8Batch (interp/fast.go:282-379, internal/kernels/

@@ -620,30 +620,36 @@ EncodeTiledFn encode_fn() {
 }
 
 // The 2-D map of a weight matrix: rows of row_bytes as u64 elements, box
-// [box_bytes/8, 16 rows], zero fill past either edge.  Cached per matrix.
-bool weight_tmap(const GemvSeg &sg, long long K, CUtensorMap *out) {
-    const long long rb = row_bytes(sg.dt, K);
-    if (rb % 16 || ((uintptr_t)sg.w & 15) || sg.n <= 0) return false;
-    static std::mutex mu;
-    static std::unordered_map<const void *, std::pair<long long, CUtensorMap>> cache;
-    std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(sg.w);
-    if (it != cache.end() && it->second.first == rb * 1000003LL + sg.n) {
-        *out = it->second.second;
-        return true;
-    }
+// [box_bytes/8, 16 rows], zero fill past either edge.
+bool encode_weight_tmap(const GemvSeg &sg, long long rb, CUtensorMap *out) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)(rb / 8), (cuuint64_t)sg.n};
     const cuuint64_t strides[1] = {(cuuint64_t)rb};
     const cuuint32_t box[2] = {(cuuint32_t)(box_bytes(sg.dt) / 8), (cuuint32_t)kRowsW};
     const cuuint32_t estr[2] = {1, 1};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, (void *)sg.w, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The map of a weight matrix, cached per matrix in a host table (cache) or
+// encoded afresh on the stack (!cache: nothing is allocated).
+bool weight_tmap(const GemvSeg &sg, long long K, CUtensorMap *out, bool cache) {
+    const long long rb = row_bytes(sg.dt, K);
+    if (rb % 16 || ((uintptr_t)sg.w & 15) || sg.n <= 0) return false;
+    if (!cache) return encode_weight_tmap(sg, rb, out);
+    static std::mutex mu;
+    static std::unordered_map<const void *, std::pair<long long, CUtensorMap>> table;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = table.find(sg.w);
+    if (it != table.end() && it->second.first == rb * 1000003LL + sg.n) {
+        *out = it->second.second;
+        return true;
+    }
     CUtensorMap m;
-    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, (void *)sg.w, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return false;
-    cache[sg.w] = {rb * 1000003LL + sg.n, m};
+    if (!encode_weight_tmap(sg, rb, &m)) return false;
+    table[sg.w] = {rb * 1000003LL + sg.n, m};
     *out = m;
     return true;
 }
@@ -667,7 +673,7 @@ cudaError_t gemv_a8_prepare() {
 }
 
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl) {
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps) {
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
     if (rows == 0 || K == 0) return cudaSuccess;
     A8Params p = {};
@@ -690,7 +696,7 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
     p.slot = ((min(kKC, p.nb) * maxbb + 32 + 127) & ~127) + 16;
     // 2-D tiled TMA when every matrix's rows are 16-byte multiples
     p.tma2d = 1;
-    for (int i = 0; i < nseg && p.tma2d; i++) p.tma2d = weight_tmap(segs[i], K, &p.tmap[i]) ? 1 : 0;
+    for (int i = 0; i < nseg && p.tma2d; i++) p.tma2d = weight_tmap(segs[i], K, &p.tmap[i], cache_maps) ? 1 : 0;
     p.stage_bytes = p.tma2d ? kWarps * kRowsW * kBoxMax : kRowsCta * p.slot;
     // split K across the warps of a CTA when there are too few row groups
     // to give every SM several warps

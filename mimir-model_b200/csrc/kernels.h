@@ -49,8 +49,10 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, long long ld
 // sharing the activations.  x is the f32 input, used for refused rows.
 // Sets the kernel attributes the GEMV launches need (call outside stream capture).
 cudaError_t gemv_a8_prepare();
+// cache_maps: keep each weight's TMA descriptor in a host table (false:
+// encode it on the stack every launch, allocating nothing).
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl);
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true);
 // dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
 cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
                             cudaStream_t st, bool pdl);

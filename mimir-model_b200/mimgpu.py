@@ -45,6 +45,7 @@ SIGNATURES = {
     "mimgpu_embedding": (I32, [P, P, P, I64, P]),
     "mimgpu_dequant_matmul_a8_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "mimgpu_dequant_matmul_dev": (I32, [P, P, P, I64, I64, P, P, P]),
+    "mimgpu_dequant_matmul_a8_static": (I32, [P, P, P, I64, I64, P, P, P]),
     "mimgpu_q8_new": (I32, [P, I64, I64, C.POINTER(P)]),
     "mimgpu_q8_free": (None, [P]),
     "mimgpu_q8_quantize_dev": (I32, [P, P, P, P]),
