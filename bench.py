@@ -42,6 +42,7 @@ F32, Q4_K, Q6_K = 1, 66, 67
 CFG8B = dict(layers=32, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=128256,
              rope_theta=500000.0, norm_eps=1e-5)
 PROMPT = 128
+GEMV_TRAFFIC_PER_ALGO_BYTE = (66_127_104 + 537_856) / 66_179_904
 
 
 def layout(cfg):
@@ -242,14 +243,15 @@ def run_gpu(args):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    cfg = CFG8B
-    context = PROMPT + args.warmup + args.steps + 2 * args.e2e_steps + 8
+    cfg = dict(CFG8B, layers=args.layers)
+    prompt = args.prompt
+    context = prompt + args.warmup + args.steps + 2 * args.e2e_steps + 8
     ctx = mimgpu.Context(local)
-    model, weights = build_model(ctx, cfg, context, PROMPT)
+    model, weights = build_model(ctx, cfg, context, prompt)
     sess = model.session()
-    ids = prompt_ids(cfg["vocab"])
-    logits = sess.run(ids, np.arange(PROMPT))[0]
-    tok, pos = int(np.argmax(logits)), PROMPT
+    ids = prompt_ids(cfg["vocab"], prompt)
+    logits = sess.run(ids, np.arange(prompt))[0]
+    tok, pos = int(np.argmax(logits)), prompt
     # warm-up (also captures the decode graph)
     out = sess.generate(tok, pos, args.warmup)
     tok, pos = int(out[-1]), pos + args.warmup
@@ -296,19 +298,16 @@ def run_gpu(args):
     bpl, spl, nl = gemv_roofline(ctx, cfg, weights, torch)
     peak, peak_kind = peaks()
     achieved = bpl / spl / 1e9
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "gemv_a8_traffic.json")) as f:
-            tr = json.load(f)
-        traffic = tr.get("bytes_per_algorithmic_byte")
-        traffic = traffic * bpl if traffic else None
-    except (OSError, ValueError):
-        pass
+    # DRAM bytes per algorithmic byte of the GEMV from one ncu capture (the
+    # 28672 x 4096 Q4_K launch: 66.13 MB read + 0.54 MB written for
+    # 66.18 MB algorithmic), applied to this run's bytes per launch
+    traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
     wpt = weight_bytes_per_token(cfg)
     ms = dev_s / args.steps * 1e3
     value = world * args.steps / dev_s
-    per_layer = 10
-    launches = args.steps * (1 + per_layer * cfg["layers"] + 4)
+    # embedding, 9 per layer (rms_norm+quant, QKV, RoPE+cache, attention, o,
+    # rms_norm+quant, gate|up, SwiGLU+quant, down), final norm, head, argmax, advance
+    launches = args.steps * (1 + 9 * cfg["layers"] + 4)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -316,8 +315,8 @@ def run_gpu(args):
         "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)",
         "config": {"workload": "8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)",
                    "layers": cfg["layers"], "d_model": cfg["embed"], "heads": cfg["heads"],
-                   "kv_heads": cfg["kv_heads"], "ffn": cfg["ffn"], "vocab": cfg["vocab"], "prompt": PROMPT,
-                   "context_cache": context, "positions_timed": [PROMPT + args.warmup, pos - 1 - args.e2e_steps - 2],
+                   "kv_heads": cfg["kv_heads"], "ffn": cfg["ffn"], "vocab": cfg["vocab"], "prompt": prompt,
+                   "context_cache": context, "positions_timed": [prompt + args.warmup, pos - 1 - args.e2e_steps - 2],
                    "matmul": "dequant_matmul_a8.v2 block 256 (bit-exact dotQ8KRef)", "kv_cache": "f16",
                    "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2: 4.88 GB of weights streamed per token vs 126 MB L2"},
@@ -326,9 +325,9 @@ def run_gpu(args):
                 "api": "mimgpu_session_run (pinned host token/position in, logits out, host argmax)"},
         "step_roofline": {"bound": "hbm", "bytes_per_token": wpt, "achieved": round(wpt / (ms / 1e3) / 1e9, 1),
                           "peak": peak, "unit": "GB/s", "frac": round(wpt / (ms / 1e3) / 1e9 / peak, 4)},
-        "roofline": {"kernel": "gemv_a8_kernel (dequant_matmul_a8.v2, decode shapes of all 32 layers + head)",
+        "roofline": {"kernel": f"gemv_a8_kernel (dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)",
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": round(bpl),
+                     "frac": round(achieved / peak, 4), "traffic": round(traffic), "bytes_per_launch": round(bpl),
                      "us_per_launch": round(spl * 1e6, 3), "launches": nl, "peak_kind": peak_kind},
         "clocks": clocks.summary(),
         "gpu_launches": launches,
@@ -450,6 +449,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--layers", type=int, default=CFG8B["layers"],
+                    help="decoder layers (default: the 8B shape's 32; fewer only for profiling runs)")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before the timed decode steps")
     ap.add_argument("--gemv", default="", help="GEMV-only mode: N,K,q4_k|q6_k[,rows]")
     ap.add_argument("--gemv-hot", action="store_true", help="GEMV-only mode with one weight copy (L2-hot)")
     args = ap.parse_args()
