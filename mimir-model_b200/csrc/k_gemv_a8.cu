@@ -69,6 +69,7 @@ struct __align__(64) A8Params {
     int slot;                  // 1-D mode: bytes per row slot of a stage
     int stage_bytes;           // bytes of one stage
     int act_bytes;             // shared-memory bytes of the activations
+    int act_bulk;              // 1: every activation array is 16-byte aligned: one bulk copy each
     unsigned *status;
 };
 
@@ -91,9 +92,21 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
-__device__ __forceinline__ int find_seg(const A8Params &p, int g) {
+// Dynamic shared memory header: mbarriers (bytes 0..127) and the segment
+// table (from byte 128); the activations follow.
+constexpr int kHeader = 512;
+
+// The launch's matrices, copied into shared memory at CTA start so that the
+// hot loops index them without dynamic accesses to the parameter space.
+struct SegTable {
+    GemvSeg seg[kMaxSegs];
+    int g0[kMaxSegs + 1];
+    int nseg;
+};
+static_assert(128 + sizeof(SegTable) <= kHeader, "segment table exceeds the shared-memory header");
+__device__ __forceinline__ int find_seg(const SegTable &t, int g) {
     int s = 0;
-    while (s + 1 < p.nseg && g >= p.seg_g0[s + 1]) s++;
+    while (s + 1 < t.nseg && g >= t.g0[s + 1]) s++;
     return s;
 }
 
@@ -325,9 +338,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + kStages;
     int *badw = (int *)(empty + kStages);            // [kWarps] bad-row masks of parts > 0
-    uint8_t *actp = smem + 128;
+    uint8_t *actp = smem + kHeader;
     uint8_t *recp = actp + p.act_bytes;               // [kWarps][rec_bytes] per-block values of parts > 0
-    uint8_t *tiles = smem + ((128 + p.act_bytes + kWarps * p.rec_bytes + 127) & ~127);  // 128-byte aligned
+    uint8_t *tiles = smem + ((kHeader + p.act_bytes + kWarps * p.rec_bytes + 127) & ~127);  // 128-byte aligned
+    uint64_t *actbar = (uint64_t *)(smem + 64);      // completion of the activations' bulk copies
+    // the segment table also lives in the dynamic header: a static __shared__
+    // variable would move the dynamic base off the 128-byte alignment the
+    // 2-D TMA destinations need
+    SegTable &tab = *(SegTable *)(smem + 128);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.split, slots = kWarps / S;
     const int total = p.seg_g0[p.nseg];
@@ -338,7 +356,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
         }
+        mbar_init(actbar, 1);
         fence_barrier_init();
+#pragma unroll
+        for (int i = 0; i < kMaxSegs; i++) tab.seg[i] = p.seg[i];
+#pragma unroll
+        for (int i = 0; i <= kMaxSegs; i++) tab.g0[i] = p.seg_g0[i];
+        tab.nseg = p.nseg;
     }
     __syncthreads();
     pdl_launch_dependents();
@@ -369,10 +393,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
                     const bool act = g < total && c < p.chunks;
                     int bb = 0, bx = 0, r0 = 0;
                     if (act) {
-                        si = find_seg(p, g);
-                        bb = block_bytes(p.seg[si].dt);
-                        bx = box_bytes(p.seg[si].dt);
-                        r0 = (g - p.seg_g0[si]) * kRowsW;
+                        si = find_seg(tab, g);
+                        bb = block_bytes(tab.seg[si].dt);
+                        bx = box_bytes(tab.seg[si].dt);
+                        r0 = (g - tab.g0[si]) * kRowsW;
                     }
                     const unsigned bytes = __reduce_add_sync(FULL, act ? (unsigned)(kRowsW * bx) : 0u);
                     if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes);
@@ -395,9 +419,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
                         const int g = group_of(blockIdx.x, w / S, slots, t);
                         const int c = (w % S) * p.cpp + i;
                         if (g >= total || c >= p.chunks) continue;
-                        const int si = find_seg(p, g);
-                        const GemvSeg &sg = p.seg[si];
-                        const int r0 = (g - p.seg_g0[si]) * kRowsW;
+                        const int si = find_seg(tab, g);
+                        const GemvSeg &sg = tab.seg[si];
+                        const int r0 = (g - tab.g0[si]) * kRowsW;
                         if (r >= sg.n - r0) continue;
                         const int bb = block_bytes(sg.dt), kb0 = c * kKC, kbn = min(kKC, p.nb - kb0);
                         const uintptr_t a = (uintptr_t)(sg.w + (long long)(r0 + r) * row_bytes(sg.dt, p.K) +
@@ -425,34 +449,46 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
 
     // ---------------------------------------------- consumers
     pdl_wait();
-    // activations into shared memory: quants, scales, sums of 32 and 16
+    // activations into shared memory: quants, scales, sums of 32 and 16, the
+    // per-block flags -- one bulk copy each when aligned, else plain loads
     const int nr = p.rows;
     const long long K = p.K;
     const int qb = nr * (int)K, dxb = nr * p.nb * 4, xsb = nr * (int)(K / 32) * 2, ysb = nr * (int)(K / 16) * 2;
-    {
+    const int okb = nr * p.nb * 4;
+    auto pad = [](int b) { return (b + 15) & ~15; };
+    uint8_t *dxp = actp + pad(qb), *xsp = dxp + pad(dxb), *ysp = xsp + pad(xsb), *okp = ysp + pad(ysb);
+    if (p.act_bulk) {
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(actbar, (uint32_t)(pad(qb) + pad(dxb) + pad(xsb) + pad(ysb) + pad(okb)));
+            bulk_g2s(actp, p.act.q, (uint32_t)pad(qb), actbar);
+            bulk_g2s(dxp, p.act.dx, (uint32_t)pad(dxb), actbar);
+            bulk_g2s(xsp, p.act.xs, (uint32_t)pad(xsb), actbar);
+            bulk_g2s(ysp, p.act.ys, (uint32_t)pad(ysb), actbar);
+            bulk_g2s(okp, p.act.ok, (uint32_t)pad(okb), actbar);
+        }
+        mbar_wait_bounded(actbar, 0, p.status);
+    } else {
         const int tid = threadIdx.x;
         for (int i = tid * 16; i < qb; i += kWarps * 32 * 16)
             *(uint4 *)(actp + i) = __ldg((const uint4 *)((const uint8_t *)p.act.q + i));
-        uint8_t *dxp = actp + ((qb + 15) & ~15);
         for (int i = tid; i < dxb / 4; i += kWarps * 32) ((float *)dxp)[i] = __ldg(p.act.dx + i);
-        uint8_t *xsp = dxp + ((dxb + 15) & ~15);
         for (int i = tid; i < xsb / 2; i += kWarps * 32) ((int16_t *)xsp)[i] = __ldg(p.act.xs + i);
-        uint8_t *ysp = xsp + ((xsb + 15) & ~15);
         for (int i = tid; i < ysb / 2; i += kWarps * 32) ((int16_t *)ysp)[i] = __ldg(p.act.ys + i);
+        for (int i = tid; i < okb / 4; i += kWarps * 32) ((int *)okp)[i] = __ldg(p.act.ok + i);
         asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
     }
     ActSmem as;
     as.q = smem_u32(actp);
-    as.dx = as.q + ((qb + 15) & ~15);
-    as.xs = as.dx + ((dxb + 15) & ~15);
-    as.ys = as.xs + ((xsb + 15) & ~15);
+    as.dx = smem_u32(dxp);
+    as.xs = smem_u32(xsp);
+    as.ys = smem_u32(ysp);
     // a row is quantized when every one of its blocks is (q8.go:50-97)
     bool act_ok[NR];
 #pragma unroll
     for (int a = 0; a < NR; a++) {
         int bad = 0;
         if (a < nr)
-            for (int b = lane; b < p.nb; b += 32) bad |= p.act.ok[(long long)a * p.nb + b] == 0;
+            for (int b = lane; b < p.nb; b += 32) bad |= ((const int *)okp)[a * p.nb + b] == 0;
         act_ok[a] = !__any_sync(FULL, bad);
     }
 
@@ -468,13 +504,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
         int si = 0, r0 = 0, nrow = 0;
         long long rb = 0;
         if (has) {
-            si = find_seg(p, g);
-            r0 = (g - p.seg_g0[si]) * kRowsW;
-            nrow = min(kRowsW, p.seg[si].n - r0);
-            rb = row_bytes(p.seg[si].dt, K);
+            si = find_seg(tab, g);
+            r0 = (g - tab.g0[si]) * kRowsW;
+            nrow = min(kRowsW, tab.seg[si].n - r0);
+            rb = row_bytes(tab.seg[si].dt, K);
         }
-        const GemvSeg &sg = p.seg[si];
+        const GemvSeg &sg = tab.seg[si];
         const bool valid = has && rlocal < nrow;
+        // the epilogue's bias and residual, requested now so that they are
+        // in registers when the products are
+        float biasv = 0.f, resv[NR];
+#pragma unroll
+        for (int a = 0; a < NR; a++) resv[a] = 0.f;
+        if (valid && part == 0) {
+            if (sg.bias) biasv = sg.bias[r0 + rlocal];
+            if (sg.res)
+#pragma unroll
+                for (int a = 0; a < NR; a++)
+                    if (a < nr) resv[a] = sg.res[(long long)a * sg.ldy + r0 + rlocal];
+        }
         float tot[NR], off[NR];
 #pragma unroll
         for (int a = 0; a < NR; a++) tot[a] = off[a] = 0.f;
@@ -533,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
             if (valid && !(badrows & (1u << (rlocal * 2))) && act_ok[a] && (lane & 1) == 0) {
                 float r = __fsub_rn(tot[a], off[a]);
                 const int row = r0 + rlocal;
-                if (sg.bias) r = __fadd_rn(r, sg.bias[row]);
-                if (sg.res) r = __fadd_rn(sg.res[(long long)a * sg.ldy + row], r);
+                if (sg.bias) r = __fadd_rn(r, biasv);
+                if (sg.res) r = __fadd_rn(resv[a], r);
                 sg.y[(long long)a * sg.ldy + row] = r;
             }
             // rows whose weights or activations the 8-bit kernel refuses: f32 product
@@ -581,7 +629,7 @@ int blocks_per_sm(size_t smem) {
 
 template <int NR>
 cudaError_t launch_nr(A8Params &p, cudaStream_t st, bool pdl) {
-    const size_t smem = (size_t)((128 + p.act_bytes + kWarps * p.rec_bytes + 127) & ~127) +
+    const size_t smem = (size_t)((kHeader + p.act_bytes + kWarps * p.rec_bytes + 127) & ~127) +
                         (size_t)kStages * p.stage_bytes;
     cudaError_t e = prepare_nr<NR>();
     if (e != cudaSuccess) return e;
@@ -658,7 +706,8 @@ int nr_tpl(int nr) { return nr == 1 ? 1 : nr == 2 ? 2 : nr <= 4 ? 4 : 8; }
 
 int act_bytes_for(int nr, long long K) {
     auto al = [](long long b) { return (b + 15) & ~15LL; };
-    return (int)(al(nr * K) + al(nr * (K / 256) * 4) + al(nr * (K / 32) * 2) + al(nr * (K / 16) * 2));
+    return (int)(al(nr * K) + al(nr * (K / 256) * 4) + al(nr * (K / 32) * 2) + al(nr * (K / 16) * 2) +
+                 al(nr * (K / 256) * 4));
 }
 
 }  // namespace
@@ -721,6 +770,10 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
         q.act.xs = act.xs + (long long)r0 * (K / 32);
         q.act.ys = act.ys + (long long)r0 * (K / 16);
         q.act.ok = act.ok + (long long)r0 * (K / 256);
+        // bulk copies need 16-byte aligned sources; the ActQ8 carving pads
+        // every array to 256 bytes, so reading up to the next 16 is in bounds
+        auto a16 = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
+        q.act_bulk = a16(q.act.q) && a16(q.act.dx) && a16(q.act.xs) && a16(q.act.ys) && a16(q.act.ok);
         for (int i = 0; i < nseg; i++) {
             q.seg[i].y = segs[i].y + (long long)r0 * segs[i].ldy;
             if (segs[i].res) q.seg[i].res = segs[i].res + (long long)r0 * segs[i].ldy;
