@@ -83,52 +83,97 @@ __global__ void rope_scatter_kernel(RopeScatterArgs a) {
 // float64 exp on the rest), the fused key-ordered weighted sum of wsumF16AVX2,
 // o = acc/sum.  The 256 outputs of the block (H*D row-major, the layout the o
 // projection reads) are then quantized to 8 bits when act.q is set.
+//
+// The block's key rows, then its value rows, stream through a ring of
+// shared-memory chunks (kAttnChunk keys of each kv head it reads) filled by
+// bulk copies on mbarriers, so every read of the cache is a shared-memory
+// read.  A thread computes a whole score: the reference's eight lane
+// accumulators a[l] (fma over elements 8c+l) with 16-byte reads.
 template <bool F16>
 __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
-    extern __shared__ float asmem[];
+    extern __shared__ __align__(128) uint8_t asm_[];
     __shared__ QuantScratch qs;
     __shared__ float red[8][8];
     __shared__ float hsum[8], hmax[8];
-    pdl_launch_dependents();
-    pdl_wait();
+    constexpr int ES = F16 ? 2 : 4;
     const int D = a.D, HPB = 256 / D, G = a.H / a.Hkv;
     const int t = blockIdx.y, h0 = blockIdx.x * HPB, tid = threadIdx.x;
-    const int nh = min(HPB, a.H - h0);  // heads of this block (fewer in a last partial block)
-    const int n = (int)(a.pos[t] + 1);
-    float *q = asmem;                   // [HPB][D]
-    float *sc = asmem + 256;            // [HPB][C]
-    if (tid / D < nh) q[tid] = a.qh[((long long)(h0 + tid / D) * a.T + t) * D + tid % D];
-    __syncthreads();
-    // scores: an 8-lane group per (key, head); group g of pass u takes item
-    // base + 32 u + g: key item / nh, head item % nh
-    const int l = tid & 7, grp = tid >> 3;
-    const int n4 = n & ~3, items = n * nh;
-    for (int base = 0; base < items; base += 32 * 4) {
-        float acc[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int item = base + 32 * u + grp;
-            acc[u] = 0.f;
-            if (item < items) {
-                const int j = item / nh, hh = item % nh;
-                const long long kr = ((long long)((h0 + hh) / G) * a.C + j) * D;
-                const float *qr = q + hh * D;
-                for (int c = 0; c < D / 8; c++) {
-                    const float kv = F16 ? h2f_bits(((const uint16_t *)a.kc)[kr + 8 * c + l])
-                                         : ((const float *)a.kc)[kr + 8 * c + l];
-                    acc[u] = __fmaf_rn(qr[8 * c + l], kv, acc[u]);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int item = base + 32 * u + grp;
-            const int j = item / nh;
-            const float v = score_combine(acc[u], j >= n4);  // the 8 lanes of a group share j
-            if (item < items && l == 0) sc[(item % nh) * a.C + j] = __fmul_rn(v, a.scale);
-        }
+    const int nh = min(HPB, a.H - h0);       // heads of this block (fewer in a last partial block)
+    const int kv0 = h0 / G, nkv = (h0 + nh - 1) / G - kv0 + 1;
+    const size_t rowb = (size_t)D * ES;      // bytes of one key or value row
+    const size_t chunkb = (size_t)nkv * kAttnChunk * rowb;
+    uint64_t *bar = (uint64_t *)asm_;        // [kAttnRing]
+    float *q = (float *)(asm_ + 128);        // [HPB][D]
+    float *sc = q + 256;                     // [HPB][C]
+    uint8_t *ring = asm_ + (((size_t)128 + sizeof(float) * (256 + (size_t)HPB * a.C) + 127) & ~(size_t)127);
+    if (tid == 0) {
+        for (int b = 0; b < kAttnRing; b++) mbar_init(&bar[b], 1);
+        fence_barrier_init();
     }
     __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait();
+    const int n = (int)(a.pos[t] + 1);
+    const int nch = (n + kAttnChunk - 1) / kAttnChunk, items = 2 * nch;  // key chunks, then value chunks
+    // item i: chunk i % nch of the keys (i < nch) or the values
+    auto issue = [&](int i) {
+        const int b = i % kAttnRing, c = i % nch;
+        const int j0 = c * kAttnChunk, len = min(kAttnChunk, n - j0);
+        const uint8_t *src = (const uint8_t *)(i < nch ? a.kc : a.vc);
+        mbar_arrive_expect_tx(&bar[b], (uint32_t)(nkv * len * rowb));
+        for (int v = 0; v < nkv; v++)
+            bulk_g2s(ring + b * chunkb + v * kAttnChunk * rowb, src + (((size_t)(kv0 + v) * a.C) + j0) * rowb,
+                     (uint32_t)(len * rowb), &bar[b]);
+    };
+    if (tid == 0)
+        for (int i = 0; i < min(items, kAttnRing); i++) issue(i);
+    if (tid / D < nh) q[tid] = a.qh[((long long)(h0 + tid / D) * a.T + t) * D + tid % D];
+    __syncthreads();
+    const int n4 = n & ~3;
+    bool ok = true;
+    // ---- scores, one thread per (key, head) of the chunk
+    for (int c = 0; c < nch; c++) {
+        const int b = c % kAttnRing, j0 = c * kAttnChunk, len = min(kAttnChunk, n - j0);
+        ok &= mbar_wait_bounded(&bar[b], (c / kAttnRing) & 1, a.status);
+        for (int it = tid; it < len * nh; it += 256) {
+            const int jj = it / nh, hh = it % nh;
+            const int kvi = (h0 + hh) / G - kv0;
+            const uint8_t *krow = ring + b * chunkb + ((size_t)kvi * kAttnChunk + jj) * rowb;
+            const float *qr = q + hh * D;
+            float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int c8 = 0; c8 < D / 8; c8++) {
+                float kv[8];
+                if (F16) {
+                    const uint4 w = *(const uint4 *)(krow + c8 * 16);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        kv[2 * u] = h2f_bits(ww[u] & 0xFFFFu);
+                        kv[2 * u + 1] = h2f_bits(ww[u] >> 16);
+                    }
+                } else {
+                    const float4 w0 = *(const float4 *)(krow + c8 * 32), w1 = *(const float4 *)(krow + c8 * 32 + 16);
+                    kv[0] = w0.x; kv[1] = w0.y; kv[2] = w0.z; kv[3] = w0.w;
+                    kv[4] = w1.x; kv[5] = w1.y; kv[6] = w1.z; kv[7] = w1.w;
+                }
+                const float4 q0 = *(const float4 *)(qr + 8 * c8), q1 = *(const float4 *)(qr + 8 * c8 + 4);
+                const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int l = 0; l < 8; l++) l8[l] = __fmaf_rn(qv[l], kv[l], l8[l]);
+            }
+            const int j = j0 + jj;
+            const float v = j < n4 ? __fadd_rn(__fadd_rn(__fadd_rn(l8[0], l8[1]), __fadd_rn(l8[2], l8[3])),
+                                               __fadd_rn(__fadd_rn(l8[4], l8[5]), __fadd_rn(l8[6], l8[7])))
+                                   : __fadd_rn(__fadd_rn(__fadd_rn(l8[0], l8[4]), __fadd_rn(l8[1], l8[5])),
+                                               __fadd_rn(__fadd_rn(l8[2], l8[6]), __fadd_rn(l8[3], l8[7])));
+            sc[hh * a.C + j] = __fmul_rn(v, a.scale);
+        }
+        __syncthreads();  // every thread is done with buffer b
+        if (tid == 0 && c + kAttnRing < items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(c + kAttnRing);
+        }
+    }
     // max per head (warp hh); exact in any order
     const int lane = tid & 31, w = tid >> 5;
     if (w < nh) {
@@ -140,7 +185,7 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
     __syncthreads();
     // exp of the scores: Cephes on the first n&~7 keys (none when n < 8)
     const int n8 = n >= 8 ? (n & ~7) : 0;
-    for (int i = tid; i < items; i += 256) {
+    for (int i = tid; i < n * nh; i += 256) {
         const int hh = i / n, j = i % n;
         const float x = __fsub_rn(sc[hh * a.C + j], hmax[hh]);
         sc[hh * a.C + j] = j < n8 ? expf_amd64(x) : (float)exp((double)x);
@@ -163,27 +208,28 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
         hsum[tid] = sum;
     }
     __syncthreads();
-    // weighted sum of the values: one fused multiply-add per key, in key order
+    // ---- weighted sum of the values: one fused multiply-add per key, in key order
     const int hh = tid / D, d = tid % D;
-    if (hh >= nh) return;  // only in a partial block, which never quantizes (E % 256 != 0)
-    const long long vr = (long long)((h0 + hh) / G) * a.C * D + d;
-    const float *e = sc + hh * a.C;
+    const int kvi = (h0 + min(hh, nh - 1)) / G - kv0;
+    const float *e = sc + min(hh, nh - 1) * a.C;
     float acc = 0.f;
-    int j = 0;
-    for (; j + 8 <= n; j += 8) {
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-            v[u] = F16 ? h2f_bits(((const uint16_t *)a.vc)[vr + (long long)(j + u) * D])
-                       : ((const float *)a.vc)[vr + (long long)(j + u) * D];
-#pragma unroll
-        for (int u = 0; u < 8; u++) acc = __fmaf_rn(e[j + u], v[u], acc);
+    for (int c = 0; c < nch; c++) {
+        const int i = nch + c, b = i % kAttnRing, j0 = c * kAttnChunk, len = min(kAttnChunk, n - j0);
+        ok &= mbar_wait_bounded(&bar[b], (i / kAttnRing) & 1, a.status);
+        const uint8_t *vb = ring + b * chunkb + (size_t)kvi * kAttnChunk * rowb + (size_t)d * ES;
+#pragma unroll 8
+        for (int jj = 0; jj < len; jj++) {
+            const float v = F16 ? h2f_bits(*(const uint16_t *)(vb + jj * rowb)) : *(const float *)(vb + jj * rowb);
+            acc = __fmaf_rn(e[j0 + jj], v, acc);
+        }
+        __syncthreads();
+        if (tid == 0 && i + kAttnRing < items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + kAttnRing);
+        }
     }
-    for (; j < n; j++) {
-        const float v = F16 ? h2f_bits(((const uint16_t *)a.vc)[vr + (long long)j * D])
-                            : ((const float *)a.vc)[vr + (long long)j * D];
-        acc = __fmaf_rn(e[j], v, acc);
-    }
+    (void)ok;
+    if (hh >= nh) return;  // only in a partial block, which never quantizes (E % 256 != 0)
     const float o = __fdiv_rn(acc, hsum[hh]);
     const int E = a.H * D;
     a.out[(long long)t * E + (long long)h0 * D + tid] = o;
@@ -217,7 +263,7 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
     if (a.D < 32 || 256 % a.D || a.Hkv <= 0 || a.H % a.Hkv || (a.act.q && a.H % (256 / a.D)))
         return cudaErrorInvalidValue;
     const int HPB = 256 / a.D;
-    const size_t smem = attn_exact_smem(a.D, a.C);
+    const size_t smem = attn_exact_smem(a.H, a.Hkv, a.D, a.C, a.cache_f16);
     if (smem > kAttnSmemMax) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = mk(dim3((a.H + HPB - 1) / HPB, a.T), dim3(256), smem, st, pdl, attr);

@@ -126,7 +126,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none};
+                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none, status};
         CK(launch_attn_exact(aa, st, pdl));
         GemvSeg o{w.o->dev, w.o->dtype, E, s->x, E, nullptr, s->x};
         if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
@@ -204,7 +204,7 @@ int mimgpu_model_new(mimgpu_ctx *ctx, const mimgpu_llama_config *cfg, mimgpu_mod
         return fail(ctx, MIMGPU_EINVAL, "rope dimension count %d for head size %d", c.rope_dims, c.head_dim);
     if (c.head_dim % 32 || 256 % c.head_dim)
         return fail(ctx, MIMGPU_ENOTHANDLED, "head size %d not served (32, 64, 128 or 256)", c.head_dim);
-    if (attn_exact_smem(c.head_dim, c.context) > kAttnSmemMax)
+    if (attn_exact_smem(c.heads, c.kv_heads, c.head_dim, c.context, c.cache_f16) > kAttnSmemMax)
         return fail(ctx, MIMGPU_ENOTHANDLED, "context %d too long for the attention scores in shared memory", c.context);
     if (c.a8 && (c.embed % 256 || c.ffn % 256))
         return fail(ctx, MIMGPU_ENOTHANDLED, "8-bit activations need E and F multiples of 256");

@@ -30,13 +30,25 @@ struct AttnArgs2 {
     float scale;
     float *out;
     ActQ8 act;
+    unsigned *status;  // device status word (bounded waits record timeouts here)
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
 // Dynamic shared memory of the attention kernel: q and the scores of the
-// 256/D heads of a block over the whole context.
-constexpr size_t kAttnSmemMax = 200 * 1024;
-inline size_t attn_exact_smem(int D, int C) { return sizeof(float) * (256 + (size_t)(256 / D) * C); }
+// 256/D heads of a block over the whole context, plus the key/value chunk
+// ring (kAttnRing buffers of kAttnChunk keys of every kv head the block
+// reads).
+constexpr size_t kAttnSmemMax = 220 * 1024;
+constexpr int kAttnChunk = 64;
+constexpr int kAttnRing = 4;
+inline int attn_kv_per_block(int H, int Hkv, int D) {
+    const int HPB = 256 / D, G = H / Hkv;
+    return G >= HPB ? 1 : HPB / G + 1;  // blocks may straddle kv heads when G < HPB
+}
+inline size_t attn_exact_smem(int H, int Hkv, int D, int C, int f16) {
+    const size_t chunk = (size_t)attn_kv_per_block(H, Hkv, D) * kAttnChunk * D * (f16 ? 2 : 4);
+    return 1024 + sizeof(float) * (256 + (size_t)(256 / D) * C) + (size_t)kAttnRing * chunk;
+}
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
 cudaError_t launch_advance(const int *argmax, int32_t *tok, int64_t *pos, int32_t *ids, int *step, cudaStream_t st,
                            bool pdl);
