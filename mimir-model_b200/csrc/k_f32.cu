@@ -216,8 +216,8 @@ __global__ void embedding_kernel(int dt, const uint8_t *__restrict__ table, long
     const long long id = ids[blockIdx.x];
     const long long rb = row_bytes(dt, E);
     float *out = y + (long long)blockIdx.x * E;
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-        out[e] = (id >= 0 && id < V) ? decode_elem(dt, table + id * rb, e) : 0.f;
+    const int e = blockIdx.y * blockDim.x + threadIdx.x;  // one element per thread
+    if (e < E) out[e] = (id >= 0 && id < V) ? decode_elem(dt, table + id * rb, e) : 0.f;
 }
 
 }  // namespace
@@ -266,7 +266,7 @@ cudaError_t launch_embedding(int dt, const uint8_t *table, long long V, int E, c
     if (n <= 0) return cudaSuccess;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    cfg.gridDim = dim3(n);
+    cfg.gridDim = dim3(n, (E + 255) / 256);
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

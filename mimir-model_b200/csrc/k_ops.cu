@@ -12,7 +12,9 @@
 //              attn_amd64.s: the vector path of rows without masked holes,
 //              the scalar path otherwise; f16 keys and values converted
 //              exactly.
-//   argmax     cmd/mim-run/main.go:184-193: first index of the maximum.
+//   argmax     cmd/mim-run/main.go:184-193: first index of the maximum
+//              (0 when v[0] is NaN), as a 64-bit key reduced by atomicMax.
+#include <algorithm>
 #include <cfloat>
 
 #include "amd64_math.cuh"
@@ -296,33 +298,35 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
 }
 
 // ------------------------------------------------------------- argmax
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ v, long long n, int *__restrict__ out) {
-    __shared__ float bvs[32];
-    __shared__ long long bis[32];
+// argmax (cmd/mim-run/main.go:184-193): best = 0; x > v[best] moves best.
+// The result is the first index of the largest non-NaN value (NaNs never
+// compare greater), or 0 when v[0] is NaN.  Each block reduces a strided
+// share to (value, index) and folds it into one 64-bit key by atomicMax:
+// the value's order-preserving bits above the complement of the index, so
+// the larger value and then the smaller index wins; -0 counts as +0, as the
+// reference's comparison does.  argmax_finish reads the key.
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long i) {
+    uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n,
+                                                     unsigned long long *__restrict__ key) {
+    __shared__ unsigned long long red[8];
     pdl_launch_dependents();
     pdl_wait();
-    float bv = 0.f;
-    long long bi = -1;
-    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+    unsigned long long best = 0;  // 0: no candidate (every real key is larger)
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += gridDim.x * 256LL) {
         const float x = v[i];
-        if (x == x && (bi < 0 || x > bv)) { bv = x; bi = i; }
+        if (x == x) best = max(best, argmax_key(x, i));
     }
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const long long oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-    }
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) { bvs[w] = bv; bis[w] = bi; }
+    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
-            if (bis[k] >= 0 && (bis[0] < 0 || bvs[k] > bvs[0] || (bvs[k] == bvs[0] && bis[k] < bis[0]))) {
-                bvs[0] = bvs[k];
-                bis[0] = bis[k];
-            }
-        const float v0 = n > 0 ? v[0] : 0.f;
-        *out = (n == 0 || v0 != v0 || bis[0] < 0) ? 0 : (int)bis[0];
+        for (int k = 1; k < 8; k++) best = max(best, red[k]);
+        if (best) atomicMax(key, best);
     }
 }
 
@@ -384,10 +388,12 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float *v, long long n, int *out, cudaStream_t st, bool pdl) {
+cudaError_t launch_argmax(const float *v, long long n, unsigned long long *key, cudaStream_t st, bool pdl) {
+    if (n <= 0) return cudaSuccess;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(1024), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, out);
+    const long long blocks = std::min<long long>((n + 1023) / 1024, 2LL * num_sms());
+    cudaLaunchConfig_t cfg = make_cfg(dim3((unsigned)std::max<long long>(1, blocks)), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, key);
 }
 
 int num_sms() {

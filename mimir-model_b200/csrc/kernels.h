@@ -85,7 +85,10 @@ struct AttnArgs {
     float *out;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
-cudaError_t launch_argmax(const float *v, long long n, int *out, cudaStream_t st, bool pdl);
+// Greedy pick over v[0..n): folds the block maxima into *key (zero before
+// the call); the index is 0xFFFFFFFF - (key & 0xFFFFFFFF), or 0 when no
+// non-NaN value exists or v[0] is NaN (the reader checks v[0]).
+cudaError_t launch_argmax(const float *v, long long n, unsigned long long *key, cudaStream_t st, bool pdl);
 
 // seeded synthetic weights (k_synth.cu)
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,

@@ -51,7 +51,8 @@ struct mimgpu_session {
     ActQ8 actE{}, actF{};
     int32_t *tok = nullptr, *ids = nullptr;
     int64_t *pos = nullptr;
-    int *amax = nullptr, *step = nullptr;
+    unsigned long long *amax = nullptr;  // argmax key, zero between steps
+    int *step = nullptr;
     cudaGraphExec_t g_step = nullptr;    // T=1 forward, logits of the row
     cudaGraphExec_t g_greedy = nullptr;  // T=1 forward + argmax + advance
 };
@@ -151,7 +152,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
     if (greedy) {
         CK(launch_argmax(s->logits, c.vocab, s->amax, st, pdl));
-        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl));
+        CK(launch_advance(s->amax, s->logits, s->tok, s->pos, s->ids, s->step, st, pdl));
     }
 #undef CK
     return cudaSuccess;
@@ -299,7 +300,7 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->pos = (int64_t *)take();
     s->ids = (int32_t *)take();
     uint8_t *misc = take();
-    s->amax = (int *)misc;
+    s->amax = (unsigned long long *)(misc + 32);
     s->step = (int *)(misc + 16);
     s->cache_bytes = (size_t)k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
     s->kc.resize(k.layers, nullptr);
@@ -333,6 +334,7 @@ int mimgpu_session_reset(mimgpu_session *s) {
         e = cudaMemsetAsync(s->kc[l], 0, s->cache_bytes, s->st);
         if (e == cudaSuccess) e = cudaMemsetAsync(s->vc[l], 0, s->cache_bytes, s->st);
     }
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->amax, 0, sizeof(unsigned long long), s->st);
     if (e != cudaSuccess) return cuda_fail(c, e, "reset");
     return sync_bounded(c, s->st);
 }

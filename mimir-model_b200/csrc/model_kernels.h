@@ -50,7 +50,7 @@ inline size_t attn_exact_smem(int H, int Hkv, int D, int C, int f16) {
     return 1024 + sizeof(float) * (256 + (size_t)(256 / D) * C) + (size_t)kAttnRing * chunk;
 }
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
-cudaError_t launch_advance(const int *argmax, int32_t *tok, int64_t *pos, int32_t *ids, int *step, cudaStream_t st,
-                           bool pdl);
+cudaError_t launch_advance(unsigned long long *key, const float *logits, int32_t *tok, int64_t *pos, int32_t *ids,
+                           int *step, cudaStream_t st, bool pdl);
 
 }  // namespace mimgpu
