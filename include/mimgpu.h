@@ -52,6 +52,7 @@ typedef struct mimgpu_ctx mimgpu_ctx;
 typedef struct mimgpu_tensor mimgpu_tensor;
 typedef struct mimgpu_model mimgpu_model;
 typedef struct mimgpu_session mimgpu_session;
+typedef struct mimgpu_tp mimgpu_tp;
 
 /* ------------------------------------------------------------ context */
 
@@ -221,6 +222,26 @@ int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int s
 /* The session's CUDA stream (a cudaStream_t), for callers that time or
  * order their own device work against the session's. */
 void *mimgpu_session_stream(mimgpu_session *s);
+
+/* ------------------------------------------------- tensor parallelism
+ * No counterpart in the reference (one process on CPU).  Ranks of one node,
+ * one process and context per GPU, share an NCCL communicator (NCCL is
+ * loaded at run time).  With a group bound, every matrix of the model is
+ * used by output rows: rank k of N computes attention heads [kH/N, (k+1)H/N),
+ * its kv heads, FFN rows and vocabulary rows likewise, each as complete
+ * block-ordered dot products, and all-gathers the activations it needs
+ * whole (attention output, residual stream, SwiGLU output), so every rank
+ * produces the single-GPU logits and greedy ids bit for bit.  The weights
+ * bound with mimgpu_model_set_weight are the full tensors (each rank reads
+ * its rows).  Needs heads, kv heads, ffn and embed divisible by N. */
+/* Rank 0 makes the group id (NCCL_UNIQUE_ID_BYTES = 128 bytes) and hands it
+ * to the others. */
+int mimgpu_tp_unique_id(void *id, size_t nbytes);
+int mimgpu_tp_new(mimgpu_ctx *ctx, const void *id, size_t nbytes, int nranks, int rank, mimgpu_tp **out);
+void mimgpu_tp_free(mimgpu_tp *tp);
+/* Binds the group before the model's first session; the group must outlive
+ * the model's sessions. */
+int mimgpu_model_set_tp(mimgpu_model *m, mimgpu_tp *tp);
 
 #ifdef __cplusplus
 }

@@ -236,15 +236,14 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
     if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 
-// After the argmax of a greedy step: the picked id (0 when v[0] is NaN or
-// nothing was picked) becomes the next input token, is appended to the
-// output ids, the position advances, and the key is cleared for the next step.
-__global__ void advance_kernel(unsigned long long *key, const float *logits, int32_t *tok, int64_t *pos,
-                               int32_t *ids, int *step) {
+// After the argmax of a greedy step: the picked id (0 when the first logit
+// is NaN -- the all-ones key -- or nothing was picked) becomes the next input
+// token, is appended to the output ids, the position advances, and the key
+// is cleared for the next step.
+__global__ void advance_kernel(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step) {
     pdl_wait();
     const unsigned long long k = *key;
-    const float v0 = logits[0];
-    const int id = (k == 0 || v0 != v0) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    const int id = (k == 0 || k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
     *key = 0;
     *tok = id;
     ids[*step] = id;
@@ -282,11 +281,11 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
     return cudaLaunchKernelEx(&cfg, attn_exact_kernel<false>, a);
 }
 
-cudaError_t launch_advance(unsigned long long *key, const float *logits, int32_t *tok, int64_t *pos, int32_t *ids,
-                           int *step, cudaStream_t st, bool pdl) {
+cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
+                           cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = mk(dim3(1), dim3(1), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, advance_kernel, key, logits, tok, pos, ids, step);
+    return cudaLaunchKernelEx(&cfg, advance_kernel, key, tok, pos, ids, step);
 }
 
 }  // namespace mimgpu

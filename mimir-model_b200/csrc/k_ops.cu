@@ -304,23 +304,27 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
 // share to (value, index) and folds it into one 64-bit key by atomicMax:
 // the value's order-preserving bits above the complement of the index, so
 // the larger value and then the smaller index wins; -0 counts as +0, as the
-// reference's comparison does.  argmax_finish reads the key.
+// reference's comparison does.  A NaN first value sets the all-ones key.
+// With tensor parallelism each rank folds its vocabulary slice (global
+// indices i0 + i) and the keys meet in a 64-bit max all-reduce.
 __device__ __forceinline__ unsigned long long argmax_key(float v, long long i) {
     uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
     b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
     return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
 }
 
-__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n,
-                                                     unsigned long long *__restrict__ key) {
+__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n, long long i0,
+                                                     int holds_first, unsigned long long *__restrict__ key) {
     __shared__ unsigned long long red[8];
     pdl_launch_dependents();
     pdl_wait();
     unsigned long long best = 0;  // 0: no candidate (every real key is larger)
     for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += gridDim.x * 256LL) {
         const float x = v[i];
-        if (x == x) best = max(best, argmax_key(x, i));
+        if (x == x) best = max(best, argmax_key(x, i0 + i));
     }
+    // a NaN first logit keeps the reference's best = 0: the all-ones key wins
+    if (holds_first && blockIdx.x == 0 && threadIdx.x == 0 && n > 0 && v[0] != v[0]) best = ~0ull;
     for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
@@ -388,12 +392,12 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float *v, long long n, unsigned long long *key, cudaStream_t st, bool pdl) {
-    if (n <= 0) return cudaSuccess;
+cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_first, unsigned long long *key,
+                          cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     const long long blocks = std::min<long long>((n + 1023) / 1024, 2LL * num_sms());
     cudaLaunchConfig_t cfg = make_cfg(dim3((unsigned)std::max<long long>(1, blocks)), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, key);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, i0, (int)holds_first, key);
 }
 
 int num_sms() {

@@ -85,10 +85,12 @@ struct AttnArgs {
     float *out;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
-// Greedy pick over v[0..n): folds the block maxima into *key (zero before
-// the call); the index is 0xFFFFFFFF - (key & 0xFFFFFFFF), or 0 when no
-// non-NaN value exists or v[0] is NaN (the reader checks v[0]).
-cudaError_t launch_argmax(const float *v, long long n, unsigned long long *key, cudaStream_t st, bool pdl);
+// Greedy pick over v[0..n) holding global indices i0..: folds the block
+// maxima into *key (zero before the call); the index is
+// 0xFFFFFFFF - (key & 0xFFFFFFFF), or 0 for a zero key or the all-ones key
+// that a NaN v[0] sets when this slice holds the first index.
+cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_first, unsigned long long *key,
+                          cudaStream_t st, bool pdl);
 
 // seeded synthetic weights (k_synth.cu)
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,

@@ -38,6 +38,7 @@ struct mimgpu_model {
     const mimgpu_tensor *embd = nullptr, *out_norm = nullptr, *out = nullptr;
     std::vector<LayerW> L;
     double *inv_freq = nullptr;  // device [rope_dims/2]
+    mimgpu_tp *tp = nullptr;     // tensor-parallel group, or null for one GPU
 };
 
 struct mimgpu_session {
@@ -48,6 +49,9 @@ struct mimgpu_session {
     void *arena = nullptr;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *qh = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr;
     float *logits = nullptr;
+    // tensor parallelism: this rank's slices before the all-gathers, and the
+    // all-gather landing buffer ([ranks][T][width])
+    float *attl = nullptr, *al = nullptr, *xl = nullptr, *logl = nullptr, *gbuf = nullptr;
     ActQ8 actE{}, actF{};
     int32_t *tok = nullptr, *ids = nullptr;
     int64_t *pos = nullptr;
@@ -71,6 +75,10 @@ bool matrix_dtype(int dt, bool a8) { return dt == Q4_K || dt == Q6_K || (!a8 && 
 int validate(mimgpu_model *m) {
     const auto &c = m->c;
     mimgpu_ctx *x = m->ctx;
+    const int N = tp_size(m->tp);
+    if (N > 1 && (c.heads % N || c.kv_heads % N || c.ffn % N || c.embed % N))
+        return fail(x, MIMGPU_ENOTHANDLED, "tensor parallelism over %d ranks needs heads %d, kv heads %d, ffn %d "
+                    "and embed %d divisible by it", N, c.heads, c.kv_heads, c.ffn, c.embed);
     const long long E = c.embed, F = c.ffn, V = c.vocab, KV = (long long)c.kv_heads * c.head_dim;
     int rc;
     if ((rc = check_shape(x, "token_embd.weight", m->embd, V, E))) return rc;
@@ -99,11 +107,24 @@ int validate(mimgpu_model *m) {
 // Enqueues one run of the graph for T tokens whose ids and positions are
 // already in s->tok / s->pos.  Logits of every row (all_rows) or of the
 // last row go to s->logits; with greedy, the argmax and step update follow.
+// Row slice [r0, r0 + rows) of a weight matrix [n, K] as a GEMV segment.
+GemvSeg slice(const mimgpu_tensor *w, long long K, long long r0, int rows, float *y, long long ldy,
+              const float *res) {
+    GemvSeg g{w->dev + r0 * row_bytes(w->dtype, K), w->dtype, rows, y, ldy, nullptr, res};
+    return g;
+}
+
 cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy, unsigned *status) {
     mimgpu_model *m = s->m;
     const auto &c = m->c;
-    const int E = c.embed, F = c.ffn, H = c.heads, Hkv = c.kv_heads, D = c.head_dim, KV = Hkv * D;
-    const long long ldq = E + 2LL * KV;
+    const int E = c.embed, F = c.ffn, H = c.heads, Hkv = c.kv_heads, D = c.head_dim;
+    // tensor parallelism: every matrix is split by output rows; rank k owns
+    // heads [k H/N, (k+1) H/N), kv heads, FFN rows, residual columns and
+    // vocabulary rows likewise, and gathers the activations it needs whole
+    const int N = tp_size(m->tp), k = tp_rank(m->tp);
+    const int Hl = H / N, Hkvl = Hkv / N, El = Hl * D, KVl = Hkvl * D, Fl = F / N;
+    const int Vl = (c.vocab + N - 1) / N, v0 = k * Vl, vn = std::max(0, std::min(Vl, c.vocab - v0));
+    const long long ldq = El + 2LL * KVl;
     const bool a8 = c.a8 != 0;
     cudaStream_t st = s->st;
     const bool pdl = true;
@@ -113,46 +134,84 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if ((e = (x)) != cudaSuccess) return e; \
     } while (0)
     const ActQ8 none{};
+    // all-gathers: this rank's [T][W] slab -> [T][N*W] in `full`
+    auto gather = [&](const float *mine, int W, float *full) -> cudaError_t {
+        if (T == 1) return tp_allgather(m->tp, mine, full, (size_t)W, st);
+        cudaError_t r = tp_allgather(m->tp, mine, s->gbuf, (size_t)T * W, st);
+        if (r == cudaSuccess) r = launch_unshard(s->gbuf, N, T, W, full, (long long)N * W, (long long)N * W, st);
+        return r;
+    };
+    // the residual after a row-split product: this rank wrote columns
+    // [k El, (k+1) El) of x; every rank needs all of them
+    auto gather_x = [&]() -> cudaError_t {
+        if (N == 1) return cudaSuccess;
+        if (T == 1) return tp_allgather(m->tp, s->x + (long long)k * El, s->x, (size_t)El, st);
+        cudaError_t r = launch_pack(s->x, T, E, (long long)k * El, El, s->xl, st);
+        if (r == cudaSuccess) r = gather(s->xl, El, s->x);
+        return r;
+    };
     CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
                                 a8 ? s->actE : none, st, pdl));
-        GemvSeg qkv[3] = {{w.q->dev, w.q->dtype, E, s->qkv, ldq, nullptr, nullptr},
-                          {w.k->dev, w.k->dtype, KV, s->qkv + E, ldq, nullptr, nullptr},
-                          {w.v->dev, w.v->dtype, KV, s->qkv + E + KV, ldq, nullptr, nullptr}};
+        GemvSeg qkv[3] = {slice(w.q, E, (long long)k * El, El, s->qkv, ldq, nullptr),
+                          slice(w.k, E, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr),
+                          slice(w.v, E, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr)};
         if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
-        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
+        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
-        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none, status};
+        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, Hl, Hkvl, D, c.context, c.cache_f16,
+                     (float)(1.0 / std::sqrt((double)D)), N > 1 ? s->attl : s->att, (a8 && N == 1) ? s->actE : none,
+                     status};
         CK(launch_attn_exact(aa, st, pdl));
-        GemvSeg o{w.o->dev, w.o->dtype, E, s->x, E, nullptr, s->x};
+        if (N > 1) {
+            CK(gather(s->attl, El, s->att));
+            if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl));
+        }
+        GemvSeg o = slice(w.o, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
         if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
+        CK(gather_x());
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
                                 a8 ? s->actE : none, st, pdl));
-        GemvSeg gu[2] = {{w.gate->dev, w.gate->dtype, F, s->gu, 2LL * F, nullptr, nullptr},
-                         {w.up->dev, w.up->dtype, F, s->gu + F, 2LL * F, nullptr, nullptr}};
+        GemvSeg gu[2] = {slice(w.gate, E, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
+                         slice(w.up, E, (long long)k * Fl, Fl, s->gu + Fl, 2LL * Fl, nullptr)};
         if (a8) CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
-        CK(launch_swiglu_quant(s->gu, s->gu + F, 2LL * F, T, F, s->a, a8 ? s->actF : none, st, pdl));
-        GemvSeg dn{w.down->dev, w.down->dtype, E, s->x, E, nullptr, s->x};
+        CK(launch_swiglu_quant(s->gu, s->gu + Fl, 2LL * Fl, T, Fl, N > 1 ? s->al : s->a,
+                               (a8 && N == 1) ? s->actF : none, st, pdl));
+        if (N > 1) {
+            CK(gather(s->al, Fl, s->a));
+            if (a8) CK(launch_quantize_a8(s->a, T, F, s->actF, st, pdl));
+        }
+        GemvSeg dn = slice(w.down, F, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
         if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl));
         else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
+        CK(gather_x());
     }
     const int first = all_rows ? 0 : T - 1, rows = T - first;
     CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
                             (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl));
     const mimgpu_tensor *head = m->out ? m->out : m->embd;
-    GemvSeg hs{head->dev, head->dtype, c.vocab, s->logits, c.vocab, nullptr, nullptr};
-    if (a8) CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl));
-    else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
+    // vocabulary rows [v0, v0 + vn); one GPU writes the logits directly
+    float *lg = N > 1 ? s->logl : s->logits;
+    const long long ldl = N > 1 ? Vl : c.vocab;
+    if (vn > 0) {
+        GemvSeg hs = slice(head, E, v0, vn, lg, ldl, nullptr);
+        if (a8) CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl));
+        else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
+    }
     if (greedy) {
-        CK(launch_argmax(s->logits, c.vocab, s->amax, st, pdl));
-        CK(launch_advance(s->amax, s->logits, s->tok, s->pos, s->ids, s->step, st, pdl));
+        CK(launch_argmax(lg, vn, v0, k == 0, s->amax, st, pdl));
+        if (N > 1) CK(tp_allreduce_max_u64(m->tp, s->amax, st));
+        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl));
+    } else if (N > 1) {
+        // the whole vocabulary on every rank: [N][rows][Vl] -> [rows][vocab]
+        CK(tp_allgather(m->tp, s->logl, s->gbuf, (size_t)rows * Vl, st));
+        CK(launch_unshard(s->gbuf, N, rows, Vl, s->logits, c.vocab, c.vocab, st));
     }
 #undef CK
     return cudaSuccess;
@@ -251,6 +310,12 @@ int mimgpu_model_set_weight(mimgpu_model *m, const char *name, const mimgpu_tens
     return fail(m->ctx, MIMGPU_EINVAL, "unknown weight %s", name);
 }
 
+int mimgpu_model_set_tp(mimgpu_model *m, mimgpu_tp *tp) {
+    if (!m) return MIMGPU_EINVAL;
+    m->tp = tp;
+    return MIMGPU_OK;
+}
+
 void mimgpu_model_free(mimgpu_model *m) {
     if (!m) return;
     cudaSetDevice(m->ctx->device);
@@ -271,11 +336,15 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->m = m;
     const long long T = k.max_tokens, E = k.embed, F = k.ffn, V = k.vocab, H = k.heads, D = k.head_dim;
     const long long KV = (long long)k.kv_heads * D;
+    const long long N = tp_size(m->tp), El = E / N, Fl = F / N, Vl = (V + N - 1) / N;
+    const long long gw = std::max(std::max(El, Fl), Vl);
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    auto tpb = [&](size_t b) { return N > 1 ? al(b) : (size_t)0; };
     size_t bytes = 0;
     const size_t sz[] = {al(T * E * 4), al(T * E * 4), al(T * (E + 2 * KV) * 4), al(T * E * 4), al(T * E * 4),
                          al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
-                         al(T * 4), al(T * 8), al(65536 * 4), al(256)};
+                         al(T * 4), al(T * 8), al(65536 * 4), al(256),
+                         tpb(T * El * 4), tpb(T * Fl * 4), tpb(T * El * 4), tpb(T * Vl * 4), tpb(N * T * gw * 4)};
     for (size_t b : sz) bytes += b;
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s->arena, bytes);
@@ -302,7 +371,12 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     uint8_t *misc = take();
     s->amax = (unsigned long long *)(misc + 32);
     s->step = (int *)(misc + 16);
-    s->cache_bytes = (size_t)k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
+    s->attl = (float *)take();
+    s->al = (float *)take();
+    s->xl = (float *)take();
+    s->logl = (float *)take();
+    s->gbuf = (float *)take();
+    s->cache_bytes = (size_t)(k.kv_heads / N) * k.context * D * (k.cache_f16 ? 2 : 4);  // this rank's kv heads
     s->kc.resize(k.layers, nullptr);
     s->vc.resize(k.layers, nullptr);
     for (int l = 0; l < k.layers && e == cudaSuccess; l++) {

@@ -7,7 +7,21 @@
 
 #include "kernels.h"
 
+struct mimgpu_tp;
+
 namespace mimgpu {
+
+// tensor parallelism (tp.cu): group size and rank (1, 0 without a group),
+// the all-gather of `count` floats per rank and the 64-bit max all-reduce
+int tp_size(const mimgpu_tp *tp);
+int tp_rank(const mimgpu_tp *tp);
+cudaError_t tp_allgather(mimgpu_tp *tp, const float *send, float *recv, size_t count, cudaStream_t st);
+cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st);
+// [N][T][W] -> rows of stride ldd, columns below wmax; and the [T][W] slab
+// of columns [c0, c0 + W) of rows of stride ld
+cudaError_t launch_unshard(const float *src, int N, int T, int W, float *dst, long long ldd, long long wmax,
+                           cudaStream_t st);
+cudaError_t launch_pack(const float *x, int T, long long ld, long long c0, int W, float *y, cudaStream_t st);
 
 struct RopeScatterArgs {
     const float *qkv;      // [T, ldq]: q (H*D) | k (Hkv*D) | v (Hkv*D)
@@ -50,7 +64,7 @@ inline size_t attn_exact_smem(int H, int Hkv, int D, int C, int f16) {
     return 1024 + sizeof(float) * (256 + (size_t)(256 / D) * C) + (size_t)kAttnRing * chunk;
 }
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
-cudaError_t launch_advance(unsigned long long *key, const float *logits, int32_t *tok, int64_t *pos, int32_t *ids,
-                           int *step, cudaStream_t st, bool pdl);
+cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
+                           cudaStream_t st, bool pdl);
 
 }  // namespace mimgpu

@@ -62,6 +62,10 @@ SIGNATURES = {
     "mimgpu_session_run": (I32, [P, P, P, I32, P, I32]),
     "mimgpu_session_generate": (I32, [P, I32, I64, I32, P]),
     "mimgpu_session_stream": (P, [P]),
+    "mimgpu_tp_unique_id": (I32, [P, SZ]),
+    "mimgpu_tp_new": (I32, [P, P, SZ, I32, I32, C.POINTER(P)]),
+    "mimgpu_tp_free": (None, [P]),
+    "mimgpu_model_set_tp": (I32, [P, P]),
 }
 
 
@@ -291,6 +295,42 @@ class Context:
         return [self.embedding(ins[0], ins[1])], True
 
 
+TP_ID_BYTES = 128  # NCCL_UNIQUE_ID_BYTES
+
+
+def tp_unique_id() -> bytes:
+    """A fresh tensor-parallel group id (made by rank 0, handed to the others)."""
+    buf = C.create_string_buffer(TP_ID_BYTES)
+    rc = lib().mimgpu_tp_unique_id(buf, TP_ID_BYTES)
+    if rc != OK:
+        raise MimGPUError(rc, "cannot make an NCCL group id")
+    return buf.raw
+
+
+class TensorParallel:
+    """One rank of a tensor-parallel group (an NCCL communicator over the
+    GPUs of one node).  Every rank binds it to its model with
+    Model.set_tp before creating sessions."""
+
+    def __init__(self, ctx: "Context", group_id: bytes, nranks: int, rank: int):
+        h = P()
+        ctx._check(lib().mimgpu_tp_new(ctx.h, group_id, len(group_id), nranks, rank, C.byref(h)))
+        self.ctx, self.h, self.nranks, self.rank = ctx, h, nranks, rank
+
+    def free(self):
+        if self.h:
+            lib().mimgpu_tp_free(self.h)
+            self.h = None
+
+
+def tp_rows(n: int, nranks: int, rank: int) -> tuple:
+    """Rows [r0, r1) of an n-row matrix that a rank computes: equal slices
+    (the vocabulary's last slice may be short)."""
+    per = (n + nranks - 1) // nranks
+    r0 = min(n, rank * per)
+    return r0, min(n, r0 + per)
+
+
 class Model:
     """The llama graph (importer/llama.go:317-547) as a device-resident decoder."""
 
@@ -308,6 +348,11 @@ class Model:
             t = arr if isinstance(arr, Tensor) else ctx.upload(dt, _shape_of(name, cfg, dt, arr), arr)
             self.weights[name] = t
             ctx._check(lib().mimgpu_model_set_weight(h, name.encode(), t.h))
+
+    def set_tp(self, tp: "TensorParallel | None"):
+        """Binds a tensor-parallel group (before the first session)."""
+        self.ctx._check(lib().mimgpu_model_set_tp(self.h, tp.h if tp is not None else None))
+        self.tp = tp
 
     def session(self) -> "Session":
         h = P()

@@ -1,0 +1,46 @@
+"""One rank of the tensor-parallel GPU test (run in a spawned process): builds
+the synthetic 8B-layer-shape model on its GPU, joins the group, and returns
+the prompt logits and greedy ids."""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def model_cfg():
+    return dict(layers=2, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=32000,
+                rope_theta=500000.0, norm_eps=1e-5)
+
+
+def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: int = 32):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "mimir-model_b200"))
+    import bench
+    import mimgpu
+    cfg = model_cfg()
+    ctx = mimgpu.Context(device)
+    model, _ = bench.build_model(ctx, cfg, 128, 16)
+    tp = None
+    if group_id is not None:
+        tp = mimgpu.TensorParallel(ctx, group_id, nranks, rank)
+        model.set_tp(tp)
+    s = model.session()
+    prompt = np.random.default_rng(3).integers(0, cfg["vocab"], 16).astype(np.int32)
+    logits = s.run(prompt, np.arange(16), all_rows=True)
+    ids = s.generate(int(np.argmax(logits[-1])), 16, steps)
+    s.free()
+    model.free()
+    if tp is not None:
+        tp.free()
+    ctx.close()
+    return logits, ids
+
+
+def rank_main(rank: int, nranks: int, group_id: bytes, q):
+    try:
+        q.put((rank, decode(rank, group_id, nranks, rank)))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
