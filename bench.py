@@ -257,6 +257,11 @@ def run_gpu(args):
         tp = mimgpu.TensorParallel(ctx, gid[0], world, rank)
         model.set_tp(tp)
     sess = model.session()
+    if world > 1:
+        # map every rank's arena: decode steps exchange over peer memory
+        hs = [None] * world
+        dist.all_gather_object(hs, sess.ipc_handle())
+        sess.set_peers(hs)
     ids = prompt_ids(cfg["vocab"], prompt)
     logits = sess.run(ids, np.arange(prompt))[0]
     tok, pos = int(np.argmax(logits)), prompt

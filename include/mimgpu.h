@@ -226,14 +226,15 @@ void *mimgpu_session_stream(mimgpu_session *s);
 /* ------------------------------------------------- tensor parallelism
  * No counterpart in the reference (one process on CPU).  Ranks of one node,
  * one process and context per GPU, share an NCCL communicator (NCCL is
- * loaded at run time).  With a group bound, every matrix of the model is
- * used by output rows: rank k of N computes attention heads [kH/N, (k+1)H/N),
- * its kv heads, FFN rows and vocabulary rows likewise, each as complete
- * block-ordered dot products, and all-gathers the activations it needs
- * whole (attention output, residual stream, SwiGLU output), so every rank
- * produces the single-GPU logits and greedy ids bit for bit.  The weights
- * bound with mimgpu_model_set_weight are the full tensors (each rank reads
- * its rows).  Needs heads, kv heads, ffn and embed divisible by N. */
+ * loaded at run time).  With a group bound, the attention block runs whole
+ * on every rank (the residual stream stays identical without an exchange)
+ * while the FFN and the output head are used by output rows: rank k of N
+ * computes gate/up rows [kF/N, (k+1)F/N), down rows [kE/N, (k+1)E/N) and its
+ * vocabulary rows as complete block-ordered dot products, and the SwiGLU
+ * output and the residual are all-gathered; every rank produces the
+ * single-GPU logits and greedy ids bit for bit.  The weights bound with
+ * mimgpu_model_set_weight are the full tensors (each rank reads its rows).
+ * Needs ffn and embed divisible by N. */
 /* Rank 0 makes the group id (NCCL_UNIQUE_ID_BYTES = 128 bytes) and hands it
  * to the others. */
 int mimgpu_tp_unique_id(void *id, size_t nbytes);
@@ -242,6 +243,16 @@ void mimgpu_tp_free(mimgpu_tp *tp);
 /* Binds the group before the model's first session; the group must outlive
  * the model's sessions. */
 int mimgpu_model_set_tp(mimgpu_model *m, mimgpu_tp *tp);
+/* Peer-memory exchanges for the one-token step: every rank exports its
+ * session's device arena (a cudaIpcMemHandle_t, 64 bytes), the handles are
+ * all-gathered by the caller (rank order) and handed to every rank's
+ * session.  From then on the SwiGLU output, the residual columns and the
+ * argmax keys of a decode step travel over NVLink inside the kernels that
+ * produce them (stores into every rank's copy, an epoch flag per exchange,
+ * bounded waits), with no collective launches; multi-token runs keep the
+ * NCCL all-gathers. */
+int mimgpu_session_ipc_handle(mimgpu_session *s, void *out, size_t nbytes);
+int mimgpu_session_set_peers(mimgpu_session *s, const void *handles, size_t each, int nranks);
 
 #ifdef __cplusplus
 }

@@ -17,6 +17,7 @@
 #include "kernels.h"
 #include "amd64_math.cuh"
 #include "quant.cuh"
+#include "p2p.cuh"
 
 namespace mimgpu {
 
@@ -50,10 +51,15 @@ ActQ8 act_q8_carve(void *base, int rows, long long K) {
 // SMs.  The refusal rule of QuantizeBlocks is recorded per block in ok;
 // a row is quantized when all its blocks are.
 
-__global__ void __launch_bounds__(256) quantize_a8_kernel(const float *__restrict__ x, long long K, ActQ8 act) {
+__global__ void __launch_bounds__(256) quantize_a8_kernel(const float *__restrict__ x, long long K, ActQ8 act,
+                                                          P2P wait) {
     __shared__ QuantScratch qs;
     pdl_launch_dependents();
     pdl_wait();
+    if (wait.N > 1) {  // every rank's slice of x has arrived
+        p2p_publish_wait(wait);
+        __syncthreads();
+    }
     const long long row = blockIdx.x;
     const int b = blockIdx.y;
     quant_block_256(x[row * K + b * 256 + threadIdx.x], row, K, b, act, qs);
@@ -84,10 +90,14 @@ __device__ __forceinline__ float rms_inv(const float *__restrict__ xr, int n, fl
 // normalises and quantizes elements [256b, 256b + 256).
 __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restrict__ x, int n,
                                                             const float *__restrict__ scale, float eps,
-                                                            float *__restrict__ y, ActQ8 act) {
+                                                            float *__restrict__ y, ActQ8 act, P2P wait) {
     __shared__ QuantScratch qs;
     pdl_launch_dependents();
     pdl_wait();
+    if (wait.N > 1) {  // every rank's columns of the residual have arrived
+        p2p_publish_wait(wait);
+        __syncthreads();
+    }
     const long long row = blockIdx.x;
     const int b = blockIdx.y, i = b * 256 + threadIdx.x;
     const float *xr = x + row * n;
@@ -105,7 +115,8 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
 // the first n&~7 elements, float64 on the rest) fused with the quantization
 // of its output for the down projection.
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *__restrict__ gate, const float *__restrict__ up,
-                                                           long long ldg, int n, float *__restrict__ y, ActQ8 act) {
+                                                           long long ldg, int n, float *__restrict__ y, ActQ8 act,
+                                                           P2P put) {
     __shared__ QuantScratch qs;
     pdl_launch_dependents();
     pdl_wait();
@@ -116,6 +127,14 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *__restri
         v = i < (n & ~7) ? silu_mul_amd64(gate[row * ldg + i], up[row * ldg + i])
                          : silu_mul_f64(gate[row * ldg + i], up[row * ldg + i]);
         y[row * n + i] = v;
+        // tensor parallelism: this rank's slice into every rank's full vector
+        for (int r = 0; r < (put.N > 1 ? put.N : 0); r++) peer_ptr<float>(put, r, put.off)[put.col0 + i] = v;
+    }
+    if (put.N > 1) {
+        // the block's peer stores are visible system-wide before the kernel
+        // ends (the next kernel on this stream publishes the exchange)
+        __syncthreads();
+        if (threadIdx.x == 0) __threadfence_system();
     }
     if (act.q) quant_block_256(v, row, n, b, act, qs);
 }
@@ -132,30 +151,35 @@ static cudaLaunchConfig_t blocks_cfg(int rows, int nblk, cudaStream_t st, bool p
     return cfg;
 }
 
-cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st, bool pdl) {
+cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st, bool pdl,
+                               const P2P *wait) {
     if (rows <= 0 || K <= 0) return cudaSuccess;
     if (K % 256) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (int)(K / 256), st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, quantize_a8_kernel, x, K, act);
+    const P2P w = wait ? *wait : P2P{};
+    return cudaLaunchKernelEx(&cfg, quantize_a8_kernel, x, K, act, w);
 }
 
 cudaError_t launch_rmsnorm_quant(const float *x, int rows, int n, const float *scale, float eps, float *y,
-                                 ActQ8 act, cudaStream_t st, bool pdl) {
+                                 ActQ8 act, cudaStream_t st, bool pdl, const P2P *wait) {
     if (rows <= 0 || n <= 0) return cudaSuccess;
     if (act.q && n % 256) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (n + 255) / 256, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, n, scale, eps, y, act);
+    const P2P w = wait ? *wait : P2P{};
+    return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, n, scale, eps, y, act, w);
 }
 
 cudaError_t launch_swiglu_quant(const float *gate, const float *up, long long ldg, int rows, int n, float *y,
-                                ActQ8 act, cudaStream_t st, bool pdl) {
+                                ActQ8 act, cudaStream_t st, bool pdl, const P2P *put) {
     if (rows <= 0 || n <= 0) return cudaSuccess;
     if (act.q && n % 256) return cudaErrorInvalidValue;
+    if (put && put->N > 1 && rows != 1) return cudaErrorInvalidValue;  // exchanges carry one row
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (n + 255) / 256, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, ldg, n, y, act);
+    const P2P p = put ? *put : P2P{};
+    return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, ldg, n, y, act, p);
 }
 
 }  // namespace mimgpu

@@ -210,9 +210,10 @@ __global__ void dequantize_kernel(int dt, const uint8_t *__restrict__ src, float
 
 // embedding.v1: one row of the table per id; out-of-range ids give zeros.
 __global__ void embedding_kernel(int dt, const uint8_t *__restrict__ table, long long V, int E,
-                                 const int32_t *__restrict__ ids, float *__restrict__ y) {
+                                 const int32_t *__restrict__ ids, float *__restrict__ y, unsigned *epoch) {
     pdl_launch_dependents();
     pdl_wait();
+    if (epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *epoch += 1;  // a new forward
     const long long id = ids[blockIdx.x];
     const long long rb = row_bytes(dt, E);
     float *out = y + (long long)blockIdx.x * E;
@@ -262,7 +263,7 @@ cudaError_t launch_dequantize(int dt, const uint8_t *src, float *dst, long long 
 }
 
 cudaError_t launch_embedding(int dt, const uint8_t *table, long long V, int E, const int32_t *ids, int n,
-                             float *y, cudaStream_t st, bool pdl) {
+                             float *y, cudaStream_t st, bool pdl, unsigned *epoch) {
     if (n <= 0) return cudaSuccess;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -273,7 +274,7 @@ cudaError_t launch_embedding(int dt, const uint8_t *table, long long V, int E, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, embedding_kernel, dt, table, V, E, ids, y);
+    return cudaLaunchKernelEx(&cfg, embedding_kernel, dt, table, V, E, ids, y, epoch);
 }
 
 }  // namespace mimgpu

@@ -29,6 +29,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "p2p.cuh"
 
 namespace mimgpu {
 
@@ -70,6 +71,7 @@ struct __align__(64) A8Params {
     int stage_bytes;           // bytes of one stage
     int act_bytes;             // shared-memory bytes of the activations
     int act_bulk;              // 1: every activation array is 16-byte aligned: one bulk copy each
+    P2P put;                   // tensor parallelism: outputs also into every rank's copy, then publish
     unsigned *status;
 };
 
@@ -584,6 +586,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
                 if (sg.bias) r = __fadd_rn(r, biasv);
                 if (sg.res) r = __fadd_rn(resv[a], r);
                 sg.y[(long long)a * sg.ldy + row] = r;
+                for (int q = 0; q < (p.put.N > 1 ? p.put.N : 0); q++)
+                    peer_ptr<float>(p.put, q, p.put.off)[p.put.col0 + row] = r;
             }
             // rows whose weights or activations the 8-bit kernel refuses: f32 product
             for (int rr = 0; rr < nrow; rr++) {
@@ -592,9 +596,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
                 float r = row_dot_f32(sg.dt, sg.w + (long long)row * rb, p.x + (long long)a * K, p.nb);
                 if (sg.bias) r = __fadd_rn(r, sg.bias[row]);
                 if (sg.res) r = __fadd_rn(sg.res[(long long)a * sg.ldy + row], r);
-                if (lane == 0) sg.y[(long long)a * sg.ldy + row] = r;
+                if (lane == 0) {
+                    sg.y[(long long)a * sg.ldy + row] = r;
+                    for (int q = 0; q < (p.put.N > 1 ? p.put.N : 0); q++)
+                        peer_ptr<float>(p.put, q, p.put.off)[p.put.col0 + row] = r;
+                }
             }
         }
+    }
+    if (p.put.N > 1) {
+        // the warp's peer stores are visible system-wide before the kernel
+        // ends (the next kernel on this stream publishes the exchange)
+        __syncwarp();
+        if (lane == 0) __threadfence_system();
     }
 }
 
@@ -722,8 +736,9 @@ cudaError_t gemv_a8_prepare() {
 }
 
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps) {
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put) {
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
+    if (put && put->N > 1 && (rows != 1 || nseg != 1)) return cudaErrorInvalidValue;  // exchanges carry one row
     if (rows == 0 || K == 0) return cudaSuccess;
     A8Params p = {};
     p.nseg = nseg;
@@ -753,6 +768,7 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
     while (p.split > 1 && p.chunks < p.split) p.split >>= 1;
     p.cpp = (p.chunks + p.split - 1) / p.split;
     p.status = status;
+    if (put) p.put = *put;
     // activation rows per launch: as many as fit the shared-memory budget
     int per = kMaxNR;
     while (per > 1 && act_bytes_for(per, K) > kActBudget) per >>= 1;

@@ -10,6 +10,7 @@
 #include "model_kernels.h"
 #include "amd64_math.cuh"
 #include "quant.cuh"
+#include "p2p.cuh"
 
 namespace mimgpu {
 
@@ -240,9 +241,16 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
 // is NaN -- the all-ones key -- or nothing was picked) becomes the next input
 // token, is appended to the output ids, the position advances, and the key
 // is cleared for the next step.
-__global__ void advance_kernel(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step) {
+__global__ void advance_kernel(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
+                               P2P wait, const unsigned long long *keys) {
     pdl_wait();
-    const unsigned long long k = *key;
+    unsigned long long k = *key;
+    if (wait.N > 1) {  // tensor parallelism: this rank's key to every rank, then the largest wins
+        for (int r = 0; r < wait.N; r++) peer_ptr<unsigned long long>(wait, r, wait.off)[wait.k] = k;
+        p2p_publish_wait(wait);
+        k = 0;
+        for (int r = 0; r < wait.N; r++) k = max(k, ((volatile const unsigned long long *)keys)[r]);
+    }
     const int id = (k == 0 || k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
     *key = 0;
     *tok = id;
@@ -282,10 +290,11 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
-                           cudaStream_t st, bool pdl) {
+                           cudaStream_t st, bool pdl, const P2P *wait, const unsigned long long *keys) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = mk(dim3(1), dim3(1), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, advance_kernel, key, tok, pos, ids, step);
+    const P2P w = wait ? *wait : P2P{};
+    return cudaLaunchKernelEx(&cfg, advance_kernel, key, tok, pos, ids, step, w, keys);
 }
 
 }  // namespace mimgpu

@@ -20,6 +20,7 @@
 #include "amd64_math.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "p2p.cuh"
 
 namespace mimgpu {
 

@@ -37,30 +37,52 @@ struct GemvSeg {
 
 constexpr int kMaxSegs = 4;
 
-cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st, bool pdl);
+// One exchange of a tensor-parallel step through peer memory (p2p.cuh):
+// N = 0 or 1 means none.  The producer stores into every rank's copy of a
+// buffer at arena offset `off` (+ column `col0`); the consumer publishes
+// this rank's part of slot `slot` and waits for every rank's.
+struct P2P {
+    const uint64_t *base;   // [N] arena base of every rank (device array; own included)
+    long long off_flags;    // byte offset of the flag array [slots][N] (u32) in the arena
+    const unsigned *epoch;  // this rank's forward counter
+    unsigned *status;       // device status word
+    int N, k, slot;
+    long long off;          // producer: arena offset of the destination buffer
+    long long col0;         // producer: first element of this rank's slice in it
+};
+
+// wait: an exchange the input depends on (consumer side), or null
+cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st, bool pdl,
+                               const P2P *wait = nullptr);
 // y = rms_norm(x) * scale, and its 8-bit blocks (fast.go:434-485 then q8.go:50-97);
 // act may have a null q (no quantization)
 cudaError_t launch_rmsnorm_quant(const float *x, int rows, int n, const float *scale, float eps, float *y,
-                                 ActQ8 act, cudaStream_t st, bool pdl);
+                                 ActQ8 act, cudaStream_t st, bool pdl, const P2P *wait = nullptr);
 // y = silu(gate)*up (attn.go:63-73, float64) and its 8-bit blocks; act.q may be null
+// put: store the (one-row) result into every rank's copy of the exchanged
+// buffer and publish (producer side), or null
 cudaError_t launch_swiglu_quant(const float *gate, const float *up, long long ldg, int rows, int n, float *y,
-                                ActQ8 act, cudaStream_t st, bool pdl);
+                                ActQ8 act, cudaStream_t st, bool pdl, const P2P *put = nullptr);
 // dequant_matmul_a8.v2 block 256 over up to kMaxSegs Q4_K/Q6_K matrices
 // sharing the activations.  x is the f32 input, used for refused rows.
 // Sets the kernel attributes the GEMV launches need (call outside stream capture).
 cudaError_t gemv_a8_prepare();
 // cache_maps: keep each weight's TMA descriptor in a host table (false:
 // encode it on the stack every launch, allocating nothing).
+// put: the (one-segment, one-row) outputs also go to every rank's copy of
+// the exchanged buffer, then the launch publishes (producer side)
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true);
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true,
+                           const P2P *put = nullptr);
 // dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
 cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
                             cudaStream_t st, bool pdl);
 
-// dequantize n elements (quant.go Dequantize) and embedding rows (fast.go:818-842)
+// dequantize n elements (quant.go Dequantize) and embedding rows (fast.go:818-842);
+// the embedding launch of a step also advances the step counter `epoch` (may be null)
 cudaError_t launch_dequantize(int dt, const uint8_t *src, float *dst, long long n, cudaStream_t st);
 cudaError_t launch_embedding(int dt, const uint8_t *table, long long V, int E, const int32_t *ids, int n,
-                             float *y, cudaStream_t st, bool pdl);
+                             float *y, cudaStream_t st, bool pdl, unsigned *epoch = nullptr);
 
 cudaError_t launch_rmsnorm(const float *x, int rows, int n, const float *scale, float eps, float *y,
                            cudaStream_t st, bool pdl);

@@ -52,6 +52,14 @@ struct mimgpu_session {
     // tensor parallelism: this rank's slices before the all-gathers, and the
     // all-gather landing buffer ([ranks][T][width])
     float *attl = nullptr, *al = nullptr, *xl = nullptr, *logl = nullptr, *gbuf = nullptr;
+    // peer-memory exchanges of the one-token step (p2p.cuh): flags [slots][N],
+    // last-arrival counters [slots], the ranks' argmax keys [N], the forward
+    // counter, and the table of every rank's arena base (IPC-mapped)
+    unsigned *flags = nullptr, *counters = nullptr, *epoch = nullptr;
+    unsigned long long *keys = nullptr;
+    uint64_t *peer_base = nullptr;
+    std::vector<void *> opened;  // peers' arenas mapped with cudaIpcOpenMemHandle
+    bool p2p = false;
     ActQ8 actE{}, actF{};
     int32_t *tok = nullptr, *ids = nullptr;
     int64_t *pos = nullptr;
@@ -76,9 +84,9 @@ int validate(mimgpu_model *m) {
     const auto &c = m->c;
     mimgpu_ctx *x = m->ctx;
     const int N = tp_size(m->tp);
-    if (N > 1 && (c.heads % N || c.kv_heads % N || c.ffn % N || c.embed % N))
-        return fail(x, MIMGPU_ENOTHANDLED, "tensor parallelism over %d ranks needs heads %d, kv heads %d, ffn %d "
-                    "and embed %d divisible by it", N, c.heads, c.kv_heads, c.ffn, c.embed);
+    if (N > 1 && (c.ffn % N || c.embed % N))
+        return fail(x, MIMGPU_ENOTHANDLED, "tensor parallelism over %d ranks needs ffn %d and embed %d divisible by it",
+                    N, c.ffn, c.embed);
     const long long E = c.embed, F = c.ffn, V = c.vocab, KV = (long long)c.kv_heads * c.head_dim;
     int rc;
     if ((rc = check_shape(x, "token_embd.weight", m->embd, V, E))) return rc;
@@ -118,13 +126,17 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     mimgpu_model *m = s->m;
     const auto &c = m->c;
     const int E = c.embed, F = c.ffn, H = c.heads, Hkv = c.kv_heads, D = c.head_dim;
-    // tensor parallelism: every matrix is split by output rows; rank k owns
-    // heads [k H/N, (k+1) H/N), kv heads, FFN rows, residual columns and
-    // vocabulary rows likewise, and gathers the activations it needs whole
+    // tensor parallelism over N ranks: the attention block (QKV, attention,
+    // o projection; 17 % of a layer's bytes at the 8B shape) runs whole on
+    // every rank, so the residual stream stays identical everywhere without an
+    // exchange; the FFN and the vocabulary are split by output rows -- rank k
+    // computes gate/up rows [k F/N, (k+1) F/N) and down rows [k E/N, (k+1) E/N)
+    // as complete block-ordered dot products -- and the SwiGLU output and the
+    // residual are all-gathered, two exchanges per layer
     const int N = tp_size(m->tp), k = tp_rank(m->tp);
-    const int Hl = H / N, Hkvl = Hkv / N, El = Hl * D, KVl = Hkvl * D, Fl = F / N;
+    const int El = E / N, Fl = F / N, KV = Hkv * D;
     const int Vl = (c.vocab + N - 1) / N, v0 = k * Vl, vn = std::max(0, std::min(Vl, c.vocab - v0));
-    const long long ldq = El + 2LL * KVl;
+    const long long ldq = E + 2LL * KV;
     const bool a8 = c.a8 != 0;
     cudaStream_t st = s->st;
     const bool pdl = true;
@@ -134,6 +146,22 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if ((e = (x)) != cudaSuccess) return e; \
     } while (0)
     const ActQ8 none{};
+    // peer-memory exchanges (the one-token step once the ranks' arenas are mapped)
+    const bool p2p = N > 1 && T == 1 && s->p2p;
+    auto aoff = [&](const void *ptr) { return (long long)((const uint8_t *)ptr - (const uint8_t *)s->arena); };
+    auto xch = [&](int slot, const void *dst, long long col0) {
+        P2P x{};
+        x.base = s->peer_base;
+        x.off_flags = aoff(s->flags);
+        x.epoch = s->epoch;
+        x.status = status;
+        x.N = N;
+        x.k = k;
+        x.slot = slot;
+        x.off = dst ? aoff(dst) : 0;
+        x.col0 = col0;
+        return x;
+    };
     // all-gathers: this rank's [T][W] slab -> [T][N*W] in `full`
     auto gather = [&](const float *mine, int W, float *full) -> cudaError_t {
         if (T == 1) return tp_allgather(m->tp, mine, full, (size_t)W, st);
@@ -141,60 +169,57 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if (r == cudaSuccess) r = launch_unshard(s->gbuf, N, T, W, full, (long long)N * W, (long long)N * W, st);
         return r;
     };
-    // the residual after a row-split product: this rank wrote columns
-    // [k El, (k+1) El) of x; every rank needs all of them
-    auto gather_x = [&]() -> cudaError_t {
-        if (N == 1) return cudaSuccess;
-        if (T == 1) return tp_allgather(m->tp, s->x + (long long)k * El, s->x, (size_t)El, st);
-        cudaError_t r = launch_pack(s->x, T, E, (long long)k * El, El, s->xl, st);
-        if (r == cudaSuccess) r = gather(s->xl, El, s->x);
-        return r;
-    };
-    CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl));
+    CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl, s->epoch));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
+        // the previous layer's residual columns from every rank
+        const P2P xin = xch(2 * (l - 1) + 1, nullptr, 0);
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
-                                a8 ? s->actE : none, st, pdl));
-        GemvSeg qkv[3] = {slice(w.q, E, (long long)k * El, El, s->qkv, ldq, nullptr),
-                          slice(w.k, E, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr),
-                          slice(w.v, E, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr)};
+                                a8 ? s->actE : none, st, pdl, (p2p && l > 0) ? &xin : nullptr));
+        GemvSeg qkv[3] = {slice(w.q, E, 0, E, s->qkv, ldq, nullptr), slice(w.k, E, 0, KV, s->qkv + E, ldq, nullptr),
+                          slice(w.v, E, 0, KV, s->qkv + E + KV, ldq, nullptr)};
         if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
-        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
+        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
-        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, Hl, Hkvl, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), N > 1 ? s->attl : s->att, (a8 && N == 1) ? s->actE : none,
-                     status};
+        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
+                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none, status};
         CK(launch_attn_exact(aa, st, pdl));
-        if (N > 1) {
-            CK(gather(s->attl, El, s->att));
-            if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl));
-        }
-        GemvSeg o = slice(w.o, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
+        GemvSeg o = slice(w.o, E, 0, E, s->x, E, s->x);
         if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
-        CK(gather_x());
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
                                 a8 ? s->actE : none, st, pdl));
         GemvSeg gu[2] = {slice(w.gate, E, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
                          slice(w.up, E, (long long)k * Fl, Fl, s->gu + Fl, 2LL * Fl, nullptr)};
         if (a8) CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
+        const P2P aput = xch(2 * l, s->a, (long long)k * Fl);
         CK(launch_swiglu_quant(s->gu, s->gu + Fl, 2LL * Fl, T, Fl, N > 1 ? s->al : s->a,
-                               (a8 && N == 1) ? s->actF : none, st, pdl));
+                               (a8 && N == 1) ? s->actF : none, st, pdl, p2p ? &aput : nullptr));
         if (N > 1) {
-            CK(gather(s->al, Fl, s->a));
-            if (a8) CK(launch_quantize_a8(s->a, T, F, s->actF, st, pdl));
+            if (!p2p) CK(gather(s->al, Fl, s->a));
+            if (a8) CK(launch_quantize_a8(s->a, T, F, s->actF, st, pdl, p2p ? &aput : nullptr));
         }
         GemvSeg dn = slice(w.down, F, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
-        if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl));
+        const P2P xput = xch(2 * l + 1, s->x, (long long)k * El);
+        if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl, true, p2p ? &xput : nullptr));
         else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
-        CK(gather_x());
+        if (N > 1 && !p2p) {
+            // this rank wrote residual columns [k El, (k+1) El); every rank needs all
+            if (T == 1) {
+                CK(tp_allgather(m->tp, s->x + (long long)k * El, s->x, (size_t)El, st));
+            } else {
+                CK(launch_pack(s->x, T, E, (long long)k * El, El, s->xl, st));
+                CK(gather(s->xl, El, s->x));
+            }
+        }
     }
     const int first = all_rows ? 0 : T - 1, rows = T - first;
+    const P2P xlast = xch(2 * (c.layers - 1) + 1, nullptr, 0);
     CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
-                            (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl));
+                            (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl, p2p ? &xlast : nullptr));
     const mimgpu_tensor *head = m->out ? m->out : m->embd;
     // vocabulary rows [v0, v0 + vn); one GPU writes the logits directly
     float *lg = N > 1 ? s->logl : s->logits;
@@ -205,9 +230,10 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
     }
     if (greedy) {
+        const P2P kput = xch(2 * c.layers, s->keys, 0);
         CK(launch_argmax(lg, vn, v0, k == 0, s->amax, st, pdl));
-        if (N > 1) CK(tp_allreduce_max_u64(m->tp, s->amax, st));
-        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl));
+        if (N > 1 && !p2p) CK(tp_allreduce_max_u64(m->tp, s->amax, st));
+        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl, p2p ? &kput : nullptr, s->keys));
     } else if (N > 1) {
         // the whole vocabulary on every rank: [N][rows][Vl] -> [rows][vocab]
         CK(tp_allgather(m->tp, s->logl, s->gbuf, (size_t)rows * Vl, st));
@@ -242,6 +268,7 @@ void free_session(mimgpu_session *s) {
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     for (void *p : s->kc) cudaFree(p);
     for (void *p : s->vc) cudaFree(p);
+    for (void *p : s->opened) cudaIpcCloseMemHandle(p);
     if (s->arena) cudaFree(s->arena);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
@@ -344,7 +371,9 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     const size_t sz[] = {al(T * E * 4), al(T * E * 4), al(T * (E + 2 * KV) * 4), al(T * E * 4), al(T * E * 4),
                          al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
                          al(T * 4), al(T * 8), al(65536 * 4), al(256),
-                         tpb(T * El * 4), tpb(T * Fl * 4), tpb(T * El * 4), tpb(T * Vl * 4), tpb(N * T * gw * 4)};
+                         tpb(T * El * 4), tpb(T * Fl * 4), tpb(T * El * 4), tpb(T * Vl * 4), tpb(N * T * gw * 4),
+                         al((size_t)(2 * k.layers + 1) * N * 4), al((size_t)(2 * k.layers + 2) * 4), al((size_t)N * 8),
+                         al(16), al((size_t)N * 8)};
     for (size_t b : sz) bytes += b;
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s->arena, bytes);
@@ -376,7 +405,14 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->xl = (float *)take();
     s->logl = (float *)take();
     s->gbuf = (float *)take();
-    s->cache_bytes = (size_t)(k.kv_heads / N) * k.context * D * (k.cache_f16 ? 2 : 4);  // this rank's kv heads
+    uint8_t *p2p0 = p;
+    s->flags = (unsigned *)take();
+    s->counters = (unsigned *)take();
+    s->keys = (unsigned long long *)take();
+    s->epoch = (unsigned *)take();
+    s->peer_base = (uint64_t *)take();
+    e = cudaMemset(p2p0, 0, (size_t)(p - p2p0));  // flags, counters, epoch start at zero
+    s->cache_bytes = (size_t)k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
     s->kc.resize(k.layers, nullptr);
     s->vc.resize(k.layers, nullptr);
     for (int l = 0; l < k.layers && e == cudaSuccess; l++) {
@@ -465,5 +501,54 @@ int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int s
 }
 
 void *mimgpu_session_stream(mimgpu_session *s) { return s ? (void *)s->st : nullptr; }
+
+int mimgpu_session_ipc_handle(mimgpu_session *s, void *out, size_t nbytes) {
+    if (!s || !out || nbytes < sizeof(cudaIpcMemHandle_t)) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, s->arena);
+    if (e != cudaSuccess) return cuda_fail(c, e, "ipc handle");
+    std::memcpy(out, &h, sizeof(h));
+    return MIMGPU_OK;
+}
+
+int mimgpu_session_set_peers(mimgpu_session *s, const void *handles, size_t each, int nranks) {
+    if (!s || !handles || each < sizeof(cudaIpcMemHandle_t)) return MIMGPU_EINVAL;
+    mimgpu_model *m = s->m;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    const int N = tp_size(m->tp), k = tp_rank(m->tp);
+    if (N < 2 || nranks != N) return fail(c, MIMGPU_EINVAL, "set_peers: %d handles for a group of %d", nranks, N);
+    if (s->p2p) return fail(c, MIMGPU_EINVAL, "set_peers: the peers are already mapped");
+    int rc = use_device(c);
+    if (rc) return rc;
+    std::vector<uint64_t> base(N);
+    cudaError_t e = cudaSuccess;
+    for (int r = 0; r < N && e == cudaSuccess; r++) {
+        if (r == k) {
+            base[r] = (uint64_t)(uintptr_t)s->arena;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, (const uint8_t *)handles + (size_t)r * each, sizeof(h));
+        void *ptr = nullptr;
+        e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e == cudaSuccess) {
+            s->opened.push_back(ptr);
+            base[r] = (uint64_t)(uintptr_t)ptr;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(s->peer_base, base.data(), N * sizeof(uint64_t), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(c, e, "set_peers");
+    // graphs captured before now exchange through NCCL; recapture
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    s->g_step = s->g_greedy = nullptr;
+    s->p2p = true;
+    return MIMGPU_OK;
+}
 
 }  // extern "C"

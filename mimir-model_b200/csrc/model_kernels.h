@@ -64,7 +64,9 @@ inline size_t attn_exact_smem(int H, int Hkv, int D, int C, int f16) {
     return 1024 + sizeof(float) * (256 + (size_t)(256 / D) * C) + (size_t)kAttnRing * chunk;
 }
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
+// wait / keys: tensor parallelism, the ranks' keys arrive in keys[0..N)
 cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
-                           cudaStream_t st, bool pdl);
+                           cudaStream_t st, bool pdl, const P2P *wait = nullptr,
+                           const unsigned long long *keys = nullptr);
 
 }  // namespace mimgpu

@@ -1,12 +1,12 @@
 // tp.cu -- tensor parallelism of the decode step across the GPUs of one node.
 //
-// Layout (see model.cu): every matrix is split by OUTPUT rows, so each rank
-// computes complete dot products over the whole K in the reference's block
-// order (q8k_test.go:35-117 of gsoultan/mimir-model) and the ranks' results
-// are the single-GPU results bit for bit.  The activations that a rank's
-// rows need in full -- the attention output, the residual stream and the
-// SwiGLU output -- are all-gathered over NCCL (NVLink / NVSwitch); the
-// greedy pick is a 64-bit max-reduce of the packed (value, index) keys.
+// Layout (see model.cu): the FFN and output-head matrices are split by OUTPUT
+// rows, so each rank computes complete dot products over the whole K in the
+// reference's block order (q8k_test.go:35-117 of gsoultan/mimir-model) and
+// the ranks' results are the single-GPU results bit for bit; the attention
+// block runs whole on every rank.  The SwiGLU output and the residual stream
+// are all-gathered over NCCL (NVLink / NVSwitch); the greedy pick is a
+// 64-bit max-reduce of the packed (value, index) keys.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2), so a process that
 // never asks for a communicator does not need it.

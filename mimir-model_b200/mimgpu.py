@@ -66,6 +66,8 @@ SIGNATURES = {
     "mimgpu_tp_new": (I32, [P, P, SZ, I32, I32, C.POINTER(P)]),
     "mimgpu_tp_free": (None, [P]),
     "mimgpu_model_set_tp": (I32, [P, P]),
+    "mimgpu_session_ipc_handle": (I32, [P, P, SZ]),
+    "mimgpu_session_set_peers": (I32, [P, P, SZ, I32]),
 }
 
 
@@ -390,6 +392,18 @@ class Session:
         out = np.empty((t.size if all_rows else 1, self.m.vocab), np.float32)
         self.m.ctx._check(lib().mimgpu_session_run(self.h, _p(t), _p(p), t.size, _p(out), int(all_rows)))
         return out
+
+    def ipc_handle(self) -> bytes:
+        """This session's device arena as a CUDA IPC handle (tensor parallelism)."""
+        buf = C.create_string_buffer(64)
+        self.m.ctx._check(lib().mimgpu_session_ipc_handle(self.h, buf, 64))
+        return buf.raw
+
+    def set_peers(self, handles: list):
+        """Maps every rank's arena (handles in rank order, this rank's included)
+        so that decode steps exchange over peer memory."""
+        blob = b"".join(handles)
+        self.m.ctx._check(lib().mimgpu_session_set_peers(self.h, blob, 64, len(handles)))
 
     def generate(self, token: int, pos: int, steps: int) -> np.ndarray:
         ids = np.empty(steps, np.int32)

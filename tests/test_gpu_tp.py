@@ -16,16 +16,29 @@ def _gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
+@pytest.fixture(scope="module")
+def one_gpu():
+    import tp_worker
+    return tp_worker.decode(0, None, 1, 0)
+
+
 @pytest.mark.skipif("_gpus() < 2")
-def test_tp2_bit_identical_to_one_gpu():
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "peer-memory"])
+def test_tp2_bit_identical_to_one_gpu(one_gpu, p2p):
+    """Prompt (16 tokens: NCCL all-gathers) and 32 greedy steps (NCCL, or
+    peer-memory exchanges inside the kernels) on 2 ranks."""
+    import socket
     import tp_worker
     import mimgpu
-    want_logits, want_ids = tp_worker.decode(0, None, 1, 0)
+    want_logits, want_ids = one_gpu
     gid = mimgpu.tp_unique_id()
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=tp_worker.rank_main, args=(r, 2, gid, q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_worker.rank_main, args=(r, 2, gid, port, p2p, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}

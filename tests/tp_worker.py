@@ -15,7 +15,7 @@ def model_cfg():
                 rope_theta=500000.0, norm_eps=1e-5)
 
 
-def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: int = 32):
+def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: int = 32, exchange=None):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "mimir-model_b200"))
     import bench
@@ -28,6 +28,8 @@ def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: i
         tp = mimgpu.TensorParallel(ctx, group_id, nranks, rank)
         model.set_tp(tp)
     s = model.session()
+    if exchange is not None:  # map every rank's arena: decode steps exchange over peer memory
+        s.set_peers(exchange(s.ipc_handle()))
     prompt = np.random.default_rng(3).integers(0, cfg["vocab"], 16).astype(np.int32)
     logits = s.run(prompt, np.arange(16), all_rows=True)
     ids = s.generate(int(np.argmax(logits[-1])), 16, steps)
@@ -39,8 +41,19 @@ def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: i
     return logits, ids
 
 
-def rank_main(rank: int, nranks: int, group_id: bytes, q):
+def rank_main(rank: int, nranks: int, group_id: bytes, port: int, p2p: bool, q):
+    import torch.distributed as dist
+    from datetime import timedelta
     try:
-        q.put((rank, decode(rank, group_id, nranks, rank)))
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=nranks,
+                                timeout=timedelta(seconds=120))
+
+        def exchange(handle):
+            out = [None] * nranks
+            dist.all_gather_object(out, handle)
+            return out
+
+        q.put((rank, decode(rank, group_id, nranks, rank, exchange=exchange if p2p else None)))
+        dist.destroy_process_group()
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
