@@ -404,7 +404,8 @@ def run_gemv(args):
     print(json.dumps({"metric": "quant-GEMV HBM GB/s", "value": round(algo / med / 1e9, 1), "unit": "GB/s",
                       "shape": [N, K], "dtype": parts[2], "rows": rows, "us_median": round(med * 1e6, 3),
                       "us_min": round(ts[0] * 1e6, 3), "frac": round(algo / med / 1e9 / peak, 4),
-                      "algorithmic_bytes": algo, "copies": copies, "launches": n, "peak_kind": kind}), flush=True)
+                      "algorithmic_bytes": algo, "copies": copies, "launches": n, "peak_kind": kind,
+                      "int8_tops": round(2 * N * K * rows / med / 1e12, 2)}), flush=True)
     lib.mimgpu_q8_free(q8)
     ctx.close()
 

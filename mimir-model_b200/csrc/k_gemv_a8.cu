@@ -29,6 +29,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "a8_refused.cuh"
 #include "p2p.cuh"
 
 namespace mimgpu {
@@ -120,45 +121,6 @@ __device__ __forceinline__ int group_of(int b, int gi, int slots, int t) { retur
 struct ActSmem {
     uint32_t q, dx, xs, ys;  // shared addresses of each array (row-major by activation row)
 };
-
-// Exact f32 product of one weight row (decoded as quant.go does) with x, for
-// rows the 8-bit path refuses.  Warp-collective; its own summation order
-// (the reference's f32 kernels are tolerance-bound).
-__device__ float row_dot_f32(int dt, const uint8_t *row, const float *x, int nb) {
-    const int lane = threadIdx.x & 31;
-    float acc = 0.f;
-    for (int b = 0; b < nb; b++) {
-        const float *xb = x + (long long)b * 256;
-        if (dt == Q4_K) {
-            const uint8_t *blk = row + (long long)b * 144;
-            const float d = f16_to_f32(blk[0] | (blk[1] << 8)), dmin = f16_to_f32(blk[2] | (blk[3] << 8));
-            uint32_t sw[3];
-            for (int i = 0; i < 3; i++)
-                sw[i] = blk[4 + 4 * i] | (blk[5 + 4 * i] << 8) | (blk[6 + 4 * i] << 16) | ((uint32_t)blk[7 + 4 * i] << 24);
-            for (int e = lane; e < 256; e += 32) {
-                const int c = e >> 6, hi = (e >> 5) & 1, l = e & 31;
-                int sc, m;
-                q4k_scale_min(sw, 2 * c + hi, sc, m);
-                const int qv = hi ? (blk[16 + 32 * c + l] >> 4) : (blk[16 + 32 * c + l] & 15);
-                const float w = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)qv), __fmul_rn(dmin, (float)m));
-                acc = __fmaf_rn(xb[e], w, acc);
-            }
-        } else {
-            const uint8_t *blk = row + (long long)b * 210;
-            const float d = f16_to_f32(blk[208] | (blk[209] << 8));
-            for (int e = lane; e < 256; e += 32) {
-                const int h = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
-                const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
-                const int lowb = (quarter & 1) ? ql[l + 32] : ql[l];
-                const int low = (quarter >> 1) ? (lowb >> 4) : (lowb & 15);
-                const int qv = (low | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
-                const int sc = (int8_t)blk[192 + 8 * h + (l >> 4) + 2 * quarter];
-                acc = __fmaf_rn(xb[e], __fmul_rn(__fmul_rn(d, (float)sc), (float)qv), acc);
-            }
-        }
-    }
-    return warp_sum(acc);
-}
 
 __device__ __forceinline__ float f16f(uint32_t h) {  // f16 -> f32 by the hardware conversion (exact)
     float f;
@@ -731,6 +693,7 @@ cudaError_t gemv_a8_prepare() {
     if (e == cudaSuccess) e = prepare_nr<2>();
     if (e == cudaSuccess) e = prepare_nr<4>();
     if (e == cudaSuccess) e = prepare_nr<8>();
+    if (e == cudaSuccess) e = gemm_a8_tc_prepare();
     num_sms();
     return e;
 }
@@ -740,6 +703,9 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
     if (put && put->N > 1 && (rows != 1 || nseg != 1)) return cudaErrorInvalidValue;  // exchanges carry one row
     if (rows == 0 || K == 0) return cudaSuccess;
+    // many activation rows: the tensor-core GEMM (same results bit for bit)
+    if ((!put || put->N <= 1) && gemm_a8_tc_ok(segs, nseg, act, rows, K))
+        return launch_gemm_a8_tc(segs, nseg, x, act, rows, K, status, st, pdl);
     A8Params p = {};
     p.nseg = nseg;
     int maxbb = 0, g = 0;

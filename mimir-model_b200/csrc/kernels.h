@@ -74,6 +74,13 @@ cudaError_t gemv_a8_prepare();
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
                            unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true,
                            const P2P *put = nullptr);
+// The same product on the tensor cores (tcgen05 kind::i8) for launches of
+// at least kTcMinRows activation rows; launch_gemv_a8 dispatches to it.
+constexpr int kTcMinRows = 16;
+bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, long long K);
+cudaError_t gemm_a8_tc_prepare();
+cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
+                              unsigned *status, cudaStream_t st, bool pdl);
 // dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
 cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
                             cudaStream_t st, bool pdl);
