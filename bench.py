@@ -410,6 +410,123 @@ def run_gemv(args):
     ctx.close()
 
 
+# ------------------------------------------------- prefill mode (config 4)
+
+def tensor_peak():
+    """Dense int8 tensor peak in TOP/s: twice the measured bf16 cuBLAS burst
+    (NVIDIA's dense int8 : bf16 ratio), or twice the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return 2.0 * float(json.load(f)["bf16_tflops"]), "2 x measured bf16 burst"
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1590.0, "2 x fallback bf16"
+
+
+def gemm_shape_time(ctx, lib, torch, st, N, K, dt, rows, reps):
+    """Event time of one dequant_matmul_a8.v2 launch of [rows, K] x [N, K]^T
+    (the tensor-core GEMM from 16 rows), rotating over weight copies larger
+    than L2 together."""
+    wb = nbytes(dt, (N, K))
+    copies = max(2, min(16, int(2 * 126e6 // wb) + 1))
+    ws = [ctx.synth(dt, (N, K), 4000 + i) for i in range(copies)]
+    x = torch.randn(rows, K, device="cuda", dtype=torch.float32)
+    y = torch.empty(rows, N, device="cuda", dtype=torch.float32)
+    q8 = C.c_void_p()
+    ctx._check(lib.mimgpu_q8_new(ctx.h, rows, K, C.byref(q8)))
+    ctx._check(lib.mimgpu_q8_quantize_dev(ctx.h, st.cuda_stream, x.data_ptr(), q8))
+    ts = []
+    with torch.cuda.stream(st):
+        for i in range(reps + 3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            ctx._check(lib.mimgpu_gemv_q8_dev(ctx.h, st.cuda_stream, q8, x.data_ptr(), ws[i % copies].h, None,
+                                              y.data_ptr()))
+            b.record(st)
+            b.synchronize()
+            if i >= 3:
+                ts.append(a.elapsed_time(b) / 1e3)
+    lib.mimgpu_q8_free(q8)
+    for w in ws:
+        w.free()
+    return statistics.median(ts)
+
+
+def run_prefill(args):
+    """Config 4: the 8B-shape prompt pass at T tokens (one sequence), timed on
+    the device around mimgpu_session_run, and the tensor-core GEMM alone on
+    the decoder's matrix shapes at M = T."""
+    import torch
+    import mimgpu
+    lib = mimgpu.lib()
+    torch.cuda.set_device(0)
+    cfg = dict(CFG8B, layers=args.layers)
+    Ts = [int(t) for t in args.prefill.split(",")]
+    ctx = mimgpu.Context(0)
+    model, weights = build_model(ctx, cfg, max(Ts) + 8, max(Ts))
+    sess = model.session()
+    stream = torch.cuda.ExternalStream(sess.stream)
+    E, F, KV = cfg["embed"], cfg["ffn"], cfg["kv_heads"] * cfg["head_dim"]
+    params = sum(int(np.prod(shape)) for name, dt, shape, _, _ in layout(cfg)
+                 if dt != F32 and name != "token_embd.weight")
+    peak, peak_kind = tensor_peak()
+    st = torch.cuda.Stream()
+    for T in Ts:
+        ids = prompt_ids(cfg["vocab"], T, seed=20261202)
+        pos = np.arange(T)
+        for _ in range(args.warmup):
+            sess.run(ids, pos)
+        torch.cuda.synchronize()
+        dev, wall = [], []
+        clocks = Clocks(0)
+        with clocks:
+            for _ in range(args.steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0 = time.perf_counter()
+                a.record(stream)
+                sess.run(ids, pos)
+                b.record(stream)
+                b.synchronize()
+                wall.append(time.perf_counter() - t0)
+                dev.append(a.elapsed_time(b) / 1e3)
+        d, w = statistics.median(dev), statistics.median(wall)
+        # the GEMM alone on the shapes of one layer (Q, K, V, O, gate, up, down) at M = T
+        shapes = [(E, E, Q4_K), (KV, E, Q4_K), (KV, E, Q6_K), (E, E, Q4_K), (F, E, Q4_K), (F, E, Q4_K), (E, F, Q6_K)]
+        g_t, g_ops = 0.0, 0.0
+        per = {}
+        for N, K, dt in shapes:
+            t = gemm_shape_time(ctx, lib, torch, st, N, K, dt, T, 5)
+            g_t += t
+            g_ops += 2.0 * N * K * T
+            per[f"{N}x{K} {'q4_k' if dt == Q4_K else 'q6_k'}"] = round(2.0 * N * K * T / t / 1e12, 1)
+        useful = g_ops / g_t / 1e12
+        executed = 3 * useful  # three int8 digit planes per weight
+        print(json.dumps({
+            "metric": "8B-shape Q4_K_M prefill tok/s (BASELINE config 4)", "value": round(T / d, 1),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(d * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded "
+                                     "random prompt ids)",
+            "config": {"workload": f"8B-shape prompt pass, {T} tokens, logits of the last position",
+                       "layers": cfg["layers"], "prompt": T,
+                       "l2": "inputs larger than L2: 4.88 GB of weights per pass vs 126 MB L2"},
+            "e2e": {"value": round(T / w, 1), "unit": "tok/s", "h2d_bytes_per_step": 12 * T,
+                    "d2h_bytes_per_step": 4 * cfg["vocab"], "api": "mimgpu_session_run (host ids/positions in, "
+                                                                  "host logits out)"},
+            "gemm": {"useful_int8_tops_per_shape": per, "layer_gemm_ms": round(g_t * 1e3, 3),
+                     "layer_gemm_share_of_pass": round(g_t * cfg["layers"] / d, 3)},
+            "roofline": {"kernel": "gemm_a8_tc_kernel (one layer's seven matrices at M = T)", "bound": "tensor",
+                         "achieved": round(executed, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                         "frac": round(executed / peak, 4), "useful_tops": round(useful, 1),
+                         "traffic": None, "peak_kind": peak_kind,
+                         "note": "achieved counts the MMAs executed: three int8 planes per weight element"},
+            "model_flops_tops": round(2.0 * params * T / d / 1e12, 1),
+            "clocks": clocks.summary(),
+        }), flush=True)
+    sess.free()
+    model.free()
+    ctx.close()
+
+
 # ----------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -471,11 +588,14 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before the timed decode steps")
     ap.add_argument("--gemv", default="", help="GEMV-only mode: N,K,q4_k|q6_k[,rows]")
     ap.add_argument("--gemv-hot", action="store_true", help="GEMV-only mode with one weight copy (L2-hot)")
+    ap.add_argument("--prefill", default="", help="prefill mode (config 4): prompt lengths, e.g. 512,2048")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.gemv:
         run_gemv(args)
+    elif args.prefill:
+        run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

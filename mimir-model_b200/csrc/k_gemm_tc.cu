@@ -3,25 +3,38 @@
 //
 // Same results as the GEMV (k_gemv_a8.cu) and the reference's dotQ8KRef
 // (internal/kernels/q8k_test.go:35-117 of gsoultan/mimir-model), bit for
-// bit: the exact int32 block sums S (and M for Q4_K), then the block-ordered
-// f32 chain tot = fma(float(S), d*dx, tot), off = fma(float(M), dmin*dx, off).
+// bit, as the reference's own prompt tile kernels are (amx.go:24-51,
+// vnni.go:22-32): the exact int32 block sums S (and M for Q4_K), then the
+// block-ordered f32 chain tot = fma(float(S), d*dx, tot),
+// off = fma(float(M), dmin*dx, off), result tot - off.
 //
-// A CTA owns 128 weight rows x 32 activation rows.  For every 256-element
-// block it decodes the rows' quants into shared memory as int8 "digit
-// planes" whose products with the int8 activations fit the MMA operands
-// exactly, and sums each plane over the block with tcgen05.mma kind::i8
-// (M 128, N 32, K 32) into TMEM:
-//   Q4_K  sc = lo + 8 hi (3-bit digits):  planes q*lo and q*hi in [0, 105],
-//         S = A0 + 8 A1 (sub-block scales folded in, per row and sub-block);
+// A CTA owns 128 weight rows (TMEM lanes) x 64 activation rows.  For every
+// 256-element block the rows' quants become int8 "digit planes" whose
+// products with the int8 activations are exact MMA operands, and
+// tcgen05.mma kind::i8 (M 128, N 64, K 32) sums each plane over the block
+// into TMEM:
+//   Q4_K  sc = lo + 8 hi (3-bit digits): planes q*lo, q*hi in [0, 105] and
+//         the sub-block mins m in [0, 63]:  S = P0 + 8 P1,  M = P2;
 //   Q6_K  sc = d0 + 8 d1 + 64 d2 (digits in [-3, 4]): planes (q-32)*d in
-//         [-128, 124], S = A0 + 8 A1 + 64 A2.
-// The 4 warps read the accumulators back (tcgen05.ld, one row per thread)
-// and continue each (row, activation row) chain in registers.  The mins of
-// Q4_K, M = sum m_j xs_j, are 8 products on the CUDA cores.
-//
-// Operands use the K-major canonical layout without swizzle: core matrices
-// of 8 rows x 16 bytes (128 contiguous bytes), 8-row groups SBO = 128 bytes
-// apart, 16-byte K chunks LBO = rows * 16 bytes apart.
+//         [-128, 124]:  S = P0 + 8 P1 + 64 P2.
+// Data flow per block: one control thread (warp 0) fetches the tile's raw
+// weight blocks and the activation tile of the block by TMA into a 4-slot
+// input ring (refilled a quarter block after a slot's MMAs are done);
+// warps 1-4 (one weight row per thread, the thread's TMEM lane) unpack
+// their rows a quarter block at a time into the planes, written straight
+// into TMEM with tcgen05.st (two stages of 3 x 16 columns), so the MMA reads
+// A from TMEM and only the activation tile from shared memory; once every
+// decoder has filled a stage, the control thread issues its 6 MMAs into one
+// of two TMEM accumulator sets and commits them to the barriers that free
+// the stage, the input slot and hand the set on; warps 5-12 (one row and 32
+// activation rows per thread) read the sums back with tcgen05.ld, convert
+// them exactly and continue the block-ordered chain in registers, and
+// write the outputs at the end (bias, residual, refused pairs).
+// Every wait is bounded (2 s, or sooner once another role has given up):
+// the kernel then sets DEV_TIMEOUT, drains the MMAs it issued, frees TMEM
+// and returns.
+#include <cuda.h>  // CUtensorMap (types only)
+
 #include <cstdint>
 
 #include "a8_refused.cuh"
@@ -30,41 +43,73 @@
 
 namespace mimgpu {
 
+void *tmap_encode_fn();  // cuTensorMapEncodeTiled from the driver (k_gemv_a8.cu)
+
 namespace {
 
-constexpr int TM = 128;              // weight rows per CTA (MMA M, one TMEM lane each)
-constexpr int TN = 32;               // activation rows per CTA (MMA N)
-constexpr int kThr = 128;            // 4 warps
+constexpr int TM = 128;                          // weight rows per CTA = MMA M = TMEM lanes
+constexpr int NT = 64;                           // activation rows per CTA = MMA N
 constexpr int kPlanes = 3;
-constexpr uint32_t kTmemCols = 128;  // 3 planes x 32 columns, rounded to a power of two
-constexpr int kRawPitch = 240;       // bytes of one staged raw block row (210 + 16-byte phase, rounded)
-constexpr int kPlaneBytes = TM * 256;
-constexpr int kBBytes = TN * 256;
+constexpr int kQuarter = 64;                     // K elements per plane stage
+constexpr int kStages = 2;                       // plane stages in TMEM
+constexpr int kNin = 4;                          // input ring slots
+constexpr int kRawPitch = 240;                   // Q6_K box width: a 210-byte block from its 16-byte boundary
+constexpr int kBBlock = NT * 256;                // activation tile of one block: two 128-byte-swizzled boxes
+constexpr int kInQ4 = TM * 144 + kBBlock;        // input slot: raw rows, then the activation tile
+constexpr int kInQ6 = TM * kRawPitch + kBBlock;
+constexpr int kMeta = 4;                         // per-block scale ring between decoders and epilogue
+constexpr int kDec = 128, kEpi = 256;
+constexpr int kThreads = 32 + kDec + kEpi;
+constexpr int kEpiTok = NT / 2;                  // activation rows per epilogue thread
+constexpr uint32_t kAccCols = kPlanes * NT;      // one accumulator set
+constexpr uint32_t kACol0 = 2 * kAccCols;        // plane stages after the two accumulator sets
+constexpr uint32_t kAStageCols = kPlanes * kQuarter / 4;  // 4 int8 per 32-bit column
+constexpr uint32_t kTmemCols = 512;
+static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "TMEM columns");
+
+struct Meta {
+    float d[TM], dmin[TM];
+    float dx[NT];
+    int ok[NT];
+};
+
+struct Bars {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t accfull[2], accempty[2];
+    uint64_t infull[kNin], inempty[kNin];
+    uint64_t metafull[kMeta], metaempty[kMeta];
+    uint64_t drain;
+    uint32_t tmem;
+    int abort;
+};
+
+constexpr int kOffMeta = 256;
+constexpr int kOffIn = 7168;
+constexpr int kSmemTc = kOffIn + kNin * kInQ6;
+static_assert(sizeof(Bars) <= kOffMeta, "barrier block");
+static_assert(kOffMeta + kMeta * (int)sizeof(Meta) <= kOffIn, "meta ring");
+static_assert(kOffIn % 1024 == 0 && kInQ4 % 1024 == 0 && kInQ6 % 1024 == 0, "alignment");
+static_assert(kSmemTc <= 227 * 1024, "shared memory");
 
 struct TcParams {
+    CUtensorMap tmap[kMaxSegs];  // raw weights [n, row bytes] u8, box [box width, 128]
+    CUtensorMap amap;            // activation quants [rows, K] u8, box [128, 64], 128-byte swizzle
     GemvSeg seg[kMaxSegs];
-    int seg_t0[kMaxSegs + 1];  // first 128-row tile of each segment
+    int seg_t0[kMaxSegs + 1];    // first 128-row tile of each segment
     int nseg;
-    ActQ8 act;                 // rows x K
-    const float *x;            // f32 activations (refused rows)
+    ActQ8 act;
+    const float *x;              // f32 activations (refused pairs)
     int rows;
     long long K;
     int nb;
     unsigned *status;
 };
 
-// shared-memory layout (bytes)
-constexpr int kOffBar = 0;       // mbarrier of the MMA commits
-constexpr int kOffTmem = 16;     // TMEM base address written by tcgen05.alloc
-constexpr int kOffMeta = 128;    // per block: dx [TN] f32, ok [TN] i32, xs [TN][8] i16
-constexpr int kOffRaw = 1024;
-constexpr int kOffPlanes = kOffRaw + TM * kRawPitch;
-constexpr int kOffB = kOffPlanes + kPlanes * kPlaneBytes;
-constexpr int kSmemTc = kOffB + kBBytes;
-
-// byte offset of (row, k) in a K-major no-swizzle operand of `R` rows x 256
-__device__ __forceinline__ uint32_t canon(int row, int k, int R) {
-    return (uint32_t)(((k >> 4) * (R >> 3) + (row >> 3)) * 128 + (row & 7) * 16 + (k & 15));
+// byte offset of (row, 16-byte K chunk c) in a K-major no-swizzle operand of
+// R rows: core matrices of 8 rows x 16 bytes, 8-row groups 128 bytes apart
+// (SBO), K chunks R*16 bytes apart (LBO)
+__device__ __forceinline__ uint32_t canon(int row, int c, int R) {
+    return (uint32_t)((c * (R >> 3) + (row >> 3)) * 128 + (row & 7) * 16);
 }
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -72,287 +117,533 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);  // version 1, no swizzle
 }
 
-// kind::i8 instruction descriptor: D s32, A and B signed int8, both K-major,
-// N = 32, M = 128
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+// K-major operand in the 128-byte swizzle layout (what a TMA box of 128-byte
+// rows with CU_TENSOR_MAP_SWIZZLE_128B writes): 8-row atoms of 1024 bytes
+// (SBO), 1024-byte aligned; K steps inside an atom advance the start address
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+// kind::i8 instruction descriptor: D s32, A and B signed 8-bit, K-major, N = NT, M = TM
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+
+// D (TMEM) += A (TMEM: lane = row, 4 int8 of K per column) x B (shared memory)
+__device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
 }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-
-// Digits of a Q6_K scale in base 8, each in [-3, 4]: sc = d0 + 8 d1 + 64 d2.
-__device__ __forceinline__ void q6_digits(int sc, int &d0, int &d1, int &d2) {
-    d0 = ((sc + 3) & 7) - 3;
-    int t = (sc - d0) >> 3;
-    d1 = ((t + 3) & 7) - 3;
-    d2 = (t - d1) >> 3;
+__device__ __forceinline__ uint4 ld16(const uint8_t *p) { return *(const uint4 *)p; }
+__device__ __forceinline__ void st16(uint8_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    *(uint4 *)p = make_uint4(a, b, c, d);
 }
 
-__global__ void __launch_bounds__(kThr, 1) gemm_a8_tc_kernel(const __grid_constant__ TcParams p) {
-    extern __shared__ __align__(1024) uint8_t sm[];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint64_t *bar = (uint64_t *)(sm + kOffBar);
-    uint32_t *tmem_slot = (uint32_t *)(sm + kOffTmem);
-    float *mdx = (float *)(sm + kOffMeta);
-    int *mok = (int *)(sm + kOffMeta + 4 * TN);
-    int16_t *mxs = (int16_t *)(sm + kOffMeta + 8 * TN);
-    uint8_t *raw = sm + kOffRaw;
-    uint8_t *planes = sm + kOffPlanes;
-    uint8_t *bt = sm + kOffB;
+// Bounded wait that also gives up once another role has: false means the
+// kernel is aborting (DEV_TIMEOUT is set by whoever timed out first).
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars &B, unsigned *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0) {
+            if (*(volatile int *)&B.abort) return false;
+            if (global_ns() - t0 > 2000000000ull) {
+                *(volatile int *)&B.abort = 1;
+                atomicOr(status, (unsigned)DEV_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
 
-    // the tile: segment, its 128 rows, the 32 activation rows
-    const int tile = blockIdx.x;
+// exact int -> f32 for |v| < 2^22
+__device__ __forceinline__ float small_i2f(uint32_t v) {
+    return __fsub_rn(__int_as_float((int)(v + 0x4B400000u)), 12582912.0f);
+}
+
+// Digits of a Q6_K scale in base 8, each in [-3, 4]: sc = d0 + 8 d1 + 64 d2.
+__device__ __forceinline__ void q6_digits(int sc, int (&dg)[3]) {
+    dg[0] = ((sc + 3) & 7) - 3;
+    const int t = (sc - dg[0]) >> 3;
+    dg[1] = ((t + 3) & 7) - 3;
+    dg[2] = (t - dg[1]) >> 3;
+}
+
+// ------------------------------------------------------------ decode: Q4_K
+// The thread's row, quarter qi (elements 64qi..64qi+63: qs bytes
+// [32qi, 32qi+32), low nibbles then high nibbles) of the block at `blk`
+// (144 bytes, 16-byte aligned in shared memory), as the three planes' 16
+// columns at TMEM address `ta` (this warp's lanes).
+__device__ __forceinline__ void decode_q4k_quarter(const uint8_t *blk, int qi, uint32_t ta) {
+    const uint4 hdr = ld16(blk);
+    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
+    const uint4 g0 = ld16(blk + 16 + 32 * qi), g1 = ld16(blk + 32 + 32 * qi);
+    const uint32_t qw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    uint32_t a0[16], a1[16], mp[16];
+#pragma unroll
+    for (int up = 0; up < 2; up++) {  // sub-block 2qi + up
+        int sc, m;
+        q4k_scale_min(sw, 2 * qi + up, sc, m);
+        const uint32_t lo = (uint32_t)(sc & 7), hi = (uint32_t)(sc >> 3), mw = (uint32_t)m * 0x01010101u;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const uint32_t nib = up ? ((qw[k] >> 4) & 0x0F0F0F0Fu) : (qw[k] & 0x0F0F0F0Fu);
+            a0[8 * up + k] = nib * lo;  // bytes q*lo <= 105: no carries
+            a1[8 * up + k] = nib * hi;
+            mp[8 * up + k] = mw;
+        }
+    }
+    tmem_st16(ta, a0);
+    tmem_st16(ta + kQuarter / 4, a1);
+    tmem_st16(ta + 2 * kQuarter / 4, mp);
+}
+
+// ------------------------------------------------------------ decode: Q6_K
+// The block starts at byte 4*WO + sh/8 of the 16-byte aligned window `win`
+// (sh is 0 or 16: blocks are 2-byte aligned).  Quarter qi is half h = qi/2,
+// quarters qq = 2(qi&1), 2(qi&1)+1 of it: scales 8h + 4(qi&1) .. +4.
+template <int WO>
+__device__ __forceinline__ void decode_q6k_quarter(const uint8_t *win, int sh, int qi, uint32_t ta) {
+    const int h = qi >> 1, odd = qi & 1;
+    // ql bytes [64h, 64h+64): window chunks 4h..4h+4
+    uint32_t u[20];
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        const uint4 v = ld16(win + 64 * h + 16 * i);
+        u[4 * i] = v.x; u[4 * i + 1] = v.y; u[4 * i + 2] = v.z; u[4 * i + 3] = v.w;
+    }
+    uint32_t ql[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) ql[i] = __funnelshift_r(u[WO + i], u[WO + i + 1], sh);
+    // qh bytes [128 + 32h, +32): window chunks 8+2h..10+2h
+    uint32_t v3[12];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const uint4 v = ld16(win + 128 + 32 * h + 16 * i);
+        v3[4 * i] = v.x; v3[4 * i + 1] = v.y; v3[4 * i + 2] = v.z; v3[4 * i + 3] = v.w;
+    }
+    uint32_t qh[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) qh[i] = __funnelshift_r(v3[WO + i], v3[WO + i + 1], sh);
+    // the quarter's 4 scales: bytes [192 + 8h + 4 odd, +4): window chunks 12, 13
+    const uint4 s0 = ld16(win + 192), s1 = ld16(win + 208);
+    const uint32_t t[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const int wi = 2 * h + odd;  // word of the scales relative to the block's scale region
+    const uint32_t scw = __funnelshift_r(wi == 0 ? t[WO] : wi == 1 ? t[WO + 1] : wi == 2 ? t[WO + 2] : t[WO + 3],
+                                         wi == 0 ? t[WO + 1] : wi == 1 ? t[WO + 2] : wi == 2 ? t[WO + 3] : t[WO + 4], sh);
+    uint32_t w[3][16];
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+        // elements 64qi + 16cc ..: quarter qq = 2 odd + cc/2, l in [16(cc&1), +16), scale byte cc
+        const int qq = 2 * odd + (cc >> 1), g = 2 * (qq & 1) + (cc & 1);
+        const int sc = (int)(int8_t)((scw >> (8 * cc)) & 0xFF);
+        int dg[3];
+        q6_digits(sc, dg);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t q = ((ql[4 * g + k] >> (4 * (qq >> 1))) & 0x0F0F0F0Fu) |
+                               (((qh[4 * (cc & 1) + k] >> (2 * qq)) & 0x03030303u) << 4);
+            const uint32_t xa = __byte_perm(q, 0, 0x4140), xb = __byte_perm(q, 0, 0x4342);  // 16-bit lanes
+#pragma unroll
+            for (int p = 0; p < 3; p++) {
+                // lanes (q-32)*d + 256 in [128, 380]: their low bytes are the int8 products
+                const uint32_t c = (uint32_t)(256 - 32 * dg[p]) * 0x00010001u;
+                const uint32_t ra = xa * (uint32_t)dg[p] + c, rb = xb * (uint32_t)dg[p] + c;
+                w[p][4 * cc + k] = __byte_perm(ra, rb, 0x6420);
+            }
+        }
+    }
+    tmem_st16(ta, w[0]);
+    tmem_st16(ta + kQuarter / 4, w[1]);
+    tmem_st16(ta + 2 * kQuarter / 4, w[2]);
+}
+
+// One block of the chain for the thread's row and its 32 activation rows:
+// the block sums from TMEM (accumulator columns from `col`, this warp's
+// lanes), converted exactly and folded in block order.
+template <bool Q4>
+__device__ __forceinline__ void epi_block(uint32_t col, const float *dxs, float d, float dmin,
+                                          float (&tot)[kEpiTok], float (&off)[kEpiTok]) {
+#pragma unroll
+    for (int c = 0; c < kEpiTok / 16; c++) {
+        float dx[16];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; j4++) {
+            const float4 v = *(const float4 *)(dxs + 16 * c + 4 * j4);
+            dx[4 * j4] = v.x; dx[4 * j4 + 1] = v.y; dx[4 * j4 + 2] = v.z; dx[4 * j4 + 3] = v.w;
+        }
+        uint32_t a0[16], a1[16];
+        tmem_ld16(col + 16 * c, a0);
+        tmem_ld16(col + NT + 16 * c, a1);
+        tmem_wait_ld();
+        if (Q4) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float fs = __fmaf_rn(small_i2f(a1[j]), 8.0f, small_i2f(a0[j]));  // = float(P0 + 8 P1)
+                tot[16 * c + j] = __fmaf_rn(fs, __fmul_rn(d, dx[j]), tot[16 * c + j]);
+            }
+            tmem_ld16(col + 2 * NT + 16 * c, a0);  // the mins plane
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                off[16 * c + j] = __fmaf_rn(small_i2f(a0[j]), __fmul_rn(dmin, dx[j]), off[16 * c + j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) a0[j] += 8u * a1[j];
+            tmem_ld16(col + 2 * NT + 16 * c, a1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int S = (int)(a0[j] + 64u * a1[j]);
+                tot[16 * c + j] = __fmaf_rn(__int2float_rn(S), __fmul_rn(d, dx[j]), tot[16 * c + j]);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_2d(const CUtensorMap *map, uint8_t *dst, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((const void *)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    Bars &B = *(Bars *)sm;
+    Meta *meta = (Meta *)(sm + kOffMeta);
+    uint8_t *inring = sm + kOffIn;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // the tile: segment, its 128 rows, the 64 activation rows
+    const int tile = blockIdx.y;
     int si = 0;
     while (si + 1 < p.nseg && tile >= p.seg_t0[si + 1]) si++;
     GemvSeg sg = p.seg[0];
+    const CUtensorMap *map = &p.tmap[0];
 #pragma unroll
     for (int i = 1; i < kMaxSegs; i++)
-        if (i == si) sg = p.seg[i];
+        if (i == si) {
+            sg = p.seg[i];
+            map = &p.tmap[i];
+        }
     const int r0 = (tile - p.seg_t0[si]) * TM, nrow = min(TM, sg.n - r0);
-    const int n0 = blockIdx.y * TN, ntok = min(TN, p.rows - n0);
-    const int dt = sg.dt, bb = block_bytes(dt);
-    const long long rb = row_bytes(dt, p.K);
-    const int P = dt == Q4_K ? 2 : 3;
+    const int n0 = blockIdx.x * NT, ntok = min(NT, p.rows - n0);
+    const int dt = sg.dt, bb = block_bytes(dt), nb = p.nb;
+    const bool q4 = dt == Q4_K;
+    const int pitch = q4 ? 144 : kRawPitch;      // raw box width = row pitch in the slot
+    const int nin = kNin;
+    const int inbytes = q4 ? kInQ4 : kInQ6;
+    const uint32_t rawbox = (uint32_t)(pitch * TM);
 
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+    if (tid == 0) {
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(&B.full[i], kDec);
+            mbar_init(&B.empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&B.accfull[i], 1);
+            mbar_init(&B.accempty[i], kEpi);
+        }
+        for (int i = 0; i < kNin; i++) {
+            mbar_init(&B.infull[i], 1);
+            mbar_init(&B.inempty[i], kDec + 1);  // the decoders and the block's last MMA commit
+        }
+        for (int i = 0; i < kMeta; i++) {
+            mbar_init(&B.metafull[i], kDec);
+            mbar_init(&B.metaempty[i], kEpi);
+        }
+        mbar_init(&B.drain, 1);
+        B.abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        fence_barrier_init();
-    }
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = B.tmem;
     pdl_launch_dependents();
-    pdl_wait();
 
-    const int row = tid;                       // this thread's weight row in the tile
-    const bool has_row = row < nrow;
-    float tot[TN], off[TN];
-#pragma unroll
-    for (int n = 0; n < TN; n++) tot[n] = off[n] = 0.f;
-    bool rowbad = false;
-    uint32_t tokbad = 0;                       // activation rows refused (bit n)
-    bool failed = false;
-    uint32_t phase = 0;
-    const uint32_t planes_s = smem_u32(planes), bt_s = smem_u32(bt);
-
-    for (int kb = 0; kb < p.nb; kb++) {
-        // ---- raw weight block of every row (16-byte aligned window) -> shared
-        {
-            const uintptr_t a = has_row ? (uintptr_t)(sg.w + (long long)(r0 + row) * rb + (long long)kb * bb) : 0;
-            const uintptr_t lo = a & ~(uintptr_t)15;
-            const int nchunk = has_row ? (int)(((a + bb + 15) & ~(uintptr_t)15) - lo) / 16 : 0;
-            uint4 *dst = (uint4 *)(raw + row * kRawPitch);
-            for (int c = 0; c < nchunk; c++) dst[c] = __ldg((const uint4 *)lo + c);
-        }
-        // ---- activation block of the 32 rows -> B operand; dx, ok, xs
-        for (int id = tid; id < TN * 16; id += kThr) {
-            const int n = id >> 4, c = id & 15;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (n < ntok) v = __ldg((const uint4 *)(p.act.q + (long long)(n0 + n) * p.K + (long long)kb * 256 + c * 16));
-            *(uint4 *)(bt + canon(n, c * 16, TN)) = v;
-        }
-        if (tid < TN) {
-            const bool in = tid < ntok;
-            mdx[tid] = in ? p.act.dx[(long long)(n0 + tid) * p.nb + kb] : 0.f;
-            mok[tid] = in ? p.act.ok[(long long)(n0 + tid) * p.nb + kb] : 1;
-        }
-        for (int id = tid; id < TN * 8; id += kThr) {
-            const int n = id >> 3, j = id & 7;
-            mxs[id] = n < ntok ? p.act.xs[(long long)(n0 + n) * (p.K / 32) + (long long)kb * 8 + j] : (int16_t)0;
-        }
-        __syncwarp();  // each thread reads back only its own raw row
-        // ---- this row's quants as digit planes in the canonical layout
-        const uint8_t *blk = raw + row * kRawPitch +
-                             (has_row ? (int)(((uintptr_t)sg.w + (uintptr_t)((r0 + row) * rb) + (uintptr_t)kb * bb) & 15) : 0);
-        float d = 0.f, dmin = 0.f;
-        int sc8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, mn8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (dt == Q4_K) {
-            const uint32_t dm = has_row ? (uint32_t)blk[0] | ((uint32_t)blk[1] << 8) | ((uint32_t)blk[2] << 16) |
-                                              ((uint32_t)blk[3] << 24)
-                                        : 0u;
-            rowbad |= has_row && (!f16_finite(dm & 0xFFFFu) || !f16_finite(dm >> 16));
-            d = f16_to_f32(dm & 0xFFFFu);
-            dmin = f16_to_f32(dm >> 16);
-            uint32_t sw[3] = {0, 0, 0};
-            if (has_row)
-                for (int i = 0; i < 3; i++)
-                    sw[i] = blk[4 + 4 * i] | (blk[5 + 4 * i] << 8) | (blk[6 + 4 * i] << 16) | ((uint32_t)blk[7 + 4 * i] << 24);
-#pragma unroll
-            for (int j = 0; j < 8; j++) q4k_scale_min(sw, j, sc8[j], mn8[j]);
-#pragma unroll 4
-            for (int ch = 0; ch < 16; ch++) {
-                // elements 16ch..16ch+15: sub-block j = ch/2, qs bytes [32c + l0, +16)
-                const int j = ch >> 1, c = ch >> 2, hi = (ch >> 1) & 1, l0 = (ch & 1) * 16;
-                const int lo3 = sc8[j] & 7, hi3 = sc8[j] >> 3;
-                uint32_t w0[4], w1[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    uint32_t a0 = 0, a1 = 0;
-#pragma unroll
-                    for (int v = 0; v < 4; v++) {
-                        const int b = has_row ? blk[16 + 32 * c + l0 + 4 * u + v] : 0;
-                        const int q = hi ? (b >> 4) : (b & 15);
-                        a0 |= (uint32_t)(q * lo3) << (8 * v);
-                        a1 |= (uint32_t)(q * hi3) << (8 * v);
+    if (warp == 0) {
+        // ------------------------------------------- control: TMA and MMA issue
+        if (lane == 0) {
+            // block kb's inputs into slot kb % nin: raw weights, then the activation tile
+            auto fetch_raw = [&](int kb) {
+                uint8_t *slot = inring + (kb % nin) * inbytes;
+                mbar_arrive_expect_tx(&B.infull[kb % nin], rawbox + (uint32_t)kBBlock);
+                tma_2d(map, slot, (kb * bb) & ~15, r0, &B.infull[kb % nin]);
+            };
+            auto fetch_act = [&](int kb) {  // two boxes of 64 rows x 128 bytes
+                uint8_t *slot = inring + (kb % nin) * inbytes + TM * pitch;
+                tma_2d(&p.amap, slot, kb * 256, n0, &B.infull[kb % nin]);
+                tma_2d(&p.amap, slot + NT * 128, kb * 256 + 128, n0, &B.infull[kb % nin]);
+            };
+            for (int kb = 0; kb < min(nin, nb); kb++) fetch_raw(kb);  // weights are read-only
+            pdl_wait();
+            for (int kb = 0; kb < min(nin, nb); kb++) fetch_act(kb);
+            const uint32_t in0 = smem_u32(inring) + (uint32_t)(TM * pitch);
+            bool ok = true;
+            for (int kb = 0; kb < nb && ok; kb++) {
+                const int j = kb % nin, b = kb & 1;
+                if (!wait_bar(&B.accempty[b], ((kb >> 1) & 1) ^ 1, B, p.status)) break;
+                for (int qi = 0; qi < 4; qi++) {
+                    const int i = 4 * kb + qi, s = i % kStages;
+                    if (!wait_bar(&B.full[s], (i / kStages) & 1, B, p.status)) {
+                        ok = false;
+                        break;
                     }
-                    w0[u] = a0;
-                    w1[u] = a1;
-                }
-                *(uint4 *)(planes + canon(row, ch * 16, TM)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-                *(uint4 *)(planes + kPlaneBytes + canon(row, ch * 16, TM)) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-            }
-        } else {
-            const uint32_t dh = has_row ? (uint32_t)blk[208] | ((uint32_t)blk[209] << 8) : 0u;
-            rowbad |= has_row && !f16_finite(dh);
-            d = f16_to_f32(dh);
-#pragma unroll 2
-            for (int ch = 0; ch < 16; ch++) {
-                // elements 16ch..16ch+15: half h, quarter qq, l in [l0, l0 + 16); one scale
-                const int e0 = ch * 16, h = e0 >> 7, qq = (e0 & 127) >> 5, l0 = e0 & 31;
-                const int sc = has_row ? (int)(int8_t)blk[192 + 8 * h + (l0 >> 4) + 2 * qq] : 0;
-                int dg[3];
-                q6_digits(sc, dg[0], dg[1], dg[2]);
-                uint32_t w[3][4];
+                    fence_after_sync();
+                    // quarter qi: box qi/2, bytes 64 (qi&1) + 32 ks of each 128-byte row
+                    const uint64_t bd = smem_desc_sw128(in0 + (uint32_t)(j * inbytes + (qi >> 1) * NT * 128 + (qi & 1) * 64));
+                    const uint32_t dcol = tmem + (uint32_t)(b * kAccCols), acol = tmem + kACol0 + (uint32_t)(s * kAStageCols);
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    uint32_t a[3] = {0, 0, 0};
-#pragma unroll
-                    for (int v = 0; v < 4; v++) {
-                        const int l = l0 + 4 * u + v;
-                        int q = 0;
-                        if (has_row) {
-                            const int lowb = (qq & 1) ? blk[64 * h + l + 32] : blk[64 * h + l];
-                            const int low = (qq >> 1) ? (lowb >> 4) : (lowb & 15);
-                            q = (low | (((blk[128 + 32 * h + l] >> (2 * qq)) & 3) << 4)) - 32;
+                    for (int pl = 0; pl < kPlanes; pl++) {
+                        mma_i8_ts(dcol + pl * NT, acol + pl * (kQuarter / 4), bd, qi ? 1u : 0u);
+                        mma_i8_ts(dcol + pl * NT, acol + pl * (kQuarter / 4) + 8, bd + 2, 1u);  // + 32 bytes
+                    }
+                    mma_commit(&B.empty[s]);
+                    if (qi == 3) {
+                        mma_commit(&B.accfull[b]);
+                        mma_commit(&B.inempty[j]);
+                    } else if (qi == 1 && kb >= 1 && kb - 1 + nin < nb) {
+                        // refill the previous block's slot, whose MMAs are done by now
+                        if (!wait_bar(&B.inempty[(kb - 1) % nin], ((kb - 1) / nin) & 1, B, p.status)) {
+                            ok = false;
+                            break;
                         }
-#pragma unroll
-                        for (int pl = 0; pl < 3; pl++) a[pl] |= (uint32_t)(q * dg[pl] & 0xFF) << (8 * v);
+                        fetch_raw(kb - 1 + nin);
+                        fetch_act(kb - 1 + nin);
                     }
-#pragma unroll
-                    for (int pl = 0; pl < 3; pl++) w[pl][u] = a[pl];
                 }
-#pragma unroll
-                for (int pl = 0; pl < 3; pl++)
-                    *(uint4 *)(planes + pl * kPlaneBytes + canon(row, e0, TM)) =
-                        make_uint4(w[pl][0], w[pl][1], w[pl][2], w[pl][3]);
             }
+            // every MMA issued has completed before TMEM is released
+            mma_commit(&B.drain);
+            mbar_wait_bounded(&B.drain, 0, p.status);
         }
-        // ---- operands visible to the tensor cores; one thread issues the MMAs
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        fence_before_sync();
-        __syncthreads();
-        fence_after_sync();
-        if (tid == 0) {
-            for (int pl = 0; pl < P; pl++)
-                for (int s = 0; s < 8; s++)  // K = 32 per instruction: chunks 2s, 2s + 1
-                    mma_i8(tmem + (uint32_t)(pl * TN),
-                           smem_desc(planes_s + pl * kPlaneBytes + (uint32_t)(2 * s * TM * 16), TM * 16, 128),
-                           smem_desc(bt_s + (uint32_t)(2 * s * TN * 16), TN * 16, 128), s > 0 ? 1u : 0u);
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             smem_u32(bar))
-                         : "memory");
+        __syncwarp();
+    } else if (warp <= 4) {
+        // ------------------------------------------------------- decoders
+        const int r = 32 * (warp & 3) + lane;  // row = TMEM lane (warp w reaches lanes 32(w%4)..)
+        const uint32_t ta0 = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kACol0;
+        pdl_wait();
+        // activation-row scales, one block ahead
+        float dx_next = 0.f;
+        int ok_next = 1;
+        if (r < ntok) {
+            dx_next = p.act.dx[(long long)(n0 + r) * nb];
+            ok_next = p.act.ok[(long long)(n0 + r) * nb];
         }
-        failed = __syncthreads_or(!mbar_wait_bounded(bar, phase, p.status));
-        if (failed) break;  // the commit never arrived: DEV_TIMEOUT is set
-        phase ^= 1u;
-        fence_after_sync();
-        // ---- block sums back (lane = row) and the block-ordered chain
-        {
-            uint32_t acc[kPlanes][32];
-            const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-            tmem_ld32(lane_base + 0, acc[0]);
-            tmem_ld32(lane_base + TN, acc[1]);
-            if (P == 3) tmem_ld32(lane_base + 2 * TN, acc[2]);
-#pragma unroll
-            for (int n = 0; n < TN; n++) {
-                int S = (int)acc[0][n] + 8 * (int)acc[1][n];
-                if (P == 3) S += 64 * (int)acc[2][n];
-                const float dx = mdx[n];
-                tot[n] = __fmaf_rn(__int2float_rn(S), __fmul_rn(d, dx), tot[n]);
-                if (dt == Q4_K) {
-                    int M = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; j++) M += mn8[j] * (int)mxs[n * 8 + j];
-                    off[n] = __fmaf_rn(__int2float_rn(M), __fmul_rn(dmin, dx), off[n]);
+        for (int kb = 0; kb < nb; kb++) {
+            const int j = kb % nin, ms = kb % kMeta;
+            // tcgen05.st is warp-collective: the warp goes on only if every lane's waits succeeded
+            const bool got = wait_bar(&B.infull[j], (kb / nin) & 1, B, p.status) &&
+                             wait_bar(&B.metaempty[ms], ((kb / kMeta) & 1) ^ 1, B, p.status);
+            if (!__all_sync(0xFFFFFFFFu, got)) break;
+            const int ph = (kb * bb) & 15;
+            const uint8_t *win = inring + j * inbytes + r * pitch;
+            // per-block scales of the row and of the activation rows
+            Meta &m = meta[ms];
+            if (q4) {
+                const uint32_t dm = *(const uint32_t *)win;
+                m.d[r] = f16_to_f32(dm & 0xFFFFu);
+                m.dmin[r] = f16_to_f32(dm >> 16);
+            } else {
+                const uint32_t wd = *(const uint32_t *)(win + ((ph + 208) & ~3));
+                m.d[r] = f16_to_f32((wd >> (8 * (ph & 3))) & 0xFFFFu);
+                m.dmin[r] = 0.f;
+            }
+            if (r < NT) {
+                m.dx[r] = dx_next;
+                m.ok[r] = ok_next;
+                if (r < ntok && kb + 1 < nb) {
+                    dx_next = p.act.dx[(long long)(n0 + r) * nb + kb + 1];
+                    ok_next = p.act.ok[(long long)(n0 + r) * nb + kb + 1];
                 }
-                if (!mok[n]) tokbad |= 1u << n;
+            }
+            mbar_arrive(&B.metafull[ms]);
+            bool ok = true;
+            for (int qi = 0; qi < 4; qi++) {
+                const int i = 4 * kb + qi, s = i % kStages;
+                if (!__all_sync(0xFFFFFFFFu, wait_bar(&B.empty[s], ((i / kStages) & 1) ^ 1, B, p.status))) {
+                    ok = false;
+                    break;
+                }
+                fence_after_sync();
+                const uint32_t ta = ta0 + (uint32_t)(s * kAStageCols);
+                if (q4) {
+                    decode_q4k_quarter(win, qi, ta);
+                } else {
+                    const int sh = 8 * (ph & 3);
+                    switch (ph >> 2) {
+                    case 0: decode_q6k_quarter<0>(win, sh, qi, ta); break;
+                    case 1: decode_q6k_quarter<1>(win, sh, qi, ta); break;
+                    case 2: decode_q6k_quarter<2>(win, sh, qi, ta); break;
+                    default: decode_q6k_quarter<3>(win, sh, qi, ta); break;
+                    }
+                }
+                tmem_wait_st();
+                fence_before_sync();
+                mbar_arrive(&B.full[s]);
+            }
+            if (!ok) break;
+            mbar_arrive(&B.inempty[j]);  // this thread is done with the slot's raw rows
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int q = warp & 3;                  // TMEM lane quarter (warp % 4): rows 32q..32q+31
+        const int th = (warp - 5) >> 2;          // activation rows 32th..32th+31
+        const int r = 32 * q + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(th * kEpiTok);
+        pdl_wait();
+        float tot[kEpiTok], off[kEpiTok];
+#pragma unroll
+        for (int n = 0; n < kEpiTok; n++) tot[n] = off[n] = 0.f;
+        bool rowbad = false, done = true;
+        uint32_t tokbad = 0;
+        for (int kb = 0; kb < nb; kb++) {
+            const int b = kb & 1, ms = kb % kMeta;
+            // tcgen05.ld is warp-collective: the warp goes on only if every lane's waits succeeded
+            const bool got = wait_bar(&B.metafull[ms], (kb / kMeta) & 1, B, p.status) &&
+                             wait_bar(&B.accfull[b], (kb >> 1) & 1, B, p.status);
+            if (!__all_sync(0xFFFFFFFFu, got)) {
+                done = false;
+                break;
+            }
+            fence_after_sync();
+            const Meta &m = meta[ms];
+            const float d = m.d[r], dmin = m.dmin[r];
+            rowbad |= !isfinite(d) || !isfinite(dmin);
+            const uint32_t col = lane_base + (uint32_t)(b * kAccCols);
+            if (dt == Q4_K)
+                epi_block<true>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
+            else
+                epi_block<false>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
+            fence_before_sync();
+            mbar_arrive(&B.accempty[b]);
+#pragma unroll
+            for (int n = 0; n < kEpiTok; n++)
+                if (!m.ok[th * kEpiTok + n]) tokbad |= 1u << n;
+            mbar_arrive(&B.metaempty[ms]);
+        }
+        if (__all_sync(0xFFFFFFFFu, done)) {
+            // outputs: tot - off (+ bias, + residual) ...
+            const int grow = r0 + r, t0 = n0 + th * kEpiTok, nt = min(kEpiTok, ntok - th * kEpiTok);
+            if (r < nrow && !rowbad) {
+                const float bias = sg.bias ? sg.bias[grow] : 0.f;
+#pragma unroll
+                for (int n = 0; n < kEpiTok; n++) {
+                    if (n >= nt) break;
+                    if (tokbad >> n & 1u) continue;
+                    float v = __fsub_rn(tot[n], off[n]);
+                    if (sg.bias) v = __fadd_rn(v, bias);
+                    if (sg.res) v = __fadd_rn(sg.res[(long long)(t0 + n) * sg.ldy + grow], v);
+                    sg.y[(long long)(t0 + n) * sg.ldy + grow] = v;
+                }
+            }
+            // ... and the refused pairs: the GEMV's warp-collective f32 product
+            const unsigned badr = __ballot_sync(0xFFFFFFFFu, r < nrow && rowbad);
+            if (badr || tokbad) {
+                for (int rr = 0; rr < 32 && 32 * q + rr < nrow; rr++) {
+                    const int gr = r0 + 32 * q + rr;
+                    for (int n = 0; n < nt; n++) {
+                        if (!(badr >> rr & 1u) && !(tokbad >> n & 1u)) continue;
+                        float v = row_dot_f32(dt, sg.w + (long long)gr * row_bytes(dt, p.K),
+                                              p.x + (long long)(t0 + n) * p.K, nb);
+                        if (sg.bias) v = __fadd_rn(v, sg.bias[gr]);
+                        if (sg.res) v = __fadd_rn(sg.res[(long long)(t0 + n) * sg.ldy + gr], v);
+                        if (lane == 0) sg.y[(long long)(t0 + n) * sg.ldy + gr] = v;
+                    }
+                }
             }
         }
-        fence_before_sync();
-        __syncthreads();  // planes, B and TMEM free for the next block
     }
-
-    // ---- outputs: tot - off (+ bias, + residual)
-    const int grow = r0 + row;
-    if (has_row && !failed && !rowbad) {
-        const float bias = sg.bias ? sg.bias[grow] : 0.f;
-        for (int n = 0; n < ntok; n++) {
-            if (tokbad >> n & 1u) continue;
-            float v = __fsub_rn(tot[n], off[n]);
-            if (sg.bias) v = __fadd_rn(v, bias);
-            if (sg.res) v = __fadd_rn(sg.res[(long long)(n0 + n) * sg.ldy + grow], v);
-            sg.y[(long long)(n0 + n) * sg.ldy + grow] = v;
-        }
-    }
-    // refused pairs: the GEMV's warp-collective f32 product, row by row
-    const unsigned badr = __ballot_sync(0xFFFFFFFFu, has_row && rowbad);
-    if (!failed && (badr || tokbad)) {
-        for (int rr = 0; rr < 32; rr++) {
-            const int gr = r0 + warp * 32 + rr;
-            if (warp * 32 + rr >= nrow) break;
-            for (int n = 0; n < ntok; n++) {
-                if (!(badr >> rr & 1u) && !(tokbad >> n & 1u)) continue;
-                float v = row_dot_f32(dt, sg.w + (long long)gr * rb, p.x + (long long)(n0 + n) * p.K, p.nb);
-                if (sg.bias) v = __fadd_rn(v, sg.bias[gr]);
-                if (sg.res) v = __fadd_rn(sg.res[(long long)(n0 + n) * sg.ldy + gr], v);
-                if (lane == 0) sg.y[(long long)(n0 + n) * sg.ldy + gr] = v;
-            }
-        }
-    }
-    // after a timeout, give the MMAs in flight one more bounded wait before
-    // the accumulator columns are released
-    if (failed) mbar_wait_bounded(bar, phase, nullptr);
     fence_before_sync();
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [n, row bytes] u8 map of a weight matrix, box [one block from its 16-byte
+// boundary, 128 rows], zero fill past either edge
+bool raw_tmap(const GemvSeg &sg, long long K, CUtensorMap *out) {
+    const EncodeTiledFn fn = (EncodeTiledFn)tmap_encode_fn();
+    if (!fn) return false;
+    const long long rb = row_bytes(sg.dt, K);
+    const cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)sg.n};
+    const cuuint64_t strides[1] = {(cuuint64_t)rb};
+    const cuuint32_t boxd[2] = {(cuuint32_t)(sg.dt == Q4_K ? 144 : kRawPitch), (cuuint32_t)TM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)sg.w, dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [rows, K] u8 map of the activation quants, box [128 bytes, 64 rows] in the
+// 128-byte swizzle: one box is the MMA's B operand for half a block
+bool act_tmap(const int8_t *q, int rows, long long K, CUtensorMap *out) {
+    const EncodeTiledFn fn = (EncodeTiledFn)tmap_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t boxd[2] = {128, (cuuint32_t)NT};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)q, dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
 bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, long long K) {
     if (rows < kTcMinRows || K <= 0 || K % 256 || nseg <= 0 || nseg > kMaxSegs) return false;
-    if ((uintptr_t)act.q & 15) return false;  // 16-byte activation reads
-    for (int i = 0; i < nseg; i++)
+    if ((uintptr_t)act.q & 15) return false;  // 2-D TMA of the activation quants
+    for (int i = 0; i < nseg; i++) {
         if (segs[i].dt != Q4_K && segs[i].dt != Q6_K) return false;
+        // 2-D TMA of the raw blocks: 16-byte aligned rows
+        if (((uintptr_t)segs[i].w & 15) || row_bytes(segs[i].dt, K) % 16) return false;
+    }
     return true;
 }
 
@@ -374,9 +665,11 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
         p.seg[i] = segs[i];
         p.seg_t0[i] = t;
         t += (segs[i].n + TM - 1) / TM;
+        if (segs[i].n > 0 && !raw_tmap(segs[i], K, &p.tmap[i])) return cudaErrorInvalidValue;
     }
     p.seg_t0[nseg] = t;
     if (t == 0) return cudaSuccess;
+    if (!act_tmap(act.q, rows, K, &p.amap)) return cudaErrorInvalidValue;
     p.act = act;
     p.x = x;
     p.rows = rows;
@@ -387,8 +680,8 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
-    cfg.gridDim = dim3(t, (rows + TN - 1) / TN);
-    cfg.blockDim = dim3(kThr);
+    cfg.gridDim = dim3((rows + NT - 1) / NT, t);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemTc;
     cfg.stream = st;
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -678,6 +678,12 @@ bool weight_tmap(const GemvSeg &sg, long long K, CUtensorMap *out, bool cache) {
     return true;
 }
 
+}  // namespace
+
+void *tmap_encode_fn() { return (void *)encode_fn(); }
+
+namespace {
+
 int nr_tpl(int nr) { return nr == 1 ? 1 : nr == 2 ? 2 : nr <= 4 ? 4 : 8; }
 
 int act_bytes_for(int nr, long long K) {

@@ -108,3 +108,25 @@ def test_gemm_batch_invariance(ctx):
             part = ctx.dequant_matmul(x[lo:hi], t, a8_block=256)
             assert np.array_equal(bits(part), bits(full[lo:hi]))
         t.free()
+
+
+def test_prompt_rows_equal_single_token_steps(ctx):
+    """Model-level batch invariance (interp/transformer_test.go:297-354): an
+    80-token prompt in one pass -- every projection on the tensor-core GEMM,
+    two activation-row tiles -- gives the same logits, bit for bit, as the
+    same tokens fed one at a time through the GEMV."""
+    import mimgpu
+    from test_gpu_model import _synthetic
+    cfg, w = _synthetic(2, 4096, 32, 8, 14336, 4096)
+    T, C = 80, 128
+    prompt = np.random.default_rng(5).integers(0, cfg["vocab"], T).astype(np.int32)
+    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=T), w)
+    a = m.session()
+    together = a.run(prompt, np.arange(T), all_rows=True)
+    b = m.session()
+    for i in range(T):
+        one = b.run(prompt[i:i + 1], np.arange(i, i + 1))[0]
+        assert np.array_equal(bits(one), bits(together[i])), i
+    a.free()
+    b.free()
+    m.free()
