@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
         }
         for (int i = 0; i < kNin; i++) {
             mbar_init(&B.infull[i], 1);
-            mbar_init(&B.inempty[i], kDec + 1);  // the decoders and the block's last MMA commit
+            mbar_init(&B.inempty[i], kDec);  // the decoders are done with the raw rows
         }
         for (int i = 0; i < kMeta; i++) {
             mbar_init(&B.metafull[i], kDec);
@@ -442,10 +442,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                     mma_commit(&B.empty[s]);
                     if (qi == 3) {
                         mma_commit(&B.accfull[b]);
-                        mma_commit(&B.inempty[j]);
                     } else if (qi == 1 && kb >= 1 && kb - 1 + nin < nb) {
-                        // refill the previous block's slot, whose MMAs are done by now
-                        if (!wait_bar(&B.inempty[(kb - 1) % nin], ((kb - 1) / nin) & 1, B, p.status)) {
+                        // refill the previous block's slot once the decoders are done with
+                        // it and its MMAs have completed (the block's accumulator commit;
+                        // one commit fewer per block: each costs a pipeline drain)
+                        if (!wait_bar(&B.inempty[(kb - 1) % nin], ((kb - 1) / nin) & 1, B, p.status) ||
+                            !wait_bar(&B.accfull[(kb - 1) & 1], ((kb - 1) >> 1) & 1, B, p.status)) {
                             ok = false;
                             break;
                         }
