@@ -42,7 +42,7 @@ F32, Q4_K, Q6_K = 1, 66, 67
 CFG8B = dict(layers=32, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=128256,
              rope_theta=500000.0, norm_eps=1e-5)
 PROMPT = 128
-GEMV_TRAFFIC_PER_ALGO_BYTE = (66_127_104 + 537_856) / 66_179_904
+GEMV_TRAFFIC_PER_ALGO_BYTE = (66_130_944 + 483_584) / 66_179_904
 
 
 def layout(cfg):
@@ -312,7 +312,7 @@ def run_gpu(args):
     peak, peak_kind = peaks()
     achieved = bpl / spl / 1e9
     # DRAM bytes per algorithmic byte of the GEMV from one ncu capture (the
-    # 28672 x 4096 Q4_K launch: 66.13 MB read + 0.54 MB written for
+    # 28672 x 4096 Q4_K launch: 66.13 MB read + 0.48 MB written for
     # 66.18 MB algorithmic), applied to this run's bytes per launch
     traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
     wpt = weight_bytes_per_token(cfg)
