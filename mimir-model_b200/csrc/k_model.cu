@@ -237,6 +237,251 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
     if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 
+// attention.v2 for many query rows at once (a prompt pass), f16 cache, D = 128:
+// the same arithmetic as attn_exact_kernel row by row -- scores in the eight-
+// lane orders, Cephes expf on the first n&~7 keys of the row, ExpSumF32's
+// lane-sum order, the key-ordered fused weighted sum, o = acc/sum -- so every
+// row's output has the bits the one-row kernel gives it.  A block takes one kv
+// head and PQ query rows x its G heads (32 rows), so each key and value row
+// read from the cache serves 32 rows instead of one.  Two passes over the
+// keys: the first finds each row's maximum score, the second recomputes the
+// scores (the same bits), exponentiates, sums and accumulates the values.
+// Keys stream through a ring of 32-key chunks (bulk copies on mbarriers),
+// widened to f32 once per chunk in shared memory.  Register tiles: a lane
+// scores 4 rows against 1 key (rows and keys in rows of 132 floats, so the
+// 16-byte reads of a warp hit distinct banks), and accumulates 4 rows x 4
+// head elements of the weighted sum.
+constexpr int kPfChunk = 32;
+constexpr int kPfRing = 3;
+constexpr int kPfRows = 32;
+constexpr int kPfPitch = 132;  // floats per row of widened keys and of q
+constexpr int kPfEPitch = 36;  // floats per key row of the exponentials ([key][row])
+constexpr size_t kPfSlot = (size_t)2 * kPfChunk * 128 * 2;  // f16 keys then values of a chunk
+constexpr size_t kPfSmem = 128 + kPfRing * kPfSlot +
+                           sizeof(float) * ((size_t)kPfChunk * kPfPitch + kPfChunk * 128 + kPfRows * kPfPitch +
+                                            kPfChunk * kPfEPitch);
+
+__global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
+    extern __shared__ __align__(128) uint8_t pf_[];
+    __shared__ float rmaxw[8][kPfRows], rmax[kPfRows], rsum[kPfRows], red[kPfRows][8], tailv[kPfRows][8];
+    __shared__ int rn[kPfRows];
+    constexpr int D = 128;
+    uint64_t *bar = (uint64_t *)pf_;
+    uint8_t *ring = pf_ + 128;
+    float *kf = (float *)(ring + kPfRing * kPfSlot);  // [kPfChunk][kPfPitch]
+    float *vf = kf + kPfChunk * kPfPitch;             // [kPfChunk][D]
+    float *qs = vf + kPfChunk * D;                    // [kPfRows][kPfPitch]
+    float *es = qs + kPfRows * kPfPitch;              // [kPfChunk][kPfEPitch]
+    const int G = a.H / a.Hkv, PQ = kPfRows / G;
+    const int kv = blockIdx.x, t0 = blockIdx.y * PQ, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int b = 0; b < kPfRing; b++) mbar_init(&bar[b], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait();
+    // row r: query t0 + r / G, head kv*G + r % G; keys [0, n_r) (0 past the last query)
+    if (tid < kPfRows) {
+        const int t = t0 + tid / G;
+        rn[tid] = t < a.T ? (int)(a.pos[t] + 1) : 0;
+    }
+    for (int i = tid; i < kPfRows * D; i += 256) {
+        const int r = i / D, t = t0 + r / G, h = kv * G + r % G;
+        qs[r * kPfPitch + i % D] = t < a.T ? a.qh[((long long)h * a.T + t) * D + i % D] : 0.f;
+    }
+    __syncthreads();
+    int nmax = 0, nmin = 1 << 30;  // over the rows of real queries
+    for (int r = 0; r < kPfRows; r++)
+        if (rn[r] > 0) {
+            nmax = max(nmax, rn[r]);
+            nmin = min(nmin, rn[r]);
+        }
+    const int nch = (nmax + kPfChunk - 1) / kPfChunk, items = 2 * nch;
+    const uint8_t *kbase = (const uint8_t *)a.kc + (size_t)kv * a.C * D * 2;
+    const uint8_t *vbase = (const uint8_t *)a.vc + (size_t)kv * a.C * D * 2;
+    // item i < nch: keys of chunk i (pass 1); else keys and values of chunk i - nch
+    auto issue = [&](int i) {
+        const int b = i % kPfRing, c = i % nch, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
+        const uint32_t bytes = (uint32_t)(len * D * 2);
+        mbar_arrive_expect_tx(&bar[b], i < nch ? bytes : 2 * bytes);
+        bulk_g2s(ring + b * kPfSlot, kbase + (size_t)j0 * D * 2, bytes, &bar[b]);
+        if (i >= nch) bulk_g2s(ring + b * kPfSlot + kPfChunk * D * 2, vbase + (size_t)j0 * D * 2, bytes, &bar[b]);
+    };
+    if (tid == 0)
+        for (int i = 0; i < min(items, kPfRing); i++) issue(i);
+    // scoring lane: rows rg + 8i (i < 4), key jj of the chunk
+    const int rg = lane & 7, jj = 4 * warp + (lane >> 3);
+    auto scores = [&](int j0, float (&s)[4]) {
+        float l8[4][8];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+#pragma unroll
+            for (int l = 0; l < 8; l++) l8[q][l] = 0.f;
+        const float *kr = kf + jj * kPfPitch;
+#pragma unroll 2
+        for (int c8 = 0; c8 < D / 8; c8++) {
+            const float4 k0 = *(const float4 *)(kr + 8 * c8), k1 = *(const float4 *)(kr + 8 * c8 + 4);
+            const float kv8[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float *qr = qs + (rg + 8 * q) * kPfPitch + 8 * c8;
+                const float4 q0 = *(const float4 *)qr, q1 = *(const float4 *)(qr + 4);
+                const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int l = 0; l < 8; l++) l8[q][l] = __fmaf_rn(qv[l], kv8[l], l8[q][l]);
+            }
+        }
+        const int j = j0 + jj;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int n4 = rn[rg + 8 * q] & ~3;
+            const float v =
+                j < n4 ? __fadd_rn(__fadd_rn(__fadd_rn(l8[q][0], l8[q][1]), __fadd_rn(l8[q][2], l8[q][3])),
+                                   __fadd_rn(__fadd_rn(l8[q][4], l8[q][5]), __fadd_rn(l8[q][6], l8[q][7])))
+                       : __fadd_rn(__fadd_rn(__fadd_rn(l8[q][0], l8[q][4]), __fadd_rn(l8[q][1], l8[q][5])),
+                                   __fadd_rn(__fadd_rn(l8[q][2], l8[q][6]), __fadd_rn(l8[q][3], l8[q][7])));
+            s[q] = __fmul_rn(v, a.scale);
+        }
+    };
+    // widen the f16 chunk in slot b (keys, and values when vtoo) into kf / vf
+    auto widen = [&](int b, int len, bool vtoo) {
+        const uint32_t *k16 = (const uint32_t *)(ring + b * kPfSlot);
+        for (int i = tid; i < kPfChunk * D / 2; i += 256) {
+            const int kj = i / (D / 2), d2 = i % (D / 2);
+            const uint32_t w = kj < len ? k16[i] : 0u;
+            *(float2 *)(kf + kj * kPfPitch + 2 * d2) = make_float2(h2f_bits(w & 0xFFFFu), h2f_bits(w >> 16));
+            if (vtoo) {
+                const uint32_t u = kj < len ? k16[kPfChunk * D / 2 + i] : 0u;
+                *(float2 *)(vf + kj * D + 2 * d2) = make_float2(h2f_bits(u & 0xFFFFu), h2f_bits(u >> 16));
+            }
+        }
+    };
+    bool ok = true;
+    // ---- pass 1: each row's maximum score (exact in any order)
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int c = 0; c < nch; c++) {
+        const int b = c % kPfRing, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
+        ok &= mbar_wait_bounded(&bar[b], (c / kPfRing) & 1, a.status);
+        widen(b, len, false);
+        __syncthreads();  // widened; slot b free
+        if (tid == 0 && c + kPfRing < items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(c + kPfRing);
+        }
+        float s[4];
+        scores(j0, s);
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (j0 + jj < rn[rg + 8 * q]) m4[q] = fmaxf(m4[q], s[q]);
+        __syncthreads();  // kf read by every warp before the next widening
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {  // lanes rg, rg+8, rg+16, rg+24 hold the same rows
+        float m = m4[q];
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 16));
+        if (lane < 8) rmaxw[warp][rg + 8 * q] = m;
+    }
+    __syncthreads();
+    if (tid < kPfRows) {
+        float m = rmaxw[0][tid];
+        for (int w = 1; w < 8; w++) m = fmaxf(m, rmaxw[w][tid]);
+        rmax[tid] = m;
+    }
+    __syncthreads();
+    // ---- pass 2: exponentials, their sums and the weighted sum of the values
+    const int sr = tid >> 3, sl = tid & 7;  // summing thread: row sr, ExpSumF32 lane sl
+    const int srn = rn[sr], srn8 = srn >= 8 ? (srn & ~7) : 0;
+    float lanesum = 0.f;
+    int ntail = 0;
+    const int ar = 4 * (lane & 7), ad = 4 * (4 * warp + (lane >> 3));  // accumulating thread: rows ar.., d ad..
+    int an[4];
+#pragma unroll
+    for (int ri = 0; ri < 4; ri++) an[ri] = rn[ar + ri];
+    float acc[4][4];
+#pragma unroll
+    for (int ri = 0; ri < 4; ri++)
+#pragma unroll
+        for (int di = 0; di < 4; di++) acc[ri][di] = 0.f;
+    for (int c = 0; c < nch; c++) {
+        const int i = nch + c, b = i % kPfRing, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
+        ok &= mbar_wait_bounded(&bar[b], (i / kPfRing) & 1, a.status);
+        widen(b, len, true);
+        __syncthreads();
+        if (tid == 0 && i + kPfRing < items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + kPfRing);
+        }
+        float s[4];
+        scores(j0, s);
+        const int j = j0 + jj;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int r = rg + 8 * q, n = rn[r], n8 = n >= 8 ? (n & ~7) : 0;
+            float e = 0.f;
+            if (j < n) {
+                const float x = __fsub_rn(s[q], rmax[r]);
+                e = j < n8 ? expf_amd64(x) : (float)exp((double)x);
+            }
+            es[jj * kPfEPitch + r] = e;
+        }
+        __syncthreads();
+        // ExpSumF32's lane sums: key j to lane j % 8 below n8 (j0 is a multiple of 8), in key order
+        for (int k = sl; k < len; k += 8)
+            if (j0 + k < srn8) lanesum = __fadd_rn(lanesum, es[k * kPfEPitch + sr]);
+        if (sl == 0)  // the tail keys [n8, n), kept in order
+            for (int k = 0; k < len; k++) {
+                const int jg = j0 + k;
+                if (jg >= srn8 && jg < srn) tailv[sr][ntail++] = es[k * kPfEPitch + sr];
+            }
+        // one fused multiply-add per key and element, in key order; keys every row
+        // of the block admits first, the others only for the rows that admit them
+        const int kall = min(len, max(0, nmin - j0));
+        for (int k = 0; k < kall; k++) {
+            const float4 e4 = *(const float4 *)(es + k * kPfEPitch + ar);
+            const float4 v4 = *(const float4 *)(vf + k * D + ad);
+            const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int ri = 0; ri < 4; ri++)
+#pragma unroll
+                for (int di = 0; di < 4; di++) acc[ri][di] = __fmaf_rn(ev[ri], vv[di], acc[ri][di]);
+        }
+        for (int k = kall; k < len; k++) {
+            const float4 e4 = *(const float4 *)(es + k * kPfEPitch + ar);
+            const float4 v4 = *(const float4 *)(vf + k * D + ad);
+            const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int ri = 0; ri < 4; ri++)
+                if (j0 + k < an[ri])
+#pragma unroll
+                    for (int di = 0; di < 4; di++) acc[ri][di] = __fmaf_rn(ev[ri], vv[di], acc[ri][di]);
+        }
+        __syncthreads();  // es, kf, vf free
+    }
+    red[sr][sl] = lanesum;
+    __syncthreads();
+    if (sl == 0) {
+        const float *r8 = red[sr];
+        float sum = 0.f;
+        if (srn8) sum = __fadd_rn(__fadd_rn(__fadd_rn(r8[0], r8[4]), __fadd_rn(r8[1], r8[5])),
+                                  __fadd_rn(__fadd_rn(r8[2], r8[6]), __fadd_rn(r8[3], r8[7])));
+        for (int k = 0; k < ntail; k++) sum = __fadd_rn(sum, tailv[sr][k]);
+        rsum[sr] = sum;
+    }
+    __syncthreads();
+    (void)ok;
+#pragma unroll
+    for (int ri = 0; ri < 4; ri++) {
+        const int r = ar + ri, t = t0 + r / G, h = kv * G + r % G;
+        if (t >= a.T) continue;
+        const float sum = rsum[r];
+        const float4 o = make_float4(__fdiv_rn(acc[ri][0], sum), __fdiv_rn(acc[ri][1], sum),
+                                     __fdiv_rn(acc[ri][2], sum), __fdiv_rn(acc[ri][3], sum));
+        *(float4 *)(a.out + (long long)t * a.H * D + (long long)h * D + ad) = o;
+    }
+}
+
 // After the argmax of a greedy step: the picked id (0 when the first logit
 // is NaN -- the all-ones key -- or nothing was picked) becomes the next input
 // token, is appended to the output ids, the position advances, and the key
@@ -268,8 +513,27 @@ cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool 
     return cudaLaunchKernelEx(&cfg, rope_scatter_kernel, a);
 }
 
+bool attn_prefill_ok(const AttnArgs2 &a) {
+    return a.T >= kAttnPrefillMinRows && a.cache_f16 && a.D == 128 && a.Hkv > 0 && a.H % a.Hkv == 0 &&
+           kPfRows % (a.H / a.Hkv) == 0 && !a.act.q;
+}
+
+cudaError_t launch_attn_prefill(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const int PQ = kPfRows / (a.H / a.Hkv);
+    cudaLaunchAttribute attr1[1];
+    cudaLaunchConfig_t cfg = mk(dim3(a.Hkv, (a.T + PQ - 1) / PQ), dim3(256), kPfSmem, st, pdl, attr1);
+    return cudaLaunchKernelEx(&cfg, attn_prefill_kernel, a);
+}
+
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
     if (a.T <= 0) return cudaSuccess;
+    if (attn_prefill_ok(a)) return launch_attn_prefill(a, st, pdl);
     // heads of 32..256 elements dividing 256; the fused quantization needs
     // whole blocks of 256 outputs
     if (a.D < 32 || 256 % a.D || a.Hkv <= 0 || a.H % a.Hkv || (a.act.q && a.H % (256 / a.D)))

@@ -184,8 +184,15 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, a8 ? s->actE : none, status};
-        CK(launch_attn_exact(aa, st, pdl));
+                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status};
+        if (attn_prefill_ok(aa)) {
+            // a prompt pass: the many-row kernel, then the 8-bit blocks of its output
+            CK(launch_attn_exact(aa, st, pdl));
+            if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl));
+        } else {
+            if (a8) aa.act = s->actE;  // quantized inside the one-row kernel
+            CK(launch_attn_exact(aa, st, pdl));
+        }
         GemvSeg o = slice(w.o, E, 0, E, s->x, E, s->x);
         if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));

@@ -48,11 +48,18 @@ struct AttnArgs2 {
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
+// whether launch_attn_exact runs these arguments through the many-row kernel
+// (given act.q null)
+bool attn_prefill_ok(const AttnArgs2 &a);
 // Dynamic shared memory of the attention kernel: q and the scores of the
 // 256/D heads of a block over the whole context, plus the key/value chunk
 // ring (kAttnRing buffers of kAttnChunk keys of every kv head the block
 // reads).
 constexpr size_t kAttnSmemMax = 220 * 1024;
+// From this many query rows (a prompt pass) with an f16 cache and D = 128,
+// the rows go through the many-row kernel (same bits per row) and the
+// caller quantizes the outputs separately (act.q must be null then).
+constexpr int kAttnPrefillMinRows = 8;
 constexpr int kAttnChunk = 64;
 constexpr int kAttnRing = 4;
 inline int attn_kv_per_block(int H, int Hkv, int D) {
