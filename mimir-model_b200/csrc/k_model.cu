@@ -243,11 +243,12 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
 // lane-sum order, the key-ordered fused weighted sum, o = acc/sum -- so every
 // row's output has the bits the one-row kernel gives it.  A block takes one kv
 // head and PQ query rows x its G heads (32 rows), so each key and value row
-// read from the cache serves 32 rows instead of one.  Two passes over the
-// keys: the first finds each row's maximum score, the second recomputes the
-// scores (the same bits), exponentiates, sums and accumulates the values.
-// Keys stream through a ring of 32-key chunks (bulk copies on mbarriers),
-// widened to f32 once per chunk in shared memory.  Register tiles: a lane
+// read from the cache serves 32 rows instead of one.  Two passes: the first
+// computes the scores into a global scratch (L2-resident for short prompts)
+// and each row's maximum, the second reads them back, exponentiates, sums
+// and accumulates the values.  Keys, then values, stream through a ring of
+// 32-row chunks (bulk copies on mbarriers), widened to f32 once per chunk in
+// shared memory.  Register tiles: a lane
 // scores 4 rows against 1 key (rows and keys in rows of 132 floats, so the
 // 16-byte reads of a warp hit distinct banks), and accumulates 4 rows x 4
 // head elements of the weighted sum.
@@ -256,7 +257,7 @@ constexpr int kPfRing = 3;
 constexpr int kPfRows = 32;
 constexpr int kPfPitch = 132;  // floats per row of widened keys and of q
 constexpr int kPfEPitch = 36;  // floats per key row of the exponentials ([key][row])
-constexpr size_t kPfSlot = (size_t)2 * kPfChunk * 128 * 2;  // f16 keys then values of a chunk
+constexpr size_t kPfSlot = (size_t)kPfChunk * 128 * 2;  // f16 keys or values of a chunk
 constexpr size_t kPfSmem = 128 + kPfRing * kPfSlot +
                            sizeof(float) * ((size_t)kPfChunk * kPfPitch + kPfChunk * 128 + kPfRows * kPfPitch +
                                             kPfChunk * kPfEPitch);
@@ -298,15 +299,15 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
             nmin = min(nmin, rn[r]);
         }
     const int nch = (nmax + kPfChunk - 1) / kPfChunk, items = 2 * nch;
+    float *srow = a.scores + (size_t)(kv * gridDim.y + blockIdx.y) * kPfRows * a.C;  // [kPfRows][C]
     const uint8_t *kbase = (const uint8_t *)a.kc + (size_t)kv * a.C * D * 2;
     const uint8_t *vbase = (const uint8_t *)a.vc + (size_t)kv * a.C * D * 2;
-    // item i < nch: keys of chunk i (pass 1); else keys and values of chunk i - nch
+    // item i < nch: keys of chunk i (pass 1); else values of chunk i - nch (pass 2)
     auto issue = [&](int i) {
         const int b = i % kPfRing, c = i % nch, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
         const uint32_t bytes = (uint32_t)(len * D * 2);
-        mbar_arrive_expect_tx(&bar[b], i < nch ? bytes : 2 * bytes);
-        bulk_g2s(ring + b * kPfSlot, kbase + (size_t)j0 * D * 2, bytes, &bar[b]);
-        if (i >= nch) bulk_g2s(ring + b * kPfSlot + kPfChunk * D * 2, vbase + (size_t)j0 * D * 2, bytes, &bar[b]);
+        mbar_arrive_expect_tx(&bar[b], bytes);
+        bulk_g2s(ring + b * kPfSlot, (i < nch ? kbase : vbase) + (size_t)j0 * D * 2, bytes, &bar[b]);
     };
     if (tid == 0)
         for (int i = 0; i < min(items, kPfRing); i++) issue(i);
@@ -344,17 +345,15 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
             s[q] = __fmul_rn(v, a.scale);
         }
     };
-    // widen the f16 chunk in slot b (keys, and values when vtoo) into kf / vf
-    auto widen = [&](int b, int len, bool vtoo) {
+    // widen the f16 chunk in slot b into kf (keys) or vf (values)
+    auto widen = [&](int b, int len, bool values) {
         const uint32_t *k16 = (const uint32_t *)(ring + b * kPfSlot);
+        float *dst = values ? vf : kf;
+        const int pitch = values ? D : kPfPitch;
         for (int i = tid; i < kPfChunk * D / 2; i += 256) {
             const int kj = i / (D / 2), d2 = i % (D / 2);
             const uint32_t w = kj < len ? k16[i] : 0u;
-            *(float2 *)(kf + kj * kPfPitch + 2 * d2) = make_float2(h2f_bits(w & 0xFFFFu), h2f_bits(w >> 16));
-            if (vtoo) {
-                const uint32_t u = kj < len ? k16[kPfChunk * D / 2 + i] : 0u;
-                *(float2 *)(vf + kj * D + 2 * d2) = make_float2(h2f_bits(u & 0xFFFFu), h2f_bits(u >> 16));
-            }
+            *(float2 *)(dst + kj * pitch + 2 * d2) = make_float2(h2f_bits(w & 0xFFFFu), h2f_bits(w >> 16));
         }
     };
     bool ok = true;
@@ -373,7 +372,10 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
         scores(j0, s);
 #pragma unroll
         for (int q = 0; q < 4; q++)
-            if (j0 + jj < rn[rg + 8 * q]) m4[q] = fmaxf(m4[q], s[q]);
+            if (j0 + jj < rn[rg + 8 * q]) {
+                m4[q] = fmaxf(m4[q], s[q]);
+                srow[(size_t)(rg + 8 * q) * a.C + j0 + jj] = s[q];  // read back by this thread in pass 2
+            }
         __syncthreads();  // kf read by every warp before the next widening
     }
 #pragma unroll
@@ -406,6 +408,10 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
         for (int di = 0; di < 4; di++) acc[ri][di] = 0.f;
     for (int c = 0; c < nch; c++) {
         const int i = nch + c, b = i % kPfRing, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
+        const int j = j0 + jj;
+        float s[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) s[q] = j < rn[rg + 8 * q] ? srow[(size_t)(rg + 8 * q) * a.C + j] : 0.f;
         ok &= mbar_wait_bounded(&bar[b], (i / kPfRing) & 1, a.status);
         widen(b, len, true);
         __syncthreads();
@@ -413,9 +419,6 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(i + kPfRing);
         }
-        float s[4];
-        scores(j0, s);
-        const int j = j0 + jj;
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             const int r = rg + 8 * q, n = rn[r], n8 = n >= 8 ? (n & ~7) : 0;
@@ -515,7 +518,13 @@ cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool 
 
 bool attn_prefill_ok(const AttnArgs2 &a) {
     return a.T >= kAttnPrefillMinRows && a.cache_f16 && a.D == 128 && a.Hkv > 0 && a.H % a.Hkv == 0 &&
-           kPfRows % (a.H / a.Hkv) == 0 && !a.act.q;
+           kPfRows % (a.H / a.Hkv) == 0 && !a.act.q && a.scores;
+}
+
+size_t attn_prefill_scores_bytes(int T, int H, int Hkv, int C) {
+    if (Hkv <= 0 || H % Hkv || kPfRows % (H / Hkv)) return 0;
+    const int PQ = kPfRows / (H / Hkv);
+    return (size_t)Hkv * ((T + PQ - 1) / PQ) * kPfRows * C * sizeof(float);
 }
 
 cudaError_t launch_attn_prefill(const AttnArgs2 &a, cudaStream_t st, bool pdl) {

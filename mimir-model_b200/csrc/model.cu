@@ -46,6 +46,7 @@ struct mimgpu_session {
     cudaStream_t st = nullptr;
     std::vector<void *> kc, vc;
     size_t cache_bytes = 0;
+    float *scores = nullptr;  // score scratch of the many-row attention (prompt passes), or null
     void *arena = nullptr;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *qh = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr;
     float *logits = nullptr;
@@ -184,7 +185,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
         CK(launch_rope_scatter(ra, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status};
+                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status, s->scores};
         if (attn_prefill_ok(aa)) {
             // a prompt pass: the many-row kernel, then the 8-bit blocks of its output
             CK(launch_attn_exact(aa, st, pdl));
@@ -277,6 +278,7 @@ void free_session(mimgpu_session *s) {
     for (void *p : s->vc) cudaFree(p);
     for (void *p : s->opened) cudaIpcCloseMemHandle(p);
     if (s->arena) cudaFree(s->arena);
+    if (s->scores) cudaFree(s->scores);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
 }
@@ -426,6 +428,11 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
         e = cudaMalloc(&s->kc[l], s->cache_bytes);
         if (e == cudaSuccess) e = cudaMalloc(&s->vc[l], s->cache_bytes);
     }
+    // prompt passes of kAttnPrefillMinRows tokens or more: the many-row attention's score scratch
+    const size_t sb = k.max_tokens >= kAttnPrefillMinRows && k.cache_f16 && D == 128
+                          ? attn_prefill_scores_bytes((int)k.max_tokens, (int)H, k.kv_heads, k.context)
+                          : 0;
+    if (e == cudaSuccess && sb) e = cudaMalloc(&s->scores, sb);
     if (e != cudaSuccess) {
         free_session(s);
         return cuda_fail(c, e, "key-value cache");

@@ -45,12 +45,14 @@ struct AttnArgs2 {
     float *out;
     ActQ8 act;
     unsigned *status;  // device status word (bounded waits record timeouts here)
+    float *scores;     // many-row kernel: score scratch of attn_prefill_scores_bytes, or null
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
 // whether launch_attn_exact runs these arguments through the many-row kernel
 // (given act.q null)
 bool attn_prefill_ok(const AttnArgs2 &a);
+size_t attn_prefill_scores_bytes(int T, int H, int Hkv, int C);
 // Dynamic shared memory of the attention kernel: q and the scores of the
 // 256/D heads of a block over the whole context, plus the key/value chunk
 // ring (kAttnRing buffers of kAttnChunk keys of every kv head the block
