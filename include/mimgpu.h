@@ -219,6 +219,22 @@ int mimgpu_session_run(mimgpu_session *s, const int32_t *tokens, const int64_t *
  * the first maximum of the logits, feeds it back, `steps` times; writes the
  * picked ids.  One step is one device-resident graph launch. */
 int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int steps, int32_t *ids_out);
+/* Batched decoding (no counterpart in the reference, whose sessions hold one
+ * sequence): a session of `slots` independent sequences, each with its own
+ * key-value cache (1 <= slots <= max_tokens).  mimgpu_session_new is
+ * mimgpu_session_new_slots(m, 1, out). */
+int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out);
+/* One run of t rows, row i token tokens[i] of sequence slot_ids[i] at
+ * positions[i]; logits [t, vocab].  Rows all of one sequence are a prompt
+ * pass of that sequence; otherwise each row attends to its own sequence's
+ * cache.  Every row's logits are the bits a single-sequence session gives. */
+int mimgpu_session_run_slots(mimgpu_session *s, const int32_t *tokens, const int32_t *slot_ids,
+                             const int64_t *positions, int t, float *logits);
+/* Greedy decode of sequences 0..b-1 together: sequence i is fed tokens[i] at
+ * positions[i], then its own picks, `steps` times; ids_out [steps][b].  One
+ * step of all b sequences is one device-resident graph launch. */
+int mimgpu_session_generate_slots(mimgpu_session *s, const int32_t *tokens, const int64_t *positions, int b,
+                                  int steps, int32_t *ids_out);
 /* The session's CUDA stream (a cudaStream_t), for callers that time or
  * order their own device work against the session's. */
 void *mimgpu_session_stream(mimgpu_session *s);

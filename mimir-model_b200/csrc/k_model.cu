@@ -44,7 +44,8 @@ __global__ void rope_scatter_kernel(RopeScatterArgs a) {
     if (hi >= a.H + a.Hkv) {  // value head
         const int head = hi - a.H - a.Hkv;
         const float v = row[nq + nk + head * D + e];
-        const long long at = ((long long)head * a.C + pos) * D + e;
+        const long long at = (a.slot ? a.slot[t] : a.slot0) * cache_slot_elems(a.Hkv, a.C, D) +
+                             ((long long)head * a.C + pos) * D + e;
         if (a.cache_f16) ((uint16_t *)a.vc)[at] = f32_to_f16(v);
         else ((float *)a.vc)[at] = v;
         return;
@@ -70,7 +71,8 @@ __global__ void rope_scatter_kernel(RopeScatterArgs a) {
         a.qh[((long long)head * a.T + t) * D + e] = out;
         return;
     }
-    const long long at = ((long long)head * a.C + pos) * D + e;
+    const long long at = (a.slot ? a.slot[t] : a.slot0) * cache_slot_elems(a.Hkv, a.C, D) +
+                         ((long long)head * a.C + pos) * D + e;
     if (a.cache_f16) ((uint16_t *)a.kc)[at] = f32_to_f16(out);
     else ((float *)a.kc)[at] = out;
 }
@@ -117,10 +119,11 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
     const int n = (int)(a.pos[t] + 1);
     const int nch = (n + kAttnChunk - 1) / kAttnChunk, items = 2 * nch;  // key chunks, then value chunks
     // item i: chunk i % nch of the keys (i < nch) or the values
+    const size_t slot_off = (size_t)(a.slot ? a.slot[t] : a.slot0) * cache_slot_elems(a.Hkv, a.C, D) * ES;
     auto issue = [&](int i) {
         const int b = i % kAttnRing, c = i % nch;
         const int j0 = c * kAttnChunk, len = min(kAttnChunk, n - j0);
-        const uint8_t *src = (const uint8_t *)(i < nch ? a.kc : a.vc);
+        const uint8_t *src = (const uint8_t *)(i < nch ? a.kc : a.vc) + slot_off;
         mbar_arrive_expect_tx(&bar[b], (uint32_t)(nkv * len * rowb));
         for (int v = 0; v < nkv; v++)
             bulk_g2s(ring + b * chunkb + v * kAttnChunk * rowb, src + (((size_t)(kv0 + v) * a.C) + j0) * rowb,
@@ -300,8 +303,9 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
         }
     const int nch = (nmax + kPfChunk - 1) / kPfChunk, items = 2 * nch;
     float *srow = a.scores + (size_t)(kv * gridDim.y + blockIdx.y) * kPfRows * a.C;  // [kPfRows][C]
-    const uint8_t *kbase = (const uint8_t *)a.kc + (size_t)kv * a.C * D * 2;
-    const uint8_t *vbase = (const uint8_t *)a.vc + (size_t)kv * a.C * D * 2;
+    const size_t slot_off = (size_t)a.slot0 * cache_slot_elems(a.Hkv, a.C, D) * 2;
+    const uint8_t *kbase = (const uint8_t *)a.kc + slot_off + (size_t)kv * a.C * D * 2;
+    const uint8_t *vbase = (const uint8_t *)a.vc + slot_off + (size_t)kv * a.C * D * 2;
     // item i < nch: keys of chunk i (pass 1); else values of chunk i - nch (pass 2)
     auto issue = [&](int i) {
         const int b = i % kPfRing, c = i % nch, j0 = c * kPfChunk, len = min(kPfChunk, nmax - j0);
@@ -488,23 +492,31 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(AttnArgs2 a) {
 // After the argmax of a greedy step: the picked id (0 when the first logit
 // is NaN -- the all-ones key -- or nothing was picked) becomes the next input
 // token, is appended to the output ids, the position advances, and the key
-// is cleared for the next step.
+// is cleared for the next step; one thread per sequence of a batched step
+// (ids [step][rows]).
 __global__ void advance_kernel(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
-                               P2P wait, const unsigned long long *keys) {
+                               P2P wait, const unsigned long long *keys, int rows) {
     pdl_wait();
-    unsigned long long k = *key;
-    if (wait.N > 1) {  // tensor parallelism: this rank's key to every rank, then the largest wins
-        for (int r = 0; r < wait.N; r++) peer_ptr<unsigned long long>(wait, r, wait.off)[wait.k] = k;
-        p2p_publish_wait(wait);
-        k = 0;
-        for (int r = 0; r < wait.N; r++) k = max(k, ((volatile const unsigned long long *)keys)[r]);
+    const int r = threadIdx.x;
+    unsigned long long k = r < rows ? key[r] : 0ull;
+    if (wait.N > 1) {  // tensor parallelism (one row): this rank's key to every rank, then the largest wins
+        if (r == 0) {
+            for (int q = 0; q < wait.N; q++) peer_ptr<unsigned long long>(wait, q, wait.off)[wait.k] = k;
+            p2p_publish_wait(wait);
+            k = 0;
+            for (int q = 0; q < wait.N; q++) k = max(k, ((volatile const unsigned long long *)keys)[q]);
+        }
     }
-    const int id = (k == 0 || k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-    *key = 0;
-    *tok = id;
-    ids[*step] = id;
-    *step += 1;
-    *pos += 1;
+    const int s0 = *step;
+    __syncthreads();
+    if (r < rows) {
+        const int id = (k == 0 || k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        key[r] = 0;
+        tok[r] = id;
+        ids[(long long)s0 * rows + r] = id;
+        pos[r] += 1;
+    }
+    if (r == 0) *step = s0 + 1;
 }
 
 }  // namespace
@@ -518,7 +530,7 @@ cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool 
 
 bool attn_prefill_ok(const AttnArgs2 &a) {
     return a.T >= kAttnPrefillMinRows && a.cache_f16 && a.D == 128 && a.Hkv > 0 && a.H % a.Hkv == 0 &&
-           kPfRows % (a.H / a.Hkv) == 0 && !a.act.q && a.scores;
+           kPfRows % (a.H / a.Hkv) == 0 && !a.act.q && a.scores && !a.slot;
 }
 
 size_t attn_prefill_scores_bytes(int T, int H, int Hkv, int C) {
@@ -563,11 +575,12 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
-                           cudaStream_t st, bool pdl, const P2P *wait, const unsigned long long *keys) {
+                           cudaStream_t st, bool pdl, const P2P *wait, const unsigned long long *keys, int rows) {
+    if (rows < 1 || rows > 1024 || (wait && wait->N > 1 && rows != 1)) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = mk(dim3(1), dim3(1), 0, st, pdl, attr);
+    cudaLaunchConfig_t cfg = mk(dim3(1), dim3((rows + 31) / 32 * 32), 0, st, pdl, attr);
     const P2P w = wait ? *wait : P2P{};
-    return cudaLaunchKernelEx(&cfg, advance_kernel, key, tok, pos, ids, step, w, keys);
+    return cudaLaunchKernelEx(&cfg, advance_kernel, key, tok, pos, ids, step, w, keys, rows);
 }
 
 }  // namespace mimgpu

@@ -315,10 +315,13 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, long long i) {
 }
 
 __global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n, long long i0,
-                                                     int holds_first, unsigned long long *__restrict__ key) {
+                                                     int holds_first, unsigned long long *__restrict__ key,
+                                                     long long ldv) {
     __shared__ unsigned long long red[8];
     pdl_launch_dependents();
     pdl_wait();
+    v += blockIdx.y * ldv;  // row blockIdx.y of a batched step
+    key += blockIdx.y;
     unsigned long long best = 0;  // 0: no candidate (every real key is larger)
     for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += gridDim.x * 256LL) {
         const float x = v[i];
@@ -394,11 +397,13 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
 }
 
 cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_first, unsigned long long *key,
-                          cudaStream_t st, bool pdl) {
+                          cudaStream_t st, bool pdl, int rows, long long ldv) {
+    if (rows < 1 || rows > 65535) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    const long long blocks = std::min<long long>((n + 1023) / 1024, 2LL * num_sms());
-    cudaLaunchConfig_t cfg = make_cfg(dim3((unsigned)std::max<long long>(1, blocks)), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, i0, (int)holds_first, key);
+    const long long blocks = std::min<long long>((n + 1023) / 1024, std::max<long long>(1, 2LL * num_sms() / rows));
+    cudaLaunchConfig_t cfg =
+        make_cfg(dim3((unsigned)std::max<long long>(1, blocks), rows), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, i0, (int)holds_first, key, ldv);
 }
 
 int num_sms() {

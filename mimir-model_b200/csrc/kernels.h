@@ -119,7 +119,7 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 // 0xFFFFFFFF - (key & 0xFFFFFFFF), or 0 for a zero key or the all-ones key
 // that a NaN v[0] sets when this slice holds the first index.
 cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_first, unsigned long long *key,
-                          cudaStream_t st, bool pdl);
+                          cudaStream_t st, bool pdl, int rows = 1, long long ldv = 0);
 
 // seeded synthetic weights (k_synth.cu)
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,

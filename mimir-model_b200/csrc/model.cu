@@ -64,10 +64,18 @@ struct mimgpu_session {
     ActQ8 actE{}, actF{};
     int32_t *tok = nullptr, *ids = nullptr;
     int64_t *pos = nullptr;
-    unsigned long long *amax = nullptr;  // argmax key, zero between steps
+    unsigned long long *amax = nullptr;  // argmax keys [max_tokens], zero between steps
     int *step = nullptr;
     cudaGraphExec_t g_step = nullptr;    // T=1 forward, logits of the row
     cudaGraphExec_t g_greedy = nullptr;  // T=1 forward + argmax + advance
+    // batched decoding: `slots` sequences, one cache each; a batched run's row
+    // sequences (device [max_tokens]); the sequence of single-sequence runs
+    int slots = 1;
+    int32_t *slot = nullptr;
+    int slot0 = 0;
+    bool batched = false;                // the run in flight uses `slot`
+    cudaGraphExec_t g_batch = nullptr;   // batched greedy step of g_batch_rows rows
+    int g_batch_rows = 0;
 };
 
 namespace {
@@ -182,10 +190,12 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
         RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
-                           c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l]};
+                           c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l],
+                           s->batched ? s->slot : nullptr, s->slot0};
         CK(launch_rope_scatter(ra, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status, s->scores};
+                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status, s->scores,
+                     s->batched ? s->slot : nullptr, s->slot0};
         if (attn_prefill_ok(aa)) {
             // a prompt pass: the many-row kernel, then the 8-bit blocks of its output
             CK(launch_attn_exact(aa, st, pdl));
@@ -239,9 +249,10 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     }
     if (greedy) {
         const P2P kput = xch(2 * c.layers, s->keys, 0);
-        CK(launch_argmax(lg, vn, v0, k == 0, s->amax, st, pdl));
-        if (N > 1 && !p2p) CK(tp_allreduce_max_u64(m->tp, s->amax, st));
-        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl, p2p ? &kput : nullptr, s->keys));
+        CK(launch_argmax(lg, vn, v0, k == 0, s->amax, st, pdl, rows, ldl));
+        if (N > 1 && !p2p) CK(tp_allreduce_max_u64(m->tp, s->amax, st, (size_t)rows));
+        CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl, p2p ? &kput : nullptr, s->keys,
+                          rows));
     } else if (N > 1) {
         // the whole vocabulary on every rank: [N][rows][Vl] -> [rows][vocab]
         CK(tp_allgather(m->tp, s->logl, s->gbuf, (size_t)rows * Vl, st));
@@ -251,12 +262,15 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     return cudaSuccess;
 }
 
-int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out) {
+// rows > 1: a batched step (row r of sequence slot[r], logits of every row)
+int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out, int rows = 1) {
     mimgpu_ctx *c = s->m->ctx;
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return cuda_fail(c, e, "begin capture");
-    cudaError_t fe = enqueue_forward(s, 1, false, greedy, c->status);
+    s->batched = rows > 1;
+    cudaError_t fe = enqueue_forward(s, rows, rows > 1, greedy, c->status);
+    s->batched = false;
     e = cudaStreamEndCapture(s->st, &g);
     if (fe != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -274,6 +288,7 @@ void free_session(mimgpu_session *s) {
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->g_step) cudaGraphExecDestroy(s->g_step);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    if (s->g_batch) cudaGraphExecDestroy(s->g_batch);
     for (void *p : s->kc) cudaFree(p);
     for (void *p : s->vc) cudaFree(p);
     for (void *p : s->opened) cudaIpcCloseMemHandle(p);
@@ -359,11 +374,15 @@ void mimgpu_model_free(mimgpu_model *m) {
     delete m;
 }
 
-int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
+int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) { return mimgpu_session_new_slots(m, 1, out); }
+
+int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
     if (!m || !out) return MIMGPU_EINVAL;
     mimgpu_ctx *c = m->ctx;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     *out = nullptr;
+    if (slots < 1 || slots > m->c.max_tokens || slots > 1024)
+        return fail(c, MIMGPU_EINVAL, "%d sequences; a session holds 1..min(max_tokens, 1024)", slots);
     int rc = validate(m);
     if (rc || (rc = use_device(c))) return rc;
     if ((rc = cuda_fail(c, gemv_a8_prepare(), "gemv setup"))) return rc;
@@ -382,7 +401,7 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
                          al(T * 4), al(T * 8), al(65536 * 4), al(256),
                          tpb(T * El * 4), tpb(T * Fl * 4), tpb(T * El * 4), tpb(T * Vl * 4), tpb(N * T * gw * 4),
                          al((size_t)(2 * k.layers + 1) * N * 4), al((size_t)(2 * k.layers + 2) * 4), al((size_t)N * 8),
-                         al(16), al((size_t)N * 8)};
+                         al(16), al((size_t)N * 8), al(T * 8), al(T * 4)};
     for (size_t b : sz) bytes += b;
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s->arena, bytes);
@@ -407,7 +426,6 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->pos = (int64_t *)take();
     s->ids = (int32_t *)take();
     uint8_t *misc = take();
-    s->amax = (unsigned long long *)(misc + 32);
     s->step = (int *)(misc + 16);
     s->attl = (float *)take();
     s->al = (float *)take();
@@ -421,7 +439,10 @@ int mimgpu_session_new(mimgpu_model *m, mimgpu_session **out) {
     s->epoch = (unsigned *)take();
     s->peer_base = (uint64_t *)take();
     e = cudaMemset(p2p0, 0, (size_t)(p - p2p0));  // flags, counters, epoch start at zero
-    s->cache_bytes = (size_t)k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
+    s->amax = (unsigned long long *)take();
+    s->slot = (int32_t *)take();
+    s->slots = slots;
+    s->cache_bytes = (size_t)slots * k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
     s->kc.resize(k.layers, nullptr);
     s->vc.resize(k.layers, nullptr);
     for (int l = 0; l < k.layers && e == cudaSuccess; l++) {
@@ -458,7 +479,7 @@ int mimgpu_session_reset(mimgpu_session *s) {
         e = cudaMemsetAsync(s->kc[l], 0, s->cache_bytes, s->st);
         if (e == cudaSuccess) e = cudaMemsetAsync(s->vc[l], 0, s->cache_bytes, s->st);
     }
-    if (e == cudaSuccess) e = cudaMemsetAsync(s->amax, 0, sizeof(unsigned long long), s->st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->amax, 0, sizeof(unsigned long long) * s->m->c.max_tokens, s->st);
     if (e != cudaSuccess) return cuda_fail(c, e, "reset");
     return sync_bounded(c, s->st);
 }
@@ -478,6 +499,8 @@ int mimgpu_session_run(mimgpu_session *s, const int32_t *tokens, const int64_t *
     cudaError_t e = cudaMemcpyAsync(s->tok, tokens, T * 4, cudaMemcpyHostToDevice, s->st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, positions, T * 8, cudaMemcpyHostToDevice, s->st);
     if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    s->slot0 = 0;
+    s->batched = false;
     if (T == 1) {
         if (!s->g_step && (rc = capture(s, false, &s->g_step))) return rc;
         e = cudaGraphLaunch(s->g_step, s->st);
@@ -510,6 +533,81 @@ int mimgpu_session_generate(mimgpu_session *s, int32_t token, int64_t pos, int s
     if (!s->g_greedy && (rc = capture(s, true, &s->g_greedy))) return rc;
     for (int i = 0; i < steps && e == cudaSuccess; i++) e = cudaGraphLaunch(s->g_greedy, s->st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(ids_out, s->ids, steps * 4, cudaMemcpyDeviceToHost, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "generate");
+    return sync_bounded(c, s->st);
+}
+
+int mimgpu_session_run_slots(mimgpu_session *s, const int32_t *tokens, const int32_t *slot_ids,
+                             const int64_t *positions, int T, float *logits) {
+    if (!s || !tokens || !slot_ids || !positions || !logits) return MIMGPU_EINVAL;
+    mimgpu_model *m = s->m;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (T <= 0 || T > m->c.max_tokens) return fail(c, MIMGPU_EINVAL, "%d rows; the session takes 1..%d", T, m->c.max_tokens);
+    bool uniform = true;
+    for (int i = 0; i < T; i++) {
+        if (slot_ids[i] < 0 || slot_ids[i] >= s->slots)
+            return fail(c, MIMGPU_EINVAL, "sequence %d of row %d; the session holds %d", slot_ids[i], i, s->slots);
+        if (positions[i] < 0 || positions[i] >= m->c.context)
+            return fail(c, MIMGPU_EINVAL, "position %lld outside the cache of %d", (long long)positions[i], m->c.context);
+        uniform &= slot_ids[i] == slot_ids[0];
+    }
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(s->tok, tokens, T * 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, positions, T * 8, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->slot, slot_ids, T * 4, cudaMemcpyHostToDevice, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    // rows of one sequence: a prompt pass of that sequence; otherwise one row
+    // per sequence, each against its own cache
+    s->slot0 = uniform ? slot_ids[0] : 0;
+    s->batched = !uniform;
+    e = enqueue_forward(s, T, true, false, c->status);
+    s->slot0 = 0;
+    s->batched = false;
+    if (e != cudaSuccess) return cuda_fail(c, e, "forward");
+    e = cudaMemcpyAsync(logits, s->logits, (size_t)T * m->c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
+    return sync_bounded(c, s->st);
+}
+
+int mimgpu_session_generate_slots(mimgpu_session *s, const int32_t *tokens, const int64_t *positions, int B,
+                                  int steps, int32_t *ids_out) {
+    if (!s || !tokens || !positions || !ids_out || steps < 0) return MIMGPU_EINVAL;
+    mimgpu_model *m = s->m;
+    mimgpu_ctx *c = m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (B < 1 || B > s->slots) return fail(c, MIMGPU_EINVAL, "%d sequences; the session holds %d", B, s->slots);
+    if (steps > 65536 || (long long)steps * B > 65536)
+        return fail(c, MIMGPU_EINVAL, "%d steps of %d sequences exceed the id buffer", steps, B);
+    for (int i = 0; i < B; i++)
+        if (positions[i] < 0 || positions[i] + steps > m->c.context)
+            return fail(c, MIMGPU_EINVAL, "%d steps from position %lld exceed the cache of %d", steps,
+                        (long long)positions[i], m->c.context);
+    if (steps == 0) return MIMGPU_OK;
+    int rc = use_device(c);
+    if (rc) return rc;
+    std::vector<int32_t> iota(B);
+    for (int i = 0; i < B; i++) iota[i] = i;
+    const int zero = 0;
+    cudaError_t e = cudaMemcpyAsync(s->tok, tokens, B * 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, positions, B * 8, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->slot, iota.data(), B * 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->step, &zero, 4, cudaMemcpyHostToDevice, s->st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    s->slot0 = 0;
+    if (B == 1) {
+        if (!s->g_greedy && (rc = capture(s, true, &s->g_greedy))) return rc;
+    } else if (s->g_batch_rows != B) {
+        if (s->g_batch) cudaGraphExecDestroy(s->g_batch);
+        s->g_batch = nullptr;
+        s->g_batch_rows = 0;
+        if ((rc = capture(s, true, &s->g_batch, B))) return rc;
+        s->g_batch_rows = B;
+    }
+    cudaGraphExec_t g = B == 1 ? s->g_greedy : s->g_batch;
+    for (int i = 0; i < steps && e == cudaSuccess; i++) e = cudaGraphLaunch(g, s->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ids_out, s->ids, (size_t)steps * B * 4, cudaMemcpyDeviceToHost, s->st);
     if (e != cudaSuccess) return cuda_fail(c, e, "generate");
     return sync_bounded(c, s->st);
 }

@@ -16,7 +16,7 @@ namespace mimgpu {
 int tp_size(const mimgpu_tp *tp);
 int tp_rank(const mimgpu_tp *tp);
 cudaError_t tp_allgather(mimgpu_tp *tp, const float *send, float *recv, size_t count, cudaStream_t st);
-cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st);
+cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st, size_t count = 1);
 // [N][T][W] -> rows of stride ldd, columns below wmax; and the [T][W] slab
 // of columns [c0, c0 + W) of rows of stride ld
 cudaError_t launch_unshard(const float *src, int N, int T, int W, float *dst, long long ldd, long long wmax,
@@ -30,8 +30,12 @@ struct RopeScatterArgs {
     const double *inv_freq;
     int T, H, Hkv, D, C, rotary, interleaved, cache_f16;
     float *qh;             // [H, T, D]
-    void *kc, *vc;         // [Hkv, C, D]
+    void *kc, *vc;         // [slots][Hkv, C, D]
+    const int32_t *slot;   // [T] sequence (cache) of each row, or null: every row in sequence slot0
+    int slot0;
 };
+// elements of one sequence's cache of one layer
+__host__ __device__ inline long long cache_slot_elems(int Hkv, int C, int D) { return (long long)Hkv * C * D; }
 
 // Attention of the model step: q heads [H, T, D] (after RoPE) over the cache
 // [Hkv, C, D], keys [0, pos[t]] for query row t; out [T, H*D] and, when
@@ -46,6 +50,8 @@ struct AttnArgs2 {
     ActQ8 act;
     unsigned *status;  // device status word (bounded waits record timeouts here)
     float *scores;     // many-row kernel: score scratch of attn_prefill_scores_bytes, or null
+    const int32_t *slot;  // [T] sequence of each row (batched decoding), or null: sequence slot0
+    int slot0;
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);
@@ -76,6 +82,6 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
 // wait / keys: tensor parallelism, the ranks' keys arrive in keys[0..N)
 cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
                            cudaStream_t st, bool pdl, const P2P *wait = nullptr,
-                           const unsigned long long *keys = nullptr);
+                           const unsigned long long *keys = nullptr, int rows = 1);
 
 }  // namespace mimgpu

@@ -93,11 +93,11 @@ cudaError_t tp_allgather(mimgpu_tp *tp, const float *send, float *recv, size_t c
                                                                                    : cudaErrorUnknown;
 }
 
-cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st) {
+cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st, size_t count) {
     const NcclApi &api = nccl();
     if (!api.ok) return cudaErrorNotSupported;
-    return api.allReduce(buf, buf, 1, ncclUint64, ncclMax, tp->comm, st) == ncclSuccess ? cudaSuccess
-                                                                                       : cudaErrorUnknown;
+    return api.allReduce(buf, buf, count, ncclUint64, ncclMax, tp->comm, st) == ncclSuccess ? cudaSuccess
+                                                                                           : cudaErrorUnknown;
 }
 
 cudaError_t launch_unshard(const float *src, int N, int T, int W, float *dst, long long ldd, long long wmax,

@@ -61,6 +61,9 @@ SIGNATURES = {
     "mimgpu_session_reset": (I32, [P]),
     "mimgpu_session_run": (I32, [P, P, P, I32, P, I32]),
     "mimgpu_session_generate": (I32, [P, I32, I64, I32, P]),
+    "mimgpu_session_new_slots": (I32, [P, I32, C.POINTER(P)]),
+    "mimgpu_session_run_slots": (I32, [P, P, P, P, I32, P]),
+    "mimgpu_session_generate_slots": (I32, [P, P, P, I32, I32, P]),
     "mimgpu_session_stream": (P, [P]),
     "mimgpu_tp_unique_id": (I32, [P, SZ]),
     "mimgpu_tp_new": (I32, [P, P, SZ, I32, I32, C.POINTER(P)]),
@@ -356,9 +359,10 @@ class Model:
         self.ctx._check(lib().mimgpu_model_set_tp(self.h, tp.h if tp is not None else None))
         self.tp = tp
 
-    def session(self) -> "Session":
+    def session(self, slots: int = 1) -> "Session":
+        """A session of `slots` independent sequences (batched decoding)."""
         h = P()
-        self.ctx._check(lib().mimgpu_session_new(self.h, C.byref(h)))
+        self.ctx._check(lib().mimgpu_session_new_slots(self.h, int(slots), C.byref(h)))
         return Session(self, h)
 
     def free(self):
@@ -404,6 +408,23 @@ class Session:
         so that decode steps exchange over peer memory."""
         blob = b"".join(handles)
         self.m.ctx._check(lib().mimgpu_session_set_peers(self.h, blob, 64, len(handles)))
+
+    def run_slots(self, tokens, slots, positions) -> np.ndarray:
+        """One run of rows of given sequences (mimgpu_session_run_slots): logits [rows, vocab]."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        sl = np.ascontiguousarray(slots, np.int32)
+        p = np.ascontiguousarray(positions, np.int64)
+        out = np.empty((t.size, self.m.vocab), np.float32)
+        self.m.ctx._check(lib().mimgpu_session_run_slots(self.h, _p(t), _p(sl), _p(p), t.size, _p(out)))
+        return out
+
+    def generate_slots(self, tokens, positions, steps: int) -> np.ndarray:
+        """Greedy decode of sequences 0..len(tokens)-1 together: ids [steps, B]."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int64)
+        ids = np.empty((steps, t.size), np.int32)
+        self.m.ctx._check(lib().mimgpu_session_generate_slots(self.h, _p(t), _p(p), t.size, steps, _p(ids)))
+        return ids
 
     def generate(self, token: int, pos: int, steps: int) -> np.ndarray:
         ids = np.empty(steps, np.int32)
