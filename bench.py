@@ -41,6 +41,9 @@ PUBLISHED_8B = 6.7  # 8B-shape Q4_K_M random weights, 181-token pro
 F32, Q4_K, Q6_K = 1, 66, 67
 CFG8B = dict(layers=32, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=128256,
              rope_theta=500000.0, norm_eps=1e-5)
+CFG70B = dict(layers=80, embed=8192, ffn=28672, heads=64, kv_heads=8, head_dim=128, rope_dims=128, vocab=128256,
+              rope_theta=500000.0, norm_eps=1e-5)
+SHAPES = {"8b": CFG8B, "70b": CFG70B}
 PROMPT = 128
 GEMV_TRAFFIC_PER_ALGO_BYTE = (66_130_944 + 483_584) / 66_179_904
 
@@ -243,7 +246,7 @@ def run_gpu(args):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    cfg = dict(CFG8B, layers=args.layers)
+    cfg = dict(SHAPES[args.shape], layers=args.layers)
     prompt = args.prompt
     context = prompt + args.warmup + args.steps + 2 * args.e2e_steps + 8
     ctx = mimgpu.Context(local)
@@ -324,9 +327,11 @@ def run_gpu(args):
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": round(value / PUBLISHED_8B, 2), "dtype": "int8",
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": round(value / PUBLISHED_8B, 2) if args.shape == "8b" else None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)",
-        "config": {"workload": "8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)",
+        "config": {"workload": ("8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)" if args.shape == "8b"
+                                else "70B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 5)"),
                    "layers": cfg["layers"], "d_model": cfg["embed"], "heads": cfg["heads"],
                    "kv_heads": cfg["kv_heads"], "ffn": cfg["ffn"], "vocab": cfg["vocab"], "prompt": prompt,
                    "context_cache": context, "positions_timed": [prompt + args.warmup, pos - 1 - args.e2e_steps - 2],
@@ -459,7 +464,7 @@ def run_prefill(args):
     import mimgpu
     lib = mimgpu.lib()
     torch.cuda.set_device(0)
-    cfg = dict(CFG8B, layers=args.layers)
+    cfg = dict(SHAPES[args.shape], layers=args.layers)
     Ts = [int(t) for t in args.prefill.split(",")]
     ctx = mimgpu.Context(0)
     model, weights = build_model(ctx, cfg, max(Ts) + 8, max(Ts))
@@ -537,7 +542,7 @@ def run_batch(args):
     import torch
     import mimgpu
     torch.cuda.set_device(0)
-    cfg = dict(CFG8B, layers=args.layers)
+    cfg = dict(SHAPES[args.shape], layers=args.layers)
     B, C = args.batch, args.context
     prompt = C - args.warmup - args.steps - args.e2e_steps - 8
     ctx = mimgpu.Context(0)
@@ -574,12 +579,14 @@ def run_batch(args):
     wpt = weight_bytes_per_token(cfg)
     peak, peak_kind = peaks()
     print(json.dumps({
-        "metric": f"8B-shape Q4_K_M batched decode tok/s (BASELINE config 4, batch {B})", "value": round(value, 1),
+        "metric": (f"8B-shape Q4_K_M batched decode tok/s (BASELINE config 4, batch {B})" if args.shape == "8b"
+                   else f"70B-shape Q4_K_M batched decode tok/s (BASELINE config 5, batch {B})"),
+        "value": round(value, 1),
         "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dev_s / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)",
-        "config": {"workload": f"8B-shape greedy decode of {B} sequences together, {C}-token cache",
+        "config": {"workload": f"{args.shape.upper()}-shape greedy decode of {B} sequences together, {C}-token cache",
                    "layers": cfg["layers"], "batch": B, "context_cache": C, "prompt_per_sequence": prompt,
                    "prefill_s": round(prefill_s, 2),
                    "l2": "inputs larger than L2: 4.88 GB of weights streamed per step vs 126 MB L2"},
@@ -652,8 +659,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-budget", type=float, default=120.0)
-    ap.add_argument("--layers", type=int, default=CFG8B["layers"],
-                    help="decoder layers (default: the 8B shape's 32; fewer only for profiling runs)")
+    ap.add_argument("--shape", default="8b", choices=sorted(SHAPES),
+                    help="model shape: 8b (configs 3-4) or 70b (config 5)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers (default: the shape's own; fewer only for profiling runs)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before the timed decode steps")
     ap.add_argument("--gemv", default="", help="GEMV-only mode: N,K,q4_k|q6_k[,rows]")
     ap.add_argument("--gemv-hot", action="store_true", help="GEMV-only mode with one weight copy (L2-hot)")
@@ -661,6 +670,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="batched decode mode (config 4): sequences, e.g. 32")
     ap.add_argument("--context", type=int, default=1024, help="key-value cache per sequence in --batch mode")
     args = ap.parse_args()
+    if not args.layers:
+        args.layers = SHAPES[args.shape]["layers"]
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.gemv:
