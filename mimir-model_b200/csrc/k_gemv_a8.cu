@@ -700,6 +700,7 @@ cudaError_t gemv_a8_prepare() {
     if (e == cudaSuccess) e = prepare_nr<4>();
     if (e == cudaSuccess) e = prepare_nr<8>();
     if (e == cudaSuccess) e = gemm_a8_tc_prepare();
+    if (e == cudaSuccess) e = gemv_row_prepare();
     num_sms();
     return e;
 }
@@ -712,6 +713,8 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
     // many activation rows: the tensor-core GEMM (same results bit for bit)
     if ((!put || put->N <= 1) && gemm_a8_tc_ok(segs, nseg, act, rows, K))
         return launch_gemm_a8_tc(segs, nseg, x, act, rows, K, status, st, pdl);
+    // one activation row: the slab-streaming kernel (same results bit for bit)
+    if (rows == 1 && gemv_row_ok(segs, nseg, act, K)) return launch_gemv_row(segs, nseg, x, act, K, status, st, pdl, put);
     A8Params p = {};
     p.nseg = nseg;
     int maxbb = 0, g = 0;

@@ -1,0 +1,539 @@
+// k_gemv_row.cu -- dequant_matmul_a8.v2 (block 256) for ONE activation row on
+// sm_100a: the GEMV of a decode step.
+//
+// The same bits as gemv_a8_kernel (k_gemv_a8.cu) and dotQ8KRef
+// (internal/kernels/q8k_test.go:35-117 of gsoultan/mimir-model): per 256-element
+// block the exact int32 S = sum_s sc_s * sum(q*y) and (Q4_K) M = sum_s m_s * xs_s,
+// then per row, in block order, tot = fma(float(S), d*dx, tot) and
+// off = fma(float(M), dmin*dx, off); the result is tot - off, plus the bias,
+// plus the residual.  Rows the reference refuses (linearA8,
+// interp/fast.go:282-379) take the f32 product of a8_refused.cuh.
+//
+// Work decomposition: one CTA per SM: a producer thread, 16 consumer warps
+// and a chain warp.
+//  * Every matrix of the launch is cut into gridDim.x slabs of consecutive
+//    rows, one per CTA, so each SM streams the same number of bytes (within
+//    one row).  Rows are 16-byte multiples, so a slab is one contiguous byte
+//    range; the producer streams it in stages of 256 blocks, one
+//    cp.async.bulk per stage, into a ring of 3 to 8 stages.  It starts
+//    before the previous kernel has finished (weights are read-only).
+//  * The 512 half-blocks of a stage go one to each consumer lane: Q4_K
+//    warps take 16 consecutive blocks, Q6_K warps the blocks 8i + (warp % 8)
+//    so that a warp's 210-byte blocks share their 16-byte phase.  The two
+//    lanes of a block add their exact sums with one shuffle; the even lane
+//    stores the block's (float(S), d*dx, float(M), dmin*dx) in a table of
+//    per-row records.
+//  * Records live in two halves, one per batch of rows.  Once every consumer
+//    warp is done with a batch (a per-batch counter in shared memory), the
+//    chain warp runs each row's chain over its records in block order (one
+//    row per lane) and stores the result (bias, residual, copies into the
+//    tensor-parallel peers); refused rows take the warp's f32 product.  The
+//    consumers overwrite a half only after the chain warp has published
+//    that it is done with it, and never stop for the chain.
+// The activation row sits in shared memory in a layout that puts the lanes
+// of a quarter-warp on distinct banks for both block orders.
+#include <cstdint>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "a8_refused.cuh"
+#include "p2p.cuh"
+
+namespace mimgpu {
+
+namespace {
+
+constexpr int kCW = 16;               // consumer warps
+constexpr int kCT = kCW * 32;         // consumer threads
+constexpr int kThreads = kCT + 64;    // + the producer warp and the chain warp
+constexpr int kSB = 256;              // blocks per stage (two lanes per block)
+constexpr int kMaxSlots = 8;
+constexpr int kSmemMax = 227 * 1024;
+constexpr unsigned FULL = 0xffffffffu;
+
+struct RowParams {
+    GemvSeg seg[kMaxSegs];
+    int nseg;
+    const float *x;     // f32 activations (refused rows)
+    ActQ8 act;
+    long long K;
+    int nb;             // blocks per row
+    float inv_nb;
+    int lr;             // rows in the record ring = 1 << lr
+    int slots, slot_bytes;
+    int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
+    P2P put;
+    unsigned *status;
+};
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ float f16f(uint32_t h) {  // f16 -> f32 by the hardware conversion (exact)
+    float f;
+    asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"((unsigned short)h));
+    return f;
+}
+__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFF); }
+__device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xFF); }
+
+// Byte offset of half h of activation block kb.  Rows of 288 bytes (two
+// halves of 128 quants + 16 spare), plus 32 bytes every 8 blocks: the
+// 16-byte unit of chunk a is 2kb + 2(kb/8) + h + a (mod 8), distinct across
+// the 8 lanes of a quarter-warp whether they hold consecutive blocks (Q4_K)
+// or blocks 8 apart (Q6_K).
+__host__ __device__ __forceinline__ int act_off(int kb, int h) { return kb * 288 + (kb >> 3) * 32 + h * 144; }
+__host__ __device__ __forceinline__ int act_bytes(int nb) { return act_off(nb, 0) + 32; }
+
+// Rows [r0, r0 + nr) of an n-row matrix for CTA b of G.
+__device__ __forceinline__ void slab(int n, int b, int G, int &r0, int &nr) {
+    const long long a = (long long)n * b / G, e = (long long)n * (b + 1) / G;
+    r0 = (int)a;
+    nr = (int)(e - a);
+}
+
+// The bytes a Q6_K lane needs from one block, from aligned 16-byte loads: WO
+// is the block start's word offset within its 16-byte line (warp-uniform),
+// the remaining 0/16-bit shift comes from the address.
+template <int WO>
+__device__ __forceinline__ void q6k_load(uint32_t blk, int h, uint32_t (&ql)[16], uint32_t (&qh)[8], uint32_t &sc01,
+                                         uint32_t &sc23, uint32_t &dh) {
+    const uint32_t sh = (blk & 3u) * 8;
+    const uint32_t b16 = blk & ~15u;
+    uint32_t w[20];
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        const uint4 v = lds128(b16 + 64 * h + 16 * i);
+        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) ql[i] = __funnelshift_r(w[WO + i], w[WO + i + 1], sh);
+    uint32_t u[12];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const uint4 v = lds128(b16 + 128 + 32 * h + 16 * i);
+        u[4 * i] = v.x; u[4 * i + 1] = v.y; u[4 * i + 2] = v.z; u[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) qh[i] = __funnelshift_r(u[WO + i], u[WO + i + 1], sh);
+    const uint4 v = lds128(b16 + 192);
+    const uint4 v2 = lds128(b16 + 208);
+    const uint32_t t[8] = {v.x, v.y, v.z, v.w, v2.x, v2.y, v2.z, v2.w};
+    sc01 = __funnelshift_r(t[WO + 2 * h], t[WO + 2 * h + 1], sh);
+    sc23 = __funnelshift_r(t[WO + 2 * h + 1], t[WO + 2 * h + 2], sh);
+    dh = __funnelshift_r(t[WO + 4], t[WO + 5], sh) & 0xFFFFu;
+}
+
+// Half h of a Q4_K block at shared address blk: sub-blocks 4h..4h+3.  The
+// exact partial sums S and M of the half, and the block's two scales.
+__device__ __forceinline__ void q4k_half(uint32_t blk, int h, uint32_t ya, uint32_t hdr_a, int &S, int &M,
+                                         uint32_t &dh, uint32_t &mh, float &dx) {
+    const uint4 hdr = lds128(blk);
+    uint4 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) q[i] = lds128(blk + 16 + 64 * h + 16 * i);
+    dh = hdr.x & 0xFFFFu;
+    mh = hdr.x >> 16;
+    // the 4 scales and mins of sub-blocks 4h..4h+3 as packed bytes (getScaleMinK4, quant.go:246-254)
+    const uint32_t scw = h ? ((hdr.w & 0x0F0F0F0Fu) | (((hdr.y >> 6) & 0x03030303u) << 4)) : (hdr.y & 0x3F3F3F3Fu);
+    const uint32_t mw = h ? (((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4)) : (hdr.z & 0x3F3F3F3Fu);
+    const uint32_t qw[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                             q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
+    // activation chunk a (quants 16a..16a+15 of the half) pairs with the low
+    // (a & 2 == 0) or high nibbles of qs chunk 2(a >> 2) + (a & 1)
+    int s[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int a = 0; a < 8; a++) {
+        const uint4 y = lds128(ya + 16 * a);
+        const int c = 2 * (a >> 2) + (a & 1), sub = a >> 1;
+        const int sh = (a & 2) ? 4 : 0;
+        s[sub] = __dp4a((int)((qw[4 * c] >> sh) & 0x0F0F0F0Fu), (int)y.x, s[sub]);
+        s[sub] = __dp4a((int)((qw[4 * c + 1] >> sh) & 0x0F0F0F0Fu), (int)y.y, s[sub]);
+        s[sub] = __dp4a((int)((qw[4 * c + 2] >> sh) & 0x0F0F0F0Fu), (int)y.z, s[sub]);
+        s[sub] = __dp4a((int)((qw[4 * c + 3] >> sh) & 0x0F0F0F0Fu), (int)y.w, s[sub]);
+    }
+    S = ubyte(scw, 0) * s[0] + ubyte(scw, 1) * s[1] + ubyte(scw, 2) * s[2] + ubyte(scw, 3) * s[3];
+    const uint4 ah = lds128(hdr_a);  // xs of the half's 4 runs of 32, dx, ok
+    M = ubyte(mw, 0) * (int)(int16_t)(ah.x & 0xFFFF) + ubyte(mw, 1) * (int)(int16_t)(ah.x >> 16) +
+        ubyte(mw, 2) * (int)(int16_t)(ah.y & 0xFFFF) + ubyte(mw, 3) * (int)(int16_t)(ah.y >> 16);
+    dx = __uint_as_float(ah.z);
+}
+
+// Half h of a Q6_K block (elements 128h + l + 32q, scales sc[8h + l/16 + 2q],
+// quant.go:318-344): the exact partial sum S.
+template <int WO>
+__device__ __forceinline__ void q6k_half(uint32_t blk, int h, uint32_t ya, uint32_t ys_a, int &S, uint32_t &dh) {
+    uint32_t ql[16], qh[8], sc01, sc23;
+    q6k_load<WO>(blk, h, ql, qh, sc01, sc23, dh);
+    const uint4 ysv = lds128(ys_a);
+    const uint32_t ysw[4] = {ysv.x, ysv.y, ysv.z, ysv.w};
+    S = 0;
+#pragma unroll
+    for (int qq = 0; qq < 4; qq++) {
+#pragma unroll
+        for (int lh = 0; lh < 2; lh++) {
+            const uint4 v = lds128(ya + 32 * qq + 16 * lh);
+            const int sh = 2 * qq;
+            const uint32_t qs0 = (qq & 1) ? ql[8 + 4 * lh] : ql[4 * lh];
+            const uint32_t qs1 = (qq & 1) ? ql[8 + 4 * lh + 1] : ql[4 * lh + 1];
+            const uint32_t qs2 = (qq & 1) ? ql[8 + 4 * lh + 2] : ql[4 * lh + 2];
+            const uint32_t qs3 = (qq & 1) ? ql[8 + 4 * lh + 3] : ql[4 * lh + 3];
+            const int nsh = (qq >> 1) * 4;
+            int g = 0;
+            g = __dp4a((int)(((qs0 >> nsh) & 0x0F0F0F0Fu) | (((qh[4 * lh] >> sh) & 0x03030303u) << 4)), (int)v.x, g);
+            g = __dp4a((int)(((qs1 >> nsh) & 0x0F0F0F0Fu) | (((qh[4 * lh + 1] >> sh) & 0x03030303u) << 4)), (int)v.y, g);
+            g = __dp4a((int)(((qs2 >> nsh) & 0x0F0F0F0Fu) | (((qh[4 * lh + 2] >> sh) & 0x03030303u) << 4)), (int)v.z, g);
+            g = __dp4a((int)(((qs3 >> nsh) & 0x0F0F0F0Fu) | (((qh[4 * lh + 3] >> sh) & 0x03030303u) << 4)), (int)v.w, g);
+            const int gi = 2 * qq + lh;  // group of 16: ys index and scale index
+            const int ys = (int)(int16_t)((ysw[gi >> 1] >> (16 * (gi & 1))) & 0xFFFF);
+            const int sc = sbyte(gi < 4 ? sc01 : sc23, gi & 3);
+            S += sc * (g - 32 * ys);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_constant__ RowParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = (uint64_t *)smem;       // stage landed (producer's bytes)
+    uint64_t *cons = full + kMaxSlots;       // stage consumed (16 consumer warps)
+    uint64_t *empty = cons + kMaxSlots;      // stage released by the chain warp
+    int *misc = (int *)(smem + 3 * kMaxSlots * 8);  // [0] activation row quantized
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x, nb = p.nb;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.slots; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&cons[s], kCW);
+            mbar_init(&empty[s], 1);
+        }
+        misc[0] = 1;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kCW) {
+        // ------------------------------------------------ producer (one thread)
+        if (lane != 0) return;
+        uint8_t *ring = smem + p.off_ring;
+        int n = 0;
+        bool ok = true;
+        for (int s = 0; s < p.nseg && ok; s++) {
+            int r0, nr;
+            slab(p.seg[s].n, cta, G, r0, nr);
+            const int bb = block_bytes(p.seg[s].dt);
+            const int nblk = nr * nb;
+            const uint8_t *src = p.seg[s].w + (long long)r0 * nb * bb;
+            for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
+                const int slot = n % p.slots;
+                if (n >= p.slots && !mbar_wait_bounded(&empty[slot], ((n / p.slots) - 1) & 1, p.status)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t bytes = (uint32_t)(min(kSB, nblk - k0) * bb);
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_g2s(ring + (size_t)slot * p.slot_bytes, src + (long long)k0 * bb, bytes, &full[slot]);
+            }
+        }
+        // copies still in flight land before the block exits
+        for (int u = max(0, n - p.slots); u < n; u++)
+            mbar_wait_bounded(&full[u % p.slots], (u / p.slots) & 1, p.status);
+        return;
+    }
+
+    // ------------------------------------------- consumers and the chain warp
+    const int tid = threadIdx.x;
+    pdl_wait();
+    if (warp < kCW) {
+        // the activation row into shared memory (act_off layout), the
+        // per-half headers (xs of the 4 runs of 32, dx, ok), the sums of 16
+        const int nq = (int)(p.K / 16);
+        for (int c = tid; c < nq; c += kCT) {
+            const int kb = c >> 4, h = (c >> 3) & 1, a = c & 7;
+            *(uint4 *)(smem + p.off_act + act_off(kb, h) + 16 * a) = *(const uint4 *)(p.act.q + (long long)c * 16);
+        }
+        for (int hb = tid; hb < 2 * nb; hb += kCT) {
+            const int kb = hb >> 1, h = hb & 1;
+            const uint2 xs = *(const uint2 *)(p.act.xs + kb * 8 + 4 * h);
+            const float dx = p.act.dx[kb];
+            const int okb = p.act.ok[kb];
+            *(uint4 *)(smem + p.off_hdr + hb * 16) = make_uint4(xs.x, xs.y, __float_as_uint(dx), (unsigned)okb);
+            *(uint4 *)(smem + p.off_ys + hb * 16) = *(const uint4 *)(p.act.ys + kb * 16 + 8 * h);
+            if (!okb) misc[0] = 0;  // a row is quantized when every one of its blocks is (q8.go:50-97)
+        }
+        for (int i = tid; i < (1 << p.lr); i += kCT) smem[p.off_bad + i] = 0;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kCT + 32) : "memory");
+    const bool act_ok = misc[0] != 0;
+    const int R1 = (1 << p.lr) - 1, rstride = (nb + 1) * 16;  // record rows padded by 16 bytes: no bank conflicts
+    const uint32_t rec_s = smem_u32(smem + p.off_rec);
+    uint8_t *bad = smem + p.off_bad;  // [R] rows with a non-finite block scale
+    bool failed = false;              // a wait gave up: skip the work, keep the protocol
+
+    if (warp == kCW + 1) {
+        // ------------------------------------------------ chain warp
+        // After the consumers are done with stage n it releases the slot to
+        // the producer, then finishes the rows whose last block was in the
+        // stage: the block-ordered chain (one row per lane), bias, residual,
+        // stores; refused rows take the warp's f32 product.
+        int n = 0, gbase = 0;
+        for (int s = 0; s < p.nseg; s++) {
+            const GemvSeg &sg = p.seg[s];
+            int r0, nr;
+            slab(sg.n, cta, G, r0, nr);
+            const int dt = sg.dt;
+            const int nblk = nr * nb;
+            const long long rb = row_bytes(dt, p.K);
+            int lo = 0;  // first row not finished
+            for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
+                const int slot = n % p.slots;
+                if (!failed && !mbar_wait_bounded(&cons[slot], (n / p.slots) & 1, p.status)) failed = true;
+                failed = __any_sync(FULL, failed);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                const int done = min(nblk, k0 + kSB);
+                const int hi = done == nblk ? nr : done / nb;  // rows complete after this stage
+                for (int t0 = lo; t0 < hi; t0 += 32) {
+                    const int row = t0 + lane;
+                    const bool valid = row < hi;
+                    const int idx = (gbase + (valid ? row : lo)) & R1;
+                    const uint32_t rr = rec_s + (uint32_t)(idx * rstride);
+                    float tot = 0.f, off = 0.f;
+                    if (valid) {
+                        if (dt == Q4_K) {
+#pragma unroll 8
+                            for (int k = 0; k < nb; k++) {
+                                const uint4 v = lds128(rr + 16 * k);
+                                tot = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y), tot);
+                                off = __fmaf_rn(__uint_as_float(v.z), __uint_as_float(v.w), off);
+                            }
+                        } else {
+#pragma unroll 8
+                            for (int k = 0; k < nb; k++) {
+                                const uint4 v = lds128(rr + 16 * k);
+                                tot = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y), tot);
+                            }
+                        }
+                    }
+                    const bool refused = valid && (bad[idx] != 0 || !act_ok);
+                    if (valid) bad[idx] = 0;
+                    const int orow = r0 + row;
+                    if (valid && !refused && !failed) {
+                        float r = __fsub_rn(tot, off);
+                        if (sg.bias) r = __fadd_rn(r, sg.bias[orow]);
+                        if (sg.res) r = __fadd_rn(sg.res[orow], r);
+                        sg.y[orow] = r;
+                        for (int k = 0; k < (p.put.N > 1 ? p.put.N : 0); k++)
+                            peer_ptr<float>(p.put, k, p.put.off)[p.put.col0 + orow] = r;
+                    }
+                    // rows whose weights or activations the 8-bit kernel refuses: f32 product
+                    unsigned rm = __ballot_sync(FULL, refused && !failed);
+                    while (rm) {
+                        const int i = __ffs(rm) - 1;
+                        rm &= rm - 1;
+                        const int frow = r0 + t0 + i;
+                        float r = row_dot_f32(dt, sg.w + (long long)frow * rb, p.x, nb);
+                        if (sg.bias) r = __fadd_rn(r, sg.bias[frow]);
+                        if (sg.res) r = __fadd_rn(sg.res[frow], r);
+                        if (lane == 0) {
+                            sg.y[frow] = r;
+                            for (int k = 0; k < (p.put.N > 1 ? p.put.N : 0); k++)
+                                peer_ptr<float>(p.put, k, p.put.off)[p.put.col0 + frow] = r;
+                        }
+                    }
+                }
+                lo = hi;
+            }
+            gbase += nr;
+        }
+        if (p.put.N > 1) {
+            // the peer stores are visible system-wide before the kernel ends
+            // (the next kernel on this stream publishes the exchange)
+            __syncwarp();
+            if (lane == 0) __threadfence_system();
+        }
+        return;
+    }
+
+    // ---------------------------------------------------- consumer warps
+    const uint32_t act_s = smem_u32(smem + p.off_act), hdr_s = smem_u32(smem + p.off_hdr);
+    const uint32_t ys_s = smem_u32(smem + p.off_ys), ring_s = smem_u32(smem + p.off_ring);
+    const int h = lane & 1;
+    int n = 0, gbase = 0;
+    for (int s = 0; s < p.nseg; s++) {
+        const GemvSeg &sg = p.seg[s];
+        int r0, nr;
+        slab(sg.n, cta, G, r0, nr);
+        const int dt = sg.dt;
+        const int nblk = nr * nb;  // < 2^24 (gemv_row_ok)
+        // this lane's block within every stage
+        const int blk = dt == Q4_K ? 16 * warp + (lane >> 1) : 8 * (16 * (warp >> 3) + (lane >> 1)) + (warp & 7);
+        const int bb = dt == Q4_K ? 144 : 210;
+        for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
+            const int slot = n % p.slots;
+            if (!failed && !mbar_wait_bounded(&full[slot], (n / p.slots) & 1, p.status)) failed = true;
+            failed = __any_sync(FULL, failed);
+            const int g = k0 + blk;
+            const bool active = !failed && g < nblk;
+            int S = 0, M = 0, row = 0, kb = 0;
+            uint32_t dh = 0, mh = 0;
+            float dx = 0.f;
+            if (active) {
+                // row and block of the slab's block g (g < 2^24: the float quotient is off by at most one)
+                row = (int)((float)g * p.inv_nb);
+                kb = g - row * nb;
+                if (kb < 0) {
+                    row--;
+                    kb += nb;
+                } else if (kb >= nb) {
+                    row++;
+                    kb -= nb;
+                }
+                const uint32_t ba = ring_s + (uint32_t)(slot * p.slot_bytes + blk * bb);
+                const uint32_t ya = act_s + (uint32_t)act_off(kb, h);
+                if (dt == Q4_K) {
+                    q4k_half(ba, h, ya, hdr_s + (uint32_t)((2 * kb + h) * 16), S, M, dh, mh, dx);
+                } else {
+                    const uint32_t ysa = ys_s + (uint32_t)((2 * kb + h) * 16);
+                    switch ((warp & 7) >> 1) {
+                    case 0: q6k_half<0>(ba, h, ya, ysa, S, dh); break;
+                    case 1: q6k_half<1>(ba, h, ya, ysa, S, dh); break;
+                    case 2: q6k_half<2>(ba, h, ya, ysa, S, dh); break;
+                    default: q6k_half<3>(ba, h, ya, ysa, S, dh); break;
+                    }
+                    dx = __uint_as_float(lds128(hdr_s + (uint32_t)((2 * kb + h) * 16)).z);
+                }
+            }
+            S += __shfl_xor_sync(FULL, S, 1);
+            M += __shfl_xor_sync(FULL, M, 1);
+            if (active && h == 0) {
+                const int idx = (gbase + row) & R1;
+                const float d = f16f(dh);
+                float fm = 0.f, pm = 0.f;
+                bool nf = !f16_finite(dh);
+                if (dt == Q4_K) {
+                    fm = __int2float_rn(M);
+                    pm = __fmul_rn(f16f(mh), dx);
+                    nf |= !f16_finite(mh);
+                }
+                sts128(rec_s + (uint32_t)(idx * rstride + kb * 16), __float_as_uint(__int2float_rn(S)),
+                       __float_as_uint(__fmul_rn(d, dx)), __float_as_uint(fm), __float_as_uint(pm));
+                if (nf) bad[idx] = 1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&cons[slot]);
+        }
+        gbase += nr;
+    }
+}
+
+struct RowPlan {
+    int lr, slots, slot_bytes, smem;
+    int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
+};
+
+bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
+    if (K % 256 || K <= 0 || K > (1LL << 20)) return false;
+    const int nb = (int)(K / 256);
+    int maxbb = 0;
+    for (int i = 0; i < nseg; i++) maxbb = max(maxbb, block_bytes(segs[i].dt));
+    auto al = [](int v, int a) { return (v + a - 1) / a * a; };
+    pl.slot_bytes = kSB * maxbb;
+    for (int slots = kMaxSlots; slots >= 3; slots--) {
+        // rows with records outstanding: the consumers run at most `slots`
+        // stages ahead of the stage whose rows the chain warp finishes, a
+        // row may start before that stage, and one more is partial
+        const int need = (slots + 1) * kSB / nb + 3;
+        pl.lr = 0;
+        while ((1 << pl.lr) < need) pl.lr++;
+        int o = 256;  // barriers and flags
+        pl.off_act = o;
+        o = al(o + act_bytes(nb), 16);
+        pl.off_hdr = o;
+        o += 2 * nb * 16;
+        pl.off_ys = o;
+        o += 2 * nb * 16;
+        pl.off_rec = o;
+        o += (1 << pl.lr) * (nb + 1) * 16;
+        pl.off_bad = o;
+        o = al(o + (1 << pl.lr), 128);
+        pl.off_ring = o;
+        pl.slots = slots;
+        pl.smem = o + slots * pl.slot_bytes;
+        if (pl.smem <= kSmemMax) return true;
+    }
+    return false;
+}
+
+cudaError_t prepare_row() {
+    static bool done = false;
+    if (done) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(gemv_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    if (e == cudaSuccess) done = true;
+    return e;
+}
+
+}  // namespace
+
+bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
+    if (nseg <= 0 || nseg > kMaxSegs) return false;
+    if (((uintptr_t)act.q & 15) || ((uintptr_t)act.ys & 15) || ((uintptr_t)act.xs & 7)) return false;
+    for (int i = 0; i < nseg; i++) {
+        if (segs[i].dt != Q4_K && segs[i].dt != Q6_K) return false;
+        if (row_bytes(segs[i].dt, K) % 16 || ((uintptr_t)segs[i].w & 15)) return false;
+    }
+    RowPlan pl;
+    if (!plan_row(segs, nseg, K, pl)) return false;
+    // a CTA's slab of blocks indexes below 2^24 (exact float quotients)
+    const long long per = (long long)(segs[0].n / num_sms() + 1) * (K / 256);
+    for (int i = 1; i < nseg; i++)
+        if ((long long)(segs[i].n / num_sms() + 1) * (K / 256) >= (1LL << 24)) return false;
+    return per < (1LL << 24);
+}
+
+cudaError_t gemv_row_prepare() { return prepare_row(); }
+
+cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,
+                            cudaStream_t st, bool pdl, const P2P *put) {
+    RowPlan pl;
+    if (!plan_row(segs, nseg, K, pl)) return cudaErrorInvalidValue;
+    cudaError_t e = prepare_row();
+    if (e != cudaSuccess) return e;
+    RowParams p = {};
+    for (int i = 0; i < nseg; i++) p.seg[i] = segs[i];
+    p.nseg = nseg;
+    p.x = x;
+    p.act = act;
+    p.K = K;
+    p.nb = (int)(K / 256);
+    p.inv_nb = 1.0f / (float)p.nb;
+    p.lr = pl.lr;
+    p.slots = pl.slots;
+    p.slot_bytes = pl.slot_bytes;
+    p.off_act = pl.off_act;
+    p.off_hdr = pl.off_hdr;
+    p.off_ys = pl.off_ys;
+    p.off_rec = pl.off_rec;
+    p.off_bad = pl.off_bad;
+    p.off_ring = pl.off_ring;
+    if (put) p.put = *put;
+    p.status = status;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)pl.smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_row_kernel, p);
+}
+
+}  // namespace mimgpu

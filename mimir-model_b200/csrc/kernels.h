@@ -81,6 +81,13 @@ bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, lo
 cudaError_t gemm_a8_tc_prepare();
 cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
                               unsigned *status, cudaStream_t st, bool pdl);
+// The one-activation-row product (decode steps): one slab of consecutive
+// rows per SM, streamed with bulk copies; launch_gemv_a8 dispatches to it
+// when every matrix's rows are 16-byte multiples.  Same results bit for bit.
+bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K);
+cudaError_t gemv_row_prepare();
+cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,
+                            cudaStream_t st, bool pdl, const P2P *put);
 // dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
 cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
                             cudaStream_t st, bool pdl);

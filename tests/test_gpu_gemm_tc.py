@@ -130,3 +130,26 @@ def test_prompt_rows_equal_single_token_steps(ctx):
     a.free()
     b.free()
     m.free()
+
+
+@pytest.mark.parametrize("H,Hkv,T", [(64, 8, 37), (32, 8, 9), (16, 16, 21)])
+def test_prompt_attention_group_shapes(ctx, H, Hkv, T):
+    """The many-row prompt attention for other head groupings (G = 8 as in the
+    70B shape, G = 4, G = 1) and prompt lengths that leave a partial tile:
+    the prompt's logits equal the one-token steps' bit for bit."""
+    import mimgpu
+    from test_gpu_model import _synthetic
+    E = H * 128
+    cfg, w = _synthetic(2, E, H, Hkv, 512, 1024)
+    C = 64
+    prompt = np.random.default_rng(H + T).integers(0, cfg["vocab"], T).astype(np.int32)
+    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=T), w)
+    a = m.session()
+    together = a.run(prompt, np.arange(T), all_rows=True)
+    b = m.session()
+    for i in range(T):
+        one = b.run(prompt[i:i + 1], np.arange(i, i + 1))[0]
+        assert np.array_equal(bits(one), bits(together[i])), i
+    a.free()
+    b.free()
+    m.free()

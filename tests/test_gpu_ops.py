@@ -125,6 +125,43 @@ def test_a8_edge_cases(ctx, dt):
     t.free()
 
 
+@pytest.mark.parametrize("dt,n,k,inf", [(O.Q4_K, 12288, 4096, False), (O.Q6_K, 4096, 14336, False),
+                                         (O.Q6_K, 9000, 2048, False), (O.Q4_K, 150, 256, False),
+                                         (O.Q6_K, 100, 4096, False), (O.Q4_K, 3000, 4096, True)])
+def test_a8_one_row_slabs(ctx, dt, n, k, inf):
+    """One activation row (the slab-streaming kernel): matrices whose per-SM
+    slabs span several stages and several batches of row records, fewer rows
+    than SMs, and weight rows with a non-finite block scale in different
+    batches.  Exact rows equal the oracle bit for bit; refused rows (and a
+    refused activation row) equal the multi-row kernel's f32 product."""
+    bb = 144 if dt == O.Q4_K else 210
+    rb = k // 256 * bb
+    w = bytearray(_weights(dt, n, k, 4242 + n).tobytes())
+    refused = sorted(r for r in {5, 70, n // 2 + 1, n - 1} if r < n)
+    for r in refused:
+        o = r * rb + (k // 256 - 1) * bb  # the row's last block
+        if dt == O.Q4_K:
+            w[o + 2:o + 4] = bytes([0x00, 0x7C])
+        else:
+            w[o + 208:o + 210] = bytes([0x00, 0x7E])
+    w = np.frombuffer(bytes(w), np.uint8)
+    x = O.gen_normal(11, 2 * k).reshape(2, k)
+    if inf:
+        x[0, 17] = np.inf
+    x[1] = x[0]
+    bias = O.gen_normal(4, n)
+    t = ctx.upload(dt, (n, k), w)
+    one = ctx.dequant_matmul(x[:1], t, bias, a8_block=256)
+    two = ctx.dequant_matmul(x, t, bias, a8_block=256)
+    assert np.array_equal(bits(one[0]), bits(two[0]))
+    if not inf:
+        want = O.dequant_matmul_a8(x[:1], dt, w, n, bias)
+        exact = np.ones(n, bool)
+        exact[refused] = False
+        assert np.array_equal(bits(one[0][exact]), bits(want[0][exact]))
+    t.free()
+
+
 def test_a8_batch_invariance(ctx):
     """interp/transformer_test.go:297-354: each row's result is the same bits
     alone as in any batch."""
