@@ -89,6 +89,11 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)((
 // or blocks 8 apart (Q6_K).
 __host__ __device__ __forceinline__ int act_off(int kb, int h) { return kb * 288 + (kb >> 3) * 32 + h * 144; }
 __host__ __device__ __forceinline__ int act_bytes(int nb) { return act_off(nb, 0) + 32; }
+// Byte offset of the 16-byte per-half entries (headers, sums of 16) of half
+// hb = 2kb + h: two spare entries every 16 make the lanes of a quarter-warp
+// hit distinct banks in both block orders, as in act_off.
+__host__ __device__ __forceinline__ int hdr_off(int hb) { return (hb + ((hb >> 4) << 1)) * 16; }
+__host__ __device__ __forceinline__ int hdr_bytes(int nb) { return hdr_off(2 * nb) + 32; }
 
 // Rows [r0, r0 + nr) of an n-row matrix for CTA b of G.
 __device__ __forceinline__ void slab(int n, int b, int G, int &r0, int &nr) {
@@ -262,8 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
             const uint2 xs = *(const uint2 *)(p.act.xs + kb * 8 + 4 * h);
             const float dx = p.act.dx[kb];
             const int okb = p.act.ok[kb];
-            *(uint4 *)(smem + p.off_hdr + hb * 16) = make_uint4(xs.x, xs.y, __float_as_uint(dx), (unsigned)okb);
-            *(uint4 *)(smem + p.off_ys + hb * 16) = *(const uint4 *)(p.act.ys + kb * 16 + 8 * h);
+            *(uint4 *)(smem + p.off_hdr + hdr_off(hb)) = make_uint4(xs.x, xs.y, __float_as_uint(dx), (unsigned)okb);
+            *(uint4 *)(smem + p.off_ys + hdr_off(hb)) = *(const uint4 *)(p.act.ys + kb * 16 + 8 * h);
             if (!okb) misc[0] = 0;  // a row is quantized when every one of its blocks is (q8.go:50-97)
         }
         for (int i = tid; i < (1 << p.lr); i += kCT) smem[p.off_bad + i] = 0;
@@ -397,16 +402,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                 const uint32_t ba = ring_s + (uint32_t)(slot * p.slot_bytes + blk * bb);
                 const uint32_t ya = act_s + (uint32_t)act_off(kb, h);
                 if (dt == Q4_K) {
-                    q4k_half(ba, h, ya, hdr_s + (uint32_t)((2 * kb + h) * 16), S, M, dh, mh, dx);
+                    q4k_half(ba, h, ya, hdr_s + (uint32_t)hdr_off(2 * kb + h), S, M, dh, mh, dx);
                 } else {
-                    const uint32_t ysa = ys_s + (uint32_t)((2 * kb + h) * 16);
+                    const uint32_t ysa = ys_s + (uint32_t)hdr_off(2 * kb + h);
                     switch ((warp & 7) >> 1) {
                     case 0: q6k_half<0>(ba, h, ya, ysa, S, dh); break;
                     case 1: q6k_half<1>(ba, h, ya, ysa, S, dh); break;
                     case 2: q6k_half<2>(ba, h, ya, ysa, S, dh); break;
                     default: q6k_half<3>(ba, h, ya, ysa, S, dh); break;
                     }
-                    dx = __uint_as_float(lds128(hdr_s + (uint32_t)((2 * kb + h) * 16)).z);
+                    dx = __uint_as_float(lds128(hdr_s + (uint32_t)hdr_off(2 * kb + h)).z);
                 }
             }
             S += __shfl_xor_sync(FULL, S, 1);
@@ -455,9 +460,9 @@ bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
         pl.off_act = o;
         o = al(o + act_bytes(nb), 16);
         pl.off_hdr = o;
-        o += 2 * nb * 16;
+        o += hdr_bytes(nb);
         pl.off_ys = o;
-        o += 2 * nb * 16;
+        o += hdr_bytes(nb);
         pl.off_rec = o;
         o += (1 << pl.lr) * (nb + 1) * 16;
         pl.off_bad = o;
