@@ -10,26 +10,27 @@
 // interp/fast.go:282-379) take the f32 product of a8_refused.cuh.
 //
 // Work decomposition: one CTA per SM: a producer thread, 16 consumer warps
-// and a chain warp.
+// and two chain warps.
 //  * Every matrix of the launch is cut into gridDim.x slabs of consecutive
 //    rows, one per CTA, so each SM streams the same number of bytes (within
 //    one row).  Rows are 16-byte multiples, so a slab is one contiguous byte
-//    range; the producer streams it in stages of 256 blocks, one
-//    cp.async.bulk per stage, into a ring of 3 to 8 stages.  It starts
-//    before the previous kernel has finished (weights are read-only).
-//  * The 512 half-blocks of a stage go one to each consumer lane: Q4_K
-//    warps take 16 consecutive blocks, Q6_K warps the blocks 8i + (warp % 8)
-//    so that a warp's 210-byte blocks share their 16-byte phase.  The two
+//    range; the producer streams it in stages of whole rows (the largest
+//    multiple of the row's block count up to 256 blocks), one cp.async.bulk
+//    per stage, into a ring of 3 to 8 data slots.  It starts before the
+//    previous kernel has finished (weights are read-only), and refills a
+//    slot as soon as the consumers have read it.
+//  * The half-blocks of a stage go one to each consumer lane: Q4_K warps take
+//    16 consecutive blocks, Q6_K warps the blocks 8i + (warp % 8) so that a
+//    warp's 210-byte blocks share their 16-byte phase.  A stage holds whole
+//    rows, so a lane meets the same block column in every stage.  The two
 //    lanes of a block add their exact sums with one shuffle; the even lane
-//    stores the block's (float(S), d*dx, float(M), dmin*dx) in a table of
-//    per-row records.
-//  * Records live in two halves, one per batch of rows.  Once every consumer
-//    warp is done with a batch (a per-batch counter in shared memory), the
-//    chain warp runs each row's chain over its records in block order (one
-//    row per lane) and stores the result (bias, residual, copies into the
-//    tensor-parallel peers); refused rows take the warp's f32 product.  The
-//    consumers overwrite a half only after the chain warp has published
-//    that it is done with it, and never stop for the chain.
+//    stores the block's (float(S), d*dx, float(M), dmin*dx) in a ring of
+//    per-row records with its own stages, separate from the data slots.
+//  * Chain warp c takes the record stages c, c + 2, ...: the block-ordered
+//    chain over each row's records (one row per lane), bias, residual,
+//    stores (and copies into the tensor-parallel peers); refused rows take
+//    the warp's f32 product.  The consumers reuse a record stage only after
+//    its chain warp is done with it; the data stream never waits for a chain.
 // The activation row sits in shared memory in a layout that puts the lanes
 // of a quarter-warp on distinct banks for both block orders.
 #include <cstdint>
@@ -45,8 +46,9 @@ namespace {
 
 constexpr int kCW = 16;               // consumer warps
 constexpr int kCT = kCW * 32;         // consumer threads
-constexpr int kThreads = kCT + 64;    // + the producer warp and the chain warp
-constexpr int kSB = 256;              // blocks per stage (two lanes per block)
+constexpr int kNC = 2;                // chain warps
+constexpr int kThreads = kCT + 32 + 32 * kNC;  // + the producer warp and the chain warps
+constexpr int kMaxSB = 256;           // blocks per stage at most (two lanes per block)
 constexpr int kMaxSlots = 8;
 constexpr int kSmemMax = 227 * 1024;
 constexpr unsigned FULL = 0xffffffffu;
@@ -58,8 +60,8 @@ struct RowParams {
     ActQ8 act;
     long long K;
     int nb;             // blocks per row
-    float inv_nb;
-    int lr;             // rows in the record ring = 1 << lr
+    int sb;             // blocks per stage: whole rows
+    int rstages;        // stages of rows in the record ring
     int slots, slot_bytes;
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
     P2P put;
@@ -204,17 +206,21 @@ __device__ __forceinline__ void q6k_half(uint32_t blk, int h, uint32_t ya, uint3
 
 __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_constant__ RowParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = (uint64_t *)smem;       // stage landed (producer's bytes)
-    uint64_t *cons = full + kMaxSlots;       // stage consumed (16 consumer warps)
-    uint64_t *empty = cons + kMaxSlots;      // stage released by the chain warp
-    int *misc = (int *)(smem + 3 * kMaxSlots * 8);  // [0] activation row quantized
+    uint64_t *full = (uint64_t *)smem;       // data slot landed (producer's bytes)
+    uint64_t *cons = full + kMaxSlots;       // data slot read by the 16 consumer warps
+    uint64_t *rdone = cons + kMaxSlots;      // record stage written by the 16 consumer warps
+    uint64_t *rfree = rdone + kMaxSlots;     // record stage finished by its chain warp
+    int *misc = (int *)(smem + 4 * kMaxSlots * 8);  // [0] activation row quantized
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, cta = blockIdx.x, nb = p.nb;
+    const int G = gridDim.x, cta = blockIdx.x, nb = p.nb, sb = p.sb, rps = sb / nb, RS = p.rstages;
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.slots; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&cons[s], kCW);
-            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < RS; s++) {
+            mbar_init(&rdone[s], kCW);
+            mbar_init(&rfree[s], 1);
         }
         misc[0] = 1;
         fence_barrier_init();
@@ -226,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         // ------------------------------------------------ producer (one thread)
         if (lane != 0) return;
         uint8_t *ring = smem + p.off_ring;
-        int n = 0;
+        int n = 0, slot = 0, ph = 0;
         bool ok = true;
         for (int s = 0; s < p.nseg && ok; s++) {
             int r0, nr;
@@ -234,15 +240,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
             const int bb = block_bytes(p.seg[s].dt);
             const int nblk = nr * nb;
             const uint8_t *src = p.seg[s].w + (long long)r0 * nb * bb;
-            for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
-                const int slot = n % p.slots;
-                if (n >= p.slots && !mbar_wait_bounded(&empty[slot], ((n / p.slots) - 1) & 1, p.status)) {
+            for (int k0 = 0; k0 < nblk; k0 += sb, n++) {
+                // slot reuse: the consumers are done with the stage p.slots back
+                if (n >= p.slots && !mbar_wait_bounded(&cons[slot], ph ^ 1, p.status)) {
                     ok = false;
                     break;
                 }
-                const uint32_t bytes = (uint32_t)(min(kSB, nblk - k0) * bb);
+                const uint32_t bytes = (uint32_t)(min(sb, nblk - k0) * bb);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 bulk_g2s(ring + (size_t)slot * p.slot_bytes, src + (long long)k0 * bb, bytes, &full[slot]);
+                if (++slot == p.slots) {
+                    slot = 0;
+                    ph ^= 1;
+                }
             }
         }
         // copies still in flight land before the block exits
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         return;
     }
 
-    // ------------------------------------------- consumers and the chain warp
+    // ------------------------------------------- consumers and the chain warps
     const int tid = threadIdx.x;
     pdl_wait();
     if (warp < kCW) {
@@ -271,54 +281,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
             *(uint4 *)(smem + p.off_ys + hdr_off(hb)) = *(const uint4 *)(p.act.ys + kb * 16 + 8 * h);
             if (!okb) misc[0] = 0;  // a row is quantized when every one of its blocks is (q8.go:50-97)
         }
-        for (int i = tid; i < (1 << p.lr); i += kCT) smem[p.off_bad + i] = 0;
+        for (int i = tid; i < RS * rps; i += kCT) smem[p.off_bad + i] = 0;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kCT + 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(kCT + 32 * kNC) : "memory");
     const bool act_ok = misc[0] != 0;
-    const int R1 = (1 << p.lr) - 1, rstride = (nb + 1) * 16;  // record rows padded by 16 bytes: no bank conflicts
+    const int rstride = (nb + 1) * 16;  // record rows padded by 16 bytes: no bank conflicts
     const uint32_t rec_s = smem_u32(smem + p.off_rec);
-    uint8_t *bad = smem + p.off_bad;  // [R] rows with a non-finite block scale
+    uint8_t *bad = smem + p.off_bad;  // [RS * rps] rows with a non-finite block scale
     bool failed = false;              // a wait gave up: skip the work, keep the protocol
 
-    if (warp == kCW + 1) {
-        // ------------------------------------------------ chain warp
-        // After the consumers are done with stage n it releases the slot to
-        // the producer, then finishes the rows whose last block was in the
-        // stage: the block-ordered chain (one row per lane), bias, residual,
-        // stores; refused rows take the warp's f32 product.
-        int n = 0, gbase = 0;
+    if (warp > kCW) {
+        // ------------------------------------------------ chain warps
+        // Chain warp c takes the record stages m = c (mod kNC): once the
+        // consumers have written them, the block-ordered chain of each row
+        // (one row per lane), bias, residual, stores; refused rows take the
+        // warp's f32 product.  Then the record stage is free again.
+        const int c = warp - kCW - 1;
+        int m = 0;
         for (int s = 0; s < p.nseg; s++) {
             const GemvSeg &sg = p.seg[s];
             int r0, nr;
             slab(sg.n, cta, G, r0, nr);
             const int dt = sg.dt;
-            const int nblk = nr * nb;
             const long long rb = row_bytes(dt, p.K);
-            int lo = 0;  // first row not finished
-            for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
-                const int slot = n % p.slots;
-                if (!failed && !mbar_wait_bounded(&cons[slot], (n / p.slots) & 1, p.status)) failed = true;
+            for (int lo = 0; lo < nr; lo += rps, m++) {
+                if (m % kNC != c) continue;
+                const int rs = m % RS;
+                if (!failed && !mbar_wait_bounded(&rdone[rs], (m / RS) & 1, p.status)) failed = true;
                 failed = __any_sync(FULL, failed);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-                const int done = min(nblk, k0 + kSB);
-                const int hi = done == nblk ? nr : done / nb;  // rows complete after this stage
+                const int hi = min(nr, lo + rps);  // the stage's rows
                 for (int t0 = lo; t0 < hi; t0 += 32) {
                     const int row = t0 + lane;
                     const bool valid = row < hi;
-                    const int idx = (gbase + (valid ? row : lo)) & R1;
+                    const int idx = rs * rps + (valid ? row - lo : 0);
                     const uint32_t rr = rec_s + (uint32_t)(idx * rstride);
                     float tot = 0.f, off = 0.f;
                     if (valid) {
                         if (dt == Q4_K) {
-#pragma unroll 8
+#pragma unroll 16
                             for (int k = 0; k < nb; k++) {
                                 const uint4 v = lds128(rr + 16 * k);
                                 tot = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y), tot);
                                 off = __fmaf_rn(__uint_as_float(v.z), __uint_as_float(v.w), off);
                             }
                         } else {
-#pragma unroll 8
+#pragma unroll 16
                             for (int k = 0; k < nb; k++) {
                                 const uint4 v = lds128(rr + 16 * k);
                                 tot = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y), tot);
@@ -352,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                         }
                     }
                 }
-                lo = hi;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rfree[rs]);  // the record stage is free again
             }
-            gbase += nr;
         }
         if (p.put.N > 1) {
             // the peer stores are visible system-wide before the kernel ends
@@ -369,55 +376,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
     const uint32_t act_s = smem_u32(smem + p.off_act), hdr_s = smem_u32(smem + p.off_hdr);
     const uint32_t ys_s = smem_u32(smem + p.off_ys), ring_s = smem_u32(smem + p.off_ring);
     const int h = lane & 1;
-    int n = 0, gbase = 0;
+    int m = 0, slot = 0, ph = 0, rs = 0, rph = 0;
     for (int s = 0; s < p.nseg; s++) {
         const GemvSeg &sg = p.seg[s];
         int r0, nr;
         slab(sg.n, cta, G, r0, nr);
         const int dt = sg.dt;
-        const int nblk = nr * nb;  // < 2^24 (gemv_row_ok)
-        // this lane's block within every stage
+        // this lane's block of every stage: the same column of every stage's rows
         const int blk = dt == Q4_K ? 16 * warp + (lane >> 1) : 8 * (16 * (warp >> 3) + (lane >> 1)) + (warp & 7);
+        const bool lane_on = blk < sb;
+        const int roff = blk / nb, kb = blk - roff * nb;
         const int bb = dt == Q4_K ? 144 : 210;
-        for (int k0 = 0; k0 < nblk; k0 += kSB, n++) {
-            const int slot = n % p.slots;
-            if (!failed && !mbar_wait_bounded(&full[slot], (n / p.slots) & 1, p.status)) failed = true;
+        const uint32_t ya = act_s + (uint32_t)act_off(lane_on ? kb : 0, h);
+        const uint32_t ha = (uint32_t)hdr_off(2 * (lane_on ? kb : 0) + h);
+        for (int row0 = 0; row0 < nr; row0 += rps, m++) {
+            if (!failed && !mbar_wait_bounded(&full[slot], ph, p.status)) failed = true;
+            // the record stage this one reuses has been chained
+            if (!failed && m >= RS && !mbar_wait_bounded(&rfree[rs], rph ^ 1, p.status)) failed = true;
             failed = __any_sync(FULL, failed);
-            const int g = k0 + blk;
-            const bool active = !failed && g < nblk;
-            int S = 0, M = 0, row = 0, kb = 0;
+            const int row = row0 + roff;
+            const bool active = !failed && lane_on && row < nr;
+            int S = 0, M = 0;
             uint32_t dh = 0, mh = 0;
             float dx = 0.f;
             if (active) {
-                // row and block of the slab's block g (g < 2^24: the float quotient is off by at most one)
-                row = (int)((float)g * p.inv_nb);
-                kb = g - row * nb;
-                if (kb < 0) {
-                    row--;
-                    kb += nb;
-                } else if (kb >= nb) {
-                    row++;
-                    kb -= nb;
-                }
                 const uint32_t ba = ring_s + (uint32_t)(slot * p.slot_bytes + blk * bb);
-                const uint32_t ya = act_s + (uint32_t)act_off(kb, h);
                 if (dt == Q4_K) {
-                    q4k_half(ba, h, ya, hdr_s + (uint32_t)hdr_off(2 * kb + h), S, M, dh, mh, dx);
+                    q4k_half(ba, h, ya, hdr_s + ha, S, M, dh, mh, dx);
                 } else {
-                    const uint32_t ysa = ys_s + (uint32_t)hdr_off(2 * kb + h);
                     switch ((warp & 7) >> 1) {
-                    case 0: q6k_half<0>(ba, h, ya, ysa, S, dh); break;
-                    case 1: q6k_half<1>(ba, h, ya, ysa, S, dh); break;
-                    case 2: q6k_half<2>(ba, h, ya, ysa, S, dh); break;
-                    default: q6k_half<3>(ba, h, ya, ysa, S, dh); break;
+                    case 0: q6k_half<0>(ba, h, ya, ys_s + ha, S, dh); break;
+                    case 1: q6k_half<1>(ba, h, ya, ys_s + ha, S, dh); break;
+                    case 2: q6k_half<2>(ba, h, ya, ys_s + ha, S, dh); break;
+                    default: q6k_half<3>(ba, h, ya, ys_s + ha, S, dh); break;
                     }
-                    dx = __uint_as_float(lds128(hdr_s + (uint32_t)hdr_off(2 * kb + h)).z);
+                    dx = __uint_as_float(lds128(hdr_s + ha).z);
                 }
             }
             S += __shfl_xor_sync(FULL, S, 1);
             M += __shfl_xor_sync(FULL, M, 1);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&cons[slot]);  // the data slot goes back to the producer
             if (active && h == 0) {
-                const int idx = (gbase + row) & R1;
+                const int idx = rs * rps + roff;
                 const float d = f16f(dh);
                 float fm = 0.f, pm = 0.f;
                 bool nf = !f16_finite(dh);
@@ -431,47 +432,56 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                 if (nf) bad[idx] = 1;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&cons[slot]);
+            if (lane == 0) mbar_arrive(&rdone[rs]);
+            if (++slot == p.slots) {
+                slot = 0;
+                ph ^= 1;
+            }
+            if (++rs == RS) {
+                rs = 0;
+                rph ^= 1;
+            }
         }
-        gbase += nr;
     }
 }
 
 struct RowPlan {
-    int lr, slots, slot_bytes, smem;
+    int sb, rstages, slots, slot_bytes, smem;
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
 };
 
 bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
-    if (K % 256 || K <= 0 || K > (1LL << 20)) return false;
+    if (K % 256 || K <= 0 || K / 256 > kMaxSB) return false;
     const int nb = (int)(K / 256);
     int maxbb = 0;
     for (int i = 0; i < nseg; i++) maxbb = max(maxbb, block_bytes(segs[i].dt));
+    pl.sb = kMaxSB / nb * nb;  // whole rows
+    const int rps = pl.sb / nb;
     auto al = [](int v, int a) { return (v + a - 1) / a * a; };
-    pl.slot_bytes = kSB * maxbb;
-    for (int slots = kMaxSlots; slots >= 3; slots--) {
-        // rows with records outstanding: the consumers run at most `slots`
-        // stages ahead of the stage whose rows the chain warp finishes, a
-        // row may start before that stage, and one more is partial
-        const int need = (slots + 1) * kSB / nb + 3;
-        pl.lr = 0;
-        while ((1 << pl.lr) < need) pl.lr++;
-        int o = 256;  // barriers and flags
-        pl.off_act = o;
-        o = al(o + act_bytes(nb), 16);
-        pl.off_hdr = o;
-        o += hdr_bytes(nb);
-        pl.off_ys = o;
-        o += hdr_bytes(nb);
-        pl.off_rec = o;
-        o += (1 << pl.lr) * (nb + 1) * 16;
-        pl.off_bad = o;
-        o = al(o + (1 << pl.lr), 128);
-        pl.off_ring = o;
-        pl.slots = slots;
-        pl.smem = o + slots * pl.slot_bytes;
-        if (pl.smem <= kSmemMax) return true;
-    }
+    pl.slot_bytes = pl.sb * maxbb;
+    int o = 512;  // barriers and flags
+    pl.off_act = o;
+    o = al(o + act_bytes(nb), 16);
+    pl.off_hdr = o;
+    o += hdr_bytes(nb);
+    pl.off_ys = o;
+    o += hdr_bytes(nb);
+    pl.off_rec = o;
+    const int fixed = o, rec_stage = rps * (nb + 1) * 16;
+    // the most data slots first (3 at least), then the most record stages (2 at least)
+    for (int slots = kMaxSlots; slots >= 3; slots--)
+        for (int rst = kMaxSlots; rst >= 2; rst--) {
+            int e = fixed + rst * rec_stage;
+            pl.off_bad = e;
+            e = al(e + rst * rps, 128);
+            pl.off_ring = e;
+            pl.smem = e + slots * pl.slot_bytes;
+            if (pl.smem <= kSmemMax) {
+                pl.slots = slots;
+                pl.rstages = rst;
+                return true;
+            }
+        }
     return false;
 }
 
@@ -493,12 +503,7 @@ bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
         if (row_bytes(segs[i].dt, K) % 16 || ((uintptr_t)segs[i].w & 15)) return false;
     }
     RowPlan pl;
-    if (!plan_row(segs, nseg, K, pl)) return false;
-    // a CTA's slab of blocks indexes below 2^24 (exact float quotients)
-    const long long per = (long long)(segs[0].n / num_sms() + 1) * (K / 256);
-    for (int i = 1; i < nseg; i++)
-        if ((long long)(segs[i].n / num_sms() + 1) * (K / 256) >= (1LL << 24)) return false;
-    return per < (1LL << 24);
+    return plan_row(segs, nseg, K, pl);
 }
 
 cudaError_t gemv_row_prepare() { return prepare_row(); }
@@ -516,8 +521,8 @@ cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8
     p.act = act;
     p.K = K;
     p.nb = (int)(K / 256);
-    p.inv_nb = 1.0f / (float)p.nb;
-    p.lr = pl.lr;
+    p.sb = pl.sb;
+    p.rstages = pl.rstages;
     p.slots = pl.slots;
     p.slot_bytes = pl.slot_bytes;
     p.off_act = pl.off_act;
