@@ -45,7 +45,7 @@ CFG70B = dict(layers=80, embed=8192, ffn=28672, heads=64, kv_heads=8, head_dim=1
               rope_theta=500000.0, norm_eps=1e-5)
 SHAPES = {"8b": CFG8B, "70b": CFG70B}
 PROMPT = 128
-GEMV_TRAFFIC_PER_ALGO_BYTE = (66_130_944 + 483_584) / 66_179_904
+GEMV_TRAFFIC_PER_ALGO_BYTE = (66_120_960 + 338_944) / 66_179_904
 
 
 def layout(cfg):
@@ -315,8 +315,8 @@ def run_gpu(args):
     peak, peak_kind = peaks()
     achieved = bpl / spl / 1e9
     # DRAM bytes per algorithmic byte of the GEMV from one ncu capture (the
-    # 28672 x 4096 Q4_K launch: 66.13 MB read + 0.48 MB written for
-    # 66.18 MB algorithmic), applied to this run's bytes per launch
+    # 28672 x 4096 Q4_K launch of gemv_row_kernel: 66.12 MB read + 0.34 MB
+    # written for 66.18 MB algorithmic), applied to this run's bytes per launch
     traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
     wpt = weight_bytes_per_token(cfg)
     ms = dev_s / args.steps * 1e3
@@ -344,7 +344,7 @@ def run_gpu(args):
                 "api": "mimgpu_session_run (pinned host token/position in, logits out, host argmax)"},
         "step_roofline": {"bound": "hbm", "bytes_per_token": wpt, "achieved": round(wpt / (ms / 1e3) / 1e9, 1),
                           "peak": peak, "unit": "GB/s", "frac": round(wpt / (ms / 1e3) / 1e9 / peak, 4)},
-        "roofline": {"kernel": f"gemv_a8_kernel (dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)",
+        "roofline": {"kernel": f"gemv_row_kernel (one-row dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)",
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": round(traffic), "bytes_per_launch": round(bpl),
                      "us_per_launch": round(spl * 1e6, 3), "launches": nl, "peak_kind": peak_kind},
