@@ -99,14 +99,15 @@ __host__ __device__ __forceinline__ int hdr_bytes(int nb) { return hdr_off(2 * n
 
 // Rows [r0, r0 + nr) of an n-row matrix for CTA b of G.
 __device__ __forceinline__ void slab(int n, int b, int G, int &r0, int &nr) {
-    const long long a = (long long)n * b / G, e = (long long)n * (b + 1) / G;
+    // n * G < 2^32 (gemv_row_ok): 32-bit quotients
+    const unsigned a = (unsigned)n * (unsigned)b / (unsigned)G, e = (unsigned)n * (unsigned)(b + 1) / (unsigned)G;
     r0 = (int)a;
     nr = (int)(e - a);
 }
 
-// The bytes a Q6_K lane needs from one block, from aligned 16-byte loads: WO
-// is the block start's word offset within its 16-byte line (warp-uniform),
-// the remaining 0/16-bit shift comes from the address.
+// The bytes a Q6_K lane needs from one block, read with aligned 16-byte
+// loads: WO is the block start's word offset within its 16-byte line
+// (warp-uniform), the remaining 0/16-bit shift comes from the address.
 template <int WO>
 __device__ __forceinline__ void q6k_load(uint32_t blk, int h, uint32_t (&ql)[16], uint32_t (&qh)[8], uint32_t &sc01,
                                          uint32_t &sc23, uint32_t &dh) {
@@ -497,6 +498,8 @@ cudaError_t prepare_row() {
 
 bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
     if (nseg <= 0 || nseg > kMaxSegs) return false;
+    for (int i = 0; i < nseg; i++)
+        if ((unsigned long long)segs[i].n * (unsigned long long)num_sms() >= (1ULL << 32)) return false;
     if (((uintptr_t)act.q & 15) || ((uintptr_t)act.ys & 15) || ((uintptr_t)act.xs & 7)) return false;
     for (int i = 0; i < nseg; i++) {
         if (segs[i].dt != Q4_K && segs[i].dt != Q6_K) return false;
