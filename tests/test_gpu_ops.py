@@ -127,12 +127,15 @@ def test_a8_edge_cases(ctx, dt):
 
 @pytest.mark.parametrize("dt,n,k,inf", [(O.Q4_K, 12288, 4096, False), (O.Q6_K, 4096, 14336, False),
                                          (O.Q6_K, 9000, 2048, False), (O.Q4_K, 150, 256, False),
-                                         (O.Q6_K, 100, 4096, False), (O.Q4_K, 3000, 4096, True)])
+                                         (O.Q6_K, 100, 4096, False), (O.Q4_K, 3000, 4096, True),
+                                         (O.Q4_K, 2000, 5632, False), (O.Q6_K, 1200, 6144, False),
+                                         (O.Q4_K, 301, 768, False)])
 def test_a8_one_row_slabs(ctx, dt, n, k, inf):
     """One activation row (the slab-streaming kernel): matrices whose per-SM
-    slabs span several stages and several batches of row records, fewer rows
-    than SMs, and weight rows with a non-finite block scale in different
-    batches.  Exact rows equal the oracle bit for bit; refused rows (and a
+    slabs span several stages of the record ring, fewer rows than SMs, row
+    block counts that do not divide 256 (stages of 242, 240 and 255 blocks,
+    an odd number of rows per stage), and weight rows with a non-finite
+    block scale in different stages.  Exact rows equal the oracle bit for bit; refused rows (and a
     refused activation row) equal the multi-row kernel's f32 product."""
     bb = 144 if dt == O.Q4_K else 210
     rb = k // 256 * bb
