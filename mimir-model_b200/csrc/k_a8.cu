@@ -93,19 +93,21 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
                                                             float *__restrict__ y, ActQ8 act, P2P wait) {
     __shared__ QuantScratch qs;
     pdl_launch_dependents();
+    const long long row = blockIdx.x;
+    const int b = blockIdx.y, i = b * 256 + threadIdx.x;
+    // the norm weight is read-only: fetched before the wait for the previous kernel
+    const float sc = (scale && i < n) ? scale[i] : 1.f;
     pdl_wait();
     if (wait.N > 1) {  // every rank's columns of the residual have arrived
         p2p_publish_wait(wait);
         __syncthreads();
     }
-    const long long row = blockIdx.x;
-    const int b = blockIdx.y, i = b * 256 + threadIdx.x;
     const float *xr = x + row * n;
     const float inv = rms_inv(xr, n, eps);
     float v = 0.f;
     if (i < n) {
         v = __fmul_rn(xr[i], inv);
-        if (scale) v = __fmul_rn(v, scale[i]);
+        if (scale) v = __fmul_rn(v, sc);
         y[row * n + i] = v;
     }
     if (act.q) quant_block_256(v, row, n, b, act, qs);
