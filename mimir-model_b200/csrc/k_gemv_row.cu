@@ -268,18 +268,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
     if (warp < kCW) {
         // the activation row into shared memory (act_off layout), the
         // per-half headers (xs of the 4 runs of 32, dx, ok), the sums of 16
+        // Every load of a thread is issued before its first store, so the
+        // staging costs one round trip to L2 (the previous kernel wrote the
+        // row; it is read-only from here on, hence the read-only path).
         const int nq = (int)(p.K / 16);
-        for (int c = tid; c < nq; c += kCT) {
-            const int kb = c >> 4, h = (c >> 3) & 1, a = c & 7;
-            *(uint4 *)(smem + p.off_act + act_off(kb, h) + 16 * a) = *(const uint4 *)(p.act.q + (long long)c * 16);
+        constexpr int kQ = 4;  // chunks of 16 quants per thread: K <= kQ * 16 * kCT
+        uint4 qv[kQ];
+#pragma unroll
+        for (int j = 0; j < kQ; j++) {
+            const int c = tid + j * kCT;
+            if (c < nq) qv[j] = __ldg((const uint4 *)(p.act.q + (long long)c * 16));
         }
-        for (int hb = tid; hb < 2 * nb; hb += kCT) {
-            const int kb = hb >> 1, h = hb & 1;
-            const uint2 xs = *(const uint2 *)(p.act.xs + kb * 8 + 4 * h);
-            const float dx = p.act.dx[kb];
-            const int okb = p.act.ok[kb];
+        const int hb = tid, hkb = hb >> 1, hh = hb & 1;
+        const bool hon = hb < 2 * nb;  // 2 nb <= 512: one half-block entry per thread at most
+        uint2 xs = make_uint2(0, 0);
+        uint4 ys = make_uint4(0, 0, 0, 0);
+        float dx = 0.f;
+        int okb = 1;
+        if (hon) {
+            xs = __ldg((const uint2 *)(p.act.xs + hkb * 8 + 4 * hh));
+            ys = __ldg((const uint4 *)(p.act.ys + hkb * 16 + 8 * hh));
+            dx = __ldg(p.act.dx + hkb);
+            okb = __ldg(p.act.ok + hkb);
+        }
+#pragma unroll
+        for (int j = 0; j < kQ; j++) {
+            const int c = tid + j * kCT;
+            if (c < nq) {
+                const int kb = c >> 4, h = (c >> 3) & 1, a = c & 7;
+                *(uint4 *)(smem + p.off_act + act_off(kb, h) + 16 * a) = qv[j];
+            }
+        }
+        if (hon) {
             *(uint4 *)(smem + p.off_hdr + hdr_off(hb)) = make_uint4(xs.x, xs.y, __float_as_uint(dx), (unsigned)okb);
-            *(uint4 *)(smem + p.off_ys + hdr_off(hb)) = *(const uint4 *)(p.act.ys + kb * 16 + 8 * h);
+            *(uint4 *)(smem + p.off_ys + hdr_off(hb)) = ys;
             if (!okb) misc[0] = 0;  // a row is quantized when every one of its blocks is (q8.go:50-97)
         }
         for (int i = tid; i < RS * rps; i += kCT) smem[p.off_bad + i] = 0;
@@ -452,7 +474,8 @@ struct RowPlan {
 };
 
 bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
-    if (K % 256 || K <= 0 || K / 256 > kMaxSB) return false;
+    // K <= 32768: the prologue stages at most 4 chunks of 16 quants per consumer thread
+    if (K % 256 || K <= 0 || K / 256 > kMaxSB || K > 4LL * 16 * kCT) return false;
     const int nb = (int)(K / 256);
     int maxbb = 0;
     for (int i = 0; i < nseg; i++) maxbb = max(maxbb, block_bytes(segs[i].dt));
