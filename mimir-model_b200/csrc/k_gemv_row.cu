@@ -60,7 +60,8 @@ struct RowParams {
     ActQ8 act;
     long long K;
     int nb;             // blocks per row
-    int sb;             // blocks per stage: whole rows
+    int sb;             // blocks per stage: whole rows, a multiple of `unit` rows
+    int unit;           // rows per 16-byte multiple of row bytes: slabs and stages come in these
     int rstages;        // stages of rows in the record ring
     int slots, slot_bytes;
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
@@ -97,12 +98,15 @@ __host__ __device__ __forceinline__ int act_bytes(int nb) { return act_off(nb, 0
 __host__ __device__ __forceinline__ int hdr_off(int hb) { return (hb + ((hb >> 4) << 1)) * 16; }
 __host__ __device__ __forceinline__ int hdr_bytes(int nb) { return hdr_off(2 * nb) + 32; }
 
-// Rows [r0, r0 + nr) of an n-row matrix for CTA b of G.
-__device__ __forceinline__ void slab(int n, int b, int G, int &r0, int &nr) {
+// Rows [r0, r0 + nr) of an n-row matrix for CTA b of G, cut at multiples of
+// u rows (n is one, gemv_row_ok) so that every slab starts on a 16-byte
+// boundary and spans a multiple of 16 bytes.
+__device__ __forceinline__ void slab(int n, int b, int G, int u, int &r0, int &nr) {
     // n * G < 2^32 (gemv_row_ok): 32-bit quotients
-    const unsigned a = (unsigned)n * (unsigned)b / (unsigned)G, e = (unsigned)n * (unsigned)(b + 1) / (unsigned)G;
-    r0 = (int)a;
-    nr = (int)(e - a);
+    const unsigned m = (unsigned)(n / u);
+    const unsigned a = m * (unsigned)b / (unsigned)G, e = m * (unsigned)(b + 1) / (unsigned)G;
+    r0 = (int)a * u;
+    nr = (int)(e - a) * u;
 }
 
 // The bytes a Q6_K lane needs from one block, read with aligned 16-byte
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         bool ok = true;
         for (int s = 0; s < p.nseg && ok; s++) {
             int r0, nr;
-            slab(p.seg[s].n, cta, G, r0, nr);
+            slab(p.seg[s].n, cta, G, p.unit, r0, nr);
             const int bb = block_bytes(p.seg[s].dt);
             const int nblk = nr * nb;
             const uint8_t *src = p.seg[s].w + (long long)r0 * nb * bb;
@@ -324,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         for (int s = 0; s < p.nseg; s++) {
             const GemvSeg &sg = p.seg[s];
             int r0, nr;
-            slab(sg.n, cta, G, r0, nr);
+            slab(sg.n, cta, G, p.unit, r0, nr);
             const int dt = sg.dt;
             const long long rb = row_bytes(dt, p.K);
             for (int lo = 0; lo < nr; lo += rps, m++) {
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
     for (int s = 0; s < p.nseg; s++) {
         const GemvSeg &sg = p.seg[s];
         int r0, nr;
-        slab(sg.n, cta, G, r0, nr);
+        slab(sg.n, cta, G, p.unit, r0, nr);
         const int dt = sg.dt;
         // this lane's block of every stage: the same column of every stage's rows
         const int blk = dt == Q4_K ? 16 * warp + (lane >> 1) : 8 * (16 * (warp >> 3) + (lane >> 1)) + (warp & 7);
@@ -468,8 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
     }
 }
 
+// The fewest whole rows of type dt whose bytes are a multiple of 16 (1 for
+// Q4_K; 2, 4 or 8 for Q6_K rows of 210-byte blocks).
+int row_unit(int dt, long long K) {
+    const long long rb = row_bytes(dt, K);
+    int u = 1;
+    while ((rb * u) % 16) u *= 2;
+    return u;
+}
+
 struct RowPlan {
-    int sb, rstages, slots, slot_bytes, smem;
+    int unit, sb, rstages, slots, slot_bytes, smem;
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
 };
 
@@ -479,8 +492,13 @@ bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
     const int nb = (int)(K / 256);
     int maxbb = 0;
     for (int i = 0; i < nseg; i++) maxbb = max(maxbb, block_bytes(segs[i].dt));
-    pl.sb = kMaxSB / nb * nb;  // whole rows
-    const int rps = pl.sb / nb;
+    // rows per stage: whole rows, up to 256 blocks, a multiple of the unit
+    // (a Q6_K row of 7, 14 or 28 blocks is not a 16-byte multiple)
+    pl.unit = 1;
+    for (int i = 0; i < nseg; i++) pl.unit = max(pl.unit, row_unit(segs[i].dt, K));
+    const int rps = kMaxSB / nb / pl.unit * pl.unit;
+    if (rps < 1) return false;
+    pl.sb = rps * nb;
     auto al = [](int v, int a) { return (v + a - 1) / a * a; };
     pl.slot_bytes = pl.sb * maxbb;
     int o = 512;  // barriers and flags
@@ -526,10 +544,14 @@ bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
     if (((uintptr_t)act.q & 15) || ((uintptr_t)act.ys & 15) || ((uintptr_t)act.xs & 7)) return false;
     for (int i = 0; i < nseg; i++) {
         if (segs[i].dt != Q4_K && segs[i].dt != Q6_K) return false;
-        if (row_bytes(segs[i].dt, K) % 16 || ((uintptr_t)segs[i].w & 15)) return false;
+        if (K % 256 || ((uintptr_t)segs[i].w & 15)) return false;
     }
     RowPlan pl;
-    return plan_row(segs, nseg, K, pl);
+    if (!plan_row(segs, nseg, K, pl)) return false;
+    // every matrix a whole number of units: its slabs and stages are 16-byte multiples
+    for (int i = 0; i < nseg; i++)
+        if (segs[i].n % pl.unit) return false;
+    return true;
 }
 
 cudaError_t gemv_row_prepare() { return prepare_row(); }
@@ -548,6 +570,7 @@ cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8
     p.K = K;
     p.nb = (int)(K / 256);
     p.sb = pl.sb;
+    p.unit = pl.unit;
     p.rstages = pl.rstages;
     p.slots = pl.slots;
     p.slot_bytes = pl.slot_bytes;

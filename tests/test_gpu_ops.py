@@ -129,13 +129,18 @@ def test_a8_edge_cases(ctx, dt):
                                          (O.Q6_K, 9000, 2048, False), (O.Q4_K, 150, 256, False),
                                          (O.Q6_K, 100, 4096, False), (O.Q4_K, 3000, 4096, True),
                                          (O.Q4_K, 2000, 5632, False), (O.Q6_K, 1200, 6144, False),
-                                         (O.Q4_K, 301, 768, False)])
+                                         (O.Q4_K, 301, 768, False), (O.Q6_K, 4096, 1792, False),
+                                         (O.Q6_K, 4096, 3584, False), (O.Q6_K, 2048, 7168, False),
+                                         (O.Q6_K, 1003, 3584, False), (O.Q4_K, 900, 1792, False)])
 def test_a8_one_row_slabs(ctx, dt, n, k, inf):
     """One activation row (the slab-streaming kernel): matrices whose per-SM
     slabs span several stages of the record ring, fewer rows than SMs, row
     block counts that do not divide 256 (stages of 242, 240 and 255 blocks,
-    an odd number of rows per stage), and weight rows with a non-finite
-    block scale in different stages.  Exact rows equal the oracle bit for bit; refused rows (and a
+    an odd number of rows per stage), Q6_K rows that are not 16-byte
+    multiples (7, 14 and 28 blocks: the ffn_down shards of tensor
+    parallelism, cut in units of 8, 4 and 2 rows; a row count that is not a
+    whole unit takes the multi-row kernel), and weight rows with a
+    non-finite block scale in different stages.  Exact rows equal the oracle bit for bit; refused rows (and a
     refused activation row) equal the multi-row kernel's f32 product."""
     bb = 144 if dt == O.Q4_K else 210
     rb = k // 256 * bb
