@@ -37,7 +37,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "mimir-model_b200"))
 
 METRIC = "Q4_K_M decode tok/s (8B, 70B TP 1–8 GPU); quant-GEMV HBM GB/s vs peak"
-PUBLISHED_8B = 6.7  # 8B-shape Q4_K_M random weights, 181-token prompt, 4-core Xeon
+PUBLISHED_8B = 6.7  # the reference's published 8B-shape Q4_K_M decode (random weights, 4-core Xeon)
 F32, Q4_K, Q6_K = 1, 66, 67
 CFG8B = dict(layers=32, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=128256,
              rope_theta=500000.0, norm_eps=1e-5)
@@ -74,6 +74,22 @@ def weight_bytes_per_token(cfg):
     for name, dt, shape, _, _ in layout(cfg):
         tot += nbytes(dt, shape[1:]) if name == "token_embd.weight" else nbytes(dt, shape)
     return tot
+
+
+def l2_note(cfg, what: str) -> str:
+    """The L2 statement of a bench line, with this shape's weight bytes."""
+    return f"inputs larger than L2: {weight_bytes_per_token(cfg) / 1e9:.2f} GB of weights {what} vs 126 MB L2"
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def seed_of(name: str) -> int:
@@ -212,16 +228,21 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=3):
     return total_b / launches, total_t / launches, launches
 
 
-def cpu_baseline_sample(ctx, cfg, weights, budget_s=20.0):
+PORT_NOTE = ("oracle/ C restatement of the reference's a8 decode path (portable C, gcc -O3 -march=x86-64-v3; "
+             "no hand-written AVX2/AMX kernels like the reference's internal/kernels/*_amd64.s, so slower per core "
+             "than the reference's published 6.1-6.7 tok/s on 4 cores)")
+
+
+def cpu_baseline_sample(ctx, cfg, weights, prompt, budget_s=20.0):
     """The CPU restatement (oracle/, timed here as the reference's CPU path)
-    on the same weights: a short prompt, then decode steps until the budget."""
+    on the same weights and the same prompt: decode steps until the budget."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     host = {name: (dt, ctx.download(t)) for name, (dt, t) in weights.items()}
-    m = O.Llama(dict(cfg, context=64, a8=1, cache_f16=1, interleaved=1, nthreads=O.threads()), host)
-    ids = prompt_ids(cfg["vocab"], 4)
-    logits = m.forward(ids, np.arange(4))[0]
-    tok, pos, steps, t0 = O.argmax(logits), 4, 0, time.perf_counter()
+    m = O.Llama(dict(cfg, context=prompt + 40, a8=1, cache_f16=1, interleaved=1, nthreads=O.threads()), host)
+    ids = prompt_ids(cfg["vocab"], prompt)
+    logits = m.forward(ids, np.arange(prompt))[0]
+    tok, pos, steps, t0 = O.argmax(logits), prompt, 0, time.perf_counter()
     while True:
         logits = m.forward([tok], [pos])[0]
         tok, pos, steps = O.argmax(logits), pos + 1, steps + 1
@@ -229,9 +250,9 @@ def cpu_baseline_sample(ctx, cfg, weights, budget_s=20.0):
         if el > budget_s or steps >= 32:
             break
     del m, host
-    return {"value": steps / el, "unit": "tok/s", "cores": O.threads(), "kind": "port",
-            "sample": f"{steps} greedy decode tokens of the same 8B-shape model after a 4-token prompt, "
-                      f"{el:.1f} s, oracle/ C restatement (a8 block 256, f16 cache), all threads"}
+    return {"value": steps / el, "unit": "tok/s", "cores": O.threads(), "cpu": cpu_model(), "kind": "port",
+            "sample": f"{steps} greedy decode tokens of the same model after the same {prompt}-token prompt, "
+                      f"{el:.1f} s, all threads; {PORT_NOTE}"}
 
 
 def run_gpu(args):
@@ -338,7 +359,7 @@ def run_gpu(args):
                    "matmul": "dequant_matmul_a8.v2 block 256 (bit-exact dotQ8KRef)", "kv_cache": "f16",
                    "parallelism": f"tp{world} (rows of every matrix per rank, NCCL all-gathers)" if world > 1
                    else "1 GPU",
-                   "l2": "inputs larger than L2: 4.88 GB of weights streamed per token vs 126 MB L2"},
+                   "l2": l2_note(cfg, "streamed per token")},
         "e2e": {"value": round(args.e2e_steps / e2e_s, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * cfg["vocab"],
                 "api": "mimgpu_session_run (pinned host token/position in, logits out, host argmax)"},
@@ -353,7 +374,7 @@ def run_gpu(args):
     }
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         try:
-            line["cpu_baseline"] = cpu_baseline_sample(ctx, cfg, weights)
+            line["cpu_baseline"] = cpu_baseline_sample(ctx, cfg, weights, prompt)
         except Exception as e:  # noqa: BLE001 - the baseline must not hide the GPU line
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     if rank == 0:
@@ -533,7 +554,7 @@ def run_prefill(args):
                                      "random prompt ids)",
             "config": {"workload": f"8B-shape prompt pass, {T} tokens, logits of the last position",
                        "layers": cfg["layers"], "prompt": T,
-                       "l2": "inputs larger than L2: 4.88 GB of weights per pass vs 126 MB L2"},
+                       "l2": l2_note(cfg, "per pass")},
             "e2e": {"value": round(T / w, 1), "unit": "tok/s", "h2d_bytes_per_step": 12 * T,
                     "d2h_bytes_per_step": 4 * cfg["vocab"], "api": "mimgpu_session_run (host ids/positions in, "
                                                                   "host logits out)"},
@@ -609,7 +630,7 @@ def run_batch(args):
         "config": {"workload": f"{args.shape.upper()}-shape greedy decode of {B} sequences together, {C}-token cache",
                    "layers": cfg["layers"], "batch": B, "context_cache": C, "prompt_per_sequence": prompt,
                    "prefill_s": round(prefill_s, 2),
-                   "l2": "inputs larger than L2: 4.88 GB of weights streamed per step vs 126 MB L2"},
+                   "l2": l2_note(cfg, "streamed per step")},
         "e2e": {"value": round(B * args.e2e_steps / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 16 * B,
                 "d2h_bytes_per_step": 4 * cfg["vocab"] * B,
                 "api": "mimgpu_session_run_slots (host ids/sequences/positions in, logits out, host argmax)"},
@@ -641,10 +662,13 @@ def run_reference(args):
         else:
             host[name] = (dt, O.gen_weight(dt, seed_of(name), shape[0], shape[1], sigma, nt))
     gen_s = time.perf_counter() - t0
-    context = 64 + args.warmup + args.steps
+    prompt = args.prompt
+    context = prompt + args.warmup + args.steps + 8
     m = O.Llama(dict(cfg, context=context, a8=1, cache_f16=1, interleaved=1, nthreads=nt), host)
-    ids = prompt_ids(cfg["vocab"], 4)
-    tok, pos = O.argmax(m.forward(ids, np.arange(4))[0]), 4
+    ids = prompt_ids(cfg["vocab"], prompt)
+    t0 = time.perf_counter()
+    tok, pos = O.argmax(m.forward(ids, np.arange(prompt))[0]), prompt
+    prefill_s = time.perf_counter() - t0
     for _ in range(args.warmup):
         tok, pos = O.argmax(m.forward([tok], [pos])[0]), pos + 1
     budget = args.reference_budget
@@ -657,15 +681,17 @@ def run_reference(args):
     el = time.perf_counter() - t0
     value = steps / el
     sample = (f"{steps} greedy decode tokens (of {args.steps} asked; {budget:.0f} s budget) of the 8B-shape model "
-              f"after a 4-token prompt; weights generated on the host in {gen_s:.0f} s")
+              f"after the bench's {prompt}-token prompt (prefilled in {prefill_s:.0f} s); weights generated on the "
+              f"host in {gen_s:.0f} s; {PORT_NOTE}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": 0,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(el / steps * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": round(value / PUBLISHED_8B, 3), "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the host; seeded random prompt ids)",
-        "config": {"workload": "8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)",
+        "config": {"workload": "8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)", "prompt": prompt,
                    "implementation": "oracle/ C restatement of the Go reference path (go is not installed)"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": nt, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": nt, "cpu": cpu_model(), "kind": "port",
+                         "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

@@ -135,7 +135,11 @@ int mimgpu_embedding(mimgpu_ctx *ctx, const mimgpu_tensor *table, const int32_t 
 /* ------------------------------- device-resident products (no host copies)
  * Same arithmetic as the host-buffer calls; all pointers are device memory
  * and the work is queued on `stream` (a cudaStream_t, NULL = the context's
- * stream) without waiting.  Used by callers that keep activations in HBM. */
+ * stream) without waiting.  Used by callers that keep activations in HBM.
+ * These calls return before the work runs, so a bounded device wait of
+ * theirs that runs out is reported (MIMGPU_ETIMEOUT) by the next call on the
+ * same context that waits for the device: any host-buffer call or session
+ * run. */
 int mimgpu_dequant_matmul_a8_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
                                  const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
 int mimgpu_dequant_matmul_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,

@@ -91,6 +91,20 @@ long long tensor_bytes(int dtype, int ndim, const int64_t *shape) {
     return n / be * block_bytes(dtype);
 }
 
+// checkDequantMatmul, interp/transformer.go:216-236, for a 2-D weight; and
+// the sizes the kernels index with 32-bit row counts.
+int check_matmul(mimgpu_ctx *c, int64_t rows, int64_t k, const mimgpu_tensor *w) {
+    if (!w || w->ndim != 2) return fail(c, MIMGPU_EINVAL, "dequant_matmul: w must be [N, K]");
+    if (w->shape[1] != k) return fail(c, MIMGPU_EINVAL, "dequant_matmul: x has K=%lld, w is [%lld, %lld]",
+                                      (long long)k, (long long)w->shape[0], (long long)w->shape[1]);
+    if (rows < 0) return fail(c, MIMGPU_EINVAL, "dequant_matmul: rows < 0");
+    if (w->ctx != c) return fail(c, MIMGPU_EINVAL, "dequant_matmul: w belongs to another context");
+    if (rows > INT32_MAX || w->shape[0] > INT32_MAX)
+        return fail(c, MIMGPU_EINVAL, "dequant_matmul: %lld rows x %lld outputs exceed 32-bit counts", (long long)rows,
+                    (long long)w->shape[0]);
+    return MIMGPU_OK;
+}
+
 }  // namespace mimgpu
 
 namespace {
@@ -110,15 +124,6 @@ struct Carver {
 
 size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
 
-// checkDequantMatmul, interp/transformer.go:216-236, for a 2-D weight.
-int check_matmul(mimgpu_ctx *c, int64_t rows, int64_t k, const mimgpu_tensor *w) {
-    if (!w || w->ndim != 2) return fail(c, MIMGPU_EINVAL, "dequant_matmul: w must be [N, K]");
-    if (w->shape[1] != k) return fail(c, MIMGPU_EINVAL, "dequant_matmul: x has K=%lld, w is [%lld, %lld]",
-                                      (long long)k, (long long)w->shape[0], (long long)w->shape[1]);
-    if (rows < 0) return fail(c, MIMGPU_EINVAL, "dequant_matmul: rows < 0");
-    if (w->ctx != c) return fail(c, MIMGPU_EINVAL, "dequant_matmul: w belongs to another context");
-    return MIMGPU_OK;
-}
 
 int run_matmul(mimgpu_ctx *c, bool a8, const float *x, int64_t rows, int64_t k, const mimgpu_tensor *w,
                const float *bias, float *y) {

@@ -41,6 +41,9 @@ int sync_bounded(mimgpu_ctx *c, cudaStream_t st);
 int use_device(mimgpu_ctx *c);
 // Ensures the workspace holds `bytes`.
 int ensure_ws(mimgpu_ctx *c, size_t bytes);
+// The checks every dequant_matmul entry point makes first
+// (checkDequantMatmul, interp/transformer.go:216-236).
+int check_matmul(mimgpu_ctx *c, int64_t rows, int64_t k, const mimgpu_tensor *w);
 // Bytes of a tensor of `dtype` and shape; -1 when the shape does not fit
 // the block size.
 long long tensor_bytes(int dtype, int ndim, const int64_t *shape);

@@ -18,6 +18,7 @@
 #include "amd64_math.cuh"
 #include "quant.cuh"
 #include "p2p.cuh"
+#include "rms.cuh"
 
 namespace mimgpu {
 
@@ -65,9 +66,10 @@ __global__ void __launch_bounds__(256) quantize_a8_kernel(const float *__restric
     quant_block_256(x[row * K + b * 256 + threadIdx.x], row, K, b, act, qs);
 }
 
-// Sum of squares of a row in float64 (rms_norm, interp/fast.go:434-485);
-// the reference sums in order, this is a fixed-order tree: both round the
-// mean to f32 before the square root.  Returns inv = f32(1/sqrt(mean + eps)).
+// Sum of squares of a row in float64 (rms_norm, interp/fast.go:434-485):
+// a tree sum, with the reference's in-order sum (rms.cuh) where the tree's
+// error bound straddles an f32 boundary of the mean, so the mean has the
+// reference's bits.  Returns inv = f32(1/sqrt(mean + eps)).
 __device__ __forceinline__ float rms_inv(const float *__restrict__ xr, int n, float eps) {
     __shared__ double dred[8];
     double ss = 0;
@@ -81,8 +83,14 @@ __device__ __forceinline__ float rms_inv(const float *__restrict__ xr, int n, fl
     double tot = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) tot += dred[i];
-    const float ms = (float)__ddiv_rn(tot, (double)n);
-    return (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)ms, (double)eps)));
+    float ms;
+    if (!rms_mean_certain(tot, n, n / 256 + 16, ms)) {
+        __shared__ float ms_seq;
+        if (threadIdx.x == 0) ms_seq = (float)__ddiv_rn(rms_seq_sum(xr, n), (double)n);
+        __syncthreads();
+        ms = ms_seq;
+    }
+    return rms_inv_of_mean(ms, eps);
 }
 
 // rms_norm fused with the quantization of its output: block (row, b)

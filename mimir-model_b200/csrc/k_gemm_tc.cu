@@ -650,11 +650,10 @@ bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, lo
 }
 
 cudaError_t gemm_a8_tc_prepare() {
-    static bool done = false;
-    if (done) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemm_a8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-    if (e == cudaSuccess) done = true;
-    return e;
+    static std::atomic<unsigned long long> done{0};
+    return once_per_device(done, [] {
+        return cudaFuncSetAttribute(gemm_a8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+    });
 }
 
 cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,

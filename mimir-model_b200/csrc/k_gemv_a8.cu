@@ -576,13 +576,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_a8_kernel(const __grid_const
 
 template <int NR>
 cudaError_t prepare_nr() {
-    static bool done = false;
-    if (done) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemv_a8_kernel<NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_a8_kernel<NR>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e == cudaSuccess) done = true;
-    return e;
+    static std::atomic<unsigned long long> done{0};
+    return once_per_device(done, [] {
+        cudaError_t e =
+            cudaFuncSetAttribute(gemv_a8_kernel<NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemv_a8_kernel<NR>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        return e;
+    });
 }
 
 template <int NR>

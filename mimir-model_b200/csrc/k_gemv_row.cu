@@ -528,11 +528,10 @@ bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
 }
 
 cudaError_t prepare_row() {
-    static bool done = false;
-    if (done) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemv_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-    if (e == cudaSuccess) done = true;
-    return e;
+    static std::atomic<unsigned long long> done{0};
+    return once_per_device(done, [] {
+        return cudaFuncSetAttribute(gemv_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    });
 }
 
 }  // namespace

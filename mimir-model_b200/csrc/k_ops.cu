@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "p2p.cuh"
+#include "rms.cuh"
 
 namespace mimgpu {
 
@@ -57,8 +58,15 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
     double tot = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) tot += dred[i];
-    const float ms = (float)__ddiv_rn(tot, (double)n);
-    const float inv = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)ms, (double)eps)));
+    // the reference's in-order sum where the tree sum cannot settle f32(ss/n)
+    float ms;
+    if (!rms_mean_certain(tot, n, n / 256 + 16, ms)) {
+        __shared__ float ms_seq;
+        if (t == 0) ms_seq = (float)__ddiv_rn(rms_seq_sum(xr, n), (double)n);
+        __syncthreads();
+        ms = ms_seq;
+    }
+    const float inv = rms_inv_of_mean(ms, eps);
     for (int i = t; i < n; i += 256) {
         float v = __fmul_rn(xr[i], inv);
         if (scale) v = __fmul_rn(v, scale[i]);

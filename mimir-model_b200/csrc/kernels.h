@@ -2,11 +2,27 @@
 // libmimgpu; the public C ABI is include/mimgpu.h).
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 namespace mimgpu {
+
+// Runs `set` (kernel attributes, which are per device) once for the current
+// device; `done` holds one bit per device ordinal and may be shared by
+// threads and contexts.
+template <class F>
+cudaError_t once_per_device(std::atomic<unsigned long long> &done, F set) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 // 8-bit activations in blocks of 256 (internal/kernels/q8.go:50-97):
 // q [rows,K] int8, dx [rows,K/256] scale amax/127, xs [rows,K/32] sums of
@@ -83,7 +99,9 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
                               unsigned *status, cudaStream_t st, bool pdl);
 // The one-activation-row product (decode steps): one slab of consecutive
 // rows per SM, streamed with bulk copies; launch_gemv_a8 dispatches to it
-// when every matrix's rows are 16-byte multiples.  Same results bit for bit.
+// when every matrix is a whole number of row units (the fewest rows whose
+// bytes are a 16-byte multiple: 1 for Q4_K, 1, 2, 4 or 8 for Q6_K; see
+// gemv_row_ok).  Same results bit for bit.
 bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K);
 cudaError_t gemv_row_prepare();
 cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,

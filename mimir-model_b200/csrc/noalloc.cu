@@ -16,8 +16,10 @@
 // device current).  Every byte of it that a call reads is written earlier in
 // the same call (the quantizer writes the int8 values, scales, sums and the
 // per-block ok flags before the product reads them), so nothing in it has to
-// start at zero.  The bounded waits of the product record errors in the
-// context's status word, which the context keeps at zero between calls.
+// start at zero.  The call only queues work: a bounded wait of the product
+// that runs out sets a bit in the context's status word, and the next call
+// on the context that waits for its stream (any host-buffer call, a session
+// run) reports it as MIMGPU_ETIMEOUT and clears it.
 #include <cstdint>
 #include <mutex>
 
@@ -59,23 +61,18 @@ extern "C" int mimgpu_dequant_matmul_a8_static(mimgpu_ctx *c, void *stream, cons
                                                const mimgpu_tensor *w, const float *bias, float *y) {
     if (!c) return MIMGPU_EINVAL;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
-    if (!w || w->ndim != 2) return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_static: w must be [N, K]");
-    if (w->shape[1] != k)
-        return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_static: x has K=%lld, w is [%lld, %lld]", (long long)k,
-                    (long long)w->shape[0], (long long)w->shape[1]);
-    if (rows < 0) return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_static: rows < 0");
-    if (w->ctx != c) return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_static: w belongs to another context");
+    int rc = check_matmul(c, rows, k, w);
+    if (rc) return rc;
     if (w->dtype != Q4_K && w->dtype != Q6_K)
         return fail(c, MIMGPU_ENOTHANDLED, "dequant_matmul_a8_static: dtype %d (Q4_K or Q6_K only)", w->dtype);
     if (k % 256) return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_static: K=%lld is not a multiple of 256", (long long)k);
     const size_t need = act_q8_bytes((int)rows, k);
-    if (rows > INT32_MAX || need > kA8StaticBytes)
+    if (need > kA8StaticBytes)
         return fail(c, MIMGPU_EINVAL,
                     "dequant_matmul_a8_static: %lld rows of K=%lld need %zu bytes of activation scratch; "
                     "the static buffer holds %zu",
                     (long long)rows, (long long)k, need, kA8StaticBytes);
-    int rc = use_device(c);
-    if (rc) return rc;
+    if ((rc = use_device(c))) return rc;
     if (rows == 0 || w->shape[0] == 0) return MIMGPU_OK;
     void *base = nullptr;
     cudaError_t e = scratch_addr(c->device, &base);

@@ -223,18 +223,39 @@ def test_v1_within_spec_tolerance(ctx, dt, n, k, rows):
 # --------------------------------------------------------- per-token ops
 
 def test_rms_norm_matches_oracle(ctx):
-    """fast.go:434-485.  The float64 sum of squares is a tree sum here and a
-    sequential sum in the reference; the mean is rounded to f32 first, so the
-    results agree bit for bit unless the float64 sums straddle an f32
-    rounding boundary (probability ~1e-5 per row)."""
+    """fast.go:434-485, bit for bit on every row.  The float64 sum of squares
+    is a tree sum here and an in-order sum in the reference; where the
+    tree's error bound straddles an f32 boundary of the mean, the kernel
+    repeats the in-order sum."""
     x = O.gen_normal(21, 64 * 4096).reshape(64, 4096)
     x[3] *= 1e-20
     scale = O.gen_normal(22, 4096, 1.0, 0.02)
     got = ctx.rms_norm(x, scale, 1e-5)
     want = O.rms_norm(x, scale, 1e-5)
-    same_rows = np.all(bits(got) == bits(want), axis=1)
-    assert same_rows.sum() >= 63
-    assert np.allclose(got, want, rtol=(4096 + 24) * U, atol=0)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("n", [256, 4096, 8192])
+def test_rms_norm_mean_on_an_f32_midpoint(ctx, n):
+    """Rows whose mean of squares sits exactly on, or a float64 ulp beside,
+    the midpoint between two f32 values: the tree sum cannot settle the f32
+    mean there, so these rows take the in-order sum, and must still give the
+    reference's bits."""
+    a = np.float32(1 + 2.0 ** -12)  # a*a = 1 + 2^-11 + 2^-24: an f32 midpoint
+    rows = [np.full(n, a, np.float32)]
+    r = np.full(n, a, np.float32)
+    r[::7] = np.float32(1 + 2.0 ** -12 + 2.0 ** -23)  # a few ulps away from the midpoint
+    rows.append(r)
+    rng = np.random.default_rng(5)
+    for _ in range(6):
+        r = np.full(n, a, np.float32)
+        idx = rng.integers(0, n, 3)
+        r[idx] = np.nextafter(r[idx], np.float32(2))
+        rows.append(r)
+    x = np.stack(rows)
+    got = ctx.rms_norm(x, None, 1e-5)
+    want = O.rms_norm(x, None, 1e-5)
+    assert np.array_equal(bits(got), bits(want))
 
 
 @pytest.mark.parametrize("interleaved", [True, False])

@@ -50,7 +50,10 @@ def _run_static(ctx, x, w, bias=None):
     return y
 
 
-@pytest.mark.parametrize("dt,rows,n,k", [(O.Q4_K, 1, 4096, 4096), (O.Q6_K, 3, 1000, 2048), (O.Q4_K, 8, 333, 14336)])
+# 16 rows and more go through the tensor-core GEMM, whose activation tensor
+# map then points into the static buffer
+@pytest.mark.parametrize("dt,rows,n,k", [(O.Q4_K, 1, 4096, 4096), (O.Q6_K, 3, 1000, 2048), (O.Q4_K, 8, 333, 14336),
+                                         (O.Q4_K, 16, 512, 14336), (O.Q6_K, 24, 384, 4096)])
 def test_static_matches_a8_entry_two_calls(ctx, dt, rows, n, k):
     w_raw = O.gen_weight(dt, 900 + rows, n, k, 0.02)
     w = ctx.upload(dt, (n, k), w_raw)
@@ -62,6 +65,9 @@ def test_static_matches_a8_entry_two_calls(ctx, dt, rows, n, k):
     for call in range(2):
         want = ctx.dequant_matmul(xs[call], w, bias if call else None, a8_block=256)
         assert np.array_equal(gots[call].view(np.uint32), want.view(np.uint32)), f"call {call}"
+        # and the CPU restatement of the reference's kernels (dotQ8KRef)
+        ref = O.dequant_matmul_a8(xs[call], dt, w_raw, n, bias if call else None)
+        assert np.array_equal(gots[call].view(np.uint32), ref.view(np.uint32)), f"call {call} vs oracle"
     w.free()
 
 
