@@ -242,6 +242,27 @@ int mimgpu_session_generate_slots(mimgpu_session *s, const int32_t *tokens, cons
 /* The session's CUDA stream (a cudaStream_t), for callers that time or
  * order their own device work against the session's. */
 void *mimgpu_session_stream(mimgpu_session *s);
+/* How one-token steps of sequence 0 run (mimgpu_session_run with t = 1,
+ * mimgpu_session_generate; no counterpart in the reference, whose Session.Run
+ * interprets the graph op by op, interp/interp.go:409-526): on = 1 runs the
+ * whole step as one persistent kernel that streams every layer's weights
+ * through one pipeline; on = 0 launches one kernel per op.  Both give the same
+ * bits.  The persistent kernel is the default for single-GPU sessions of
+ * 8-bit-activation models with Q4_K / Q6_K matrices, E and F multiples of 256
+ * (2048..32768), head size 128, an f16 cache and interleaved RoPE; for other
+ * models on = 1 returns MIMGPU_ENOTHANDLED. */
+int mimgpu_session_set_step_kernel(mimgpu_session *s, int on);
+/* 1 when one-token steps run as one persistent kernel, else 0. */
+int mimgpu_session_uses_step_kernel(mimgpu_session *s);
+/* Profiling: with a device buffer of mimgpu_session_trace_bytes(s) bytes
+ * bound, every persistent-kernel step writes its phase timeline there (per
+ * CTA, %globaltimer nanoseconds: start, end, and per op the moments its
+ * activation was ready and staged, its stages consumed and chained, and its
+ * first and last weight stage issued; the slot layout is documented in the
+ * repository's step.h).  NULL unbinds.  The size is 0 when the session does
+ * not use the persistent kernel. */
+size_t mimgpu_session_trace_bytes(mimgpu_session *s);
+int mimgpu_session_set_trace(mimgpu_session *s, void *dev_buf, size_t nbytes);
 
 /* ------------------------------------------------- tensor parallelism
  * No counterpart in the reference (one process on CPU).  Ranks of one node,

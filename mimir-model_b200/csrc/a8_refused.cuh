@@ -50,4 +50,18 @@ static __device__ __noinline__ float row_dot_f32(int dt, const uint8_t *row, con
     return warp_sum(acc);
 }
 
+// The same product with the activation element e given by xf(e) (callers
+// whose f32 activation is not stored as a vector, e.g. recomputed from the
+// residual).  Warp-collective.
+template <class XF>
+__device__ __forceinline__ float row_dot_f32_fn(int dt, const uint8_t *row, int nb, XF xf) {
+    const int lane = threadIdx.x & 31;
+    float acc = 0.f;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t *blk = row + (long long)b * block_bytes(dt);
+        for (int e = lane; e < 256; e += 32) acc = __fmaf_rn(xf(b * 256 + e), decode_elem(dt, blk, e), acc);
+    }
+    return warp_sum(acc);
+}
+
 }  // namespace mimgpu

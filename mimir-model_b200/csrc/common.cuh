@@ -95,6 +95,56 @@ __device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int &s
     }
 }
 
+// Element i of a row of block-dtype values, decoded exactly as Dequantize
+// does (quant.go:197-344).
+__device__ __forceinline__ float decode_elem(int dt, const uint8_t *src, long long i) {
+    if (dt == Q4_K) {
+        const uint8_t *blk = src + (i / 256) * 144;
+        const int e = (int)(i % 256), c = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+        const float d = f16_to_f32(blk[0] | (blk[1] << 8)), dmin = f16_to_f32(blk[2] | (blk[3] << 8));
+        uint32_t sw[3];
+        for (int k = 0; k < 3; k++)
+            sw[k] = blk[4 + 4 * k] | (blk[5 + 4 * k] << 8) | (blk[6 + 4 * k] << 16) | ((uint32_t)blk[7 + 4 * k] << 24);
+        int sc, m;
+        q4k_scale_min(sw, 2 * c + hi, sc, m);
+        const int q = hi ? (blk[16 + 32 * c + l] >> 4) : (blk[16 + 32 * c + l] & 15);
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+    }
+    if (dt == Q6_K) {
+        const uint8_t *blk = src + (i / 256) * 210;
+        const int e = (int)(i % 256), h = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
+        const float d = f16_to_f32(blk[208] | (blk[209] << 8));
+        const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+        const int lowb = (quarter & 1) ? ql[l + 32] : ql[l];
+        const int low = (quarter >> 1) ? (lowb >> 4) : (lowb & 15);
+        const int q = (low | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
+        const int sc = (int8_t)blk[192 + 8 * h + (l >> 4) + 2 * quarter];
+        return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+    }
+    if (dt == Q8_0) {
+        const uint8_t *blk = src + (i / 32) * 34;
+        return __fmul_rn(f16_to_f32(blk[0] | (blk[1] << 8)), (float)(int8_t)blk[2 + i % 32]);
+    }
+    if (dt == F16) return f16_to_f32(src[2 * i] | (src[2 * i + 1] << 8));
+    return ((const float *)src)[i];
+}
+
+// ------------------------------------------------------------- argmax
+// argmax (cmd/mim-run/main.go:184-193): best = 0; x > v[best] moves best.
+// The result is the first index of the largest non-NaN value (NaNs never
+// compare greater), or 0 when v[0] is NaN.  Each block reduces a strided
+// share to (value, index) and folds it into one 64-bit key by atomicMax:
+// the value's order-preserving bits above the complement of the index, so
+// the larger value and then the smaller index wins; -0 counts as +0, as the
+// reference's comparison does.  A NaN first value sets the all-ones key.
+// With tensor parallelism each rank folds its vocabulary slice (global
+// indices i0 + i) and the keys meet in a 64-bit max all-reduce.
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long i) {
+    uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+}
+
 // ------------------------------------------------------- mbarrier / bulk copy
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -159,6 +209,35 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// The same copy with an L2 eviction policy (createpolicy): evict_first for
+// bytes read once, so they do not push out data that is read again.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                              uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+// Asynchronous prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_hint(const void *src, uint32_t bytes, uint64_t pol) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol)
+                 : "memory");
 }
 
 // Streaming 128-bit global load that does not allocate in L1.

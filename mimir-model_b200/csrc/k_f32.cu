@@ -170,39 +170,6 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_f32_kernel(const __grid_cons
     }
 }
 
-// Decodes one block-dtype element range: thread per element.
-__device__ __forceinline__ float decode_elem(int dt, const uint8_t *src, long long i) {
-    if (dt == Q4_K) {
-        const uint8_t *blk = src + (i / 256) * 144;
-        const int e = (int)(i % 256), c = e >> 6, hi = (e >> 5) & 1, l = e & 31;
-        const float d = f16_to_f32(blk[0] | (blk[1] << 8)), dmin = f16_to_f32(blk[2] | (blk[3] << 8));
-        uint32_t sw[3];
-        for (int k = 0; k < 3; k++)
-            sw[k] = blk[4 + 4 * k] | (blk[5 + 4 * k] << 8) | (blk[6 + 4 * k] << 16) | ((uint32_t)blk[7 + 4 * k] << 24);
-        int sc, m;
-        q4k_scale_min(sw, 2 * c + hi, sc, m);
-        const int q = hi ? (blk[16 + 32 * c + l] >> 4) : (blk[16 + 32 * c + l] & 15);
-        return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
-    }
-    if (dt == Q6_K) {
-        const uint8_t *blk = src + (i / 256) * 210;
-        const int e = (int)(i % 256), h = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
-        const float d = f16_to_f32(blk[208] | (blk[209] << 8));
-        const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
-        const int lowb = (quarter & 1) ? ql[l + 32] : ql[l];
-        const int low = (quarter >> 1) ? (lowb >> 4) : (lowb & 15);
-        const int q = (low | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
-        const int sc = (int8_t)blk[192 + 8 * h + (l >> 4) + 2 * quarter];
-        return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
-    }
-    if (dt == Q8_0) {
-        const uint8_t *blk = src + (i / 32) * 34;
-        return __fmul_rn(f16_to_f32(blk[0] | (blk[1] << 8)), (float)(int8_t)blk[2 + i % 32]);
-    }
-    if (dt == F16) return f16_to_f32(src[2 * i] | (src[2 * i + 1] << 8));
-    return ((const float *)src)[i];
-}
-
 __global__ void dequantize_kernel(int dt, const uint8_t *__restrict__ src, float *__restrict__ dst, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         dst[i] = decode_elem(dt, src, i);

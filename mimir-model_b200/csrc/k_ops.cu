@@ -306,21 +306,6 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
     }
 }
 
-// ------------------------------------------------------------- argmax
-// argmax (cmd/mim-run/main.go:184-193): best = 0; x > v[best] moves best.
-// The result is the first index of the largest non-NaN value (NaNs never
-// compare greater), or 0 when v[0] is NaN.  Each block reduces a strided
-// share to (value, index) and folds it into one 64-bit key by atomicMax:
-// the value's order-preserving bits above the complement of the index, so
-// the larger value and then the smaller index wins; -0 counts as +0, as the
-// reference's comparison does.  A NaN first value sets the all-ones key.
-// With tensor parallelism each rank folds its vocabulary slice (global
-// indices i0 + i) and the keys meet in a 64-bit max all-reduce.
-__device__ __forceinline__ unsigned long long argmax_key(float v, long long i) {
-    uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
-    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
-}
 
 __global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n, long long i0,
                                                      int holds_first, unsigned long long *__restrict__ key,

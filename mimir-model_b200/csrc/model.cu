@@ -20,6 +20,7 @@
 #include "ctx.h"
 #include "kernels.h"
 #include "model_kernels.h"
+#include "step.h"
 
 using namespace mimgpu;
 
@@ -76,6 +77,12 @@ struct mimgpu_session {
     bool batched = false;                // the run in flight uses `slot`
     cudaGraphExec_t g_batch = nullptr;   // batched greedy step of g_batch_rows rows
     int g_batch_rows = 0;
+    // the one-kernel decode step (k_step.cu), when the model qualifies
+    bool step_ok = false, use_step = false;
+    StepLayer *step_layers = nullptr;    // device [layers]
+    float2 *rope_cs = nullptr;           // device [context][rope_dims / 2]
+    unsigned *step_sync = nullptr;       // grid counters, then [2] steps completed / CTA exits
+    unsigned long long *trace = nullptr; // caller's timeline buffer of the step kernel, or null
 };
 
 namespace {
@@ -262,6 +269,50 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     return cudaSuccess;
 }
 
+// The T = 1 step of sequence 0 as one persistent kernel (k_step.cu); with
+// greedy, the key folded by the head's chain warps becomes the next token.
+cudaError_t enqueue_step(mimgpu_session *s, bool greedy, unsigned *status) {
+    const mimgpu_model *m = s->m;
+    const auto &c = m->c;
+    const mimgpu_tensor *head = m->out ? m->out : m->embd;
+    StepParams p{};
+    p.layers = s->step_layers;
+    p.L = c.layers;
+    p.E = c.embed;
+    p.F = c.ffn;
+    p.H = c.heads;
+    p.Hkv = c.kv_heads;
+    p.D = c.head_dim;
+    p.V = c.vocab;
+    p.C = c.context;
+    p.rotary = c.rope_dims;
+    p.eps = (float)c.norm_eps;
+    p.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    p.embd = m->embd->dev;
+    p.embd_dt = m->embd->dtype;
+    p.head = head->dev;
+    p.head_dt = head->dtype;
+    p.out_norm = (const float *)m->out_norm->dev;
+    p.rope_cs = s->rope_cs;
+    p.tok = s->tok;
+    p.pos = s->pos;
+    p.x = s->x;
+    p.qh = s->qh;
+    p.att = s->att;
+    p.a = s->a;
+    p.logits = s->logits;
+    p.actE = s->actE;
+    p.actF = s->actF;
+    p.amax = greedy ? s->amax : nullptr;
+    p.sync = s->step_sync;
+    p.epoch = s->step_sync + step_sync_words(c.layers, c.ffn);
+    p.status = status;
+    p.trace = s->trace;
+    cudaError_t e = launch_step(p, s->st);
+    if (e == cudaSuccess && greedy) e = launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, s->st, false);
+    return e;
+}
+
 // rows > 1: a batched step (row r of sequence slot[r], logits of every row)
 int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out, int rows = 1) {
     mimgpu_ctx *c = s->m->ctx;
@@ -269,7 +320,8 @@ int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out, int rows = 1) 
     cudaError_t e = cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return cuda_fail(c, e, "begin capture");
     s->batched = rows > 1;
-    cudaError_t fe = enqueue_forward(s, rows, rows > 1, greedy, c->status);
+    cudaError_t fe = (rows == 1 && s->use_step) ? enqueue_step(s, greedy, c->status)
+                                                : enqueue_forward(s, rows, rows > 1, greedy, c->status);
     s->batched = false;
     e = cudaStreamEndCapture(s->st, &g);
     if (fe != cudaSuccess) {
@@ -282,6 +334,53 @@ int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out, int rows = 1) 
     return cuda_fail(c, e, "instantiate");
 }
 
+// Device state of the one-kernel step for a single-GPU a8 model whose
+// dimensions qualify (step_ok): the layer table, the RoPE cos/sin table and
+// the grid counters (zero; they only ever grow).
+int setup_step(mimgpu_session *s) {
+    mimgpu_model *m = s->m;
+    const auto &c = m->c;
+    mimgpu_ctx *x = m->ctx;
+    const mimgpu_tensor *head = m->out ? m->out : m->embd;
+    bool ok = tp_size(m->tp) == 1 && c.a8 && (head->dtype == Q4_K || head->dtype == Q6_K) &&
+              step_ok(c.embed, c.ffn, c.heads, c.kv_heads, c.head_dim, c.context, c.rope_dims, c.interleaved,
+                      c.cache_f16);
+    for (int l = 0; l < c.layers && ok; l++) {
+        const LayerW &w = m->L[l];
+        const mimgpu_tensor *mats[7] = {w.q, w.k, w.v, w.o, w.gate, w.up, w.down};
+        for (auto *t : mats) ok &= t->dtype == Q4_K || t->dtype == Q6_K;
+        ok &= w.gate->dtype == w.up->dtype;
+    }
+    if (!ok) return MIMGPU_OK;
+    std::vector<StepLayer> host(c.layers);
+    for (int l = 0; l < c.layers; l++) {
+        const LayerW &w = m->L[l];
+        const mimgpu_tensor *mats[7] = {w.q, w.k, w.v, w.o, w.gate, w.up, w.down};
+        for (int i = 0; i < 7; i++) {
+            host[l].w[i] = mats[i]->dev;
+            host[l].dt[i] = mats[i]->dtype;
+        }
+        host[l].attn_norm = (const float *)w.attn_norm->dev;
+        host[l].ffn_norm = (const float *)w.ffn_norm->dev;
+        host[l].kc = s->kc[l];
+        host[l].vc = s->vc[l];
+    }
+    const size_t words = step_sync_words(c.layers, c.ffn) + 2;
+    const int half = c.rope_dims / 2;
+    cudaError_t e = cudaMalloc(&s->step_layers, host.size() * sizeof(StepLayer));
+    if (e == cudaSuccess) e = cudaMalloc(&s->rope_cs, (size_t)c.context * half * sizeof(float2));
+    if (e == cudaSuccess) e = cudaMalloc(&s->step_sync, words * sizeof(unsigned));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(s->step_layers, host.data(), host.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(s->step_sync, 0, words * sizeof(unsigned));
+    if (e == cudaSuccess) e = launch_rope_table(m->inv_freq, c.context, half, s->rope_cs, s->st);
+    if (e == cudaSuccess) e = step_prepare();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+    if (e != cudaSuccess) return cuda_fail(x, e, "step kernel setup");
+    s->step_ok = s->use_step = true;
+    return MIMGPU_OK;
+}
+
 void free_session(mimgpu_session *s) {
     if (!s) return;
     cudaSetDevice(s->m->ctx->device);
@@ -289,6 +388,9 @@ void free_session(mimgpu_session *s) {
     if (s->g_step) cudaGraphExecDestroy(s->g_step);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     if (s->g_batch) cudaGraphExecDestroy(s->g_batch);
+    if (s->step_layers) cudaFree(s->step_layers);
+    if (s->rope_cs) cudaFree(s->rope_cs);
+    if (s->step_sync) cudaFree(s->step_sync);
     for (void *p : s->kc) cudaFree(p);
     for (void *p : s->vc) cudaFree(p);
     for (void *p : s->opened) cudaIpcCloseMemHandle(p);
@@ -462,6 +564,10 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
         free_session(s);
         return rc;
     }
+    if ((rc = setup_step(s))) {
+        free_session(s);
+        return rc;
+    }
     *out = s;
     return MIMGPU_OK;
 }
@@ -613,6 +719,46 @@ int mimgpu_session_generate_slots(mimgpu_session *s, const int32_t *tokens, cons
 }
 
 void *mimgpu_session_stream(mimgpu_session *s) { return s ? (void *)s->st : nullptr; }
+
+int mimgpu_session_set_step_kernel(mimgpu_session *s, int on) {
+    if (!s) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (on && !s->step_ok) return fail(c, MIMGPU_ENOTHANDLED, "the model does not run through the step kernel");
+    if ((on != 0) == s->use_step) return MIMGPU_OK;
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaStreamSynchronize(s->st);
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    s->g_step = s->g_greedy = nullptr;
+    s->use_step = on != 0;
+    return MIMGPU_OK;
+}
+
+int mimgpu_session_uses_step_kernel(mimgpu_session *s) { return s && s->use_step ? 1 : 0; }
+
+size_t mimgpu_session_trace_bytes(mimgpu_session *s) {
+    if (!s || !s->step_ok) return 0;
+    return (size_t)num_sms() * step_trace_words(s->m->c.layers) * sizeof(unsigned long long);
+}
+
+int mimgpu_session_set_trace(mimgpu_session *s, void *dev_buf, size_t nbytes) {
+    if (!s) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (dev_buf && nbytes < mimgpu_session_trace_bytes(s))
+        return fail(c, MIMGPU_EINVAL, "trace buffer of %zu bytes; the step kernel needs %zu", nbytes,
+                    mimgpu_session_trace_bytes(s));
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaStreamSynchronize(s->st);
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    s->g_step = s->g_greedy = nullptr;
+    s->trace = (unsigned long long *)dev_buf;
+    return MIMGPU_OK;
+}
 
 int mimgpu_session_ipc_handle(mimgpu_session *s, void *out, size_t nbytes) {
     if (!s || !out || nbytes < sizeof(cudaIpcMemHandle_t)) return MIMGPU_EINVAL;

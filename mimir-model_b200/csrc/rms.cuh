@@ -40,6 +40,17 @@ static __device__ __noinline__ double rms_seq_sum(const float *xr, int n) {
     return ss;
 }
 
+// The same sum over a row other CTAs of the running kernel wrote (read
+// through L2, not a possibly stale L1 line).
+static __device__ __noinline__ double rms_seq_sum_cg(const float *xr, int n) {
+    double ss = 0.0;
+    for (int i = 0; i < n; i++) {
+        const double e = (double)__ldcg(xr + i);
+        ss = __fma_rn(e, e, ss);
+    }
+    return ss;
+}
+
 __device__ __forceinline__ float rms_inv_of_mean(float ms, float eps) {
     return (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)ms, (double)eps)));
 }

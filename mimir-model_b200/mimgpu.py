@@ -65,6 +65,10 @@ SIGNATURES = {
     "mimgpu_session_run_slots": (I32, [P, P, P, P, I32, P]),
     "mimgpu_session_generate_slots": (I32, [P, P, P, I32, I32, P]),
     "mimgpu_session_stream": (P, [P]),
+    "mimgpu_session_set_step_kernel": (I32, [P, I32]),
+    "mimgpu_session_uses_step_kernel": (I32, [P]),
+    "mimgpu_session_trace_bytes": (SZ, [P]),
+    "mimgpu_session_set_trace": (I32, [P, P, SZ]),
     "mimgpu_tp_unique_id": (I32, [P, SZ]),
     "mimgpu_tp_new": (I32, [P, P, SZ, I32, I32, C.POINTER(P)]),
     "mimgpu_tp_free": (None, [P]),
@@ -430,6 +434,22 @@ class Session:
         ids = np.empty(steps, np.int32)
         self.m.ctx._check(lib().mimgpu_session_generate(self.h, token, pos, steps, _p(ids)))
         return ids
+
+    def set_step_kernel(self, on: bool):
+        """One persistent kernel per decode step (the default where the model
+        qualifies) or the kernel-per-op path; both give the same bits."""
+        self.m.ctx._check(lib().mimgpu_session_set_step_kernel(self.h, int(on)))
+
+    def trace_bytes(self) -> int:
+        return lib().mimgpu_session_trace_bytes(self.h)
+
+    def set_trace(self, dev_ptr: int | None, nbytes: int = 0):
+        """Binds a device buffer for the step kernel's phase timeline (profiling)."""
+        self.m.ctx._check(lib().mimgpu_session_set_trace(self.h, dev_ptr, nbytes))
+
+    @property
+    def uses_step_kernel(self) -> bool:
+        return bool(lib().mimgpu_session_uses_step_kernel(self.h))
 
     @property
     def stream(self) -> int:
