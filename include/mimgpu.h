@@ -249,7 +249,8 @@ void *mimgpu_session_stream(mimgpu_session *s);
  * through one pipeline; on = 0 launches one kernel per op.  Both give the same
  * bits.  The persistent kernel is the default for single-GPU sessions of
  * 8-bit-activation models with Q4_K / Q6_K matrices, E and F multiples of 256
- * (2048..32768), head size 128, an f16 cache and interleaved RoPE; for other
+ * (E 2048..8192, F 2048..32768), head size 128, an f16 cache and interleaved
+ * RoPE; for other
  * models on = 1 returns MIMGPU_ENOTHANDLED. */
 int mimgpu_session_set_step_kernel(mimgpu_session *s, int on);
 /* 1 when one-token steps run as one persistent kernel, else 0. */

@@ -66,6 +66,7 @@ constexpr int kChunkB = kKeys * 128 * 2;        // bytes of an attention chunk
 constexpr int kAttnSlots = 4;                   // attention chunk ring: slots at most
 constexpr uint32_t kPrefetch = 256 * 1024;      // weight bytes a CTA prefetches into L2 beyond the stage it issues
 constexpr int kMaxK = 4 * 16 * kCT;             // activation staging: 4 chunks of 16 quants per thread
+constexpr int kMaxE = 2 * 256 * kCW;            // RMSNorm: two 256-element blocks per consumer warp
 constexpr unsigned FULLM = 0xffffffffu;
 constexpr int kRoles = 1 + kCW + kNC;
 
@@ -74,7 +75,7 @@ enum { J_QKV = 0, J_O = 1, J_GU = 2, J_DOWN = 3, J_HEAD = 4 };
 enum { C_QKV = 0, C_ATT = 1, C_O = 2, C_QUANT = 3, C_DOWN = 4 };
 
 struct Smem {
-    int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring, ring;
+    int off_lt, off_act, off_hdr, off_ys, off_rec, off_bad, off_ring, ring;
 };
 
 // misc words after the barriers
@@ -170,7 +171,7 @@ struct Seg {
 __device__ __forceinline__ int njobs(const StepParams &p) { return 4 * p.L + 1; }
 __device__ __forceinline__ int nsegs(int kind) { return kind == J_QKV ? 3 : 1; }
 
-__device__ Seg get_seg(const StepParams &p, int job, int s) {
+__device__ Seg get_seg(const StepParams &p, const StepLayer *lt, int job, int s) {
     const int kind = job == 4 * p.L ? J_HEAD : job & 3;
     Seg g;
     g.w2 = nullptr;
@@ -180,7 +181,7 @@ __device__ Seg get_seg(const StepParams &p, int job, int s) {
         g.dt = p.head_dt;
         g.n = p.V;
     } else {
-        const StepLayer &ly = p.layers[job >> 2];
+        const StepLayer &ly = lt[job >> 2];
         const int i = kind == J_QKV ? s : kind == J_O ? 3 : kind == J_GU ? 4 : 6;
         g.w = ly.w[i];
         g.dt = ly.dt[i];
@@ -205,26 +206,26 @@ struct Cursor {
     Seg g;
 };
 __device__ __forceinline__ int kind_of(const StepParams &p, int j) { return j == 4 * p.L ? J_HEAD : j & 3; }
-__device__ void cur_fix(Cursor &c, const StepParams &p, int nj) {
+__device__ void cur_fix(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
     while (c.j < nj && c.row0 >= c.nr) {
         c.row0 = 0;
         if (++c.s >= nsegs(kind_of(p, c.j))) {
             c.s = 0;
             if (++c.j >= nj) break;
         }
-        c.g = get_seg(p, c.j, c.s);
+        c.g = get_seg(p, lt, c.j, c.s);
         slab(c.g.n, blockIdx.x, gridDim.x, c.g.unit, c.r0, c.nr);
     }
 }
-__device__ void cur_start(Cursor &c, const StepParams &p, int nj) {
+__device__ void cur_start(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
     c.j = c.s = c.row0 = 0;
-    c.g = get_seg(p, 0, 0);
+    c.g = get_seg(p, lt, 0, 0);
     slab(c.g.n, blockIdx.x, gridDim.x, c.g.unit, c.r0, c.nr);
-    cur_fix(c, p, nj);
+    cur_fix(c, p, lt, nj);
 }
-__device__ __forceinline__ void cur_step(Cursor &c, const StepParams &p, int nj) {
+__device__ __forceinline__ void cur_step(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
     c.row0 += c.g.rps;
-    cur_fix(c, p, nj);
+    cur_fix(c, p, lt, nj);
 }
 
 // Next stage's ring offset (producer and consumers compute the same sequence).
@@ -316,10 +317,27 @@ __device__ __forceinline__ void quant_store_smem(uint8_t *smem, const Smem &sm, 
 // rms_norm of the residual (fast.go:434-485, mean bit-exact: rms.cuh) times
 // the norm weight, quantized block by block into shared memory.  Every CTA
 // computes the whole row for itself.  Consumer threads only.
+// The wait for the residual (grid counter wctr at target) happens in here,
+// after the norm weights, which are constant, are already on their way.
 __device__ void norm_phase(const StepParams &p, const float *__restrict__ wn, uint8_t *smem, const Smem &sm,
-                           Misc &ms, int slot) {
+                           Misc &ms, int slot, const unsigned *wctr, unsigned target, int ready_slot) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nblk = p.E / 256, bpw = (nblk + kCW - 1) / kCW;  // blocks per warp
+    constexpr int kBpw = kMaxE / 256 / kCW;                     // blocks per warp at most
+    float4 wreg[2 * kBpw];
+#pragma unroll
+    for (int j = 0; j < kBpw; j++) {
+        const int kb = warp + kCW * j;
+        if (j < bpw && kb < nblk) {
+            wreg[2 * j] = __ldg((const float4 *)(wn + kb * 256 + 8 * lane));
+            wreg[2 * j + 1] = __ldg((const float4 *)(wn + kb * 256 + 8 * lane) + 1);
+        }
+    }
+    if (threadIdx.x == 0) {
+        grid_wait(wctr, target, p.status, ms);
+        stamp(p, ready_slot);
+    }
+    bar_cons();
     double ss = 0.0;
     for (int j = 0; j < bpw; j++) {
         const int kb = warp + kCW * j;
@@ -348,13 +366,14 @@ __device__ void norm_phase(const StepParams &p, const float *__restrict__ wn, ui
     bar_cons();
     const float inv = ms.inv[slot];
     bool all_ok = true;
-    for (int j = 0; j < bpw; j++) {
+#pragma unroll
+    for (int j = 0; j < kBpw; j++) {
         const int kb = warp + kCW * j;
-        if (kb >= nblk) break;
+        if (j >= bpw || kb >= nblk) break;
         const int e0 = kb * 256 + 8 * lane;
         const float4 *src = (const float4 *)(p.x + e0);
         const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
-        const float4 w0 = __ldg((const float4 *)(wn + e0)), w1 = __ldg((const float4 *)(wn + e0) + 1);
+        const float4 w0 = wreg[2 * j], w1 = wreg[2 * j + 1];
         const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float v[8];
@@ -427,8 +446,8 @@ __host__ __device__ inline int attn_fixed_bytes(int HU, int n) {
 // layer started); the token's own key and value rows, written this step by
 // other CTAs, are read through L2 and patched into the chunk.  `au` counts
 // each ring barrier's completed phases (identical in every consumer thread).
-__device__ void attn_unit(const StepParams &p, int l, int unit, int HU, uint8_t *smem, const Smem &sm, Misc &ms,
-                          int (&au)[kAttnSlots]) {
+__device__ void attn_unit(const StepParams &p, const StepLayer *lt, int l, int unit, int HU, uint8_t *smem,
+                          const Smem &sm, Misc &ms, int (&au)[kAttnSlots]) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = 128, G = p.H / p.Hkv, h0 = unit * HU, kvh = h0 / G;
     const int pos = (int)__ldcg(p.pos), n = pos + 1, n4 = n & ~3, n8 = n >= 8 ? (n & ~7) : 0;
@@ -438,7 +457,7 @@ __device__ void attn_unit(const StepParams &p, int l, int unit, int HU, uint8_t 
     float *sc = obuf + HU * D;                // [HU][n]
     uint8_t *ring = smem + sm.off_act + attn_fixed_bytes(HU, n);
     const int nsl = min(kAttnSlots, (sm.off_bad - sm.off_act - attn_fixed_bytes(HU, n)) / kChunkB);  // >= 2
-    const StepLayer &ly = p.layers[l];
+    const StepLayer &ly = lt[l];
     const uint8_t *kbase = (const uint8_t *)ly.kc + (size_t)kvh * p.C * D * 2;
     const uint8_t *vbase = (const uint8_t *)ly.vc + (size_t)kvh * p.C * D * 2;
     auto parity = [&](int i) { return (uint32_t)((au[i % nsl] + i / nsl) & 1); };
@@ -612,6 +631,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         fence_barrier_init();
     }
     for (int i = threadIdx.x; i < kRS * kRowsCap; i += kThreads) smem[sm.off_bad + i] = 0;
+    // the layer table in shared memory: every role reads it at each op
+    StepLayer *lt = (StepLayer *)(smem + sm.off_lt);
+    for (int i = threadIdx.x; i < p.L * (int)(sizeof(StepLayer) / 8); i += kThreads)
+        ((uint2 *)lt)[i] = __ldg((const uint2 *)p.layers + i);
     __syncthreads();
     uint8_t *ring = smem + sm.off_ring;
 
@@ -628,8 +651,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             bool ok = true;
             const uint64_t pol = l2_policy_evict_first();
             Cursor ic, pc;
-            cur_start(ic, p, nj);
-            cur_start(pc, p, nj);
+            cur_start(ic, p, lt, nj);
+            cur_start(pc, p, lt, nj);
             while (ic.j < nj && ok) {
                 while (pc.j < nj && ahead < kPrefetch) {
                     const uint32_t part = (uint32_t)(min(pc.g.rps, pc.nr - pc.row0) * pc.g.rb);
@@ -637,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                     prefetch_l2(pc.g.w + src, part);
                     if (pc.g.w2) prefetch_l2(pc.g.w2 + src, part);
                     ahead += part * (pc.g.w2 ? 2u : 1u);
-                    cur_step(pc, p, nj);
+                    cur_step(pc, p, lt, nj);
                 }
                 if (ic.j != lastj) {
                     if (lastj >= 0) stamp(p, jslot(lastj, 6));
@@ -670,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 if (g.w2) bulk_g2s_hint(ring + off + part, g.w2 + src, part, fb, pol);
                 ahead -= min(ahead, bytes);
                 m++;
-                cur_step(ic, p, nj);
+                cur_step(ic, p, lt, nj);
             }
             if (lastj >= 0) stamp(p, jslot(lastj, 6));
             // copies still in flight land before the block exits
@@ -694,9 +717,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         bar_chain();
         for (int j = 0; j < nj; j++) {
             const int kind = j == 4 * p.L ? J_HEAD : j & 3, l = j >> 2;
-            const StepLayer *ly = kind == J_HEAD ? nullptr : &p.layers[l];
+            const StepLayer *ly = kind == J_HEAD ? nullptr : &lt[l];
             for (int s = 0; s < nsegs(kind); s++) {
-                const Seg g = get_seg(p, j, s);
+                const Seg g = get_seg(p, lt, j, s);
                 int r0, nr;
                 slab(g.n, cta, G, g.unit, r0, nr);
                 const int nb = g.nb, rstride = (nb + 1) * 16;
@@ -817,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 // this CTA's gate rows by 256-element block of the SwiGLU output: the
                 // CTA whose rows complete a block quantizes it for the down product
                 // (the two chain warps take alternate completed blocks)
-                const Seg g = get_seg(p, j, 0);
+                const Seg g = get_seg(p, lt, j, 0);
                 int r0, nr;
                 slab(g.n, cta, G, g.unit, r0, nr);
                 const int b0 = r0 / 256, nbk = nr > 0 ? (r0 + nr - 1) / 256 - b0 + 1 : 0;
@@ -826,7 +849,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                     if (lane < nbk) {
                         const int b = b0 + lane;
                         const int rin = min(r0 + nr, 256 * (b + 1)) - max(r0, 256 * b);
-                        __threadfence();
                         last = atom_acqrel(&blkctr[l * nfb + b], (unsigned)rin) + (unsigned)rin == 256u * (ep + 1);
                     }
                     const unsigned mask = __ballot_sync(FULLM, last);
@@ -850,12 +872,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                     done++;
                 }
                 __syncwarp();
-                if (lane == 0 && done) {
-                    __threadfence();
-                    red_rel(&ctr[1 + 5 * l + C_QUANT], done);
-                }
+                if (lane == 0 && done) red_rel(&ctr[1 + 5 * l + C_QUANT], done);
             } else if (c == 0 && lane == 0) {
-                __threadfence();
                 red_rel(&ctr[1 + 5 * l + (kind == J_QKV ? C_QKV : kind == J_O ? C_O : C_DOWN)], 1u);
             }
         }
@@ -887,10 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 __stcg(p.x + e0 + i, v);
             }
             bar_cons();
-            if (threadIdx.x == 0) {
-                __threadfence();
-                red_rel(&ctr[0], 1u);
-            }
+            if (threadIdx.x == 0) red_rel(&ctr[0], 1u);
         }
         for (int j = 0; j < nj; j++) {
             const int kind = j == 4 * p.L ? J_HEAD : j & 3, l = j >> 2;
@@ -901,31 +916,25 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 if (pos > 0) {
                     const uint64_t keep = l2_policy_evict_last();
                     const size_t kvoff = (size_t)((cta * HU) / (p.H / p.Hkv)) * p.C * p.D * 2;
-                    prefetch_l2_hint((const uint8_t *)p.layers[l].kc + kvoff, (uint32_t)pos * p.D * 2, keep);
-                    prefetch_l2_hint((const uint8_t *)p.layers[l].vc + kvoff, (uint32_t)pos * p.D * 2, keep);
+                    prefetch_l2_hint((const uint8_t *)lt[l].kc + kvoff, (uint32_t)pos * p.D * 2, keep);
+                    prefetch_l2_hint((const uint8_t *)lt[l].vc + kvoff, (uint32_t)pos * p.D * 2, keep);
                 }
             }
             if (kind == J_QKV || kind == J_GU || kind == J_HEAD) {
                 const unsigned *w = kind == J_QKV ? (l == 0 ? &ctr[0] : &ctr[1 + 5 * (l - 1) + C_DOWN])
                                     : kind == J_GU ? &ctr[1 + 5 * l + C_O]
                                                    : &ctr[1 + 5 * (p.L - 1) + C_DOWN];
-                if (threadIdx.x == 0) {
-                    grid_wait(w, (unsigned)G * (ep + 1), p.status, ms);
-                    stamp(p, jslot(j, 0));
-                }
-                bar_cons();
-                const float *wn = kind == J_QKV ? p.layers[l].attn_norm : kind == J_GU ? p.layers[l].ffn_norm
-                                                                                         : p.out_norm;
-                norm_phase(p, wn, smem, sm, ms, kind == J_QKV ? 0 : kind == J_GU ? 1 : 2);
+                const float *wn = kind == J_QKV ? lt[l].attn_norm : kind == J_GU ? lt[l].ffn_norm : p.out_norm;
+                norm_phase(p, wn, smem, sm, ms, kind == J_QKV ? 0 : kind == J_GU ? 1 : 2, w, (unsigned)G * (ep + 1),
+                           jslot(j, 0));
             } else if (kind == J_O) {
                 // attention units on the first CTAs, once every q / k / v row is written
                 if (cta < units) {
                     if (threadIdx.x == 0) grid_wait(&ctr[1 + 5 * l + C_QKV], (unsigned)G * (ep + 1), p.status, ms);
                     bar_cons();
-                    if (!aborted(ms)) attn_unit(p, l, cta, HU, smem, sm, ms, au);
+                    if (!aborted(ms)) attn_unit(p, lt, l, cta, HU, smem, sm, ms, au);
                     bar_cons();
                     if (threadIdx.x == 0) {
-                        __threadfence();
                         red_rel(&ctr[1 + 5 * l + C_ATT], 1u);
                         stamp(p, jslot(j, 3));
                     }
@@ -948,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             if (threadIdx.x == 0) stamp(p, jslot(j, 1));
             // ---- the product's stages
             for (int s = 0; s < nsegs(kind); s++) {
-                const Seg g = get_seg(p, j, s);
+                const Seg g = get_seg(p, lt, j, s);
                 int r0, nr;
                 slab(g.n, cta, G, g.unit, r0, nr);
                 const int nb = g.nb, sbk = (g.w2 ? 2 : 1) * g.rps * nb;
@@ -1031,7 +1040,7 @@ int act_region(int nbmax) {
 }  // namespace
 
 bool step_ok(int E, int F, int H, int Hkv, int D, int C, int rotary, int interleaved, int cache_f16) {
-    if (E % 256 || F % 256 || E < 2048 || F < 2048 || E > kMaxK || F > kMaxK) return false;
+    if (E % 256 || F % 256 || E < 2048 || F < 2048 || E > kMaxE || F > kMaxK) return false;
     if (D != 128 || Hkv <= 0 || H % Hkv || H * D != E || !interleaved || !cache_f16 || rotary % 2 || rotary > D)
         return false;
     const int G = H / Hkv, HU = G >= 4 ? 4 : G;
@@ -1056,7 +1065,8 @@ cudaError_t launch_step(const StepParams &p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     Smem sm;
     const int nbmax = (p.E > p.F ? p.E : p.F) / 256;
-    sm.off_act = (kMiscOff + (int)sizeof(Misc) + 127) & ~127;
+    sm.off_lt = (kMiscOff + (int)sizeof(Misc) + 15) & ~15;
+    sm.off_act = (sm.off_lt + p.L * (int)sizeof(StepLayer) + 127) & ~127;
     sm.off_hdr = sm.off_act + ((act_bytes(nbmax) + 15) & ~15);
     sm.off_ys = sm.off_hdr + hdr_bytes(nbmax);
     sm.off_rec = (sm.off_ys + hdr_bytes(nbmax) + 127) & ~127;

@@ -50,8 +50,8 @@ struct StepParams {
 __host__ __device__ inline size_t step_trace_words(int L) { return 2 + 8 * (size_t)(4 * L + 1); }
 
 // Whether a model of these dimensions runs through the step kernel (else the
-// kernel-per-op path): Q4_K / Q6_K matrices, K a multiple of 256 up to
-// 28672, head size 128 with 2, 4, 8 ... query heads per kv head, an f16 cache
+// kernel-per-op path): Q4_K / Q6_K matrices, E a multiple of 256 up to 8192,
+// F up to 32768, head size 128 with 2, 4, 8 ... query heads per kv head, an f16 cache
 // whose attention scratch fits shared memory, interleaved RoPE.
 bool step_ok(int E, int F, int H, int Hkv, int D, int C, int rotary, int interleaved, int cache_f16);
 size_t step_sync_words(int L, int F);
