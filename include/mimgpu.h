@@ -67,8 +67,21 @@ void mimgpu_close(mimgpu_ctx *ctx);
 /* Text of the last error on this context ("" if none).  Valid until the
  * next call on the context. */
 const char *mimgpu_last_error(mimgpu_ctx *ctx);
-/* Upper bound, in milliseconds, of every wait on the device (default 60000). */
+/* Upper bound, in milliseconds, of the waits of this context: a host call
+ * waiting for device work (default 60000) and each bounded wait inside a
+ * kernel -- on a barrier, a grid counter or a peer's flag -- (default 2000
+ * until this is called).  A device wait that runs out ends its kernel early
+ * and the call that waits for it returns MIMGPU_ETIMEOUT; the context stays
+ * usable. */
 int mimgpu_set_timeout_ms(mimgpu_ctx *ctx, int64_t ms);
+/* Queues, on `stream` (NULL = the context's stream), a wait until the 32-bit
+ * word at `addr` (device or mapped host memory, 4-byte aligned) equals
+ * `value`: the device-side doorbell a caller uses to hold this context's work
+ * until another process, GPU or the host writes a flag.  No counterpart in
+ * the reference.  The wait is bounded by the context's limit
+ * (mimgpu_set_timeout_ms); when it runs out, the next call that waits for the
+ * device returns MIMGPU_ETIMEOUT. */
+int mimgpu_stream_wait_value(mimgpu_ctx *ctx, void *stream, const uint32_t *addr, uint32_t value);
 
 /* ------------------------------------------------------------ weights */
 

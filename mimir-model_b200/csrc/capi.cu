@@ -170,8 +170,11 @@ int mimgpu_open(int device, mimgpu_ctx **out) {
     if (cudaSetDevice(device) != cudaSuccess) return MIMGPU_ECUDA;
     auto *c = new mimgpu_ctx;
     c->device = device;
+    // status block: [0] DevStatus bits, [2..3] the wait limit of a device wait (ns)
+    const unsigned long long limit = kDefaultWaitNs;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&c->status, 256) != cudaSuccess || cudaMemset(c->status, 0, 256) != cudaSuccess) {
+        cudaMalloc(&c->status, 256) != cudaSuccess || cudaMemset(c->status, 0, 256) != cudaSuccess ||
+        cudaMemcpy(c->status + 2, &limit, sizeof limit, cudaMemcpyHostToDevice) != cudaSuccess) {
         if (c->stream) cudaStreamDestroy(c->stream);
         delete c;
         return MIMGPU_ECUDA;
@@ -194,8 +197,27 @@ const char *mimgpu_last_error(mimgpu_ctx *c) { return c ? c->err.c_str() : "no c
 
 int mimgpu_set_timeout_ms(mimgpu_ctx *c, int64_t ms) {
     if (!c || ms <= 0) return MIMGPU_EINVAL;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = use_device(c);
+    if (rc) return rc;
+    // kernels read the limit when a wait is slow, so no launch has to change;
+    // the copy is ordered after the work already queued on the stream
+    const unsigned long long ns = (unsigned long long)ms * 1000000ull;
+    cudaError_t e = cudaMemcpyAsync(c->status + 2, &ns, sizeof ns, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "set_timeout_ms");
     c->timeout_ms = ms;
     return MIMGPU_OK;
+}
+
+int mimgpu_stream_wait_value(mimgpu_ctx *c, void *stream, const uint32_t *addr, uint32_t value) {
+    if (!c || !addr) return MIMGPU_EINVAL;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if ((uintptr_t)addr & 3) return fail(c, MIMGPU_EINVAL, "stream_wait_value: address not 4-byte aligned");
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    return cuda_fail(c, launch_wait_value(addr, value, c->status, st), "stream_wait_value");
 }
 
 int mimgpu_upload(mimgpu_ctx *c, int dtype, int ndim, const int64_t *shape, const void *bytes, size_t nbytes,

@@ -185,14 +185,22 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Waits for the phase with the given parity to complete.  Gives up after
-// `limit_ns` nanoseconds of wall time (2 s by default), sets DEV_TIMEOUT in
+// The context's limit of one bounded device wait, in nanoseconds: the
+// 64-bit word after the status word (mimgpu_set_timeout_ms; 2 s until set).
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+__device__ __forceinline__ uint64_t dev_wait_limit(const unsigned *status) {
+    if (!status) return kDefaultWaitNs;
+    const uint64_t v = *(volatile const unsigned long long *)(status + 2);
+    return v ? v : kDefaultWaitNs;
+}
+
+// Waits for the phase with the given parity to complete.  Gives up after the
+// context's wait limit (dev_wait_limit) of wall time, sets DEV_TIMEOUT in
 // *status and returns false, so a lost arrival ends the kernel with an error
 // the host reads instead of a hang.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *status,
-                                                  uint64_t limit_ns = 2000000000ull) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *status) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
+    const uint64_t t0 = global_ns(), limit_ns = dev_wait_limit(status);
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255) == 0 && global_ns() - t0 > limit_ns) break;

@@ -174,12 +174,12 @@ __device__ __forceinline__ void st16(uint8_t *p, uint32_t a, uint32_t b, uint32_
 // kernel is aborting (DEV_TIMEOUT is set by whoever timed out first).
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, Bars &B, unsigned *status) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
+    const uint64_t t0 = global_ns(), limit = dev_wait_limit(status);
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255) == 0) {
             if (*(volatile int *)&B.abort) return false;
-            if (global_ns() - t0 > 2000000000ull) {
+            if (global_ns() - t0 > limit) {
                 *(volatile int *)&B.abort = 1;
                 atomicOr(status, (unsigned)DEV_TIMEOUT);
                 return false;

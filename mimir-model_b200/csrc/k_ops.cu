@@ -399,6 +399,27 @@ cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_
     return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, i0, (int)holds_first, key, ldv);
 }
 
+namespace {
+__global__ void wait_value_kernel(const uint32_t *addr, uint32_t value, unsigned *status) {
+    const uint64_t t0 = global_ns(), limit = dev_wait_limit(status);
+    for (uint32_t i = 0;; i++) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+        if (v == value) return;
+        if ((i & 63) == 63) {
+            if (global_ns() - t0 > limit) break;
+            __nanosleep(256);
+        }
+    }
+    atomicOr(status, (unsigned)DEV_TIMEOUT);
+}
+}  // namespace
+
+cudaError_t launch_wait_value(const uint32_t *addr, uint32_t value, unsigned *status, cudaStream_t st) {
+    wait_value_kernel<<<1, 1, 0, st>>>(addr, value, status);
+    return cudaGetLastError();
+}
+
 int num_sms() {
     static int n = 0;
     if (n == 0) {

@@ -108,10 +108,7 @@ __device__ __forceinline__ unsigned atom_acqrel(unsigned *p, unsigned v) {
 __device__ __forceinline__ void bar_cons() { asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory"); }
 __device__ __forceinline__ void bar_chain() { asm volatile("bar.sync 2, %0;" ::"r"(32 * kNC) : "memory"); }
 
-__device__ __forceinline__ uint64_t wait_limit(const unsigned *status) {
-    const uint64_t v = *(volatile const unsigned long long *)(status + 2);
-    return v ? v : 2000000000ull;
-}
+__device__ __forceinline__ uint64_t wait_limit(const unsigned *status) { return dev_wait_limit(status); }
 
 // A wait of this CTA gave up: later waits return at once.
 __device__ __forceinline__ bool aborted(const Misc &ms) { return *(volatile const int *)&ms.abort != 0; }

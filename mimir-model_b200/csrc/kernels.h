@@ -146,6 +146,10 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
 cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_first, unsigned long long *key,
                           cudaStream_t st, bool pdl, int rows = 1, long long ldv = 0);
 
+// One thread waits (bounded by the context's limit, acquire at system
+// scope) until *addr == value; a wait that runs out sets DEV_TIMEOUT.
+cudaError_t launch_wait_value(const uint32_t *addr, uint32_t value, unsigned *status, cudaStream_t st);
+
 // seeded synthetic weights (k_synth.cu)
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,
                          cudaStream_t st);

@@ -9,8 +9,9 @@
 // that follows it on the same stream publishes -- its first thread writes the
 // step's epoch into slot `slot`, entry `k` (this rank), of every rank's flag
 // array after a system-scope fence, one fence per exchange -- and then waits
-// until all N entries of the slot hold the epoch (bounded: 2 s, then
-// DEV_TIMEOUT in the status word and the kernel goes on with what it reads).  The epoch advances once per
+// until all N entries of the slot hold the epoch (bounded by the context's
+// wait limit, then DEV_TIMEOUT in the status word and the kernel goes on with
+// what it reads).  The epoch advances once per
 // forward, so flags never need resetting.  A rank can be at most one
 // exchange ahead of another (each exchange waits for every rank's previous
 // one), which is what keeps a producer from overwriting a buffer a slower
@@ -59,11 +60,11 @@ __device__ __forceinline__ void p2p_publish_wait(const P2P &x) {
     if (blockIdx.x == 0 && blockIdx.y == 0) p2p_publish(x);
     const unsigned e = *(volatile const unsigned *)x.epoch;
     const unsigned *f = peer_ptr<unsigned>(x, x.k, x.off_flags) + x.slot * x.N;
-    const uint64_t t0 = global_ns();
+    const uint64_t t0 = global_ns(), limit = dev_wait_limit(x.status);
     for (int r = 0; r < x.N; r++) {
         for (uint32_t i = 0;; i++) {
             if (ld_acquire_sys(f + r) == e) break;
-            if ((i & 63) == 63 && global_ns() - t0 > 2000000000ull) {
+            if ((i & 63) == 63 && global_ns() - t0 > limit) {
                 atomicOr(x.status, (unsigned)DEV_TIMEOUT);
                 return;
             }

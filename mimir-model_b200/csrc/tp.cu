@@ -13,8 +13,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "common.cuh"
 #include "ctx.h"
@@ -33,7 +35,10 @@ namespace {
 
 struct NcclApi {
     ncclResult_t (*getUniqueId)(ncclUniqueId *) = nullptr;
-    ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*commInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+    ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*commFinalize)(ncclComm_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
@@ -53,13 +58,16 @@ const NcclApi &nccl() {
             return;
         }
         api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
-        api.commInitRank = (decltype(api.commInitRank))dlsym(h, "ncclCommInitRank");
+        api.commInitRankConfig = (decltype(api.commInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+        api.commGetAsyncError = (decltype(api.commGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+        api.commAbort = (decltype(api.commAbort))dlsym(h, "ncclCommAbort");
+        api.commFinalize = (decltype(api.commFinalize))dlsym(h, "ncclCommFinalize");
         api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
         api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
         api.allReduce = (decltype(api.allReduce))dlsym(h, "ncclAllReduce");
         api.errorString = (decltype(api.errorString))dlsym(h, "ncclGetErrorString");
-        api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.allGather && api.allReduce &&
-                 api.errorString;
+        api.ok = api.getUniqueId && api.commInitRankConfig && api.commGetAsyncError && api.commAbort &&
+                 api.commFinalize && api.commDestroy && api.allGather && api.allReduce && api.errorString;
         if (!api.ok) api.why = "libnccl.so.2 lacks a required symbol";
     });
     return api;
@@ -84,20 +92,38 @@ __global__ void pack_kernel(const float *__restrict__ x, int T, long long ld, lo
     y[i] = x[(i / W) * ld + c0 + i % W];
 }
 
+// The communicators are non-blocking (ncclConfig_t.blocking = 0), so no NCCL
+// call can hang the host: a call that returns ncclInProgress is polled with
+// ncclCommGetAsyncError until it settles or `deadline_ms` passes.
+ncclResult_t settle(ncclComm_t comm, ncclResult_t r, int64_t deadline_ms) {
+    const NcclApi &api = nccl();
+    if (r != ncclInProgress) return r;
+    const auto end = std::chrono::steady_clock::now() + std::chrono::milliseconds(deadline_ms);
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        if (api.commGetAsyncError(comm, &st) != ncclSuccess) return ncclSystemError;
+        if (st != ncclInProgress) return st;
+        if (std::chrono::steady_clock::now() > end) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
 }  // namespace
 
 cudaError_t tp_allgather(mimgpu_tp *tp, const float *send, float *recv, size_t count, cudaStream_t st) {
     const NcclApi &api = nccl();
     if (!api.ok) return cudaErrorNotSupported;
-    return api.allGather(send, recv, count, ncclFloat32, tp->comm, st) == ncclSuccess ? cudaSuccess
-                                                                                   : cudaErrorUnknown;
+    const ncclResult_t r = settle(tp->comm, api.allGather(send, recv, count, ncclFloat32, tp->comm, st),
+                                  tp->ctx->timeout_ms);
+    return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
 
 cudaError_t tp_allreduce_max_u64(mimgpu_tp *tp, unsigned long long *buf, cudaStream_t st, size_t count) {
     const NcclApi &api = nccl();
     if (!api.ok) return cudaErrorNotSupported;
-    return api.allReduce(buf, buf, count, ncclUint64, ncclMax, tp->comm, st) == ncclSuccess ? cudaSuccess
-                                                                                           : cudaErrorUnknown;
+    const ncclResult_t r = settle(tp->comm, api.allReduce(buf, buf, count, ncclUint64, ncclMax, tp->comm, st),
+                                  tp->ctx->timeout_ms);
+    return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
 
 cudaError_t launch_unshard(const float *src, int N, int T, int W, float *dst, long long ldd, long long wmax,
@@ -149,10 +175,19 @@ int mimgpu_tp_new(mimgpu_ctx *c, const void *id, size_t nbytes, int nranks, int 
     tp->ctx = c;
     tp->nranks = nranks;
     tp->rank = rank;
-    const ncclResult_t r = api.commInitRank(&tp->comm, nranks, u, rank);
+    // non-blocking: a rank that never joins ends in MIMGPU_ETIMEOUT after the
+    // context's timeout (ncclCommAbort), not in a hang
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = api.commInitRankConfig(&tp->comm, nranks, u, rank, &cfg);
+    if (tp->comm) r = settle(tp->comm, r, c->timeout_ms);
     if (r != ncclSuccess) {
+        if (tp->comm) api.commAbort(tp->comm);
         delete tp;
-        return fail(c, MIMGPU_ENCCL, "tp: ncclCommInitRank: %s", api.errorString(r));
+        if (r == ncclInProgress)
+            return fail(c, MIMGPU_ETIMEOUT, "tp: rank %d of %d: the group did not form within %lld ms", rank, nranks,
+                        (long long)c->timeout_ms);
+        return fail(c, MIMGPU_ENCCL, "tp: ncclCommInitRankConfig: %s", api.errorString(r));
     }
     *out = tp;
     return MIMGPU_OK;
@@ -162,7 +197,13 @@ void mimgpu_tp_free(mimgpu_tp *tp) {
     if (!tp) return;
     const NcclApi &api = nccl();
     cudaSetDevice(tp->ctx->device);
-    if (api.ok && tp->comm) api.commDestroy(tp->comm);
+    if (api.ok && tp->comm) {
+        // a clean finalize when the peers take part; otherwise abort
+        if (settle(tp->comm, api.commFinalize(tp->comm), tp->ctx->timeout_ms) == ncclSuccess)
+            api.commDestroy(tp->comm);
+        else
+            api.commAbort(tp->comm);
+    }
     delete tp;
 }
 

@@ -32,6 +32,7 @@ SIGNATURES = {
     "mimgpu_close": (None, [P]),
     "mimgpu_last_error": (C.c_char_p, [P]),
     "mimgpu_set_timeout_ms": (I32, [P, I64]),
+    "mimgpu_stream_wait_value": (I32, [P, P, P, C.c_uint32]),
     "mimgpu_upload": (I32, [P, I32, I32, P, P, SZ, C.POINTER(P)]),
     "mimgpu_tensor_free": (None, [P]),
     "mimgpu_tensor_device_ptr": (P, [P]),
