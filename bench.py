@@ -46,6 +46,9 @@ CFG70B = dict(layers=80, embed=8192, ffn=28672, heads=64, kv_heads=8, head_dim=1
 SHAPES = {"8b": CFG8B, "70b": CFG70B}
 PROMPT = 128
 GEMV_TRAFFIC_PER_ALGO_BYTE = (66_120_960 + 338_944) / 66_179_904
+# DRAM bytes per algorithmic byte of step_kernel from one ncu capture of the
+# same command (profiles/), or None until one exists
+STEP_TRAFFIC_PER_ALGO_BYTE = None
 
 
 def layout(cfg):
@@ -331,20 +334,29 @@ def run_gpu(args):
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    # dominant kernel alone (the full matrices; every rank holds them)
-    bpl, spl, nl = gemv_roofline(ctx, cfg, weights, torch)
-    peak, peak_kind = peaks()
-    achieved = bpl / spl / 1e9
-    # DRAM bytes per algorithmic byte of the GEMV from one ncu capture (the
-    # 28672 x 4096 Q4_K launch of gemv_row_kernel: 66.12 MB read + 0.34 MB
-    # written for 66.18 MB algorithmic), applied to this run's bytes per launch
-    traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
     wpt = weight_bytes_per_token(cfg)
     ms = dev_s / args.steps * 1e3
     value = args.steps / dev_s  # one sequence, whole job
-    # embedding, 9 per layer (rms_norm+quant, QKV, RoPE+cache, attention, o,
-    # rms_norm+quant, gate|up, SwiGLU+quant, down), final norm, head, argmax, advance
-    launches = args.steps * (1 + 9 * cfg["layers"] + 4)
+    peak, peak_kind = peaks()
+    step_path = sess.uses_step_kernel
+    if step_path:
+        # the dominant kernel is the whole step: one step_kernel launch per token
+        # (the one-thread advance kernel that follows it is inside the event
+        # pair); algorithmic bytes = every weight once + the key/value rows read
+        kv_avg = prompt + args.warmup + (args.steps + 1) / 2
+        kv = 2 * cfg["layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * kv_avg
+        bpl, spl, nl = wpt + kv, dev_s / args.steps, args.steps
+        kernel = "step_kernel (persistent decode step, k_step.cu; event time includes the advance kernel)"
+        traffic = STEP_TRAFFIC_PER_ALGO_BYTE * bpl if STEP_TRAFFIC_PER_ALGO_BYTE else None
+        launches = args.steps * 2
+    else:
+        # the kernel-per-op path: its dominant kernel, the one-row GEMV, alone over the decode shapes
+        bpl, spl, nl = gemv_roofline(ctx, cfg, weights, torch)
+        kernel = f"gemv_row_kernel (one-row dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)"
+        traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
+        # embedding, 9 per layer, final norm, head, argmax, advance
+        launches = args.steps * (1 + 9 * cfg["layers"] + 4)
+    achieved = bpl / spl / 1e9
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -357,6 +369,8 @@ def run_gpu(args):
                    "kv_heads": cfg["kv_heads"], "ffn": cfg["ffn"], "vocab": cfg["vocab"], "prompt": prompt,
                    "context_cache": context, "positions_timed": [prompt + args.warmup, pos - 1 - args.e2e_steps - 2],
                    "matmul": "dequant_matmul_a8.v2 block 256 (bit-exact dotQ8KRef)", "kv_cache": "f16",
+                   "decode_path": ("one persistent step kernel per token" if step_path
+                                   else "one kernel per op (~9 per layer)"),
                    "parallelism": f"tp{world} (rows of every matrix per rank, NCCL all-gathers)" if world > 1
                    else "1 GPU",
                    "l2": l2_note(cfg, "streamed per token")},
@@ -365,9 +379,10 @@ def run_gpu(args):
                 "api": "mimgpu_session_run (pinned host token/position in, logits out, host argmax)"},
         "step_roofline": {"bound": "hbm", "bytes_per_token": wpt, "achieved": round(wpt / (ms / 1e3) / 1e9, 1),
                           "peak": peak, "unit": "GB/s", "frac": round(wpt / (ms / 1e3) / 1e9 / peak, 4)},
-        "roofline": {"kernel": f"gemv_row_kernel (one-row dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)",
+        "roofline": {"kernel": kernel,
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": round(traffic), "bytes_per_launch": round(bpl),
+                     "frac": round(achieved / peak, 4), "traffic": round(traffic) if traffic else None,
+                     "bytes_per_launch": round(bpl),
                      "us_per_launch": round(spl * 1e6, 3), "launches": nl, "peak_kind": peak_kind},
         "clocks": clocks.summary(),
         "gpu_launches": launches,

@@ -61,10 +61,6 @@ constexpr int kMaxSB = 256;                     // blocks per stage (one half bl
 constexpr int kRowsCap = 32;                    // rows per stage at most (K >= 2048)
 constexpr int kRecStage = 4608;                 // bytes of a record stage: rows * (nb + 1) * 16 <= 4608
 constexpr int kSmem = 227 * 1024;
-constexpr int kKeys = 32;                       // keys per attention chunk (32 x 128 f16 = 8 KB)
-constexpr int kChunkB = kKeys * 128 * 2;        // bytes of an attention chunk
-constexpr int kAttnSlots = 4;                   // attention chunk ring: slots at most
-constexpr uint32_t kPrefetch = 256 * 1024;      // weight bytes a CTA prefetches into L2 beyond the stage it issues
 constexpr int kMaxK = 4 * 16 * kCT;             // activation staging: 4 chunks of 16 quants per thread
 constexpr int kMaxE = 2 * 256 * kCW;            // RMSNorm: two 256-element blocks per consumer warp
 constexpr unsigned FULLM = 0xffffffffu;
@@ -81,7 +77,6 @@ struct Smem {
 // misc words after the barriers
 constexpr int kMiscOff = 256;
 struct Misc {
-    uint64_t abar[kAttnSlots];  // attention chunk ring barriers
     int act_ok;
     int roles_done;
     int abort;
@@ -156,30 +151,71 @@ __device__ __forceinline__ bool mbar_wait_s(uint64_t *bar, uint32_t parity, unsi
 __device__ __forceinline__ void stamp(const StepParams &p, int slot) {
     if (p.trace) p.trace[(size_t)blockIdx.x * step_trace_words(p.L) + slot] = global_ns();
 }
-__device__ __forceinline__ int jslot(int j, int k) { return 2 + 8 * j + k; }
+__device__ __forceinline__ int jslot(int j, int k) { return 2 + 16 * j + k; }
 
 // ------------------------------------------------------------ the jobs
+// One segment of a job: a weight matrix cut into slabs of rows across the
+// CTAs, or (kv) the key or value rows of one attention unit's kv head,
+// streamed whole to the CTA that runs the unit.
 struct Seg {
     const uint8_t *w, *w2;  // the matrix; w2: the up matrix of a paired gate|up stage
     int dt, n, nb, bb, unit, rps;
     int rb;
+    int kv;                 // 1: key / value rows of an attention unit (no records, no chain)
 };
 
-__device__ __forceinline__ int njobs(const StepParams &p) { return 4 * p.L + 1; }
-__device__ __forceinline__ int nsegs(int kind) { return kind == J_QKV ? 3 : 1; }
+// Attention units: HU query heads of one kv head each, one per CTA of the
+// first `units` CTAs.
+__device__ __forceinline__ int attn_hu(const StepParams &p) { return p.H / p.Hkv >= 4 ? 4 : p.H / p.Hkv; }
+__device__ __forceinline__ int attn_units(const StepParams &p) { return p.H / attn_hu(p); }
 
-__device__ Seg get_seg(const StepParams &p, const StepLayer *lt, int job, int s) {
+constexpr int kKvRows = 64;  // keys per key / value stage (16 KB)
+
+__device__ __forceinline__ int njobs(const StepParams &p) { return 4 * p.L + 1; }
+// q|k|v: q, k, v; o: the unit's keys, its values, o; others one matrix
+__device__ __forceinline__ int nsegs(int kind) { return kind == J_QKV || kind == J_O ? 3 : 1; }
+
+// The rows of segment g this CTA takes: a slab of the matrix, or every key
+// of its attention unit.
+__device__ __forceinline__ void seg_rows(const Seg &g, int cta, int G, int &r0, int &nr) {
+    if (g.kv) {
+        r0 = 0;
+        nr = g.n;
+        return;
+    }
+    slab(g.n, cta, G, g.unit, r0, nr);
+}
+
+// nk: keys of this step (position + 1)
+__device__ Seg get_seg(const StepParams &p, const StepLayer *lt, int job, int s, int nk) {
     const int kind = job == 4 * p.L ? J_HEAD : job & 3;
     Seg g;
     g.w2 = nullptr;
+    g.kv = 0;
     int K = p.E;
+    if (kind == J_O && s < 2) {
+        const int unit = blockIdx.x;
+        const bool mine = unit < attn_units(p);
+        const int kvh = mine ? unit * attn_hu(p) / (p.H / p.Hkv) : 0;
+        const StepLayer &ly = lt[job >> 2];
+        g.w = (const uint8_t *)(s == 0 ? ly.kc : ly.vc) + (size_t)kvh * p.C * p.D * 2;
+        g.dt = F16;
+        g.n = mine ? nk : 0;
+        g.nb = 0;
+        g.bb = 0;
+        g.rb = p.D * 2;
+        g.unit = 1;
+        g.rps = kKvRows;
+        g.kv = 1;
+        return g;
+    }
     if (kind == J_HEAD) {
         g.w = p.head;
         g.dt = p.head_dt;
         g.n = p.V;
     } else {
         const StepLayer &ly = lt[job >> 2];
-        const int i = kind == J_QKV ? s : kind == J_O ? 3 : kind == J_GU ? 4 : 6;
+        const int i = kind == J_QKV ? s : kind == J_O ? 3 : kind == J_GU ? 4 : 6;  // (o is segment 2)
         g.w = ly.w[i];
         g.dt = ly.dt[i];
         g.n = kind == J_QKV ? (s == 0 ? p.E : p.Hkv * p.D) : kind == J_GU ? p.F : p.E;
@@ -203,26 +239,26 @@ struct Cursor {
     Seg g;
 };
 __device__ __forceinline__ int kind_of(const StepParams &p, int j) { return j == 4 * p.L ? J_HEAD : j & 3; }
-__device__ void cur_fix(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
+__device__ void cur_fix(Cursor &c, const StepParams &p, const StepLayer *lt, int nj, int nk) {
     while (c.j < nj && c.row0 >= c.nr) {
         c.row0 = 0;
         if (++c.s >= nsegs(kind_of(p, c.j))) {
             c.s = 0;
             if (++c.j >= nj) break;
         }
-        c.g = get_seg(p, lt, c.j, c.s);
-        slab(c.g.n, blockIdx.x, gridDim.x, c.g.unit, c.r0, c.nr);
+        c.g = get_seg(p, lt, c.j, c.s, nk);
+        seg_rows(c.g, blockIdx.x, gridDim.x, c.r0, c.nr);
     }
 }
-__device__ void cur_start(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
+__device__ void cur_start(Cursor &c, const StepParams &p, const StepLayer *lt, int nj, int nk) {
     c.j = c.s = c.row0 = 0;
-    c.g = get_seg(p, lt, 0, 0);
-    slab(c.g.n, blockIdx.x, gridDim.x, c.g.unit, c.r0, c.nr);
-    cur_fix(c, p, lt, nj);
+    c.g = get_seg(p, lt, 0, 0, nk);
+    seg_rows(c.g, blockIdx.x, gridDim.x, c.r0, c.nr);
+    cur_fix(c, p, lt, nj, nk);
 }
-__device__ __forceinline__ void cur_step(Cursor &c, const StepParams &p, const StepLayer *lt, int nj) {
+__device__ __forceinline__ void cur_step(Cursor &c, const StepParams &p, const StepLayer *lt, int nj, int nk) {
     c.row0 += c.g.rps;
-    cur_fix(c, p, lt, nj);
+    cur_fix(c, p, lt, nj, nk);
 }
 
 // Next stage's ring offset (producer and consumers compute the same sequence).
@@ -426,105 +462,87 @@ __device__ void stage_phase(const ActQ8 &act, int K, uint8_t *smem, const Smem &
 }
 
 // Layout of the attention scratch (the activation + record regions, free
-// while attention runs): q [HU][128], outputs [HU * 128], scores [HU][n],
-// then a ring of 8 KB key / value chunks (128-byte aligned).
-__host__ __device__ inline int attn_fixed_bytes(int HU, int n) {
-    return ((2 * HU * 128 + HU * n) * 4 + 127) & ~127;
-}
+// while attention runs): q [HU][128], outputs [HU * 128], scores [HU][n].
+__host__ __device__ inline int attn_scratch_bytes(int HU, int n) { return (2 * HU * 128 + HU * n) * 4; }
 
 // One attention unit: query heads h0..h0+HU-1 (one kv head) of the step's
-// token over keys [0, pos] of the f16 cache, exactly as attendRow
+// token over its nk keys [0, pos] of the f16 cache, exactly as attendRow
 // (interp/fast.go:728-751) with the reference's amd64 kernels: scores in the
 // eight-lane orders of scoresF16AVX2, ExpSumF32 (Cephes expf below n&~7,
 // float64 exp above, its lane-sum order), the key-ordered fused weighted sum
 // of wsumF16AVX2, o = acc / sum; then the 8-bit blocks of the unit's
-// outputs.  Key chunks, then value chunks, arrive by bulk copies through a
-// ring of up to kAttnSlots slots (the rows were prefetched into L2 when the
-// layer started); the token's own key and value rows, written this step by
-// other CTAs, are read through L2 and patched into the chunk.  `au` counts
-// each ring barrier's completed phases (identical in every consumer thread).
-__device__ void attn_unit(const StepParams &p, const StepLayer *lt, int l, int unit, int HU, uint8_t *smem,
-                          const Smem &sm, Misc &ms, int (&au)[kAttnSlots]) {
+// outputs.  The kv head's key rows, then its value rows, are stages of this
+// CTA's weight stream (segments 0 and 1 of the o job), so the producer has
+// loaded them while the CTA was busy with q|k|v; the token's own key and
+// value rows, written this step by other CTAs, are read through L2 and
+// patched into their stage.  m / head: the consumers' stage counter and
+// ring offset, advanced past the stages read here.
+__device__ void attn_unit(const StepParams &p, int l, int unit, int HU, int nk, uint8_t *smem, const Smem &sm,
+                          Misc &ms, uint8_t *ring, uint64_t *full, uint64_t *cons, int &m, uint32_t &head, int tj) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = 128, G = p.H / p.Hkv, h0 = unit * HU, kvh = h0 / G;
-    const int pos = (int)__ldcg(p.pos), n = pos + 1, n4 = n & ~3, n8 = n >= 8 ? (n & ~7) : 0;
-    const int nch = (n + kKeys - 1) / kKeys, items = 2 * nch;
+    const int n = nk, pos = nk - 1, n4 = n & ~3, n8 = n >= 8 ? (n & ~7) : 0;
     float *q = (float *)(smem + sm.off_act);  // [HU][128]
     float *obuf = q + HU * D;                 // [HU * 128]
     float *sc = obuf + HU * D;                // [HU][n]
-    uint8_t *ring = smem + sm.off_act + attn_fixed_bytes(HU, n);
-    const int nsl = min(kAttnSlots, (sm.off_bad - sm.off_act - attn_fixed_bytes(HU, n)) / kChunkB);  // >= 2
-    const StepLayer &ly = lt[l];
-    const uint8_t *kbase = (const uint8_t *)ly.kc + (size_t)kvh * p.C * D * 2;
-    const uint8_t *vbase = (const uint8_t *)ly.vc + (size_t)kvh * p.C * D * 2;
-    auto parity = [&](int i) { return (uint32_t)((au[i % nsl] + i / nsl) & 1); };
-    // item i < nch: key chunk i; else value chunk i - nch
-    auto issue = [&](int i) {
-        const int b = i % nsl, c = i % nch, j0 = c * kKeys, len = min(kKeys, n - j0);
-        mbar_arrive_expect_tx(&ms.abar[b], (uint32_t)(len * D * 2));
-        bulk_g2s(ring + b * kChunkB, (i < nch ? kbase : vbase) + (size_t)j0 * D * 2, (uint32_t)(len * D * 2),
-                 &ms.abar[b]);
-    };
-    if (tid == 0)
-        for (int i = 0; i < min(items, nsl); i++) issue(i);
     for (int i = tid; i < HU * D; i += kCT) q[i] = __ldcg(p.qh + h0 * D + i);
-    // wait for item i's chunk; the last chunk gets the token's own row
-    auto land = [&](int i) -> uint8_t * {
-        uint8_t *slot = ring + (i % nsl) * kChunkB;
-        mbar_wait_s(&ms.abar[i % nsl], parity(i), p.status, ms);
-        if (i % nch == nch - 1) {
+    const uint8_t *own[2] = {(const uint8_t *)p.layers[l].kc, (const uint8_t *)p.layers[l].vc};
+    // the next stage of keys (part 0) or values (part 1): wait, patch row pos
+    auto land = [&](int part, int j0, int rows) -> const uint8_t * {
+        const uint32_t off = ring_next(head, (uint32_t)(rows * D * 2), (uint32_t)sm.ring);
+        mbar_wait_s(&full[m % kStg], (m / kStg) & 1, p.status, ms);
+        uint8_t *chunk = ring + off;
+        if (pos < j0 + rows) {
             if (tid < 16) {
-                const uint8_t *src = (i < nch ? kbase : vbase) + (size_t)pos * D * 2;
-                *(uint4 *)(slot + (pos - (nch - 1) * kKeys) * D * 2 + tid * 16) = __ldcg((const uint4 *)src + tid);
+                const uint8_t *src = own[part] + ((size_t)kvh * p.C + pos) * D * 2;
+                *(uint4 *)(chunk + (pos - j0) * D * 2 + tid * 16) = __ldcg((const uint4 *)src + tid);
+                // generic writes into a slot the producer's bulk copies reuse
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
         }
         bar_cons();
-        return slot;
+        return chunk;
     };
-    // the slot of item i is read: refill it with item i + nsl
-    auto release = [&](int i) {
-        bar_cons();
-        if (tid == 0 && i + nsl < items) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(i + nsl);
-        }
+    auto done = [&]() {  // every warp is done with the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cons[m % kStg]);
+        m++;
     };
-    float mx[2] = {-INFINITY, -INFINITY};
-    for (int c = 0; c < nch; c++) {
-        const uint8_t *chunk = land(c);
+    // scores: a warp takes one key at a time; lane = (head hq, reference lane
+    // l8), so the 32 lanes read one 16-byte piece of the key row together
+    // (a broadcast) and each lane keeps its 16 q values in registers
+    const int hq = lane >> 3, l8 = lane & 7;
+    bar_cons();  // q in shared memory
+    float qreg[16];
 #pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const int task = tid + r * kCT;  // (head, key, lane of 8)
-            const int l8 = task & 7, jj = (task >> 3) & 31, hh = task >> 8;
-            if (hh >= HU) break;  // warp-uniform
-            const float *qr = q + hh * D;
+    for (int c8 = 0; c8 < 16; c8++) qreg[c8] = hq < HU ? q[hq * D + 8 * c8 + l8] : 0.f;
+    float mx = -INFINITY;
+    for (int j0 = 0; j0 < n; j0 += kKvRows) {
+        const int rows = min(kKvRows, n - j0);
+        const uint8_t *chunk = land(0, j0, rows);
+        if (j0 == 0 && tid == 0) stamp(p, jslot(tj, 9));
+        for (int jj = warp; jj < rows; jj += kCW) {
             const uint16_t *kr = (const uint16_t *)(chunk + jj * D * 2);
             float acc = 0.f;
 #pragma unroll
-            for (int c8 = 0; c8 < D / 8; c8++) acc = __fmaf_rn(qr[8 * c8 + l8], h2f_bits(kr[8 * c8 + l8]), acc);
-            const int j = c * kKeys + jj;
+            for (int c8 = 0; c8 < 16; c8++) acc = __fmaf_rn(qreg[c8], h2f_bits(kr[8 * c8 + l8]), acc);
+            const int j = j0 + jj;
             const float sv = __fmul_rn(score_combine(acc, j >= n4), p.scale);
-            if (l8 == 0 && j < n) {
-                sc[hh * n + j] = sv;
-                mx[r] = fmaxf(mx[r], sv);
+            if (l8 == 0 && hq < HU) {
+                sc[hq * n + j] = sv;
+                mx = fmaxf(mx, sv);
             }
         }
-        release(c);
+        done();
     }
-    // per-head maximum: warp w holds heads (w >> 3) (r = 0) and (w >> 3) + 2 (r = 1)
-#pragma unroll
-    for (int r = 0; r < 2; r++) mx[r] = warp_max(mx[r]);
-    if (lane == 0) {
-        ms.red[warp][0] = mx[0];
-        ms.red[warp][1] = mx[1];
-    }
+    // per-head maximum: lanes 8hq hold head hq's
+    if (l8 == 0 && hq < HU) ms.red[warp][hq] = mx;
     bar_cons();
+    if (tid == 0) stamp(p, jslot(tj, 10));
     if (tid < HU) {
-        float m = -INFINITY;
-        for (int w = 0; w < kCW; w++)
-            for (int r = 0; r < 2; r++)
-                if ((w >> 3) + 2 * r == tid) m = fmaxf(m, ms.red[w][r]);
-        ms.hmax[tid] = m;
+        float mm = -INFINITY;
+        for (int w = 0; w < kCW; w++) mm = fmaxf(mm, ms.red[w][tid]);
+        ms.hmax[tid] = mm;
     }
     bar_cons();
     for (int i = tid; i < HU * n; i += kCT) {
@@ -547,28 +565,41 @@ __device__ void attn_unit(const StepParams &p, const StepLayer *lt, int l, int u
                                 __fadd_rn(__fadd_rn(r[2], r[6]), __fadd_rn(r[3], r[7])));
         for (int j = n8; j < n; j++) sum = __fadd_rn(sum, sc[tid * n + j]);
         ms.hsum[tid] = sum;
+        if (tid == 0) stamp(p, jslot(tj, 11));
     }
-    // weighted sum of the values, one fused multiply-add per key in key order
-    const int hh = tid >> 7, d = tid & 127;
-    float acc = 0.f;
-    for (int c = 0; c < nch; c++) {
-        const uint8_t *chunk = land(nch + c);
+    // weighted sum of the values, one fused multiply-add per key in key
+    // order: warp hh (< HU) takes head hh, lane dq its head elements
+    // 4dq..4dq+3 (four independent chains, 8-byte reads)
+    const int hh = warp, dq = lane;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < n; j0 += kKvRows) {
+        const int rows = min(kKvRows, n - j0);
+        const uint8_t *chunk = land(1, j0, rows);
         if (hh < HU) {
-            const uint16_t *vr = (const uint16_t *)chunk + d;
-            const float *e = sc + hh * n + c * kKeys;
-            const int len = min(kKeys, n - c * kKeys);
-#pragma unroll 8
-            for (int jj = 0; jj < len; jj++) acc = __fmaf_rn(e[jj], h2f_bits(vr[jj * D]), acc);
+            const float *e = sc + hh * n + j0;
+#pragma unroll 4
+            for (int jj = 0; jj < rows; jj++) {
+                const uint2 v = *(const uint2 *)(chunk + jj * D * 2 + 8 * dq);
+                const float ev = e[jj];
+                acc[0] = __fmaf_rn(ev, h2f_bits(v.x & 0xFFFFu), acc[0]);
+                acc[1] = __fmaf_rn(ev, h2f_bits(v.x >> 16), acc[1]);
+                acc[2] = __fmaf_rn(ev, h2f_bits(v.y & 0xFFFFu), acc[2]);
+                acc[3] = __fmaf_rn(ev, h2f_bits(v.y >> 16), acc[3]);
+            }
         }
-        release(nch + c);
+        done();
     }
-    for (int b = 0; b < nsl; b++) au[b] += (items - b + nsl - 1) / nsl;
     if (hh < HU) {
-        const float o = __fdiv_rn(acc, ms.hsum[hh]);
-        obuf[tid] = o;
-        __stcg(p.att + h0 * D + tid, o);
+        float4 o;
+        o.x = __fdiv_rn(acc[0], ms.hsum[hh]);
+        o.y = __fdiv_rn(acc[1], ms.hsum[hh]);
+        o.z = __fdiv_rn(acc[2], ms.hsum[hh]);
+        o.w = __fdiv_rn(acc[3], ms.hsum[hh]);
+        *(float4 *)(obuf + hh * D + 4 * dq) = o;
+        __stcg((float4 *)(p.att + (h0 + hh) * D + 4 * dq), o);
     }
     bar_cons();
+    if (tid == 0) stamp(p, jslot(tj, 12));
     // the unit's 8-bit blocks (HU * 128 / 256 of them), one warp each
     if (warp < HU * D / 256) {
         const int kb = (h0 * D) / 256 + warp;
@@ -608,6 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const unsigned ep = __ldcg(p.epoch);  // steps completed: grid counters aim at arrivals x (ep + 1)
+    const int nk = (int)__ldcg(p.pos) + 1;  // keys of this step's attention
     const int nj = njobs(p);
     unsigned *ctr = p.sync;               // [0] embedding, [1 + 5 l + c] layer counters
     unsigned *blkctr = p.sync + 1 + 5 * p.L;  // [l][F / 256] SwiGLU block rows
@@ -621,7 +653,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             mbar_init(&rdone[s], kCW);
             mbar_init(&rfree[s], 1);
         }
-        for (int s = 0; s < kAttnSlots; s++) mbar_init(&ms.abar[s], 1);
         ms.act_ok = 1;
         ms.roles_done = 0;
         ms.abort = 0;
@@ -637,28 +668,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
 
     if (warp == kCW) {
         // -------------------------------------------------- producer
-        // Stages go into the shared-memory ring in order; a second cursor runs
-        // up to kPrefetch bytes ahead and prefetches the stages after them into
-        // L2, so the weight stream keeps going while the ring is full (the CTA
-        // waiting for an activation).  The ring copies mark their lines
-        // evict-first: they are read once.
+        // Stages go into the shared-memory ring in order.  The ring copies
+        // mark their lines evict-first: they are read once.  (Prefetching the
+        // stages after them into L2 as well was measured slower: 2.83 vs
+        // 2.55 ms per 8B token; the prefetch traffic delays the
+        // latency-bound loads of the small ops.)
         if (lane == 0) {
-            uint32_t head = 0, lo[kStg], hi[kStg], ahead = 0;
+            uint32_t head = 0, lo[kStg], hi[kStg];
             int m = 0, oldest = 0, lastj = -1;
             bool ok = true;
             const uint64_t pol = l2_policy_evict_first();
-            Cursor ic, pc;
-            cur_start(ic, p, lt, nj);
-            cur_start(pc, p, lt, nj);
+            Cursor ic;
+            cur_start(ic, p, lt, nj, nk);
             while (ic.j < nj && ok) {
-                while (pc.j < nj && ahead < kPrefetch) {
-                    const uint32_t part = (uint32_t)(min(pc.g.rps, pc.nr - pc.row0) * pc.g.rb);
-                    const long long src = (long long)(pc.r0 + pc.row0) * pc.g.rb;
-                    prefetch_l2(pc.g.w + src, part);
-                    if (pc.g.w2) prefetch_l2(pc.g.w2 + src, part);
-                    ahead += part * (pc.g.w2 ? 2u : 1u);
-                    cur_step(pc, p, lt, nj);
-                }
                 if (ic.j != lastj) {
                     if (lastj >= 0) stamp(p, jslot(lastj, 6));
                     stamp(p, jslot(ic.j, 5));
@@ -688,9 +710,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 const long long src = (long long)(ic.r0 + ic.row0) * g.rb;
                 bulk_g2s_hint(ring + off, g.w + src, part, fb, pol);
                 if (g.w2) bulk_g2s_hint(ring + off + part, g.w2 + src, part, fb, pol);
-                ahead -= min(ahead, bytes);
                 m++;
-                cur_step(ic, p, lt, nj);
+                cur_step(ic, p, lt, nj, nk);
             }
             if (lastj >= 0) stamp(p, jslot(lastj, 6));
             // copies still in flight land before the block exits
@@ -716,9 +737,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             const int kind = j == 4 * p.L ? J_HEAD : j & 3, l = j >> 2;
             const StepLayer *ly = kind == J_HEAD ? nullptr : &lt[l];
             for (int s = 0; s < nsegs(kind); s++) {
-                const Seg g = get_seg(p, lt, j, s);
+                const Seg g = get_seg(p, lt, j, s, nk);
+                if (g.kv) continue;  // attention stages: no records
                 int r0, nr;
-                slab(g.n, cta, G, g.unit, r0, nr);
+                seg_rows(g, cta, G, r0, nr);
                 const int nb = g.nb, rstride = (nb + 1) * 16;
                 for (int lo = 0; lo < nr; lo += g.rps, m++) {
                     if (m % kNC != c) continue;
@@ -837,9 +859,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 // this CTA's gate rows by 256-element block of the SwiGLU output: the
                 // CTA whose rows complete a block quantizes it for the down product
                 // (the two chain warps take alternate completed blocks)
-                const Seg g = get_seg(p, lt, j, 0);
+                const Seg g = get_seg(p, lt, j, 0, nk);
                 int r0, nr;
-                slab(g.n, cta, G, g.unit, r0, nr);
+                seg_rows(g, cta, G, r0, nr);
                 const int b0 = r0 / 256, nbk = nr > 0 ? (r0 + nr - 1) / 256 - b0 + 1 : 0;
                 if (c == 0) {
                     bool last = false;
@@ -887,9 +909,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         const int h = lane & 1;
         const int G2 = p.H / p.Hkv, HU = G2 >= 4 ? 4 : G2, units = p.H / HU;
         uint32_t head = 0;
-        int m = 0;
+        int m = 0, mr = 0;  // data stages (ring) and record stages consumed
         bool failed = false;
-        int au[kAttnSlots] = {0, 0, 0, 0};  // attention ring barrier phases
         if (threadIdx.x == 0) stamp(p, 0);
         // the token's embedding row (fast.go:818-842): this CTA's slice of x
         {
@@ -907,16 +928,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         for (int j = 0; j < nj; j++) {
             const int kind = j == 4 * p.L ? J_HEAD : j & 3, l = j >> 2;
             // ---- the activation of this product into shared memory
-            if (kind == J_QKV && cta < units && threadIdx.x == 0) {
-                // this layer's attention unit: its key / value rows of earlier steps into L2 now
-                const int pos = (int)__ldcg(p.pos);
-                if (pos > 0) {
-                    const uint64_t keep = l2_policy_evict_last();
-                    const size_t kvoff = (size_t)((cta * HU) / (p.H / p.Hkv)) * p.C * p.D * 2;
-                    prefetch_l2_hint((const uint8_t *)lt[l].kc + kvoff, (uint32_t)pos * p.D * 2, keep);
-                    prefetch_l2_hint((const uint8_t *)lt[l].vc + kvoff, (uint32_t)pos * p.D * 2, keep);
-                }
-            }
             if (kind == J_QKV || kind == J_GU || kind == J_HEAD) {
                 const unsigned *w = kind == J_QKV ? (l == 0 ? &ctr[0] : &ctr[1 + 5 * (l - 1) + C_DOWN])
                                     : kind == J_GU ? &ctr[1 + 5 * l + C_O]
@@ -927,9 +938,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             } else if (kind == J_O) {
                 // attention units on the first CTAs, once every q / k / v row is written
                 if (cta < units) {
-                    if (threadIdx.x == 0) grid_wait(&ctr[1 + 5 * l + C_QKV], (unsigned)G * (ep + 1), p.status, ms);
+                    if (threadIdx.x == 0) {
+                        grid_wait(&ctr[1 + 5 * l + C_QKV], (unsigned)G * (ep + 1), p.status, ms);
+                        stamp(p, jslot(j, 8));
+                    }
                     bar_cons();
-                    if (!aborted(ms)) attn_unit(p, lt, l, cta, HU, smem, sm, ms, au);
+                    attn_unit(p, l, cta, HU, nk, smem, sm, ms, ring, full, cons, m, head, j);
                     bar_cons();
                     if (threadIdx.x == 0) {
                         red_rel(&ctr[1 + 5 * l + C_ATT], 1u);
@@ -954,9 +968,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             if (threadIdx.x == 0) stamp(p, jslot(j, 1));
             // ---- the product's stages
             for (int s = 0; s < nsegs(kind); s++) {
-                const Seg g = get_seg(p, lt, j, s);
+                const Seg g = get_seg(p, lt, j, s, nk);
+                if (g.kv) continue;  // the attention unit read its stages already
                 int r0, nr;
-                slab(g.n, cta, G, g.unit, r0, nr);
+                seg_rows(g, cta, G, r0, nr);
                 const int nb = g.nb, sbk = (g.w2 ? 2 : 1) * g.rps * nb;
                 const int dt = g.dt, bb = g.bb, rstride = (nb + 1) * 16;
                 const int blk = dt == Q4_K ? 16 * warp + (lane >> 1) : 8 * (16 * (warp >> 3) + (lane >> 1)) + (warp & 7);
@@ -964,12 +979,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 const int roff = blk / nb, kb = blk - roff * nb;
                 const uint32_t ya = act_s + (uint32_t)act_off(lane_on ? kb : 0, h);
                 const uint32_t ha = (uint32_t)hdr_off(2 * (lane_on ? kb : 0) + h);
-                for (int row0 = 0; row0 < nr; row0 += g.rps, m++) {
+                for (int row0 = 0; row0 < nr; row0 += g.rps, m++, mr++) {
                     const int rows = min(g.rps, nr - row0), srows = g.w2 ? 2 * rows : rows;
                     const uint32_t off = ring_next(head, (uint32_t)(srows * g.rb), (uint32_t)sm.ring);
-                    const int slot = m % kStg, rs = m % kRS;
+                    const int slot = m % kStg, rs = mr % kRS;
                     if (!failed && !mbar_wait_s(&full[slot], (m / kStg) & 1, p.status, ms)) failed = true;
-                    if (!failed && m >= kRS && !mbar_wait_s(&rfree[rs], ((m / kRS) & 1) ^ 1, p.status, ms))
+                    if (!failed && mr >= kRS && !mbar_wait_s(&rfree[rs], ((mr / kRS) & 1) ^ 1, p.status, ms))
                         failed = true;
                     failed = __any_sync(FULLM, failed);
                     const bool active = !failed && lane_on && roff < srows;
@@ -1042,10 +1057,10 @@ bool step_ok(int E, int F, int H, int Hkv, int D, int C, int rotary, int interle
         return false;
     const int G = H / Hkv, HU = G >= 4 ? 4 : G;
     if (G % 2 || G % HU || (HU * D) % 256) return false;
-    // attention scratch in the act + record regions: q, outputs, HU x C scores and two chunk slots
+    // attention scratch in the act + record regions: q, outputs and HU x C scores
     const int nbmax = (E > F ? E : F) / 256;
     const long long scratch = (long long)act_region(nbmax) + kRS * kRecStage;
-    return (long long)attn_fixed_bytes(HU, C) + 2LL * kChunkB <= scratch;
+    return (long long)attn_scratch_bytes(HU, C) <= scratch;
 }
 
 size_t step_sync_words(int L, int F) { return 1 + 5 * (size_t)L + (size_t)L * (F / 256); }

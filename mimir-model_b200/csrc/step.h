@@ -43,11 +43,13 @@ struct StepParams {
     unsigned long long *trace;  // phase timeline [G][step_trace_words(L)] (%globaltimer ns), or null
 };
 
-// Timeline slots of one CTA: [0] start, [1] end, then 8 per job (4 per layer +
-// the head): 0 activation ready, 1 activation in shared memory, 2 consumer
-// stages done, 3 attention unit done, 4 chain warps done, 5 first stage
-// issued, 6 last stage issued, 7 unused.
-__host__ __device__ inline size_t step_trace_words(int L) { return 2 + 8 * (size_t)(4 * L + 1); }
+// Timeline slots of one CTA: [0] start, [1] end, then 16 per job (4 per
+// layer + the head): 0 activation ready, 1 activation in shared memory, 2
+// consumer stages done, 3 attention unit done, 4 chain warps done, 5 first
+// stage issued, 6 last stage issued; for the o job of an attention CTA also
+// 8 q|k|v rows of every CTA written, 9 first key stage landed, 10 scores done,
+// 11 softmax sums done, 12 weighted sums done.
+__host__ __device__ inline size_t step_trace_words(int L) { return 2 + 16 * (size_t)(4 * L + 1); }
 
 // Whether a model of these dimensions runs through the step kernel (else the
 // kernel-per-op path): Q4_K / Q6_K matrices, E a multiple of 256 up to 8192,
