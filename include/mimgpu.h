@@ -259,8 +259,9 @@ void *mimgpu_session_stream(mimgpu_session *s);
  * mimgpu_session_generate; no counterpart in the reference, whose Session.Run
  * interprets the graph op by op, interp/interp.go:409-526): on = 1 runs the
  * whole step as one persistent kernel that streams every layer's weights
- * through one pipeline; on = 0 launches one kernel per op.  Both give the same
- * bits.  The persistent kernel is the default for single-GPU sessions of
+ * through one pipeline; on = 0 (the default) launches one kernel per op, which
+ * measured faster on B200 (8B shape 2.08 vs 2.45 ms per token).  Both give the
+ * same bits.  The persistent kernel serves single-GPU sessions of
  * 8-bit-activation models with Q4_K / Q6_K matrices, E and F multiples of 256
  * (E 2048..8192, F 2048..32768), head size 128, an f16 cache and interleaved
  * RoPE; for other

@@ -55,7 +55,7 @@ constexpr int kCW = 16;                         // consumer warps
 constexpr int kCT = kCW * 32;                   // consumer threads
 constexpr int kNC = 2;                          // chain warps
 constexpr int kThreads = kCT + 32 + 32 * kNC;   // 608
-constexpr int kStg = 8;                         // data stages in flight at most
+constexpr int kStg = 16;                        // data stages in flight at most
 constexpr int kRS = 4;                          // record stages
 constexpr int kMaxSB = 256;                     // blocks per stage (one half block per consumer lane)
 constexpr int kRowsCap = 32;                    // rows per stage at most (K >= 2048)
@@ -75,7 +75,7 @@ struct Smem {
 };
 
 // misc words after the barriers
-constexpr int kMiscOff = 256;
+constexpr int kMiscOff = 512;  // after the barriers: 2 x kStg + 2 x kRS mbarriers
 struct Misc {
     int act_ok;
     int roles_done;
@@ -149,7 +149,12 @@ __device__ __forceinline__ bool mbar_wait_s(uint64_t *bar, uint32_t parity, unsi
 
 // Timeline stamp (profiling sessions only).
 __device__ __forceinline__ void stamp(const StepParams &p, int slot) {
-    if (p.trace) p.trace[(size_t)blockIdx.x * step_trace_words(p.L) + slot] = global_ns();
+    if (p.trace) p.trace[(size_t)blockIdx.x * step_trace_cta_words(p.L) + slot] = global_ns();
+}
+// CTA 0's per-stage log (profiling sessions only)
+__device__ __forceinline__ void stage_stamp(const StepParams &p, int m, int k) {
+    if (p.trace && blockIdx.x == 0 && m < kStageLog)
+        p.trace[(size_t)gridDim.x * step_trace_cta_words(p.L) + 4 * m + k] = global_ns();
 }
 __device__ __forceinline__ int jslot(int j, int k) { return 2 + 16 * j + k; }
 
@@ -166,7 +171,7 @@ struct Seg {
 
 // Attention units: HU query heads of one kv head each, one per CTA of the
 // first `units` CTAs.
-__device__ __forceinline__ int attn_hu(const StepParams &p) { return p.H / p.Hkv >= 4 ? 4 : p.H / p.Hkv; }
+__device__ __forceinline__ int attn_hu(const StepParams &p) { return 2; }  // H / Hkv is even (step_ok)
 __device__ __forceinline__ int attn_units(const StepParams &p) { return p.H / attn_hu(p); }
 
 constexpr int kKvRows = 64;  // keys per key / value stage (16 KB)
@@ -511,37 +516,40 @@ __device__ void attn_unit(const StepParams &p, int l, int unit, int HU, int nk, 
     // scores: a warp takes one key at a time; lane = (head hq, reference lane
     // l8), so the 32 lanes read one 16-byte piece of the key row together
     // (a broadcast) and each lane keeps its 16 q values in registers
-    const int hq = lane >> 3, l8 = lane & 7;
+    // (4 / HU keys per warp at a time: lane = (key kk, head hq, lane l8))
+    const int l8 = lane & 7, hq = (lane >> 3) % HU, kk = lane / (8 * HU), kpw = 4 / HU;
     bar_cons();  // q in shared memory
     float qreg[16];
 #pragma unroll
-    for (int c8 = 0; c8 < 16; c8++) qreg[c8] = hq < HU ? q[hq * D + 8 * c8 + l8] : 0.f;
+    for (int c8 = 0; c8 < 16; c8++) qreg[c8] = q[hq * D + 8 * c8 + l8];
     float mx = -INFINITY;
     for (int j0 = 0; j0 < n; j0 += kKvRows) {
         const int rows = min(kKvRows, n - j0);
         const uint8_t *chunk = land(0, j0, rows);
         if (j0 == 0 && tid == 0) stamp(p, jslot(tj, 9));
-        for (int jj = warp; jj < rows; jj += kCW) {
-            const uint16_t *kr = (const uint16_t *)(chunk + jj * D * 2);
+        for (int jb = warp * kpw; jb < rows; jb += kCW * kpw) {
+            const int jj = jb + kk, jr = min(jj, rows - 1);  // past the last key: a valid row, result unused
+            const uint16_t *kr = (const uint16_t *)(chunk + jr * D * 2);
             float acc = 0.f;
 #pragma unroll
             for (int c8 = 0; c8 < 16; c8++) acc = __fmaf_rn(qreg[c8], h2f_bits(kr[8 * c8 + l8]), acc);
             const int j = j0 + jj;
             const float sv = __fmul_rn(score_combine(acc, j >= n4), p.scale);
-            if (l8 == 0 && hq < HU) {
+            if (l8 == 0 && jj < rows) {
                 sc[hq * n + j] = sv;
                 mx = fmaxf(mx, sv);
             }
         }
         done();
     }
-    // per-head maximum: lanes 8hq hold head hq's
-    if (l8 == 0 && hq < HU) ms.red[warp][hq] = mx;
+    // per-head maximum: lanes with l8 == 0 hold their head's
+    if (l8 == 0) ms.red[warp][lane >> 3] = mx;
     bar_cons();
     if (tid == 0) stamp(p, jslot(tj, 10));
     if (tid < HU) {
         float mm = -INFINITY;
-        for (int w = 0; w < kCW; w++) mm = fmaxf(mm, ms.red[w][tid]);
+        for (int w = 0; w < kCW; w++)
+            for (int g = tid; g < 4; g += HU) mm = fmaxf(mm, ms.red[w][g]);
         ms.hmax[tid] = mm;
     }
     bar_cons();
@@ -570,34 +578,42 @@ __device__ void attn_unit(const StepParams &p, int l, int unit, int HU, int nk, 
     // weighted sum of the values, one fused multiply-add per key in key
     // order: warp hh (< HU) takes head hh, lane dq its head elements
     // 4dq..4dq+3 (four independent chains, 8-byte reads)
-    const int hh = warp, dq = lane;
+    // (warps 0-3: head warp / (4 / HU), HU elements per lane)
+    const int hh = warp / (4 / HU), d0 = (warp % (4 / HU)) * 32 * HU + HU * lane;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int j0 = 0; j0 < n; j0 += kKvRows) {
         const int rows = min(kKvRows, n - j0);
         const uint8_t *chunk = land(1, j0, rows);
-        if (hh < HU) {
+        if (warp < 4) {
             const float *e = sc + hh * n + j0;
+            if (HU == 4) {
 #pragma unroll 4
-            for (int jj = 0; jj < rows; jj++) {
-                const uint2 v = *(const uint2 *)(chunk + jj * D * 2 + 8 * dq);
-                const float ev = e[jj];
-                acc[0] = __fmaf_rn(ev, h2f_bits(v.x & 0xFFFFu), acc[0]);
-                acc[1] = __fmaf_rn(ev, h2f_bits(v.x >> 16), acc[1]);
-                acc[2] = __fmaf_rn(ev, h2f_bits(v.y & 0xFFFFu), acc[2]);
-                acc[3] = __fmaf_rn(ev, h2f_bits(v.y >> 16), acc[3]);
+                for (int jj = 0; jj < rows; jj++) {
+                    const uint2 v = *(const uint2 *)(chunk + jj * D * 2 + 2 * d0);
+                    const float ev = e[jj];
+                    acc[0] = __fmaf_rn(ev, h2f_bits(v.x & 0xFFFFu), acc[0]);
+                    acc[1] = __fmaf_rn(ev, h2f_bits(v.x >> 16), acc[1]);
+                    acc[2] = __fmaf_rn(ev, h2f_bits(v.y & 0xFFFFu), acc[2]);
+                    acc[3] = __fmaf_rn(ev, h2f_bits(v.y >> 16), acc[3]);
+                }
+            } else {
+#pragma unroll 4
+                for (int jj = 0; jj < rows; jj++) {
+                    const uint32_t v = *(const uint32_t *)(chunk + jj * D * 2 + 2 * d0);
+                    const float ev = e[jj];
+                    acc[0] = __fmaf_rn(ev, h2f_bits(v & 0xFFFFu), acc[0]);
+                    acc[1] = __fmaf_rn(ev, h2f_bits(v >> 16), acc[1]);
+                }
             }
         }
         done();
     }
-    if (hh < HU) {
-        float4 o;
-        o.x = __fdiv_rn(acc[0], ms.hsum[hh]);
-        o.y = __fdiv_rn(acc[1], ms.hsum[hh]);
-        o.z = __fdiv_rn(acc[2], ms.hsum[hh]);
-        o.w = __fdiv_rn(acc[3], ms.hsum[hh]);
-        *(float4 *)(obuf + hh * D + 4 * dq) = o;
-        __stcg((float4 *)(p.att + (h0 + hh) * D + 4 * dq), o);
-    }
+    if (warp < 4)
+        for (int i = 0; i < HU; i++) {
+            const float o = __fdiv_rn(acc[i], ms.hsum[hh]);
+            obuf[hh * D + d0 + i] = o;
+            __stcg(p.att + (h0 + hh) * D + d0 + i, o);
+        }
     bar_cons();
     if (tid == 0) stamp(p, jslot(tj, 12));
     // the unit's 8-bit blocks (HU * 128 / 256 of them), one warp each
@@ -844,7 +860,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                         }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&rfree[rs]);
+                    if (lane == 0) {
+                        mbar_arrive(&rfree[rs]);
+                        stage_stamp(p, m, 3);
+                    }
                 }
             }
             // ---- end of the job: both chain warps are done with this CTA's rows
@@ -907,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         const uint32_t rec_s = smem_u32(smem + sm.off_rec);
         uint8_t *bad = smem + sm.off_bad;
         const int h = lane & 1;
-        const int G2 = p.H / p.Hkv, HU = G2 >= 4 ? 4 : G2, units = p.H / HU;
+        const int HU = attn_hu(p), units = p.H / HU;
         uint32_t head = 0;
         int m = 0, mr = 0;  // data stages (ring) and record stages consumed
         bool failed = false;
@@ -984,8 +1003,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                     const uint32_t off = ring_next(head, (uint32_t)(srows * g.rb), (uint32_t)sm.ring);
                     const int slot = m % kStg, rs = mr % kRS;
                     if (!failed && !mbar_wait_s(&full[slot], (m / kStg) & 1, p.status, ms)) failed = true;
+                    if (threadIdx.x == 0) stage_stamp(p, mr, 0);
                     if (!failed && mr >= kRS && !mbar_wait_s(&rfree[rs], ((mr / kRS) & 1) ^ 1, p.status, ms))
                         failed = true;
+                    if (threadIdx.x == 0) stage_stamp(p, mr, 1);
                     failed = __any_sync(FULLM, failed);
                     const bool active = !failed && lane_on && roff < srows;
                     int S = 0, M = 0;
@@ -1025,6 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&rdone[rs]);
+                    if (threadIdx.x == 0) stage_stamp(p, mr, 2);
                 }
             }
             if (threadIdx.x == 0) stamp(p, jslot(j, 2));
@@ -1055,8 +1077,8 @@ bool step_ok(int E, int F, int H, int Hkv, int D, int C, int rotary, int interle
     if (E % 256 || F % 256 || E < 2048 || F < 2048 || E > kMaxE || F > kMaxK) return false;
     if (D != 128 || Hkv <= 0 || H % Hkv || H * D != E || !interleaved || !cache_f16 || rotary % 2 || rotary > D)
         return false;
-    const int G = H / Hkv, HU = G >= 4 ? 4 : G;
-    if (G % 2 || G % HU || (HU * D) % 256) return false;
+    const int G = H / Hkv, HU = 2;  // attention units of two query heads (one 256-element block)
+    if (G % 2) return false;
     // attention scratch in the act + record regions: q, outputs and HU x C scores
     const int nbmax = (E > F ? E : F) / 256;
     const long long scratch = (long long)act_region(nbmax) + kRS * kRecStage;

@@ -49,7 +49,14 @@ struct StepParams {
 // stage issued, 6 last stage issued; for the o job of an attention CTA also
 // 8 q|k|v rows of every CTA written, 9 first key stage landed, 10 scores done,
 // 11 softmax sums done, 12 weighted sums done.
-__host__ __device__ inline size_t step_trace_words(int L) { return 2 + 16 * (size_t)(4 * L + 1); }
+// After the CTAs' slots: CTA 0's stage log, kStageLog entries of 4 words
+// (consumer warp 0 after the stage landed, after its record stage was free,
+// when its records were written; chain warp done with the record stage).
+constexpr int kStageLog = 1024;
+__host__ __device__ inline size_t step_trace_cta_words(int L) { return 2 + 16 * (size_t)(4 * L + 1); }
+__host__ __device__ inline size_t step_trace_words_total(int G, int L) {
+    return (size_t)G * step_trace_cta_words(L) + 4 * (size_t)kStageLog;
+}
 
 // Whether a model of these dimensions runs through the step kernel (else the
 // kernel-per-op path): Q4_K / Q6_K matrices, E a multiple of 256 up to 8192,

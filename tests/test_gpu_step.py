@@ -76,11 +76,13 @@ def test_step_kernel_bit_identical_to_op_path(ctx, shape, layers, vocab):
         t.free()
 
 
-def test_step_kernel_is_the_default_and_models_that_do_not_qualify_refuse_it(ctx, tiny):
+def test_step_kernel_is_opt_in_and_models_that_do_not_qualify_refuse_it(ctx, tiny):
     import mimgpu
     cfg = dict(bench.CFG8B, layers=1, vocab=4096)
     model, weights = bench.build_model(ctx, cfg, 64, 8)
     s = model.session()
+    assert not s.uses_step_kernel  # the kernel-per-op path measured faster
+    s.set_step_kernel(True)
     assert s.uses_step_kernel
     s.free()
     model.free()
