@@ -163,21 +163,44 @@ def peaks():
 
 # ----------------------------------------------------------------- GPU arm
 
-def build_model(ctx, cfg, context, max_tokens):
+def shard_rows(name, cfg, nranks, rank):
+    """(first row, rows) of a weight a tensor-parallel rank holds: its rows of
+    every split matrix, or the whole tensor (norms, the embedding table)."""
+    E, F, V, KV = cfg["embed"], cfg["ffn"], cfg["vocab"], cfg["kv_heads"] * cfg["head_dim"]
+    base = name.split(".", 2)[-1] if name.startswith("blk.") else name
+    full = {"attn_q.weight": E, "attn_output.weight": E, "ffn_down.weight": E, "attn_k.weight": KV,
+            "attn_v.weight": KV, "ffn_gate.weight": F, "ffn_up.weight": F, "output.weight": V}.get(base)
+    if full is None or nranks == 1:
+        return None
+    per = (full + nranks - 1) // nranks
+    r0 = min(full, rank * per)
+    return r0, min(full, r0 + per) - r0
+
+
+def build_model(ctx, cfg, context, max_tokens, tp=None):
+    """The benchmark model, weights made on the device; tp = (ranks, rank)
+    makes only this rank's rows of every split matrix (byte-identical to the
+    same rows of the whole tensor)."""
     import mimgpu
     weights = {}
     for name, dt, shape, mean, sigma in layout(cfg):
-        weights[name] = (dt, ctx.synth(dt, shape, seed_of(name), mean, sigma))
+        sh = shard_rows(name, cfg, *tp) if tp else None
+        if sh:
+            r0, rows = sh
+            weights[name] = (dt, ctx.synth_rows(dt, (rows,) + tuple(shape[1:]), r0, seed_of(name), mean, sigma))
+        else:
+            weights[name] = (dt, ctx.synth(dt, shape, seed_of(name), mean, sigma))
     full = dict(cfg, context=context, a8=1, cache_f16=1, interleaved=1, max_tokens=max_tokens)
     return mimgpu.Model(ctx, full, weights), weights
 
 
 def gemv_roofline(ctx, cfg, weights, torch, reps=3):
-    """The GEMV kernel alone over the decode shapes of every layer (cold L2:
-    each launch reads a different weight), the launches captured back to
-    back in one CUDA graph and timed with CUDA events on the launching stream
-    around each replay.  Returns (bytes per launch, seconds per launch,
-    launches)."""
+    """The one-row GEMV alone over the decode step's own launch list -- per
+    layer q|k|v (one fused launch), o, gate|up (one fused launch), down, then
+    the head -- captured back to back in one CUDA graph (cold L2: each launch
+    reads different weights) and timed with CUDA events on the launching
+    stream around each replay.  Returns (bytes per launch, seconds per
+    launch, launches)."""
     import mimgpu
     lib = mimgpu.lib()
     E, F = cfg["embed"], cfg["ffn"]
@@ -189,18 +212,25 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=3):
     ctx._check(lib.mimgpu_q8_new(ctx.h, 1, F, C.byref(q8f)))
     ctx._check(lib.mimgpu_q8_quantize_dev(ctx.h, st.cuda_stream, x_e.data_ptr(), q8e))
     ctx._check(lib.mimgpu_q8_quantize_dev(ctx.h, st.cuda_stream, x_f.data_ptr(), q8f))
-    y = torch.empty(max(cfg["vocab"], F), device="cuda", dtype=torch.float32)
+    y = torch.empty(4, max(cfg["vocab"], 2 * F), device="cuda", dtype=torch.float32)
     plan = []
     for l in range(cfg["layers"]):
-        for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up"):
-            plan.append((weights[f"blk.{l}.{n}.weight"][1], q8e, x_e, E))
-        plan.append((weights[f"blk.{l}.ffn_down.weight"][1], q8f, x_f, F))
-    plan.append((weights["output.weight"][1], q8e, x_e, E))
+        w = lambda n: weights[f"blk.{l}.{n}.weight"][1]
+        plan.append(([w("attn_q"), w("attn_k"), w("attn_v")], q8e, x_e, E))
+        plan.append(([w("attn_output")], q8e, x_e, E))
+        plan.append(([w("ffn_gate"), w("ffn_up")], q8e, x_e, E))
+        plan.append(([w("ffn_down")], q8f, x_f, F))
+    plan.append(([weights["output.weight"][1]], q8e, x_e, E))
+    args = []
+    for ts, q8, x, K in plan:
+        tarr = (C.c_void_p * len(ts))(*[t.h.value for t in ts])
+        yarr = (C.c_void_p * len(ts))(*[y[i].data_ptr() for i in range(len(ts))])
+        args.append((q8, x, len(ts), tarr, yarr))
     torch.cuda.synchronize()
 
     def enqueue():
-        for t, q8, x, K in plan:
-            ctx._check(lib.mimgpu_gemv_q8_dev(ctx.h, st.cuda_stream, q8, x.data_ptr(), t.h, None, y.data_ptr()))
+        for q8, x, n, tarr, yarr in args:
+            ctx._check(lib.mimgpu_gemv_q8_fused_dev(ctx.h, st.cuda_stream, q8, x.data_ptr(), n, tarr, yarr))
 
     with torch.cuda.stream(st):
         enqueue()  # warm-up: kernel attributes, tensor maps
@@ -222,9 +252,10 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=3):
             total_t += a.elapsed_time(b) / 1e3
     del g
     total_b, launches = 0, 0
-    for t, q8, x, K in plan:
-        n = t.shape[0]
-        total_b += reps * (nbytes(t.dtype, t.shape) + K + K // 256 * 4 + K // 32 * 2 + K // 16 * 2 + 4 * n)
+    for ts, q8, x, K in plan:
+        n = sum(t.shape[0] for t in ts)
+        total_b += reps * (sum(nbytes(t.dtype, t.shape) for t in ts) + K + K // 256 * 4 + K // 32 * 2 + K // 16 * 2
+                           + 4 * n)
         launches += reps
     lib.mimgpu_q8_free(q8e)
     lib.mimgpu_q8_free(q8f)
@@ -274,7 +305,8 @@ def run_gpu(args):
     prompt = args.prompt
     context = prompt + args.warmup + args.steps + 2 * args.e2e_steps + 8
     ctx = mimgpu.Context(local)
-    model, weights = build_model(ctx, cfg, context, prompt)
+    # each rank makes and holds only its own rows of every split matrix
+    model, weights = build_model(ctx, cfg, context, prompt, (world, rank) if world > 1 else None)
     tp = None
     if world > 1:
         # tensor parallelism: one sequence over all ranks (each computes its
@@ -352,7 +384,8 @@ def run_gpu(args):
     else:
         # the kernel-per-op path: its dominant kernel, the one-row GEMV, alone over the decode shapes
         bpl, spl, nl = gemv_roofline(ctx, cfg, weights, torch)
-        kernel = f"gemv_row_kernel (one-row dequant_matmul_a8.v2, decode shapes of all {cfg['layers']} layers + head)"
+        kernel = (f"gemv_row_kernel (one-row dequant_matmul_a8.v2 over the decode step's launch list: per layer "
+                  f"q|k|v fused, o, gate|up fused, down; {cfg['layers']} layers + head)")
         traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
         # embedding, 9 per layer, final norm, head, argmax, advance
         launches = args.steps * (1 + 9 * cfg["layers"] + 4)
@@ -371,8 +404,9 @@ def run_gpu(args):
                    "matmul": "dequant_matmul_a8.v2 block 256 (bit-exact dotQ8KRef)", "kv_cache": "f16",
                    "decode_path": ("one persistent step kernel per token" if step_path
                                    else "one kernel per op (~9 per layer)"),
-                   "parallelism": f"tp{world} (rows of every matrix per rank, NCCL all-gathers)" if world > 1
-                   else "1 GPU",
+                   "parallelism": (f"tp{world} (q|k|v by kv-head group, o / gate|up / down / head by output rows, "
+                                   f"each rank holding its shard; attention, residual and SwiGLU exchanged over "
+                                   f"peer memory)") if world > 1 else "1 GPU",
                    "l2": l2_note(cfg, "streamed per token")},
         "e2e": {"value": round(args.e2e_steps / e2e_s, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * cfg["vocab"],

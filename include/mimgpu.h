@@ -191,6 +191,13 @@ int mimgpu_q8_quantize_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, mi
 int mimgpu_gemv_q8_dev(mimgpu_ctx *ctx, void *stream, const mimgpu_q8 *q, const float *x_dev,
                        const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
 
+/* The same product for n (1..4) matrices sharing the activations, in one
+ * launch: ys[i] = x ws[i]^T, as the decode step runs q|k|v and gate|up (the
+ * reference runs them as separate calls of linearA8, interp/fast.go:282-379,
+ * with the same per-matrix bits). */
+int mimgpu_gemv_q8_fused_dev(mimgpu_ctx *ctx, void *stream, const mimgpu_q8 *q, const float *x_dev, int n,
+                             const mimgpu_tensor *const *ws, float *const *ys);
+
 /* ------------------------------------------------ synthetic weights, bytes
  * Not part of the reference interface: seeded random-init weights for the
  * benchmark configurations, made on the device (values from N(mean, sigma)
@@ -198,6 +205,10 @@ int mimgpu_gemv_q8_dev(mimgpu_ctx *ctx, void *stream, const mimgpu_q8 *q, const 
  * bytes back to the host. */
 int mimgpu_synth_tensor(mimgpu_ctx *ctx, int dtype, uint64_t seed, int ndim, const int64_t *shape, float mean,
                         float sigma, mimgpu_tensor **out);
+/* Rows [row0, row0 + shape[0]) of the tensor mimgpu_synth_tensor makes with the
+ * same seed (a tensor-parallel rank's shard, byte for byte). */
+int mimgpu_synth_rows(mimgpu_ctx *ctx, int dtype, uint64_t seed, int ndim, const int64_t *shape, int64_t row0,
+                      float mean, float sigma, mimgpu_tensor **out);
 int mimgpu_tensor_download(const mimgpu_tensor *t, void *bytes, size_t nbytes);
 size_t mimgpu_tensor_nbytes(const mimgpu_tensor *t);
 
@@ -282,15 +293,17 @@ int mimgpu_session_set_trace(mimgpu_session *s, void *dev_buf, size_t nbytes);
 /* ------------------------------------------------- tensor parallelism
  * No counterpart in the reference (one process on CPU).  Ranks of one node,
  * one process and context per GPU, share an NCCL communicator (NCCL is
- * loaded at run time).  With a group bound, the attention block runs whole
- * on every rank (the residual stream stays identical without an exchange)
- * while the FFN and the output head are used by output rows: rank k of N
- * computes gate/up rows [kF/N, (k+1)F/N), down rows [kE/N, (k+1)E/N) and its
- * vocabulary rows as complete block-ordered dot products, and the SwiGLU
- * output and the residual are all-gathered; every rank produces the
- * single-GPU logits and greedy ids bit for bit.  The weights bound with
- * mimgpu_model_set_weight are the full tensors (each rank reads its rows).
- * Needs ffn and embed divisible by N. */
+ * loaded at run time).  With a group of N bound, rank k computes, as complete
+ * block-ordered dot products, the q|k|v rows of its query heads
+ * [kH/N, (k+1)H/N) and kv heads [kHkv/N, (k+1)Hkv/N) (RoPE, its key-value
+ * cache and attention on those heads only), o rows [kE/N, (k+1)E/N) after an
+ * exchange of the attention output, gate/up rows [kF/N, (k+1)F/N), down rows
+ * [kE/N, (k+1)E/N) after an exchange of the SwiGLU output, and its vocabulary
+ * rows; the residual is exchanged after o and after down.  Every rank
+ * produces the single-GPU logits and greedy ids bit for bit.  A weight bound
+ * with mimgpu_model_set_weight is either the full tensor (the rank reads its
+ * rows) or exactly this rank's rows (its shard: no rank then holds another's
+ * bytes).  Needs heads, kv heads and ffn divisible by N. */
 /* Rank 0 makes the group id (NCCL_UNIQUE_ID_BYTES = 128 bytes) and hands it
  * to the others. */
 int mimgpu_tp_unique_id(void *id, size_t nbytes);

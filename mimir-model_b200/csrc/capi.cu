@@ -520,14 +520,36 @@ int mimgpu_gemv_q8_dev(mimgpu_ctx *c, void *stream, const mimgpu_q8 *q, const fl
     return cuda_fail(c, launch_gemv_a8(&seg, 1, x, q->act, (int)q->rows, q->k, c->status, st, false), "gemv_q8");
 }
 
-int mimgpu_synth_tensor(mimgpu_ctx *c, int dtype, uint64_t seed, int ndim, const int64_t *shape, float mean,
-                        float sigma, mimgpu_tensor **out) {
+int mimgpu_gemv_q8_fused_dev(mimgpu_ctx *c, void *stream, const mimgpu_q8 *q, const float *x, int n,
+                             const mimgpu_tensor *const *ws, float *const *ys) {
+    if (!c || !q || !ws || !ys) return MIMGPU_EINVAL;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if (n < 1 || n > kMaxSegs) return fail(c, MIMGPU_EINVAL, "gemv_q8_fused: %d matrices (1..%d)", n, kMaxSegs);
+    GemvSeg segs[kMaxSegs];
+    for (int i = 0; i < n; i++) {
+        int rc = check_matmul(c, q->rows, q->k, ws[i]);
+        if (rc) return rc;
+        if (ws[i]->dtype != Q4_K && ws[i]->dtype != Q6_K)
+            return fail(c, MIMGPU_ENOTHANDLED, "gemv_q8_fused: dtype %d", ws[i]->dtype);
+        if (!ys[i]) return fail(c, MIMGPU_EINVAL, "gemv_q8_fused: output %d is null", i);
+        segs[i] = GemvSeg{ws[i]->dev, ws[i]->dtype, (int)ws[i]->shape[0], ys[i], ws[i]->shape[0], nullptr, nullptr};
+    }
+    int rc = use_device(c);
+    if (rc) return rc;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    return cuda_fail(c, launch_gemv_a8(segs, n, x, q->act, (int)q->rows, q->k, c->status, st, false),
+                     "gemv_q8_fused");
+}
+
+int mimgpu_synth_rows(mimgpu_ctx *c, int dtype, uint64_t seed, int ndim, const int64_t *shape, int64_t row0,
+                      float mean, float sigma, mimgpu_tensor **out) {
     if (!c || !out) return MIMGPU_EINVAL;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     *out = nullptr;
     if (dtype != F32 && dtype != Q8_0 && dtype != Q4_K && dtype != Q6_K)
         return fail(c, MIMGPU_ENOTHANDLED, "synth: dtype %d", dtype);
     if (ndim < 1 || ndim > 8 || !shape) return fail(c, MIMGPU_EINVAL, "synth: rank %d", ndim);
+    if (row0 < 0 || shape[0] <= 0) return fail(c, MIMGPU_EINVAL, "synth: first row %lld", (long long)row0);
     long long nbytes = tensor_bytes(dtype, ndim, shape);
     if (nbytes < 0) return fail(c, MIMGPU_EINVAL, "synth: shape does not fit the blocks");
     long long n = 1;
@@ -542,7 +564,7 @@ int mimgpu_synth_tensor(mimgpu_ctx *c, int dtype, uint64_t seed, int ndim, const
     t->nbytes = (size_t)nbytes;
     cudaError_t e = cudaMalloc(&t->dev, t->nbytes + 32);
     if (e == cudaSuccess) e = cudaMemsetAsync(t->dev + t->nbytes, 0, 32, c->stream);
-    if (e == cudaSuccess) e = launch_synth(dtype, seed, n, mean, sigma, t->dev, c->stream);
+    if (e == cudaSuccess) e = launch_synth(dtype, seed, n, mean, sigma, t->dev, c->stream, row0 * (n / shape[0]));
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         if (t->dev) cudaFree(t->dev);
@@ -551,6 +573,11 @@ int mimgpu_synth_tensor(mimgpu_ctx *c, int dtype, uint64_t seed, int ndim, const
     }
     *out = t;
     return MIMGPU_OK;
+}
+
+int mimgpu_synth_tensor(mimgpu_ctx *c, int dtype, uint64_t seed, int ndim, const int64_t *shape, float mean,
+                        float sigma, mimgpu_tensor **out) {
+    return mimgpu_synth_rows(c, dtype, seed, ndim, shape, 0, mean, sigma, out);
 }
 
 int mimgpu_tensor_download(const mimgpu_tensor *t, void *bytes, size_t nbytes) {

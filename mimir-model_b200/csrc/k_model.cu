@@ -237,6 +237,13 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
     const float o = __fdiv_rn(acc, hsum[hh]);
     const int E = a.H * D;
     a.out[(long long)t * E + (long long)h0 * D + tid] = o;
+    if (a.put.N > 1) {
+        // this rank's heads of the attention output into every rank's full
+        // vector, visible system-wide before the kernel ends (the next kernel
+        // on this stream publishes the exchange)
+        for (int r = 0; r < a.put.N; r++) peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * D + tid] = o;
+        __threadfence_system();
+    }
     if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 

@@ -33,12 +33,13 @@ __device__ __forceinline__ float f16r(float f) { return f16_to_f32(f32_to_f16(f)
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; }
 
 // One thread encodes one block.
+// Block b of the output holds elements first + b*be.. of the stream.
 __global__ void synth_kernel(int dt, uint64_t seed, long long nblocks, int be, float mean, float sigma,
-                             uint8_t *__restrict__ out) {
+                             uint8_t *__restrict__ out, long long first) {
     const long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (b >= nblocks) return;
     float x[256];
-    for (int i = 0; i < be; i++) x[i] = (float)(mean + sigma * normal_at(seed, (uint64_t)(b * be + i)));
+    for (int i = 0; i < be; i++) x[i] = (float)(mean + sigma * normal_at(seed, (uint64_t)(first + b * be + i)));
     if (dt == F32) {
         ((float *)out)[b] = x[0];
         return;
@@ -130,13 +131,14 @@ __global__ void synth_kernel(int dt, uint64_t seed, long long nblocks, int be, f
 }  // namespace
 
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,
-                         cudaStream_t st) {
+                         cudaStream_t st, long long first) {
     const int be = block_elems(dt);
-    if (nelems % be) return cudaErrorInvalidValue;
+    if (nelems % be || first % be) return cudaErrorInvalidValue;
     const long long nb = nelems / be;
     if (nb == 0) return cudaSuccess;
     const int threads = 128;
-    synth_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, st>>>(dt, seed, nb, be, mean, sigma, out);
+    synth_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, st>>>(dt, seed, nb, be, mean, sigma, out,
+                                                                               first);
     return cudaGetLastError();
 }
 

@@ -151,8 +151,9 @@ cudaError_t launch_argmax(const float *v, long long n, long long i0, bool holds_
 cudaError_t launch_wait_value(const uint32_t *addr, uint32_t value, unsigned *status, cudaStream_t st);
 
 // seeded synthetic weights (k_synth.cu)
+// elements [first, first + nelems) of the seeded stream (first a multiple of the block)
 cudaError_t launch_synth(int dt, uint64_t seed, long long nelems, float mean, float sigma, uint8_t *out,
-                         cudaStream_t st);
+                         cudaStream_t st, long long first = 0);
 
 int num_sms();
 

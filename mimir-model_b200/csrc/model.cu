@@ -87,9 +87,12 @@ struct mimgpu_session {
 
 namespace {
 
-int check_shape(mimgpu_ctx *c, const char *name, const mimgpu_tensor *w, long long d0, long long d1) {
+// d0 rows (or, for a tensor-parallel rank, shard rows: its own rows only) of d1
+int check_shape(mimgpu_ctx *c, const char *name, const mimgpu_tensor *w, long long d0, long long d1,
+                long long shard = -1) {
     if (!w) return fail(c, MIMGPU_EINVAL, "weight %s is missing", name);
-    const bool ok = d1 < 0 ? (w->ndim == 1 && w->shape[0] == d0) : (w->ndim == 2 && w->shape[0] == d0 && w->shape[1] == d1);
+    const bool rows_ok = w->shape[0] == d0 || (shard >= 0 && w->shape[0] == shard);
+    const bool ok = d1 < 0 ? (w->ndim == 1 && w->shape[0] == d0) : (w->ndim == 2 && rows_ok && w->shape[1] == d1);
     if (!ok) return fail(c, MIMGPU_EINVAL, "weight %s has the wrong shape", name);
     return MIMGPU_OK;
 }
@@ -99,25 +102,29 @@ bool matrix_dtype(int dt, bool a8) { return dt == Q4_K || dt == Q6_K || (!a8 && 
 int validate(mimgpu_model *m) {
     const auto &c = m->c;
     mimgpu_ctx *x = m->ctx;
-    const int N = tp_size(m->tp);
-    if (N > 1 && (c.ffn % N || c.embed % N))
-        return fail(x, MIMGPU_ENOTHANDLED, "tensor parallelism over %d ranks needs ffn %d and embed %d divisible by it",
-                    N, c.ffn, c.embed);
+    const int N = tp_size(m->tp), k = tp_rank(m->tp);
+    if (N > 1 && (c.ffn % N || c.heads % N || c.kv_heads % N))
+        return fail(x, MIMGPU_ENOTHANDLED,
+                    "tensor parallelism over %d ranks needs ffn %d, heads %d and kv heads %d divisible by it", N, c.ffn,
+                    c.heads, c.kv_heads);
     const long long E = c.embed, F = c.ffn, V = c.vocab, KV = (long long)c.kv_heads * c.head_dim;
+    // a rank may hold only its rows of each matrix (the embedding table is read by token, whole)
+    const long long sE = N > 1 ? E / N : -1, sF = N > 1 ? F / N : -1, sKV = N > 1 ? KV / N : -1;
+    const long long Vl = (V + N - 1) / N, sV = N > 1 ? std::max(0LL, std::min(Vl, V - k * Vl)) : -1;
     int rc;
     if ((rc = check_shape(x, "token_embd.weight", m->embd, V, E))) return rc;
     if ((rc = check_shape(x, "output_norm.weight", m->out_norm, E, -1))) return rc;
-    if (m->out && (rc = check_shape(x, "output.weight", m->out, V, E))) return rc;
+    if (m->out && (rc = check_shape(x, "output.weight", m->out, V, E, sV))) return rc;
     if (m->out_norm->dtype != F32) return fail(x, MIMGPU_ENOTHANDLED, "norm weights must be f32");
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
-        const struct { const char *n; const mimgpu_tensor *t; long long d0, d1; } list[] = {
-            {"attn_norm", w.attn_norm, E, -1}, {"attn_q", w.q, E, E},       {"attn_k", w.k, KV, E},
-            {"attn_v", w.v, KV, E},           {"attn_output", w.o, E, E},  {"ffn_norm", w.ffn_norm, E, -1},
-            {"ffn_gate", w.gate, F, E},       {"ffn_up", w.up, F, E},      {"ffn_down", w.down, E, F}};
+        const struct { const char *n; const mimgpu_tensor *t; long long d0, d1, shard; } list[] = {
+            {"attn_norm", w.attn_norm, E, -1, -1}, {"attn_q", w.q, E, E, sE},      {"attn_k", w.k, KV, E, sKV},
+            {"attn_v", w.v, KV, E, sKV},          {"attn_output", w.o, E, E, sE}, {"ffn_norm", w.ffn_norm, E, -1, -1},
+            {"ffn_gate", w.gate, F, E, sF},       {"ffn_up", w.up, F, E, sF},     {"ffn_down", w.down, E, F, sE}};
         for (auto &e : list) {
             std::string n = "blk." + std::to_string(l) + "." + e.n + ".weight";
-            if ((rc = check_shape(x, n.c_str(), e.t, e.d0, e.d1))) return rc;
+            if ((rc = check_shape(x, n.c_str(), e.t, e.d0, e.d1, e.shard))) return rc;
             if (e.d1 < 0 && e.t->dtype != F32) return fail(x, MIMGPU_ENOTHANDLED, "%s must be f32", n.c_str());
             if (e.d1 >= 0 && !matrix_dtype(e.t->dtype, c.a8))
                 return fail(x, MIMGPU_ENOTHANDLED, "%s: dtype %d is not served", n.c_str(), e.t->dtype);
@@ -128,31 +135,44 @@ int validate(mimgpu_model *m) {
     return MIMGPU_OK;
 }
 
-// Enqueues one run of the graph for T tokens whose ids and positions are
-// already in s->tok / s->pos.  Logits of every row (all_rows) or of the
-// last row go to s->logits; with greedy, the argmax and step update follow.
-// Row slice [r0, r0 + rows) of a weight matrix [n, K] as a GEMV segment.
-GemvSeg slice(const mimgpu_tensor *w, long long K, long long r0, int rows, float *y, long long ldy,
+// Rows [r0, r0 + rows) of a weight matrix of `full` rows and row length K as
+// a GEMV segment: `w` is the whole matrix, or exactly this rank's rows (a
+// tensor-parallel shard, which starts at row r0 of the whole).
+GemvSeg slice(const mimgpu_tensor *w, long long K, long long full, long long r0, int rows, float *y, long long ldy,
               const float *res) {
-    GemvSeg g{w->dev + r0 * row_bytes(w->dtype, K), w->dtype, rows, y, ldy, nullptr, res};
+    const uint8_t *base = w->shape[0] == full ? w->dev + r0 * row_bytes(w->dtype, K) : w->dev;
+    GemvSeg g{base, w->dtype, rows, y, ldy, nullptr, res};
     return g;
 }
 
+// Enqueues one run of the graph for T tokens whose ids and positions are
+// already in s->tok / s->pos.  Logits of every row (all_rows) or of the
+// last row go to s->logits; with greedy, the argmax and step update follow.
+//
+// Tensor parallelism over N ranks (rank k) splits every matrix by output
+// rows, so each rank computes complete block-ordered dot products and the
+// ranks' results are the one-GPU results bit for bit:
+//   q|k|v    the rows of this rank's query heads [k H/N, (k+1) H/N) and kv
+//            heads [k Hkv/N, (k+1) Hkv/N); RoPE, the key-value cache and
+//            attention run on those heads only;
+//   exchange the attention output (this rank's E/N columns to every rank);
+//   o        output rows [k E/N, (k+1) E/N) over the whole attention output;
+//   exchange the residual columns;
+//   gate|up  rows [k F/N, (k+1) F/N); exchange the SwiGLU output;
+//   down     output rows [k E/N, (k+1) E/N); exchange the residual columns;
+//   head     vocabulary rows, then the greedy keys' maximum.
+// Four exchanges per layer: NCCL all-gathers (prompt passes, or before the
+// ranks' arenas are mapped) or peer-memory stores fused into the producing
+// kernels (p2p.cuh).  No weight byte is read by two ranks (the norms and the
+// one embedding row per token excepted).
 cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy, unsigned *status) {
     mimgpu_model *m = s->m;
     const auto &c = m->c;
     const int E = c.embed, F = c.ffn, H = c.heads, Hkv = c.kv_heads, D = c.head_dim;
-    // tensor parallelism over N ranks: the attention block (QKV, attention,
-    // o projection; 17 % of a layer's bytes at the 8B shape) runs whole on
-    // every rank, so the residual stream stays identical everywhere without an
-    // exchange; the FFN and the vocabulary are split by output rows -- rank k
-    // computes gate/up rows [k F/N, (k+1) F/N) and down rows [k E/N, (k+1) E/N)
-    // as complete block-ordered dot products -- and the SwiGLU output and the
-    // residual are all-gathered, two exchanges per layer
     const int N = tp_size(m->tp), k = tp_rank(m->tp);
-    const int El = E / N, Fl = F / N, KV = Hkv * D;
+    const int El = E / N, Fl = F / N, Hl = H / N, Hkvl = Hkv / N, KVl = Hkvl * D, KV = Hkv * D;
     const int Vl = (c.vocab + N - 1) / N, v0 = k * Vl, vn = std::max(0, std::min(Vl, c.vocab - v0));
-    const long long ldq = E + 2LL * KV;
+    const long long ldq = El + 2LL * KVl;
     const bool a8 = c.a8 != 0;
     cudaStream_t st = s->st;
     const bool pdl = true;
@@ -185,25 +205,40 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if (r == cudaSuccess) r = launch_unshard(s->gbuf, N, T, W, full, (long long)N * W, (long long)N * W, st);
         return r;
     };
+    // the residual columns [k El, (k+1) El) this rank just wrote, to every rank (NCCL)
+    auto gather_x = [&]() -> cudaError_t {
+        if (T == 1) return tp_allgather(m->tp, s->x + (long long)k * El, s->x, (size_t)El, st);
+        cudaError_t r = launch_pack(s->x, T, E, (long long)k * El, El, s->xl, st);
+        if (r == cudaSuccess) r = gather(s->xl, El, s->x);
+        return r;
+    };
     CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl, s->epoch));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
-        // the previous layer's residual columns from every rank
-        const P2P xin = xch(2 * (l - 1) + 1, nullptr, 0);
+        // exchange slots of the layer: 4l attention output, 4l+1 residual after o,
+        // 4l+2 SwiGLU output, 4l+3 residual after down
+        const P2P xin = xch(4 * (l - 1) + 3, nullptr, 0);
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
                                 a8 ? s->actE : none, st, pdl, (p2p && l > 0) ? &xin : nullptr));
-        GemvSeg qkv[3] = {slice(w.q, E, 0, E, s->qkv, ldq, nullptr), slice(w.k, E, 0, KV, s->qkv + E, ldq, nullptr),
-                          slice(w.v, E, 0, KV, s->qkv + E + KV, ldq, nullptr)};
+        GemvSeg qkv[3] = {slice(w.q, E, E, (long long)k * El, El, s->qkv, ldq, nullptr),
+                          slice(w.k, E, KV, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr),
+                          slice(w.v, E, KV, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr)};
         if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
-        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, H, Hkv, D, c.context, c.rope_dims,
+        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
                            c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l],
                            s->batched ? s->slot : nullptr, s->slot0};
         CK(launch_rope_scatter(ra, st, pdl));
-        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, H, Hkv, D, c.context, c.cache_f16,
-                     (float)(1.0 / std::sqrt((double)D)), s->att, none, status, s->scores,
+        AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, Hl, Hkvl, D, c.context, c.cache_f16,
+                     (float)(1.0 / std::sqrt((double)D)), N > 1 ? s->attl : s->att, none, status, s->scores,
                      s->batched ? s->slot : nullptr, s->slot0};
-        if (attn_prefill_ok(aa)) {
+        const P2P attx = xch(4 * l, s->att, (long long)k * El);
+        if (N > 1) {
+            if (p2p) aa.put = attx;  // the heads of this rank into every rank's attention output
+            CK(launch_attn_exact(aa, st, pdl));
+            if (!p2p) CK(gather(s->attl, El, s->att));
+            if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl, p2p ? &attx : nullptr));
+        } else if (attn_prefill_ok(aa)) {
             // a prompt pass: the many-row kernel, then the 8-bit blocks of its output
             CK(launch_attn_exact(aa, st, pdl));
             if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl));
@@ -211,51 +246,46 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
             if (a8) aa.act = s->actE;  // quantized inside the one-row kernel
             CK(launch_attn_exact(aa, st, pdl));
         }
-        GemvSeg o = slice(w.o, E, 0, E, s->x, E, s->x);
-        if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl));
+        GemvSeg o = slice(w.o, E, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
+        const P2P oput = xch(4 * l + 1, s->x, (long long)k * El);
+        if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl, true, p2p ? &oput : nullptr));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
+        if (N > 1 && !p2p) CK(gather_x());
         CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
-                                a8 ? s->actE : none, st, pdl));
-        GemvSeg gu[2] = {slice(w.gate, E, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
-                         slice(w.up, E, (long long)k * Fl, Fl, s->gu + Fl, 2LL * Fl, nullptr)};
+                                a8 ? s->actE : none, st, pdl, p2p ? &oput : nullptr));
+        GemvSeg gu[2] = {slice(w.gate, E, F, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
+                         slice(w.up, E, F, (long long)k * Fl, Fl, s->gu + Fl, 2LL * Fl, nullptr)};
         if (a8) CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl));
         else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
-        const P2P aput = xch(2 * l, s->a, (long long)k * Fl);
+        const P2P aput = xch(4 * l + 2, s->a, (long long)k * Fl);
         CK(launch_swiglu_quant(s->gu, s->gu + Fl, 2LL * Fl, T, Fl, N > 1 ? s->al : s->a,
                                (a8 && N == 1) ? s->actF : none, st, pdl, p2p ? &aput : nullptr));
         if (N > 1) {
             if (!p2p) CK(gather(s->al, Fl, s->a));
             if (a8) CK(launch_quantize_a8(s->a, T, F, s->actF, st, pdl, p2p ? &aput : nullptr));
         }
-        GemvSeg dn = slice(w.down, F, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
-        const P2P xput = xch(2 * l + 1, s->x, (long long)k * El);
+        GemvSeg dn = slice(w.down, F, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
+        const P2P xput = xch(4 * l + 3, s->x, (long long)k * El);
         if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl, true, p2p ? &xput : nullptr));
         else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
-        if (N > 1 && !p2p) {
-            // this rank wrote residual columns [k El, (k+1) El); every rank needs all
-            if (T == 1) {
-                CK(tp_allgather(m->tp, s->x + (long long)k * El, s->x, (size_t)El, st));
-            } else {
-                CK(launch_pack(s->x, T, E, (long long)k * El, El, s->xl, st));
-                CK(gather(s->xl, El, s->x));
-            }
-        }
+        if (N > 1 && !p2p) CK(gather_x());
     }
     const int first = all_rows ? 0 : T - 1, rows = T - first;
-    const P2P xlast = xch(2 * (c.layers - 1) + 1, nullptr, 0);
+    const P2P xlast = xch(4 * (c.layers - 1) + 3, nullptr, 0);
     CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
                             (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl, p2p ? &xlast : nullptr));
     const mimgpu_tensor *head = m->out ? m->out : m->embd;
-    // vocabulary rows [v0, v0 + vn); one GPU writes the logits directly
+    // vocabulary rows [v0, v0 + vn); one GPU writes the logits directly (the
+    // tied embedding, when it is the head, is bound whole on every rank)
     float *lg = N > 1 ? s->logl : s->logits;
     const long long ldl = N > 1 ? Vl : c.vocab;
     if (vn > 0) {
-        GemvSeg hs = slice(head, E, v0, vn, lg, ldl, nullptr);
+        GemvSeg hs = slice(head, E, c.vocab, v0, vn, lg, ldl, nullptr);
         if (a8) CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl));
         else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
     }
     if (greedy) {
-        const P2P kput = xch(2 * c.layers, s->keys, 0);
+        const P2P kput = xch(4 * c.layers, s->keys, 0);
         CK(launch_argmax(lg, vn, v0, k == 0, s->amax, st, pdl, rows, ldl));
         if (N > 1 && !p2p) CK(tp_allreduce_max_u64(m->tp, s->amax, st, (size_t)rows));
         CK(launch_advance(s->amax, s->tok, s->pos, s->ids, s->step, st, pdl, p2p ? &kput : nullptr, s->keys,
@@ -505,7 +535,7 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
                          al(T * 2 * F * 4), al(T * F * 4), al(T * V * 4), act_q8_bytes((int)T, E), act_q8_bytes((int)T, F),
                          al(T * 4), al(T * 8), al(65536 * 4), al(256),
                          tpb(T * El * 4), tpb(T * Fl * 4), tpb(T * El * 4), tpb(T * Vl * 4), tpb(N * T * gw * 4),
-                         al((size_t)(2 * k.layers + 1) * N * 4), al((size_t)(2 * k.layers + 2) * 4), al((size_t)N * 8),
+                         al((size_t)(4 * k.layers + 1) * N * 4), al((size_t)(4 * k.layers + 2) * 4), al((size_t)N * 8),
                          al(16), al((size_t)N * 8), al(T * 8), al(T * 4)};
     for (size_t b : sz) bytes += b;
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
@@ -547,7 +577,7 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
     s->amax = (unsigned long long *)take();
     s->slot = (int32_t *)take();
     s->slots = slots;
-    s->cache_bytes = (size_t)slots * k.kv_heads * k.context * D * (k.cache_f16 ? 2 : 4);
+    s->cache_bytes = (size_t)slots * (k.kv_heads / N) * k.context * D * (k.cache_f16 ? 2 : 4);  // this rank's kv heads
     s->kc.resize(k.layers, nullptr);
     s->vc.resize(k.layers, nullptr);
     for (int l = 0; l < k.layers && e == cudaSuccess; l++) {

@@ -52,6 +52,7 @@ struct AttnArgs2 {
     float *scores;     // many-row kernel: score scratch of attn_prefill_scores_bytes, or null
     const int32_t *slot;  // [T] sequence of each row (batched decoding), or null: sequence slot0
     int slot0;
+    P2P put;              // tensor parallelism, one row: outputs also into every rank's full vector (N > 1)
 };
 
 cudaError_t launch_rope_scatter(const RopeScatterArgs &a, cudaStream_t st, bool pdl);

@@ -51,7 +51,9 @@ SIGNATURES = {
     "mimgpu_q8_free": (None, [P]),
     "mimgpu_q8_quantize_dev": (I32, [P, P, P, P]),
     "mimgpu_gemv_q8_dev": (I32, [P, P, P, P, P, P, P]),
+    "mimgpu_gemv_q8_fused_dev": (I32, [P, P, P, P, I32, P, P]),
     "mimgpu_synth_tensor": (I32, [P, I32, C.c_uint64, I32, P, C.c_float, C.c_float, C.POINTER(P)]),
+    "mimgpu_synth_rows": (I32, [P, I32, C.c_uint64, I32, P, I64, C.c_float, C.c_float, C.POINTER(P)]),
     "mimgpu_tensor_download": (I32, [P, P, SZ]),
     "mimgpu_tensor_nbytes": (SZ, [P]),
     "mimgpu_model_new": (I32, [P, P, C.POINTER(P)]),
@@ -193,6 +195,15 @@ class Context:
         shp = np.array(shape, np.int64)
         h = P()
         self._check(lib().mimgpu_synth_tensor(self.h, dtype, seed, len(shape), _p(shp), mean, sigma, C.byref(h)))
+        t = Tensor(self, h, dtype, shape)
+        self._tensors.append(t)
+        return t
+
+    def synth_rows(self, dtype: int, shape, row0: int, seed: int, mean: float = 0.0, sigma: float = 0.02) -> Tensor:
+        """Rows [row0, row0 + shape[0]) of synth(dtype, full shape, seed): a shard."""
+        shp = np.array(shape, np.int64)
+        h = P()
+        self._check(lib().mimgpu_synth_rows(self.h, dtype, seed, len(shape), _p(shp), row0, mean, sigma, C.byref(h)))
         t = Tensor(self, h, dtype, shape)
         self._tensors.append(t)
         return t

@@ -339,24 +339,30 @@ void mo_gen_normal(uint64_t seed, int64_t n, float mean, float sigma, float *x) 
     for (int64_t i = 0; i < n; i++) x[i] = (float)(mean + sigma * normal_at(seed, (uint64_t)i));
 }
 
-typedef struct { int dt; uint64_t seed; int64_t k; float sigma; uint8_t *dst; } gen_ctx;
+typedef struct { int dt; uint64_t seed; int64_t k, row0; float sigma; uint8_t *dst; } gen_ctx;
 
 static void gen_rows(void *p, int64_t lo, int64_t hi) {
     gen_ctx *c = (gen_ctx *)p;
     float *row = (float *)malloc(sizeof(float) * (size_t)c->k);
     int64_t rb = mo_row_bytes(c->dt, c->k);
     for (int64_t r = lo; r < hi; r++) {
-        for (int64_t i = 0; i < c->k; i++) row[i] = (float)(c->sigma * normal_at(c->seed, (uint64_t)(r * c->k + i)));
+        const int64_t g = c->row0 + r; /* the row of the whole tensor */
+        for (int64_t i = 0; i < c->k; i++) row[i] = (float)(c->sigma * normal_at(c->seed, (uint64_t)(g * c->k + i)));
         mo_quantize(c->dt, row, c->dst + r * rb, c->k);
     }
     free(row);
 }
 
-int mo_gen_weight(int dt, uint64_t seed, int64_t n, int64_t k, float sigma, uint8_t *dst, int nthreads) {
-    if (mo_row_bytes(dt, k) == 0) return -1;
-    gen_ctx c = {dt, seed, k, sigma, dst};
+int mo_gen_weight_rows(int dt, uint64_t seed, int64_t row0, int64_t n, int64_t k, float sigma, uint8_t *dst,
+                       int nthreads) {
+    if (mo_row_bytes(dt, k) == 0 || row0 < 0) return -1;
+    gen_ctx c = {dt, seed, k, row0, sigma, dst};
     parallel_for(n, nthreads, gen_rows, &c);
     return 0;
+}
+
+int mo_gen_weight(int dt, uint64_t seed, int64_t n, int64_t k, float sigma, uint8_t *dst, int nthreads) {
+    return mo_gen_weight_rows(dt, seed, 0, n, k, sigma, dst, nthreads);
 }
 
 /* ------------------------------------------------------------------ */

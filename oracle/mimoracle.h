@@ -55,6 +55,9 @@ int mo_quantize(int dt, const float *x, uint8_t *dst, int64_t n);
  * generator keyed by seed, so any row range can be produced independently),
  * encoded as dt into dst (n rows of mo_row_bytes(dt,k) bytes). */
 int mo_gen_weight(int dt, uint64_t seed, int64_t n, int64_t k, float sigma, uint8_t *dst, int nthreads);
+/* Rows [row0, row0 + n) of the tensor mo_gen_weight makes with the same seed. */
+int mo_gen_weight_rows(int dt, uint64_t seed, int64_t row0, int64_t n, int64_t k, float sigma, uint8_t *dst,
+                       int nthreads);
 /* n values from N(mean, sigma) into x (f32), same generator. */
 void mo_gen_normal(uint64_t seed, int64_t n, float mean, float sigma, float *x);
 

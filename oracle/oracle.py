@@ -58,6 +58,7 @@ def lib():
             "mo_dequantize": (I32, [I32, P, P, I64]),
             "mo_quantize": (I32, [I32, P, P, I64]),
             "mo_gen_weight": (I32, [I32, C.c_uint64, I64, I64, F, P, I32]),
+            "mo_gen_weight_rows": (I32, [I32, C.c_uint64, I64, I64, I64, F, P, I32]),
             "mo_gen_normal": (None, [C.c_uint64, I64, F, F, P]),
             "mo_q8_quantize": (I32, [P, I64, I32, P, P, P, P]),
             "mo_dot_q8k_ref": (I32, [I32, P, P, P, P, I64, P]),
@@ -119,6 +120,16 @@ def gen_weight(dt: int, seed: int, n: int, k: int, sigma: float = 0.02, nthreads
     if rc != 0:
         raise ValueError("gen_weight: bad dtype or k")
     return out.reshape(n, -1)
+
+
+def gen_weight_rows(dt: int, seed: int, row0: int, n: int, k: int, sigma: float = 0.02,
+                    nthreads: int | None = None) -> np.ndarray:
+    """Rows [row0, row0 + n) of gen_weight(dt, seed, ...): a shard, byte for byte."""
+    out = np.empty(n * row_bytes(dt, k), np.uint8)
+    rc = lib().mo_gen_weight_rows(dt, seed, row0, n, k, sigma, _p(out), nthreads or threads())
+    if rc != 0:
+        raise ValueError("gen_weight_rows: bad dtype, k or row")
+    return out
 
 
 def gen_normal(seed: int, n: int, mean: float = 0.0, sigma: float = 1.0) -> np.ndarray:

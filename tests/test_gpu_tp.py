@@ -1,7 +1,9 @@
 """Tensor parallelism across 2 GPUs of one node (needs >= 2 GPUs; skipped
-otherwise): every rank computes complete block-ordered dot products over its
-output rows and all-gathers the activations it needs, so the prompt logits
-and 32 greedy ids of a 2-layer 8B-shape model are bit-identical to one GPU."""
+otherwise): every rank holds and reads only its rows of each matrix (q|k|v by
+kv-head group, o / gate|up / down / head by output rows), computes complete
+block-ordered dot products and exchanges the attention output, the residual
+and the SwiGLU output, so the prompt logits and 32 greedy ids of 8B- and
+70B-shaped layers are bit-identical to one GPU."""
 import multiprocessing as mp
 import os
 
@@ -16,21 +18,27 @@ def _gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.fixture(scope="module")
-def one_gpu():
+_ONE = {}
+
+
+def _one_gpu(shape):
     import tp_worker
-    return tp_worker.decode(0, None, 1, 0)
+    if shape not in _ONE:
+        _ONE[shape] = tp_worker.decode(0, None, 1, 0, shape=shape)
+    return _ONE[shape]
 
 
 @pytest.mark.skipif("_gpus() < 2")
-@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "peer-memory"])
-def test_tp2_bit_identical_to_one_gpu(one_gpu, p2p):
+@pytest.mark.parametrize("shape,p2p", [("8b", False), ("8b", True), ("70b", True)],
+                         ids=["8b-nccl", "8b-peer-memory", "70b-peer-memory"])
+def test_tp2_bit_identical_to_one_gpu(shape, p2p):
     """Prompt (16 tokens: NCCL all-gathers) and 32 greedy steps (NCCL, or
-    peer-memory exchanges inside the kernels) on 2 ranks."""
+    peer-memory exchanges inside the kernels) on 2 ranks, each holding only
+    its shard of every split matrix."""
     import socket
     import tp_worker
     import mimgpu
-    want_logits, want_ids = one_gpu
+    want_logits, want_ids = _one_gpu(shape)
     gid = mimgpu.tp_unique_id()
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     with socket.socket() as sk:
@@ -38,7 +46,7 @@ def test_tp2_bit_identical_to_one_gpu(one_gpu, p2p):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=tp_worker.rank_main, args=(r, 2, gid, port, p2p, q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_worker.rank_main, args=(r, 2, gid, port, p2p, q, shape)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}

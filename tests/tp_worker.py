@@ -10,19 +10,26 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 
 
-def model_cfg():
+def model_cfg(shape: str = "8b"):
+    """Two layers of the 8B shape, or one of the 70B shape (E 8192, F 28672,
+    64 / 8 heads), vocabulary 32000."""
+    if shape == "70b":
+        return dict(layers=1, embed=8192, ffn=28672, heads=64, kv_heads=8, head_dim=128, rope_dims=128,
+                    vocab=32000, rope_theta=500000.0, norm_eps=1e-5)
     return dict(layers=2, embed=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128, rope_dims=128, vocab=32000,
                 rope_theta=500000.0, norm_eps=1e-5)
 
 
-def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: int = 32, exchange=None):
+def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: int = 32, exchange=None,
+           shape: str = "8b"):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "mimir-model_b200"))
     import bench
     import mimgpu
-    cfg = model_cfg()
+    cfg = model_cfg(shape)
     ctx = mimgpu.Context(device)
-    model, _ = bench.build_model(ctx, cfg, 128, 16)
+    # a rank of a group holds only its rows of every split matrix
+    model, _ = bench.build_model(ctx, cfg, 128, 16, (nranks, rank) if group_id is not None else None)
     tp = None
     if group_id is not None:
         tp = mimgpu.TensorParallel(ctx, group_id, nranks, rank)
@@ -41,7 +48,7 @@ def decode(device: int, group_id: bytes | None, nranks: int, rank: int, steps: i
     return logits, ids
 
 
-def rank_main(rank: int, nranks: int, group_id: bytes, port: int, p2p: bool, q):
+def rank_main(rank: int, nranks: int, group_id: bytes, port: int, p2p: bool, q, shape: str = "8b"):
     import torch.distributed as dist
     from datetime import timedelta
     try:
@@ -53,7 +60,7 @@ def rank_main(rank: int, nranks: int, group_id: bytes, port: int, p2p: bool, q):
             dist.all_gather_object(out, handle)
             return out
 
-        q.put((rank, decode(rank, group_id, nranks, rank, exchange=exchange if p2p else None)))
+        q.put((rank, decode(rank, group_id, nranks, rank, exchange=exchange if p2p else None, shape=shape)))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
