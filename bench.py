@@ -305,23 +305,27 @@ def run_gpu(args):
     prompt = args.prompt
     context = prompt + args.warmup + args.steps + 2 * args.e2e_steps + 8
     ctx = mimgpu.Context(local)
-    # each rank makes and holds only its own rows of every split matrix
-    model, weights = build_model(ctx, cfg, context, prompt, (world, rank) if world > 1 else None)
+    # N > 1: tensor parallelism (one sequence over all ranks) for the 70B shape
+    # or with --tp; otherwise N independent replicas, one sequence per GPU
+    use_tp = world > 1 and (args.tp or args.shape == "70b")
+    # a tensor-parallel rank makes and holds only its own rows of every split matrix
+    model, weights = build_model(ctx, cfg, context, prompt, (world, rank) if use_tp else None)
     tp = None
-    if world > 1:
-        # tensor parallelism: one sequence over all ranks (each computes its
-        # output rows of every matrix, bit-identical to one GPU)
+    if use_tp:
+        # each rank computes its output rows of every matrix, bit-identical to one GPU
         gid = [mimgpu.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(gid, src=0)
         tp = mimgpu.TensorParallel(ctx, gid[0], world, rank)
         model.set_tp(tp)
     sess = model.session()
-    if world > 1:
+    if use_tp and args.p2p:
         # map every rank's arena: decode steps exchange over peer memory
         hs = [None] * world
         dist.all_gather_object(hs, sess.ipc_handle())
         sess.set_peers(hs)
-    ids = prompt_ids(cfg["vocab"], prompt)
+    replicas = world if world > 1 and not use_tp else 1
+    # replicas decode different sequences (a prompt of their own)
+    ids = prompt_ids(cfg["vocab"], prompt, seed=20261201 + (rank if replicas > 1 else 0))
     logits = sess.run(ids, np.arange(prompt))[0]
     tok, pos = int(np.argmax(logits)), prompt
     # warm-up (also captures the decode graph)
@@ -368,7 +372,7 @@ def run_gpu(args):
         e2e_s = float(t.item())
     wpt = weight_bytes_per_token(cfg)
     ms = dev_s / args.steps * 1e3
-    value = args.steps / dev_s  # one sequence, whole job
+    value = replicas * args.steps / dev_s  # tokens of every sequence over the slowest rank's time
     peak, peak_kind = peaks()
     step_path = sess.uses_step_kernel
     if step_path:
@@ -393,7 +397,7 @@ def run_gpu(args):
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak",
+        "scaling": "strong" if use_tp else "weak",
         "vs_baseline": round(value / PUBLISHED_8B, 2) if args.shape == "8b" else None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)",
         "config": {"workload": ("8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)" if args.shape == "8b"
@@ -405,10 +409,12 @@ def run_gpu(args):
                    "decode_path": ("one persistent step kernel per token" if step_path
                                    else "one kernel per op (~9 per layer)"),
                    "parallelism": (f"tp{world} (q|k|v by kv-head group, o / gate|up / down / head by output rows, "
-                                   f"each rank holding its shard; attention, residual and SwiGLU exchanged over "
-                                   f"peer memory)") if world > 1 else "1 GPU",
+                                   f"each rank holding its shard; attention, residual and SwiGLU exchanged by "
+                                   f"{'peer-memory stores' if args.p2p else 'NCCL all-gathers'})") if use_tp
+                   else (f"{world} independent replicas, one batch-1 sequence per GPU, no collective on the data "
+                         f"path") if world > 1 else "1 GPU",
                    "l2": l2_note(cfg, "streamed per token")},
-        "e2e": {"value": round(args.e2e_steps / e2e_s, 3), "unit": "tok/s",
+        "e2e": {"value": round(replicas * args.e2e_steps / e2e_s, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * cfg["vocab"],
                 "api": "mimgpu_session_run (pinned host token/position in, logits out, host argmax)"},
         "step_roofline": {"bound": "hbm", "bytes_per_token": wpt, "achieved": round(wpt / (ms / 1e3) / 1e9, 1),
@@ -754,6 +760,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1: tensor parallelism of one sequence (the default for --shape 70b; 8b runs replicas)")
+    ap.add_argument("--p2p", action="store_true",
+                    help="tensor parallelism: exchanges by peer-memory stores instead of NCCL all-gathers")
     ap.add_argument("--shape", default="8b", choices=sorted(SHAPES),
                     help="model shape: 8b (configs 3-4) or 70b (config 5)")
     ap.add_argument("--layers", type=int, default=0,

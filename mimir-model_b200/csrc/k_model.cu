@@ -233,17 +233,22 @@ __global__ void __launch_bounds__(256) attn_exact_kernel(AttnArgs2 a) {
         }
     }
     (void)ok;
-    if (hh >= nh) return;  // only in a partial block, which never quantizes (E % 256 != 0)
-    const float o = __fdiv_rn(acc, hsum[hh]);
     const int E = a.H * D;
-    a.out[(long long)t * E + (long long)h0 * D + tid] = o;
-    if (a.put.N > 1) {
-        // this rank's heads of the attention output into every rank's full
-        // vector, visible system-wide before the kernel ends (the next kernel
-        // on this stream publishes the exchange)
-        for (int r = 0; r < a.put.N; r++) peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * D + tid] = o;
-        __threadfence_system();
+    float o = 0.f;
+    if (hh < nh) {
+        o = __fdiv_rn(acc, hsum[hh]);
+        a.out[(long long)t * E + (long long)h0 * D + tid] = o;
+        // tensor parallelism: this rank's heads into every rank's full vector
+        for (int r = 0; r < (a.put.N > 1 ? a.put.N : 0); r++)
+            peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * D + tid] = o;
     }
+    if (a.put.N > 1) {
+        // the block's peer stores are visible system-wide before the kernel
+        // ends (the next kernel on this stream publishes the exchange)
+        __syncthreads();
+        if (tid == 0) __threadfence_system();
+    }
+    if (hh >= nh) return;  // only in a partial block, which never quantizes (E % 256 != 0)
     if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 

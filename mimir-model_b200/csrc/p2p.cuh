@@ -61,15 +61,17 @@ __device__ __forceinline__ void p2p_publish_wait(const P2P &x) {
     const unsigned e = *(volatile const unsigned *)x.epoch;
     const unsigned *f = peer_ptr<unsigned>(x, x.k, x.off_flags) + x.slot * x.N;
     const uint64_t t0 = global_ns(), limit = dev_wait_limit(x.status);
+    // relaxed polls of the (local) flag words, one acquire fence once all match
     for (int r = 0; r < x.N; r++) {
         for (uint32_t i = 0;; i++) {
-            if (ld_acquire_sys(f + r) == e) break;
+            if (*(volatile const unsigned *)(f + r) == e) break;
             if ((i & 63) == 63 && global_ns() - t0 > limit) {
                 atomicOr(x.status, (unsigned)DEV_TIMEOUT);
                 return;
             }
         }
     }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 }  // namespace mimgpu
