@@ -113,10 +113,15 @@ int mimgpu_dequant_matmul(mimgpu_ctx *ctx, const float *x, int64_t rows, int64_t
 
 /* dequant_matmul_a8.v2 (fastDequantMatmulA8V2, interp/fast.go:232-244) with
  * its `block` attribute (32 or 256; anything else is EINVAL as in
- * a8Block, interp/transformer.go:201-214).  With block 256 and Q4_K/Q6_K
- * weights the result is bit-identical to the reference's 8-bit kernels
- * (internal/kernels/q8k_test.go:35-117), rows it refuses taking the f32
- * product (interp/fast.go:282-379); other cases are the exact v1 product. */
+ * a8Block, interp/transformer.go:201-214), and dequant_matmul_a8.v1
+ * (fastDequantMatmulA8, interp/fast.go:225-230) as block 32.  With block 256
+ * and Q4_K/Q6_K weights the result is bit-identical to the reference's 8-bit
+ * kernels (dotQ8KRef, internal/kernels/q8k_test.go:35-117); with block 32
+ * and Q4_K/Q6_K/Q8_0 weights to its AVX2 block-32 kernels (dotQ4KQ8AVX2,
+ * dotQ6KQ8AVX2, dotQ8_0Q8AVX2, internal/kernels/kernels_amd64.s:441, 763,
+ * 1007; the only block-32 implementation it has).  Rows either refuses take
+ * the f32 product (interp/fast.go:282-379); other dtypes take the exact v1
+ * product, as the reference does without a kernel (fast.go:254-258). */
 int mimgpu_dequant_matmul_a8(mimgpu_ctx *ctx, int block, const float *x, int64_t rows, int64_t k,
                              const mimgpu_tensor *w, const float *bias, float *y);
 
@@ -157,6 +162,11 @@ int mimgpu_dequant_matmul_a8_dev(mimgpu_ctx *ctx, void *stream, const float *x_d
                                  const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
 int mimgpu_dequant_matmul_dev(mimgpu_ctx *ctx, void *stream, const float *x_dev, int64_t rows, int64_t k,
                               const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
+/* mimgpu_dequant_matmul_a8_dev with the block attribute of
+ * mimgpu_dequant_matmul_a8 (32 or 256; mimgpu_dequant_matmul_a8_dev is
+ * block 256). */
+int mimgpu_dequant_matmul_a8_block_dev(mimgpu_ctx *ctx, void *stream, int block, const float *x_dev, int64_t rows,
+                                       int64_t k, const mimgpu_tensor *w, const float *bias_dev, float *y_dev);
 
 /* Same as mimgpu_dequant_matmul_a8_dev for Q4_K / Q6_K weights with K a
  * multiple of 256, but the 8-bit activation scratch lives in a fixed 1 MiB

@@ -125,7 +125,42 @@ struct Carver {
 size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
 
 
-int run_matmul(mimgpu_ctx *c, bool a8, const float *x, int64_t rows, int64_t k, const mimgpu_tensor *w,
+// Which product a call takes: 256 = the block-256 8-bit kernels (v2) for
+// Q4_K/Q6_K, 32 = the block-32 ones (v1) for Q4_K/Q6_K/Q8_0, 0 = the exact
+// f32 product (every other dtype, and dequant_matmul.v1 itself), as the
+// reference falls back without a kernel (q8.go:104-115, fast.go:254-258).
+int matmul_path(int block, int dt, int64_t k) {
+    if (block == 256 && (dt == Q4_K || dt == Q6_K) && k % 256 == 0 && k > 0) return 256;
+    if (block == 32 && a8_b32_dtype_ok(dt, k)) return 32;
+    return 0;
+}
+
+size_t matmul_ws_bytes(int path, int64_t rows, int64_t k) {
+    if (path == 256) return act_q8_bytes((int)rows, k);
+    if (path == 32) return act_q8_b32_bytes((int)rows, k);
+    return 0;
+}
+
+// Queues the product of device buffers on st; the workspace from ws on must
+// already hold matmul_ws_bytes(path, rows, k).
+cudaError_t enqueue_matmul(mimgpu_ctx *c, int path, const float *dx, int64_t rows, int64_t k,
+                           const mimgpu_tensor *w, const float *db, float *dy, cudaStream_t st, void *ws) {
+    const int64_t n = w->shape[0];
+    GemvSeg seg{w->dev, w->dtype, (int)n, dy, n, db};
+    if (path == 256) {
+        ActQ8 act = act_q8_carve(ws, (int)rows, k);
+        cudaError_t e = launch_quantize_a8(dx, (int)rows, k, act, st, false);
+        return e == cudaSuccess ? launch_gemv_a8(&seg, 1, dx, act, (int)rows, k, c->status, st, false) : e;
+    }
+    if (path == 32) {
+        ActQ8 act = act_q8_b32_carve(ws, (int)rows, k);
+        cudaError_t e = launch_quantize_a8_b32(dx, (int)rows, k, act, st);
+        return e == cudaSuccess ? launch_gemv_a8_b32(seg, dx, act, (int)rows, k, st) : e;
+    }
+    return launch_gemv_f32(&seg, 1, dx, (int)rows, k, st, false);
+}
+
+int run_matmul(mimgpu_ctx *c, int block, const float *x, int64_t rows, int64_t k, const mimgpu_tensor *w,
                const float *bias, float *y) {
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     int rc = check_matmul(c, rows, k, w);
@@ -133,27 +168,33 @@ int run_matmul(mimgpu_ctx *c, bool a8, const float *x, int64_t rows, int64_t k, 
     if ((rc = use_device(c))) return rc;
     const int64_t n = w->shape[0];
     if (rows == 0 || n == 0) return MIMGPU_OK;
-    const bool q8 = a8 && (w->dtype == Q4_K || w->dtype == Q6_K) && k % 256 == 0 && k > 0;
-    size_t need = al(rows * k * 4) + al(rows * n * 4) + al(n * 4) + (q8 ? act_q8_bytes((int)rows, k) : 0);
-    if ((rc = ensure_ws(c, need))) return rc;
+    const int path = matmul_path(block, w->dtype, k);
+    const size_t io = al(rows * k * 4) + al(rows * n * 4) + al(n * 4);
+    if ((rc = ensure_ws(c, io + matmul_ws_bytes(path, rows, k)))) return rc;
     Carver cv{(uint8_t *)c->ws};
     float *dx = cv.take<float>(rows * k), *dy = cv.take<float>(rows * n), *db = cv.take<float>(n);
     cudaStream_t st = c->stream;
     cudaError_t e = cudaMemcpyAsync(dx, x, rows * k * 4, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess && bias) e = cudaMemcpyAsync(db, bias, n * 4, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
-    GemvSeg seg{w->dev, w->dtype, (int)n, dy, n, bias ? db : nullptr};
-    if (q8) {
-        ActQ8 act = act_q8_carve(cv.p, (int)rows, k);
-        e = launch_quantize_a8(dx, (int)rows, k, act, st, false);
-        if (e == cudaSuccess) e = launch_gemv_a8(&seg, 1, dx, act, (int)rows, k, c->status, st, false);
-    } else {
-        e = launch_gemv_f32(&seg, 1, dx, (int)rows, k, st, false);
-    }
+    e = enqueue_matmul(c, path, dx, rows, k, w, bias ? db : nullptr, dy, st, cv.p);
     if (e != cudaSuccess) return cuda_fail(c, e, "dequant_matmul kernels");
     e = cudaMemcpyAsync(y, dy, rows * n * 4, cudaMemcpyDeviceToHost, st);
     if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
     return sync_bounded(c, st);
+}
+
+// The device-buffer entry points: one product queued on the caller's stream.
+int run_matmul_dev(mimgpu_ctx *c, void *stream, int block, const float *x, int64_t rows, int64_t k,
+                   const mimgpu_tensor *w, const float *bias, float *y, const char *what) {
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = check_matmul(c, rows, k, w);
+    if (rc || (rc = use_device(c))) return rc;
+    if (rows == 0 || w->shape[0] == 0) return MIMGPU_OK;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    const int path = matmul_path(block, w->dtype, k);
+    if ((rc = ensure_ws(c, matmul_ws_bytes(path, rows, k)))) return rc;
+    return cuda_fail(c, enqueue_matmul(c, path, x, rows, k, w, bias, y, st, c->ws), what);
 }
 
 }  // namespace
@@ -285,7 +326,7 @@ int mimgpu_dequantize(mimgpu_ctx *c, int dtype, const void *src, size_t nbytes, 
 int mimgpu_dequant_matmul(mimgpu_ctx *c, const float *x, int64_t rows, int64_t k, const mimgpu_tensor *w,
                           const float *bias, float *y) {
     if (!c) return MIMGPU_EINVAL;
-    return run_matmul(c, false, x, rows, k, w, bias, y);
+    return run_matmul(c, 0, x, rows, k, w, bias, y);
 }
 
 int mimgpu_dequant_matmul_a8(mimgpu_ctx *c, int block, const float *x, int64_t rows, int64_t k,
@@ -293,42 +334,27 @@ int mimgpu_dequant_matmul_a8(mimgpu_ctx *c, int block, const float *x, int64_t r
     if (!c) return MIMGPU_EINVAL;
     if (block != 32 && block != 256)
         return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8: block must be 32 or 256, got %d", block);
-    // Blocks of 32 and non-K-quant weights take the exact product, as the
-    // reference does without a kernel for them (q8.go:104-115, fast.go:256-258).
-    return run_matmul(c, block == 256, x, rows, k, w, bias, y);
+    return run_matmul(c, block, x, rows, k, w, bias, y);
 }
 
 int mimgpu_dequant_matmul_a8_dev(mimgpu_ctx *c, void *stream, const float *x, int64_t rows, int64_t k,
                                  const mimgpu_tensor *w, const float *bias, float *y) {
     if (!c) return MIMGPU_EINVAL;
-    std::lock_guard<std::recursive_mutex> lk(c->mu);
-    int rc = check_matmul(c, rows, k, w);
-    if (rc || (rc = use_device(c))) return rc;
-    if (rows == 0 || w->shape[0] == 0) return MIMGPU_OK;
-    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    GemvSeg seg{w->dev, w->dtype, (int)w->shape[0], y, w->shape[0], bias};
-    cudaError_t e;
-    if ((w->dtype == Q4_K || w->dtype == Q6_K) && k % 256 == 0) {
-        if ((rc = ensure_ws(c, act_q8_bytes((int)rows, k)))) return rc;
-        ActQ8 act = act_q8_carve(c->ws, (int)rows, k);
-        e = launch_quantize_a8(x, (int)rows, k, act, st, false);
-        if (e == cudaSuccess) e = launch_gemv_a8(&seg, 1, x, act, (int)rows, k, c->status, st, false);
-    } else {
-        e = launch_gemv_f32(&seg, 1, x, (int)rows, k, st, false);
-    }
-    return cuda_fail(c, e, "dequant_matmul_a8_dev");
+    return run_matmul_dev(c, stream, 256, x, rows, k, w, bias, y, "dequant_matmul_a8_dev");
+}
+
+int mimgpu_dequant_matmul_a8_block_dev(mimgpu_ctx *c, void *stream, int block, const float *x, int64_t rows,
+                                       int64_t k, const mimgpu_tensor *w, const float *bias, float *y) {
+    if (!c) return MIMGPU_EINVAL;
+    if (block != 32 && block != 256)
+        return fail(c, MIMGPU_EINVAL, "dequant_matmul_a8_block_dev: block must be 32 or 256, got %d", block);
+    return run_matmul_dev(c, stream, block, x, rows, k, w, bias, y, "dequant_matmul_a8_block_dev");
 }
 
 int mimgpu_dequant_matmul_dev(mimgpu_ctx *c, void *stream, const float *x, int64_t rows, int64_t k,
                               const mimgpu_tensor *w, const float *bias, float *y) {
     if (!c) return MIMGPU_EINVAL;
-    std::lock_guard<std::recursive_mutex> lk(c->mu);
-    int rc = check_matmul(c, rows, k, w);
-    if (rc || (rc = use_device(c))) return rc;
-    if (rows == 0 || w->shape[0] == 0) return MIMGPU_OK;
-    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    GemvSeg seg{w->dev, w->dtype, (int)w->shape[0], y, w->shape[0], bias};
-    return cuda_fail(c, launch_gemv_f32(&seg, 1, x, (int)rows, k, st, false), "dequant_matmul_dev");
+    return run_matmul_dev(c, stream, 0, x, rows, k, w, bias, y, "dequant_matmul_dev");
 }
 
 int mimgpu_rms_norm(mimgpu_ctx *c, const float *x, int64_t rows, int64_t n, const float *scale, double eps,

@@ -106,6 +106,16 @@ bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K);
 cudaError_t gemv_row_prepare();
 cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,
                             cudaStream_t st, bool pdl, const P2P *put);
+// dequant_matmul_a8.v1: 8-bit activations in blocks of 32 (q8.go:50-97) and
+// the AVX2 block-32 row kernels restated bit for bit (k_a8_b32.cu).  The
+// activation layout is ActQ8 with dx and xs per run of 32, ok per 256
+// elements (the last one partial), ys unused.
+size_t act_q8_b32_bytes(int rows, long long K);
+ActQ8 act_q8_b32_carve(void *base, int rows, long long K);
+// Q4_K and Q6_K with K % 256 == 0, Q8_0 with K % 32 == 0 (FusedQ8, q8.go:99-103)
+bool a8_b32_dtype_ok(int dt, long long K);
+cudaError_t launch_quantize_a8_b32(const float *x, int rows, long long K, ActQ8 act, cudaStream_t st);
+cudaError_t launch_gemv_a8_b32(const GemvSeg &sg, const float *x, ActQ8 act, int rows, long long K, cudaStream_t st);
 // dequant_matmul.v1: f32 activations, weights decoded exactly (Q4_K, Q6_K, Q8_0, F16, F32)
 cudaError_t launch_gemv_f32(const GemvSeg *segs, int nseg, const float *x, int rows, long long K,
                             cudaStream_t st, bool pdl);

@@ -2,7 +2,7 @@
 
 This is the host side that tests and bench.py drive.  It mirrors the
 reference's operator interface: `Context.fast_paths` maps the same keys as
-interp/fast.go:42-59 ("dequant_matmul.v1", "dequant_matmul_a8.v2",
+interp/fast.go:42-59 ("dequant_matmul.v1", "dequant_matmul_a8.v1", "dequant_matmul_a8.v2",
 "rms_norm.v1", "rope.v1", "attention.v2", "swiglu.v1", "embedding.v1") to
 callables taking (attrs, inputs) and returning (outputs, handled), raising
 MimGPUError for the fast path's err.
@@ -45,6 +45,7 @@ SIGNATURES = {
     "mimgpu_swiglu": (I32, [P, P, P, I64, P]),
     "mimgpu_embedding": (I32, [P, P, P, I64, P]),
     "mimgpu_dequant_matmul_a8_dev": (I32, [P, P, P, I64, I64, P, P, P]),
+    "mimgpu_dequant_matmul_a8_block_dev": (I32, [P, P, I32, P, I64, I64, P, P, P]),
     "mimgpu_dequant_matmul_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "mimgpu_dequant_matmul_a8_static": (I32, [P, P, P, I64, I64, P, P, P]),
     "mimgpu_q8_new": (I32, [P, I64, I64, C.POINTER(P)]),
@@ -144,6 +145,7 @@ class Context:
         self._tensors = []
         self.fast_paths = {
             "dequant_matmul.v1": self._fp_dequant_matmul,
+            "dequant_matmul_a8.v1": self._fp_dequant_matmul_a8_v1,
             "dequant_matmul_a8.v2": self._fp_dequant_matmul_a8,
             "rms_norm.v1": self._fp_rms_norm,
             "rope.v1": self._fp_rope,
@@ -283,6 +285,13 @@ class Context:
     def _fp_dequant_matmul(self, attrs, ins):
         x, w = ins[0], ins[1]
         return [self.dequant_matmul(x, w, ins[2] if len(ins) > 2 else None)], True
+
+    def _fp_dequant_matmul_a8_v1(self, attrs, ins):
+        # fastDequantMatmulA8 (interp/fast.go:225-230): no attributes, blocks of 32
+        if attrs:
+            return None, False
+        x, w = ins[0], ins[1]
+        return [self.dequant_matmul(x, w, ins[2] if len(ins) > 2 else None, a8_block=32)], True
 
     def _fp_dequant_matmul_a8(self, attrs, ins):
         x, w = ins[0], ins[1]

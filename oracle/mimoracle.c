@@ -458,6 +458,136 @@ int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32
     return 1;
 }
 
+/* The block-32 kernels (dequant_matmul_a8.v1) exist only as AVX2 assembly in
+ * the reference; their float operations are restated here lane by lane.  A
+ * vector register is 8 f32 lanes; each lane's integer value is exact in
+ * int32 (VPMADDUBSW/VPMADDWD cannot saturate for these operand ranges:
+ * |nibble*q| pairs <= 3810, |q6*q| pairs <= 16002, |w8*q| pairs <= 32512 with
+ * q in [-127, 127]), so a lane is the plain integer sum over its 4 elements.
+ *
+ * HSUM1, internal/kernels/kernels_amd64.s:408-413: VEXTRACTF128 + VADDPS give
+ * a_i = v_i + v_{i+4}; two VHADDPS give (a0 + a1) + (a2 + a3). */
+static float hsum1(const float v[8]) {
+    float a0 = v[0] + v[4], a1 = v[1] + v[5], a2 = v[2] + v[6], a3 = v[3] + v[7];
+    return (a0 + a1) + (a2 + a3);
+}
+
+/* dotQ4KQ8AVX2, internal/kernels/kernels_amd64.s:441-562.  Per block: the
+ * offsets lane s (sub-block s) gets fma(f32(dmin*m_s), dbs_s, Y3_s) with
+ * dbs_s = f32(dx_s * xs_s) (q8.go:93-96); chunk c = sub-blocks 2c and 2c+1,
+ * lane j = elements 4j..4j+3 of each: Y0_j = fma(dx_2c, sc_2c * S_lo, Y0_j),
+ * Y1_j = fma(dx_2c+1, sc_2c+1 * S_hi, Y1_j); then Y2 = fma(d, Y0 + Y1, Y2).
+ * The row's value is HSUM1(Y2 - Y3). */
+static int dot_q4k_q8_b32(const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t nb,
+                          float *out) {
+    float y2[8] = {0}, y3[8] = {0};
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = row + 144 * b;
+        const int8_t *y = q + 256 * b;
+        const float *dx = d32 + 8 * b;
+        if (!f16_finite(blk) || !f16_finite(blk + 2)) return 0;
+        float d = mo_f16_to_f32(le16(blk)), dmin = mo_f16_to_f32(le16(blk + 2));
+        int32_t sc[8], m[8];
+        const uint8_t *s = blk + 4;
+        for (int j = 0; j < 4; j++) {
+            sc[j] = s[j] & 63;
+            m[j] = s[j + 4] & 63;
+            sc[4 + j] = (s[j + 8] & 0xF) | ((s[j] >> 6) << 4);
+            m[4 + j] = (s[j + 8] >> 4) | ((s[j + 4] >> 6) << 4);
+        }
+        for (int l = 0; l < 8; l++) {
+            float dm = dmin * (float)m[l];
+            float dbs = dx[l] * (float)xs[8 * b + l];
+            y3[l] = fmaf(dm, dbs, y3[l]);
+        }
+        float y0[8] = {0}, y1[8] = {0};
+        for (int c = 0; c < 4; c++)
+            for (int l = 0; l < 8; l++) {
+                int32_t lo = 0, hi = 0;
+                for (int e = 4 * l; e < 4 * l + 4; e++) {
+                    uint8_t v = blk[16 + 32 * c + e];
+                    lo += (int32_t)(v & 15) * y[64 * c + e];
+                    hi += (int32_t)(v >> 4) * y[64 * c + 32 + e];
+                }
+                y0[l] = fmaf(dx[2 * c], (float)(sc[2 * c] * lo), y0[l]);
+                y1[l] = fmaf(dx[2 * c + 1], (float)(sc[2 * c + 1] * hi), y1[l]);
+            }
+        for (int l = 0; l < 8; l++) y2[l] = fmaf(d, y0[l] + y1[l], y2[l]);
+    }
+    float v[8];
+    for (int l = 0; l < 8; l++) v[l] = y2[l] - y3[l];
+    *out = hsum1(v);
+    return 1;
+}
+
+/* dotQ6KQ8AVX2, internal/kernels/kernels_amd64.s:763-853.  Per half h and
+ * quarter j (32 elements), lane l = elements 4l..4l+3 with the scale
+ * sc[8h + 2j + (l >= 4)] (the q6scales shuffle masks): the lane value is
+ * sc * sum (q6 - 32) * y (VPMADDUBSW, then VPSUBW of the m32 pair sums), and
+ * acc_l = fma(dx_{4h+j}, value, acc_l) with acc = Y0 for even j, Y1 for odd
+ * j; per block Y2 = fma(d, Y0 + Y1, Y2).  The row's value is HSUM1(Y2). */
+static int dot_q6k_q8_b32(const uint8_t *row, const int8_t *q, const float *d32, int64_t nb, float *out) {
+    float y2[8] = {0};
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = row + 210 * b;
+        if (!f16_finite(blk + 208)) return 0;
+        float d = mo_f16_to_f32(le16(blk + 208));
+        float acc[2][8] = {{0}};
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+            const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);
+            const int8_t *yh = q + 256 * b + 128 * h;
+            for (int j = 0; j < 4; j++)
+                for (int l = 0; l < 8; l++) {
+                    int32_t S = 0;
+                    for (int e = 4 * l; e < 4 * l + 4; e++) {
+                        int low = (j & 1) ? ql[e + 32] : ql[e];
+                        low = (j >> 1) ? (low >> 4) : (low & 15);
+                        int32_t qv = low | (((qh[e] >> (2 * j)) & 3) << 4);
+                        S += (qv - 32) * yh[32 * j + e];
+                    }
+                    int32_t scl = sc[2 * j + (l >= 4)];
+                    acc[j & 1][l] = fmaf(d32[8 * b + 4 * h + j], (float)(scl * S), acc[j & 1][l]);
+                }
+        }
+        for (int l = 0; l < 8; l++) y2[l] = fmaf(d, acc[0][l] + acc[1][l], y2[l]);
+    }
+    *out = hsum1(y2);
+    return 1;
+}
+
+/* dotQ8_0Q8AVX2, internal/kernels/kernels_amd64.s:1007-1040.  Per block of
+ * 32: the scale f32(d_w * dx) (VMULSS), lane l = sum of w*y over elements
+ * 4l..4l+3 (VPSIGNB/VPABSB make |w| the unsigned operand; exact for
+ * q in [-127, 127]), Y0_l = fma(scale, lane, Y0_l).  The value is HSUM1(Y0). */
+static int dot_q80_q8_b32(const uint8_t *row, const int8_t *q, const float *d32, int64_t nb, float *out) {
+    float y0[8] = {0};
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = row + 34 * b;
+        if (!f16_finite(blk)) return 0;
+        float scale = mo_f16_to_f32(le16(blk)) * d32[b];
+        const int8_t *w = (const int8_t *)(blk + 2);
+        for (int l = 0; l < 8; l++) {
+            int32_t S = 0;
+            for (int e = 4 * l; e < 4 * l + 4; e++) S += (int32_t)w[e] * q[32 * b + e];
+            y0[l] = fmaf(scale, (float)S, y0[l]);
+        }
+    }
+    *out = hsum1(y0);
+    return 1;
+}
+
+/* RowDot.DotQ8 with blocks of 32, internal/kernels/q8.go:143-151. */
+int mo_dot_q8_b32(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k,
+                  float *out) {
+    switch (dt) {
+    case MO_Q4_K: return dot_q4k_q8_b32(row, q, d32, xs, k / 256, out);
+    case MO_Q6_K: return dot_q6k_q8_b32(row, q, d32, k / 256, out);
+    case MO_Q8_0: return dot_q80_q8_b32(row, q, d32, k / 32, out);
+    }
+    return 0;
+}
+
 float mo_dot_f32(const float *a, const float *b, int64_t n) {
     float s0 = 0, s1 = 0, s2 = 0, s3 = 0;
     int64_t i = 0;
@@ -519,7 +649,8 @@ static void mm_a8_cols(void *p, int64_t lo, int64_t hi) {
         for (int64_t i = 0; i < c->rows; i++) {
             float s = 0;
             if (q8 && c->quantized[i])
-                q8 = mo_dot_q8k_ref(c->dt, row, c->q + i * c->k, c->d32 + i * (c->k / 32), c->xs + i * (c->k / 32), c->k, &s);
+                q8 = (c->block == 32 ? mo_dot_q8_b32 : mo_dot_q8k_ref)(c->dt, row, c->q + i * c->k, c->d32 + i * (c->k / 32),
+                                                                      c->xs + i * (c->k / 32), c->k, &s);
             if (!q8 || !c->quantized[i]) {
                 if (!loaded) { mo_dequantize(c->dt, row, buf, c->k); loaded = 1; }
                 s = mo_dot_f32(c->x + i * c->k, buf, c->k);
@@ -543,11 +674,13 @@ static void q8_rows(void *p, int64_t lo, int64_t hi) {
 int mo_dequant_matmul_a8(const float *x, int64_t rows, int64_t k, int dt, const uint8_t *w, int64_t n,
                          const float *bias, int block, float *y, int nthreads) {
     if (block != 32 && block != 256) return -1;
-    /* FusedQ8Blocks(dt, 256) holds for Q4_K and Q6_K only (q8.go:104-115);
-     * everything else is the exact f32 product. */
-    if (block != 256 || (dt != MO_Q4_K && dt != MO_Q6_K) || k == 0)
-        return mo_dequant_matmul(x, rows, k, dt, w, n, bias, y, nthreads);
-    if (k % 256) return -1;
+    /* FusedQ8Blocks (q8.go:104-115): blocks of 256 for Q4_K and Q6_K, blocks
+     * of 32 for Q4_K, Q6_K and Q8_0 (the AVX2 kernels, the path every amd64
+     * host with AVX2 and F16C takes); everything else is the exact f32
+     * product (fast.go:254-258). */
+    int fused = (dt == MO_Q4_K || dt == MO_Q6_K) || (block == 32 && dt == MO_Q8_0);
+    if (!fused || k == 0) return mo_dequant_matmul(x, rows, k, dt, w, n, bias, y, nthreads);
+    if (k % (dt == MO_Q8_0 ? 32 : 256)) return -1;
     int8_t *q = (int8_t *)malloc((size_t)(rows * k));
     float *d32 = (float *)malloc(sizeof(float) * (size_t)(rows * k / 32));
     int16_t *xs = (int16_t *)malloc(sizeof(int16_t) * (size_t)(rows * k / 32));

@@ -74,6 +74,14 @@ int mo_q8_quantize(const float *x, int64_t k, int block, int8_t *q, float *d32, 
  * *out, or 0 when a block scale of the row is not finite. */
 int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k, float *out);
 
+/* RowDot.DotQ8 with blocks of 32 (q8.go:143-151): the AVX2 kernels
+ * dotQ4KQ8AVX2, dotQ6KQ8AVX2 and dotQ8_0Q8AVX2 (internal/kernels/
+ * kernels_amd64.s:441, 763, 1007) restated lane by lane for a Q4_K, Q6_K or
+ * Q8_0 row against activations quantized with block 32.  Returns 1 and sets
+ * *out, or 0 when a block scale of the row is not finite. */
+int mo_dot_q8_b32(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k,
+                  float *out);
+
 /* dotF32Go, internal/kernels/kernels.go:46-62: four strided accumulators. */
 float mo_dot_f32(const float *a, const float *b, int64_t n);
 
@@ -82,10 +90,11 @@ float mo_dot_f32(const float *a, const float *b, int64_t n);
  * Rows of w are decoded exactly (Dequantize) and dotted with dotF32Go. */
 int mo_dequant_matmul(const float *x, int64_t rows, int64_t k, int dt, const uint8_t *w, int64_t n,
                       const float *bias, float *y, int nthreads);
-/* dequant_matmul_a8.v2, interp/fast.go:238-379 (linearA8): each row of x is
- * quantized once (block 256 for Q4_K/Q6_K); rows or weight rows the 8-bit
- * kernels refuse go through the f32 path.  Other dtypes or block 32 use the
- * f32 path (the reference has no blocks-of-256 kernel for them). */
+/* dequant_matmul_a8.v1 (block 32) and .v2 (block 256), interp/fast.go:
+ * 238-379 (linearA8): each row of x is quantized once; rows or weight rows
+ * the 8-bit kernels refuse go through the f32 path.  Blocks of 256 take
+ * Q4_K/Q6_K (dotQ8KRef), blocks of 32 Q4_K/Q6_K/Q8_0 (mo_dot_q8_b32); other
+ * dtypes use the f32 path, as the reference does without a kernel. */
 int mo_dequant_matmul_a8(const float *x, int64_t rows, int64_t k, int dt, const uint8_t *w, int64_t n,
                          const float *bias, int block, float *y, int nthreads);
 

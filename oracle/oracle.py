@@ -62,6 +62,7 @@ def lib():
             "mo_gen_normal": (None, [C.c_uint64, I64, F, F, P]),
             "mo_q8_quantize": (I32, [P, I64, I32, P, P, P, P]),
             "mo_dot_q8k_ref": (I32, [I32, P, P, P, P, I64, P]),
+            "mo_dot_q8_b32": (I32, [I32, P, P, P, P, I64, P]),
             "mo_dot_f32": (F, [P, P, I64]),
             "mo_dequant_matmul": (I32, [P, I64, I64, I32, P, I64, P, P, I32]),
             "mo_dequant_matmul_a8": (I32, [P, I64, I64, I32, P, I64, P, I32, P, I32]),
@@ -153,6 +154,13 @@ def q8_quantize(x: np.ndarray, block: int = 256):
 def dot_q8k_ref(dt: int, row: np.ndarray, q, d32, xs, k: int):
     out = np.zeros(1, np.float32)
     ok = lib().mo_dot_q8k_ref(dt, _p(np.ascontiguousarray(row, np.uint8)), _p(q), _p(d32), _p(xs), k, _p(out))
+    return bool(ok), out[0]
+
+
+def dot_q8_b32(dt: int, row: np.ndarray, q, d32, xs, k: int):
+    """RowDot.DotQ8 with blocks of 32 (the AVX2 kernels, restated)."""
+    out = np.zeros(1, np.float32)
+    ok = lib().mo_dot_q8_b32(dt, _p(np.ascontiguousarray(row, np.uint8)), _p(q), _p(d32), _p(xs), k, _p(out))
     return bool(ok), out[0]
 
 

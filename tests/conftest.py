@@ -7,6 +7,7 @@ import base64
 import json
 import os
 import sys
+from fractions import Fraction
 
 import numpy as np
 import pytest
@@ -21,6 +22,22 @@ for sub in ("oracle", "mimir-model_b200"):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def round_f32(v: Fraction) -> np.float32:
+    """The f32 nearest the rational v, ties to even."""
+    f = np.float32(float(v))
+    best = f
+    for c in (np.nextafter(f, np.float32(-np.inf)), np.nextafter(f, np.float32(np.inf))):
+        dc, db = abs(Fraction(float(c)) - v), abs(Fraction(float(best)) - v)
+        if dc < db or (dc == db and (int(c.view(np.uint32)) & 1) == 0):
+            best = c
+    return np.float32(best)
+
+
+def fma32(a, b, c) -> np.float32:
+    """f32 fused multiply-add a*b + c, rounded once (exact rationals)."""
+    return round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
 
 
 def f32b64(s: str) -> np.ndarray:

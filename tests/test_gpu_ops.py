@@ -5,6 +5,8 @@ Bars (reference file:line in gsoultan/mimir-model):
   dequantize           bit-exact (quant.go:197-344, testdata/quant_golden.json)
   dequant_matmul_a8.v2 bit-exact with dotQ8KRef (internal/kernels/q8k_test.go:35-117),
                        batch-invariant (interp/transformer_test.go:297-354)
+  dequant_matmul_a8.v1 bit-exact with the AVX2 block-32 kernels (kernels_amd64.s:441,
+                       763, 1007) as the oracle restates them; batch-invariant
   dequant_matmul.v1    spec/stdlib.md section 3.3: |err| <= (K+1) u sum|x w| + |bias|,
                        and max relative error <= 1e-3
   rms_norm, rope, swiglu, embedding   bit-exact with the oracle except where a
@@ -194,11 +196,125 @@ def test_a8_block_attribute(ctx):
     with pytest.raises(mimgpu.MimGPUError) as e:
         ctx.dequant_matmul(x, t, a8_block=64)
     assert e.value.code == mimgpu.EINVAL
-    # block 32 on K-quants is the exact (v1) product
-    y32 = ctx.dequant_matmul(x, t, a8_block=32)
-    yv1 = ctx.dequant_matmul(x, t)
-    assert np.array_equal(bits(y32), bits(yv1))
+    # block 32 on a dtype without a block-32 kernel (F16) is the exact v1
+    # product, as the reference falls back (fast.go:254-258)
+    wf = O.gen_normal(2, 4 * 256).astype(np.float16)
+    tf = ctx.upload(O.F16, (4, 256), wf.view(np.uint8))
+    assert np.array_equal(bits(ctx.dequant_matmul(x, tf, a8_block=32)), bits(ctx.dequant_matmul(x, tf)))
+    # the v1 key takes no attributes (fastDequantMatmulA8, fast.go:225-230)
+    assert ctx.fast_paths["dequant_matmul_a8.v1"]({"block": 256}, [x, t]) == (None, False)
+    out, ok = ctx.fast_paths["dequant_matmul_a8.v1"]({}, [x, t])
+    assert ok and np.array_equal(bits(out[0]), bits(ctx.dequant_matmul(x, t, a8_block=32)))
+    tf.free()
     t.free()
+
+
+# ------------------------------------- 8-bit activations in blocks of 32 (v1)
+
+B32_BB = {O.Q4_K: 144, O.Q6_K: 210, O.Q8_0: 34}
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+@pytest.mark.parametrize("n,k,rows", [(8, 256, 1), (37, 2048, 1), (64, 5632, 3), (300, 4096, 1),
+                                      (129, 4096, 9), (24, 14336, 8), (40, 4096, 17), (1000, 4096, 1)])
+def test_a8_b32_bit_exact(ctx, dt, n, k, rows):
+    """dequant_matmul_a8.v1: bit for bit with the oracle's restatement of the
+    AVX2 block-32 kernels (kernels_amd64.s:441, 763, 1007)."""
+    w = _weights(dt, n, k, 2000 + n)
+    x = O.gen_normal(17 + rows, rows * k).reshape(rows, k)
+    bias = O.gen_normal(5, n)
+    t = ctx.upload(dt, (n, k), w)
+    want = O.dequant_matmul_a8(x, dt, w, n, bias, block=32)
+    got = ctx.dequant_matmul(x, t, bias, a8_block=32)
+    assert np.array_equal(bits(got), bits(want))
+    t.free()
+
+
+@pytest.mark.parametrize("k", [32, 96, 1056])
+def test_a8_b32_q8_0_ragged_k(ctx, k):
+    """Q8_0 rows need only K % 32 == 0: lengths that are not a whole number
+    of 256-element quantizer blocks."""
+    n, rows = 45, 3
+    w = _weights(O.Q8_0, n, k, 7 + k)
+    x = O.gen_normal(k, rows * k).reshape(rows, k)
+    t = ctx.upload(O.Q8_0, (n, k), w)
+    want = O.dequant_matmul_a8(x, O.Q8_0, w, n, block=32)
+    assert np.array_equal(bits(ctx.dequant_matmul(x, t, a8_block=32)), bits(want))
+    t.free()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+def test_a8_b32_edge_cases(ctx, dt):
+    """Tiny and huge activations, a zero block, the largest finite scales,
+    subnormal scales and a weight of -128 (q8_test.go:183-234); refused
+    activation rows (Inf, NaN) and a weight row with a non-finite scale take
+    the f32 product (fast.go:282-379)."""
+    k, n = 2048, 16
+    bb = B32_BB[dt]
+    rb = k // O.BLOCK[dt][0] * bb
+    w = bytearray(_weights(dt, n, k, 78).tobytes())
+    for o in range(rb, 2 * rb, bb):  # row 1: largest finite scales, extreme quants
+        if dt == O.Q4_K:
+            w[o:o + 4] = bytes([0xFF, 0x7B, 0xFF, 0x7B])
+            w[o + 4:o + 144] = b"\xff" * 140
+        elif dt == O.Q6_K:
+            w[o + 208:o + 210] = bytes([0xFF, 0x7B])
+            w[o:o + 192] = b"\xff" * 192
+            w[o + 192:o + 208] = b"\x80" * 16
+        else:
+            w[o:o + 2] = bytes([0xFF, 0x7B])
+            w[o + 2:o + 34] = b"\x80" * 32  # weights of -128
+    sc = {O.Q4_K: 0, O.Q6_K: 208, O.Q8_0: 0}[dt]
+    w[2 * rb + sc:2 * rb + sc + 2] = bytes([0x01, 0x00])       # row 2: subnormal d
+    w[3 * rb + bb + sc:3 * rb + bb + sc + 2] = bytes([0x00, 0x7C])  # row 3: d = inf in block 1
+    w = np.frombuffer(bytes(w), np.uint8)
+    x = O.gen_normal(6, 6 * k).reshape(6, k)
+    x[1] *= np.float32(1e-30)
+    x[2] *= np.float32(1e15)
+    x[3, :256] = 0
+    x[4, 9] = np.inf
+    x[5, 100] = np.nan
+    t = ctx.upload(dt, (n, k), w)
+    want = O.dequant_matmul_a8(x, dt, w, n, block=32)
+    got = ctx.dequant_matmul(x, t, a8_block=32)
+    exact = np.ones_like(want, bool)
+    exact[4:, :] = False  # refused rows: f32 product, tolerance
+    exact[:, 3] = False   # refused weight row
+    assert np.array_equal(bits(got[exact]), bits(want[exact]))
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(np.isinf(got), np.isinf(want))
+    fin = ~exact & np.isfinite(want)
+    wd = O.dequantize(dt, w, n * k).reshape(n, k).astype(np.float64)
+    scale = np.abs(np.nan_to_num(x.astype(np.float64), posinf=0, neginf=0)) @ np.abs(np.nan_to_num(wd)).T
+    assert np.all(np.abs(got[fin] - want[fin]) <= (k + 1) * U * 4 * scale[fin] + 1e-30)
+    t.free()
+
+
+def test_a8_b32_batch_invariance_and_dev_entry(ctx):
+    """Each row's bits alone equal its bits in a batch (transformer_test.go:
+    297-354), and the device-buffer entry point gives the host call's bits."""
+    import ctypes as C
+    import torch
+    import mimgpu
+    k, n, rows = 1024, 40, 13
+    for dt in (O.Q4_K, O.Q6_K, O.Q8_0):
+        w = _weights(dt, n, k, 6)
+        x = O.gen_normal(10, rows * k).reshape(rows, k)
+        x[4, 3] = np.inf
+        t = ctx.upload(dt, (n, k), w)
+        together = ctx.dequant_matmul(x, t, a8_block=32)
+        for i in range(rows):
+            alone = ctx.dequant_matmul(x[i:i + 1], t, a8_block=32)
+            assert np.array_equal(bits(alone[0]), bits(together[i]))
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty((rows, n), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        ctx._check(mimgpu.lib().mimgpu_dequant_matmul_a8_block_dev(
+            ctx.h, stream, 32, C.c_void_p(xd.data_ptr()), rows, k, t.h, None, C.c_void_p(yd.data_ptr())))
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(yd.cpu().numpy()), bits(together))
+        t.free()
 
 
 # ------------------------------------------------------- f32 activations

@@ -10,13 +10,12 @@ Sources of the cases (paths in gsoultan/mimir-model):
   cmd/mim-run/main_test.go:179-267     tiny Llama logits and greedy ids
 """
 import base64
-from fractions import Fraction
 
 import numpy as np
 import pytest
 
 import oracle as O
-from conftest import f32b64
+from conftest import f32b64, fma32 as _fma32
 
 F16 = lambda f: int(O.lib().mo_f32_to_f16(f))  # noqa: E731
 
@@ -142,20 +141,6 @@ def test_q8_rounding_near_half():
 
 
 # ----------------------------------------------------------- dotQ8KRef
-
-def _round_f32(v: Fraction) -> np.float32:
-    f = np.float32(float(v))
-    best = f
-    for c in (np.nextafter(f, np.float32(-np.inf)), np.nextafter(f, np.float32(np.inf))):
-        dc, db = abs(Fraction(float(c)) - v), abs(Fraction(float(best)) - v)
-        if dc < db or (dc == db and (int(c.view(np.uint32)) & 1) == 0):
-            best = c
-    return np.float32(best)
-
-
-def _fma32(a, b, c):
-    return _round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
-
 
 def dot_q8k_py(dt, row, q, d32, xs, k):
     """internal/kernels/q8k_test.go:35-117 restated in Python with exact
