@@ -391,8 +391,8 @@ def run_gpu(args):
         kernel = (f"gemv_row_kernel (one-row dequant_matmul_a8.v2 over the decode step's launch list: per layer "
                   f"q|k|v fused, o, gate|up fused, down; {cfg['layers']} layers + head)")
         traffic = GEMV_TRAFFIC_PER_ALGO_BYTE * bpl
-        # embedding, 9 per layer, final norm, head, argmax, advance
-        launches = args.steps * (1 + 9 * cfg["layers"] + 4)
+        # the kernels of the captured one-token step, counted from its CUDA graph
+        launches = args.steps * sess.step_kernels
     achieved = bpl / spl / 1e9
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -407,7 +407,9 @@ def run_gpu(args):
                    "context_cache": context, "positions_timed": [prompt + args.warmup, pos - 1 - args.e2e_steps - 2],
                    "matmul": "dequant_matmul_a8.v2 block 256 (bit-exact dotQ8KRef)", "kv_cache": "f16",
                    "decode_path": ("one persistent step kernel per token" if step_path
-                                   else "one kernel per op (~9 per layer)"),
+                                   else f"CUDA graph of {sess.step_kernels} kernels per token (per layer: q|k|v "
+                                        "GEMV with rms_norm, attention with RoPE and cache write, o GEMV, gate|up "
+                                        "GEMV with rms_norm, SwiGLU, down GEMV; programmatic dependent launch)"),
                    "parallelism": (f"tp{world} (q|k|v by kv-head group, o / gate|up / down / head by output rows, "
                                    f"each rank holding its shard; attention, residual and SwiGLU exchanged by "
                                    f"{'peer-memory stores' if args.p2p else 'NCCL all-gathers'})") if use_tp

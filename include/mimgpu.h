@@ -290,6 +290,19 @@ void *mimgpu_session_stream(mimgpu_session *s);
 int mimgpu_session_set_step_kernel(mimgpu_session *s, int on);
 /* 1 when one-token steps run as one persistent kernel, else 0. */
 int mimgpu_session_uses_step_kernel(mimgpu_session *s);
+
+/* L2 prefetch between the one-token GEMVs of a decode step: once a GEMV has
+ * issued its own weight copies, each SM prefetches into L2 the first
+ * `bytes_per_sm` of its slab of the next GEMV's matrices (a multiple of 16,
+ * at most 16 MiB; 0 turns it off; default 160 KiB), so that the next GEMV
+ * starts from L2 while HBM would otherwise idle through the launch boundary
+ * and the small kernels between.  Results are unchanged. */
+int mimgpu_session_set_l2_prefetch(mimgpu_session *s, int64_t bytes_per_sm);
+
+/* Kernel launches in one replay of the session's captured one-token greedy
+ * step (mimgpu_session_generate), counted from the CUDA graph; 0 before the
+ * first capture. */
+int mimgpu_session_step_kernels(mimgpu_session *s);
 /* Profiling: with a device buffer of mimgpu_session_trace_bytes(s) bytes
  * bound, every persistent-kernel step writes its phase timeline there (per
  * CTA, %globaltimer nanoseconds: start, end, and per op the moments its

@@ -129,6 +129,26 @@ __device__ __forceinline__ float decode_elem(int dt, const uint8_t *src, long lo
     return ((const float *)src)[i];
 }
 
+// RoundToEven(127 v / amax) for |v| <= amax, 0 < amax < inf, as quantQ8
+// (internal/kernels/q8.go:75-86, 251-260 of gsoultan/mimir-model) rounds it:
+// the float64 quotient to nearest even, which is the EXACT quotient rounded
+// to nearest even (127 v is exact in float64; the float64 quotient is within
+// 2^-46 of the exact one, which is a half-integer or at least 2^-34 away from
+// one).  Here without a division per element: the estimate t / amax as
+// t * inv_a (inv_a = 1.0 / amax, once per block) is at most one off, and only
+// next to a half-integer; the remainder t - q amax is exact (both terms have
+// at most 31 significant bits, or q = 0) and moves q to the nearest integer,
+// ties to the even one.
+__device__ __forceinline__ int q8_round(float v, double a, double inv_a) {
+    const double t = 127.0 * (double)v;
+    double q = rint(__dmul_rn(t, inv_a));
+    double r = __fma_rn(-q, a, t);
+    const double h = 2.0 * fabs(r);
+    if (h > a) q += r > 0.0 ? 1.0 : -1.0;  // then |t - q amax| < amax / 2
+    else if (h == a && ((int)q & 1)) q += r > 0.0 ? 1.0 : -1.0;
+    return (int)q;
+}
+
 // ------------------------------------------------------------- argmax
 // argmax (cmd/mim-run/main.go:184-193): best = 0; x > v[best] moves best.
 // The result is the first index of the largest non-NaN value (NaNs never
@@ -246,6 +266,27 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 __device__ __forceinline__ void prefetch_l2_hint(const void *src, uint32_t bytes, uint64_t pol) {
     asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol)
                  : "memory");
+}
+
+// Loads of small read-only data every step reuses (norm weights, the RoPE
+// table) with the L2 evict_last policy, so the weight stream (evict_first)
+// does not push them out between steps.
+__device__ __forceinline__ float ldg_keep(const float *p, uint64_t pol) {
+    float v;
+    asm volatile("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ float2 ldg_keep2(const float2 *p, uint64_t pol) {
+    float2 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v2.f32 {%0,%1}, [%2], %3;" : "=f"(v.x), "=f"(v.y) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ float4 ldg_keep4(const float4 *p, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
 }
 
 // Streaming 128-bit global load that does not allocate in L1.

@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *__restr
     const long long row = blockIdx.x;
     const int b = blockIdx.y, i = b * 256 + threadIdx.x;
     // the norm weight is read-only: fetched before the wait for the previous kernel
-    const float sc = (scale && i < n) ? scale[i] : 1.f;
+    const float sc = (scale && i < n) ? ldg_keep(scale + i, l2_policy_evict_last()) : 1.f;
     pdl_wait();
     if (wait.N > 1) {  // every rank's columns of the residual have arrived
         p2p_publish_wait(wait);

@@ -178,8 +178,11 @@ __global__ void dequantize_kernel(int dt, const uint8_t *__restrict__ src, float
 // embedding.v1: one row of the table per id; out-of-range ids give zeros.
 __global__ void embedding_kernel(int dt, const uint8_t *__restrict__ table, long long V, int E,
                                  const int32_t *__restrict__ ids, float *__restrict__ y, unsigned *epoch) {
-    pdl_launch_dependents();
+    // The first kernel of a forward: its dependents launch only once the
+    // previous forward has completed, so they may read what it wrote (the
+    // position, the cache rows) before their own grid dependency wait.
     pdl_wait();
+    pdl_launch_dependents();
     if (epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *epoch += 1;  // a new forward
     const long long id = ids[blockIdx.x];
     const long long rb = row_bytes(dt, E);

@@ -707,7 +707,7 @@ cudaError_t gemv_a8_prepare() {
 }
 
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put) {
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put, const GemvPrefetch *pf, const GemvNorm *nrm) {
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
     if (put && put->N > 1 && (rows != 1 || nseg != 1)) return cudaErrorInvalidValue;  // exchanges carry one row
     if (rows == 0 || K == 0) return cudaSuccess;
@@ -715,7 +715,9 @@ cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 
     if ((!put || put->N <= 1) && gemm_a8_tc_ok(segs, nseg, act, rows, K))
         return launch_gemm_a8_tc(segs, nseg, x, act, rows, K, status, st, pdl);
     // one activation row: the slab-streaming kernel (same results bit for bit)
-    if (rows == 1 && gemv_row_ok(segs, nseg, act, K)) return launch_gemv_row(segs, nseg, x, act, K, status, st, pdl, put);
+    if (rows == 1 && gemv_row_ok(segs, nseg, act, K))
+        return launch_gemv_row(segs, nseg, x, act, K, status, st, pdl, put, pf, nrm);
+    if (nrm) return cudaErrorInvalidValue;  // the fused norm exists in the one-row kernel only
     A8Params p = {};
     p.nseg = nseg;
     int maxbb = 0, g = 0;

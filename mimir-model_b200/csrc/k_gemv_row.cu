@@ -40,6 +40,7 @@
 #include "a8_refused.cuh"
 #include "gemv_row.cuh"
 #include "p2p.cuh"
+#include "rms.cuh"
 
 namespace mimgpu {
 
@@ -68,7 +69,121 @@ struct RowParams {
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
     P2P put;
     unsigned *status;
+    GemvPrefetch pf;    // the next launch's weights into L2 (pf.nseg 0: none)
+    GemvNorm nrm;       // nrm.x set: the activation row is rms_norm(nrm.x), made here
 };
+
+// rms_norm.v1 of the residual row and its 8-bit blocks, made by the 16
+// consumer warps of every CTA in place of a separate kernel (fastRMSNorm,
+// interp/fast.go:434-485, then QuantizeBlocks, q8.go:50-97): the float64
+// sum of squares as a tree with the in-order fallback of rms.cuh, then per
+// 256-element block (warp w takes blocks w, w + 16, ...; lane l elements
+// 8l..8l+7) the normalised values, their amax and refusal, the quants in
+// the act_off layout and the per-half headers.  CTA 0 writes the normalised
+// row to nrm.h; refused rows recompute its elements from the residual,
+// 1/rms (misc[2]) and the norm weights.  Same bits as rmsnorm_quant_kernel.
+constexpr int kNormRounds = 2;  // blocks per consumer warp: K <= 2 * 16 * 256
+__device__ __forceinline__ void stage_norm(const RowParams &p, uint8_t *smem, int *misc, double *red,
+                                           const float (&nsc)[kNormRounds][8]) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, K = (int)p.K;
+    const float *x = p.nrm.x;
+    // the row once, in the quantization's layout: warp w holds blocks w, w + 16, ...
+    float xv[kNormRounds][8];
+    double ss = 0.0;
+#pragma unroll
+    for (int u = 0; u < kNormRounds; u++) {
+        const int kb = w + u * kCW;
+        if (kb < p.nb) {
+            const int e0 = kb * 256 + lane * 8;
+            const float4 xa = __ldcg((const float4 *)(x + e0)), xb = __ldcg((const float4 *)(x + e0 + 4));
+            xv[u][0] = xa.x; xv[u][1] = xa.y; xv[u][2] = xa.z; xv[u][3] = xa.w;
+            xv[u][4] = xb.x; xv[u][5] = xb.y; xv[u][6] = xb.z; xv[u][7] = xb.w;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const double e = (double)xv[u][j];
+                ss = __fma_rn(e, e, ss);  // e*e is exact in float64
+            }
+        }
+    }
+    ss = warp_sum_d(ss);
+    if (lane == 0) red[w] = ss;
+    asm volatile("bar.sync 2, %0;" ::"r"(kCT) : "memory");
+    // the kCW partials by a butterfly over the whole warp: every level adds
+    // the same two values in both lanes of a pair, so all threads get the
+    // same bits
+    double tot = lane < kCW ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(FULL, tot, o);
+    float ms;
+    // a term passes through at most 8 kNormRounds products-and-sums in its
+    // thread, 5 shuffle levels and kCW partials: a depth bound of K/kCT + 32
+    if (!rms_mean_certain(tot, K, K / kCT + 32, ms)) {  // the same decision in every thread
+        if (threadIdx.x == 0) misc[1] = __float_as_int((float)__ddiv_rn(rms_seq_sum_cg(x, K), (double)K));
+        asm volatile("bar.sync 2, %0;" ::"r"(kCT) : "memory");
+        ms = __int_as_float(misc[1]);
+    }
+    const float inv = rms_inv_of_mean(ms, p.nrm.eps);
+    if (threadIdx.x == 0) misc[2] = __float_as_int(inv);  // for the f32 product of refused rows
+#pragma unroll
+    for (int u = 0; u < kNormRounds; u++) {
+        const int kb = w + u * kCW;
+        if (kb >= p.nb) break;
+        const int e0 = kb * 256 + lane * 8;
+        float v[8];
+        float am = 0.f;
+        int bad = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            v[j] = __fmul_rn(xv[u][j], inv);
+            if (p.nrm.scale) v[j] = __fmul_rn(v[j], nsc[u][j]);
+            const float a = fabsf(v[j]);
+            const bool b = !(a <= 0x1p60f);
+            bad |= b;
+            am = fmaxf(am, b ? 0.f : a);
+        }
+        if (blockIdx.x == 0) {  // one writer: the same 16 KB stored by every CTA backs up the store queue
+            *(float4 *)(p.nrm.h + e0) = make_float4(v[0], v[1], v[2], v[3]);
+            *(float4 *)(p.nrm.h + e0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        am = warp_max(am);
+        bad = __any_sync(FULL, bad);
+        const bool quant = am != 0.f && !bad;
+        const double ad = (double)am, inv_a = quant ? __ddiv_rn(1.0, ad) : 0.0;
+        uint32_t qw[2] = {0u, 0u};
+        int s8 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int q = quant ? q8_round(v[j], ad, inv_a) : 0;
+            s8 += q;
+            qw[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+        }
+        // lane pairs hold runs of 16, quads runs of 32
+        const int s16 = s8 + __shfl_xor_sync(FULL, s8, 1);
+        const int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);
+        const int c = lane >> 1, hh = c >> 3, a = c & 7;  // chunk of 16 quants, half, chunk in the half
+        *(uint2 *)(smem + p.off_act + act_off(kb, hh) + 16 * a + 8 * (lane & 1)) = make_uint2(qw[0], qw[1]);
+        // half hh's header (runs of 32: lanes 16hh + 4r) and sums of 16 (lanes 16hh + 2r)
+        const int base = lane & 16;
+        uint32_t xs2[2], ys4[4];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int lo = __shfl_sync(FULL, s32, base + 8 * r), hi = __shfl_sync(FULL, s32, base + 8 * r + 4);
+            xs2[r] = ((uint32_t)lo & 0xFFFFu) | ((uint32_t)hi << 16);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int lo = __shfl_sync(FULL, s16, base + 4 * r), hi = __shfl_sync(FULL, s16, base + 4 * r + 2);
+            ys4[r] = ((uint32_t)lo & 0xFFFFu) | ((uint32_t)hi << 16);
+        }
+        if ((lane & 15) == 0) {
+            const int hb = 2 * kb + hh;
+            *(uint4 *)(smem + p.off_hdr + hdr_off(hb)) =
+                make_uint4(xs2[0], xs2[1], __float_as_uint(__fdiv_rn(am, 127.f)), bad ? 0u : 1u);
+            *(uint4 *)(smem + p.off_ys + hdr_off(hb)) = make_uint4(ys4[0], ys4[1], ys4[2], ys4[3]);
+        }
+        if (bad && lane == 0) misc[0] = 0;
+    }
+}
 
 __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_constant__ RowParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -100,6 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         uint8_t *ring = smem + p.off_ring;
         int n = 0, slot = 0, ph = 0;
         bool ok = true;
+        // every weight byte is read once per step: first out of L2, so the
+        // activations, caches and norm weights stay
+        const uint64_t pol = l2_policy_evict_first();
         for (int s = 0; s < p.nseg && ok; s++) {
             int r0, nr;
             slab(p.seg[s].n, cta, G, p.unit, r0, nr);
@@ -114,10 +232,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                 }
                 const uint32_t bytes = (uint32_t)(min(sb, nblk - k0) * bb);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                bulk_g2s(ring + (size_t)slot * p.slot_bytes, src + (long long)k0 * bb, bytes, &full[slot]);
+                bulk_g2s_hint(ring + (size_t)slot * p.slot_bytes, src + (long long)k0 * bb, bytes, &full[slot], pol);
                 if (++slot == p.slots) {
                     slot = 0;
                     ph ^= 1;
+                }
+            }
+        }
+        // the next launch's first bytes of this CTA's slabs into L2, while
+        // this launch's last stages are in flight
+        if (ok && p.pf.nseg > 0) {
+            uint32_t left = p.pf.bytes;
+            for (int s = 0; s < p.pf.nseg && left; s++) {
+                int r0, nr;
+                slab(p.pf.n[s], cta, G, p.pf.unit, r0, nr);
+                const long long rbn = row_bytes(p.pf.dt[s], p.pf.K);
+                const uint8_t *src = p.pf.w[s] + (long long)r0 * rbn;
+                long long avail = (long long)nr * rbn;  // a multiple of 16: slabs come in whole units
+                while (left && avail > 0) {
+                    const uint32_t take = (uint32_t)min((long long)min(left, 32768u), avail);
+                    prefetch_l2(src, take);
+                    src += take;
+                    avail -= take;
+                    left -= take;
                 }
             }
         }
@@ -129,8 +266,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
 
     // ------------------------------------------- consumers and the chain warps
     const int tid = threadIdx.x;
+    // the norm weights are read-only: in registers before the wait
+    float nsc[kNormRounds][8];
+    if (warp < kCW && p.nrm.x) {
+        const uint64_t keep = l2_policy_evict_last();
+#pragma unroll
+        for (int u = 0; u < kNormRounds; u++) {
+            const int kb = warp + u * kCW, e0 = kb * 256 + lane * 8;
+            float4 sa = make_float4(1.f, 1.f, 1.f, 1.f), sb4 = sa;
+            if (kb < p.nb && p.nrm.scale) {
+                sa = ldg_keep4((const float4 *)(p.nrm.scale + e0), keep);
+                sb4 = ldg_keep4((const float4 *)(p.nrm.scale + e0 + 4), keep);
+            }
+            nsc[u][0] = sa.x; nsc[u][1] = sa.y; nsc[u][2] = sa.z; nsc[u][3] = sa.w;
+            nsc[u][4] = sb4.x; nsc[u][5] = sb4.y; nsc[u][6] = sb4.z; nsc[u][7] = sb4.w;
+        }
+    }
     pdl_wait();
-    if (warp < kCW) {
+    if (warp < kCW && p.nrm.x) {
+        stage_norm(p, smem, misc, (double *)(smem + 4 * kMaxSlots * 8 + 16), nsc);
+        for (int i = tid; i < RS * rps; i += kCT) smem[p.off_bad + i] = 0;
+    } else if (warp < kCW) {
         // the activation row into shared memory (act_off layout), the
         // per-half headers (xs of the 4 runs of 32, dx, ok), the sums of 16
         // Every load of a thread is issued before its first store, so the
@@ -237,7 +393,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                         const int i = __ffs(rm) - 1;
                         rm &= rm - 1;
                         const int frow = r0 + t0 + i;
-                        float r = row_dot_f32(dt, sg.w + (long long)frow * rb, p.x, nb);
+                        float r;
+                        if (p.nrm.x) {  // the activation row exists only in this kernel: remake its elements
+                            const float ninv = __int_as_float(misc[2]);
+                            const float *nx = p.nrm.x, *ns = p.nrm.scale;
+                            r = row_dot_f32_fn(dt, sg.w + (long long)frow * rb, nb, [&](long long e) {
+                                const float v = __fmul_rn(__ldcg(nx + e), ninv);
+                                return ns ? __fmul_rn(v, __ldg(ns + e)) : v;
+                            });
+                        } else {
+                            r = row_dot_f32(dt, sg.w + (long long)frow * rb, p.x, nb);
+                        }
                         if (sg.bias) r = __fadd_rn(r, sg.bias[frow]);
                         if (sg.res) r = __fadd_rn(sg.res[frow], r);
                         if (lane == 0) {
@@ -416,8 +582,27 @@ bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
 
 cudaError_t gemv_row_prepare() { return prepare_row(); }
 
+bool gemv_prefetch_plan(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf) {
+    RowPlan pl;
+    pf = GemvPrefetch{};
+    if (nseg <= 0 || nseg > kMaxSegs || bytes % 16 || !plan_row(segs, nseg, K, pl)) return false;
+    for (int i = 0; i < nseg; i++) {
+        if ((segs[i].dt != Q4_K && segs[i].dt != Q6_K) || ((uintptr_t)segs[i].w & 15) || segs[i].n % pl.unit ||
+            (unsigned long long)segs[i].n * (unsigned long long)num_sms() >= (1ULL << 32))
+            return false;
+        pf.w[i] = segs[i].w;
+        pf.n[i] = segs[i].n;
+        pf.dt[i] = segs[i].dt;
+    }
+    pf.nseg = nseg;
+    pf.unit = pl.unit;
+    pf.K = K;
+    pf.bytes = bytes;
+    return true;
+}
+
 cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,
-                            cudaStream_t st, bool pdl, const P2P *put) {
+                            cudaStream_t st, bool pdl, const P2P *put, const GemvPrefetch *pf, const GemvNorm *nrm) {
     RowPlan pl;
     if (!plan_row(segs, nseg, K, pl)) return cudaErrorInvalidValue;
     cudaError_t e = prepare_row();
@@ -441,6 +626,15 @@ cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8
     p.off_bad = pl.off_bad;
     p.off_ring = pl.off_ring;
     if (put) p.put = *put;
+    if (pf) p.pf = *pf;
+    if (nrm) {
+        // 16-byte aligned rows; the in-order fallback and the staging read K floats
+        if (!nrm->x || !nrm->h || ((uintptr_t)nrm->x & 15) || ((uintptr_t)nrm->h & 15) ||
+            ((uintptr_t)nrm->scale & 15) || nrm->h != x)
+            return cudaErrorInvalidValue;
+        if (p.nb > kNormRounds * kCW) return cudaErrorInvalidValue;
+        p.nrm = *nrm;
+    }
     p.status = status;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];

@@ -87,9 +87,36 @@ cudaError_t gemv_a8_prepare();
 // encode it on the stack every launch, allocating nothing).
 // put: the (one-segment, one-row) outputs also go to every rank's copy of
 // the exchanged buffer, then the launch publishes (producer side)
+// The next one-row GEMV of a decode step, whose weights a launch prefetches
+// into L2 once its own copies are all issued: each CTA takes the first
+// `bytes` of its slabs of those matrices, the bytes the next launch's CTA of
+// the same index streams first, so the next launch starts from L2 while HBM
+// is otherwise idle (its predecessor's tail, the small kernels between).
+struct GemvPrefetch {
+    const uint8_t *w[kMaxSegs];
+    int n[kMaxSegs], dt[kMaxSegs];
+    int nseg, unit;
+    long long K;
+    uint32_t bytes;  // per CTA, a multiple of 16
+};
+// Fills pf for a launch of segs over K; false when that launch would not be
+// a one-row (slab) GEMV.
+bool gemv_prefetch_plan(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf);
+// rms_norm of the row nrm.x fused into a one-row GEMV: every CTA makes its
+// own 8-bit activations instead of reading act (CTA 0 also writes the
+// normalised row to nrm.h, which must be the launch's x); same bits as
+// launch_rmsnorm_quant followed by the GEMV.  Only where gemv_row_ok holds
+// and K <= 8192.
+struct GemvNorm {
+    const float *x;      // [K] the residual row
+    const float *scale;  // [K] or null
+    float eps;
+    float *h;            // [K] the normalised row
+};
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
                            unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true,
-                           const P2P *put = nullptr);
+                           const P2P *put = nullptr, const GemvPrefetch *pf = nullptr,
+                           const GemvNorm *nrm = nullptr);
 // The same product on the tensor cores (tcgen05 kind::i8) for launches of
 // at least kTcMinRows activation rows; launch_gemv_a8 dispatches to it.
 constexpr int kTcMinRows = 16;
@@ -105,7 +132,8 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
 bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K);
 cudaError_t gemv_row_prepare();
 cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, long long K, unsigned *status,
-                            cudaStream_t st, bool pdl, const P2P *put);
+                            cudaStream_t st, bool pdl, const P2P *put, const GemvPrefetch *pf = nullptr,
+                            const GemvNorm *nrm = nullptr);
 // dequant_matmul_a8.v1: 8-bit activations in blocks of 32 (q8.go:50-97) and
 // the AVX2 block-32 row kernels restated bit for bit (k_a8_b32.cu).  The
 // activation layout is ActQ8 with dx and xs per run of 32, ok per 256

@@ -79,6 +79,16 @@ struct mimgpu_session {
     int g_batch_rows = 0;
     // the one-kernel decode step (k_step.cu), when the model qualifies
     bool step_ok = false, use_step = false;
+    // one-row decode GEMVs prefetch the next GEMV's first bytes of each SM's
+    // slab into L2 (mimgpu_session_set_l2_prefetch; 0 = off)
+    uint32_t prefetch_bytes = 160 * 1024;
+    // one-token steps on one GPU: each rms_norm runs inside the GEMV that
+    // reads it (GemvNorm) instead of as a kernel of its own
+    bool fuse_norm = true;
+    int step_kernels = 0;  // kernel launches in one replay of the greedy one-token graph
+    // per layer: the key cache's tensor map for the decode attention
+    std::vector<CUtensorMap> kmap;
+    bool kmap_ok = false;
     StepLayer *step_layers = nullptr;    // device [layers]
     float2 *rope_cs = nullptr;           // device [context][rope_dims / 2]
     unsigned *step_sync = nullptr;       // grid counters, then [2] steps completed / CTA exits
@@ -212,50 +222,124 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if (r == cudaSuccess) r = gather(s->xl, El, s->x);
         return r;
     };
+    // The GEMV launches of a forward in order -- per layer q|k|v, o, gate|up,
+    // down, then the head -- as segments (weights and rows only), and the
+    // L2 prefetch each one-token launch issues for the launch after it (the
+    // head's is the next step's first q|k|v).
+    const mimgpu_tensor *headt = m->out ? m->out : m->embd;
+    auto segs_of = [&](int l, int which, GemvSeg *g) -> int {
+        if (which == 4) {
+            if (vn <= 0) return 0;
+            g[0] = slice(headt, E, c.vocab, v0, vn, nullptr, 0, nullptr);
+            return 1;
+        }
+        const LayerW &w = m->L[l];
+        switch (which) {
+        case 0:
+            g[0] = slice(w.q, E, E, (long long)k * El, El, nullptr, 0, nullptr);
+            g[1] = slice(w.k, E, KV, (long long)k * KVl, KVl, nullptr, 0, nullptr);
+            g[2] = slice(w.v, E, KV, (long long)k * KVl, KVl, nullptr, 0, nullptr);
+            return 3;
+        case 1: g[0] = slice(w.o, E, E, (long long)k * El, El, nullptr, 0, nullptr); return 1;
+        case 2:
+            g[0] = slice(w.gate, E, F, (long long)k * Fl, Fl, nullptr, 0, nullptr);
+            g[1] = slice(w.up, E, F, (long long)k * Fl, Fl, nullptr, 0, nullptr);
+            return 2;
+        default: g[0] = slice(w.down, F, E, (long long)k * El, El, nullptr, 0, nullptr); return 1;
+        }
+    };
+    GemvPrefetch pfbuf;
+    auto next_pf = [&](int l, int which) -> const GemvPrefetch * {
+        if (T != 1 || !a8 || s->prefetch_bytes == 0) return nullptr;
+        int nl = l, nw = which + 1;
+        if (which == 3) {
+            nl = l + 1;
+            nw = nl < c.layers ? 0 : 4;
+        } else if (which == 4) {
+            nl = 0;
+            nw = 0;
+        }
+        GemvSeg g[kMaxSegs];
+        const int ns = segs_of(nl, nw, g);
+        if (ns == 0 || !gemv_prefetch_plan(g, ns, nw == 3 ? F : E, s->prefetch_bytes, pfbuf)) return nullptr;
+        return &pfbuf;
+    };
+    auto fuse_norm = [&](const GemvSeg *g, int n) {
+        return s->fuse_norm && T == 1 && N == 1 && a8 && E <= 8192 && gemv_row_ok(g, n, s->actE, E);
+    };
     CK(launch_embedding(m->embd->dtype, m->embd->dev, c.vocab, E, s->tok, T, s->x, st, pdl, s->epoch));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &w = m->L[l];
         // exchange slots of the layer: 4l attention output, 4l+1 residual after o,
         // 4l+2 SwiGLU output, 4l+3 residual after down
         const P2P xin = xch(4 * (l - 1) + 3, nullptr, 0);
-        CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
-                                a8 ? s->actE : none, st, pdl, (p2p && l > 0) ? &xin : nullptr));
         GemvSeg qkv[3] = {slice(w.q, E, E, (long long)k * El, El, s->qkv, ldq, nullptr),
                           slice(w.k, E, KV, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr),
                           slice(w.v, E, KV, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr)};
-        if (a8) CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl));
+        const GemvNorm n_attn{s->x, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h};
+        const bool f_attn = fuse_norm(qkv, 3);
+        if (!f_attn)
+            CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h,
+                                    a8 ? s->actE : none, st, pdl, (p2p && l > 0) ? &xin : nullptr));
+        if (a8)
+            CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl, true, nullptr, next_pf(l, 0),
+                              f_attn ? &n_attn : nullptr));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
-        RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
-                           c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l],
-                           s->batched ? s->slot : nullptr, s->slot0};
-        CK(launch_rope_scatter(ra, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, Hl, Hkvl, D, c.context, c.cache_f16,
                      (float)(1.0 / std::sqrt((double)D)), N > 1 ? s->attl : s->att, none, status, s->scores,
                      s->batched ? s->slot : nullptr, s->slot0};
+        // decode rows (one token per sequence): RoPE, the cache write and the
+        // attention in one kernel; prompt passes: RoPE + scatter, then attention
+        const bool fused = s->rope_cs && s->kmap_ok && attn_decode_ok(aa);
+        auto attend = [&](const AttnArgs2 &x) -> cudaError_t {
+            if (!fused) return launch_attn_exact(x, st, pdl);
+            AttnDecodeArgs da{};
+            da.kmap = s->kmap[l];
+            da.at = x;
+            da.qkv = s->qkv;
+            da.ldq = ldq;
+            da.rope_cs = s->rope_cs;
+            da.rotary = c.rope_dims;
+            da.interleaved = c.interleaved;
+            return launch_attn_decode(da, st, pdl);
+        };
+        if (!fused) {
+            RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
+                               c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l],
+                               s->batched ? s->slot : nullptr, s->slot0};
+            CK(launch_rope_scatter(ra, st, pdl));
+        }
         const P2P attx = xch(4 * l, s->att, (long long)k * El);
         if (N > 1) {
             if (p2p) aa.put = attx;  // the heads of this rank into every rank's attention output
-            CK(launch_attn_exact(aa, st, pdl));
+            CK(attend(aa));
             if (!p2p) CK(gather(s->attl, El, s->att));
             if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl, p2p ? &attx : nullptr));
-        } else if (attn_prefill_ok(aa)) {
+        } else if (!fused && attn_prefill_ok(aa)) {
             // a prompt pass: the many-row kernel, then the 8-bit blocks of its output
             CK(launch_attn_exact(aa, st, pdl));
             if (a8) CK(launch_quantize_a8(s->att, T, E, s->actE, st, pdl));
         } else {
             if (a8) aa.act = s->actE;  // quantized inside the one-row kernel
-            CK(launch_attn_exact(aa, st, pdl));
+            CK(attend(aa));
         }
         GemvSeg o = slice(w.o, E, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
         const P2P oput = xch(4 * l + 1, s->x, (long long)k * El);
-        if (a8) CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl, true, p2p ? &oput : nullptr));
+        if (a8)
+            CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl, true, p2p ? &oput : nullptr,
+                              next_pf(l, 1)));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
         if (N > 1 && !p2p) CK(gather_x());
-        CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
-                                a8 ? s->actE : none, st, pdl, p2p ? &oput : nullptr));
         GemvSeg gu[2] = {slice(w.gate, E, F, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
                          slice(w.up, E, F, (long long)k * Fl, Fl, s->gu + Fl, 2LL * Fl, nullptr)};
-        if (a8) CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl));
+        const GemvNorm n_ffn{s->x, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h};
+        const bool f_ffn = fuse_norm(gu, 2);
+        if (!f_ffn)
+            CK(launch_rmsnorm_quant(s->x, T, E, (const float *)w.ffn_norm->dev, (float)c.norm_eps, s->h,
+                                    a8 ? s->actE : none, st, pdl, p2p ? &oput : nullptr));
+        if (a8)
+            CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl, true, nullptr, next_pf(l, 2),
+                              f_ffn ? &n_ffn : nullptr));
         else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
         const P2P aput = xch(4 * l + 2, s->a, (long long)k * Fl);
         CK(launch_swiglu_quant(s->gu, s->gu + Fl, 2LL * Fl, T, Fl, N > 1 ? s->al : s->a,
@@ -266,22 +350,29 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         }
         GemvSeg dn = slice(w.down, F, E, (long long)k * El, El, s->x + (long long)k * El, E, s->x + (long long)k * El);
         const P2P xput = xch(4 * l + 3, s->x, (long long)k * El);
-        if (a8) CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl, true, p2p ? &xput : nullptr));
+        if (a8)
+            CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl, true, p2p ? &xput : nullptr,
+                              next_pf(l, 3)));
         else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
         if (N > 1 && !p2p) CK(gather_x());
     }
     const int first = all_rows ? 0 : T - 1, rows = T - first;
     const P2P xlast = xch(4 * (c.layers - 1) + 3, nullptr, 0);
-    CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
-                            (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl, p2p ? &xlast : nullptr));
-    const mimgpu_tensor *head = m->out ? m->out : m->embd;
+    const mimgpu_tensor *head = headt;
     // vocabulary rows [v0, v0 + vn); one GPU writes the logits directly (the
     // tied embedding, when it is the head, is bound whole on every rank)
     float *lg = N > 1 ? s->logl : s->logits;
     const long long ldl = N > 1 ? Vl : c.vocab;
+    GemvSeg hs = slice(head, E, c.vocab, v0, vn > 0 ? vn : 0, lg, ldl, nullptr);
+    const GemvNorm n_out{s->x, (const float *)m->out_norm->dev, (float)c.norm_eps, s->h};
+    const bool f_out = vn > 0 && rows == 1 && fuse_norm(&hs, 1);
+    if (!f_out)
+        CK(launch_rmsnorm_quant(s->x + (long long)first * E, rows, E, (const float *)m->out_norm->dev,
+                                (float)c.norm_eps, s->h, a8 ? s->actE : none, st, pdl, p2p ? &xlast : nullptr));
     if (vn > 0) {
-        GemvSeg hs = slice(head, E, c.vocab, v0, vn, lg, ldl, nullptr);
-        if (a8) CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl));
+        if (a8)
+            CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl, true, nullptr, next_pf(0, 4),
+                              f_out ? &n_out : nullptr));
         else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
     }
     if (greedy) {
@@ -359,6 +450,18 @@ int capture(mimgpu_session *s, bool greedy, cudaGraphExec_t *out, int rows = 1) 
         return cuda_fail(c, fe, "capture forward");
     }
     if (e != cudaSuccess) return cuda_fail(c, e, "end capture");
+    // the kernel launches one replay makes (reported by mimgpu_session_step_kernels)
+    size_t nn = 0;
+    int kernels = 0;
+    if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+        std::vector<cudaGraphNode_t> nodes(nn);
+        if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+            for (size_t i = 0; i < nn; i++) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+            }
+    }
+    if (greedy && rows == 1) s->step_kernels = kernels;
     e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     return cuda_fail(c, e, "instantiate");
@@ -397,13 +500,12 @@ int setup_step(mimgpu_session *s) {
     }
     const size_t words = step_sync_words(c.layers, c.ffn) + 2;
     const int half = c.rope_dims / 2;
+    if (!s->rope_cs) return MIMGPU_OK;
     cudaError_t e = cudaMalloc(&s->step_layers, host.size() * sizeof(StepLayer));
-    if (e == cudaSuccess) e = cudaMalloc(&s->rope_cs, (size_t)c.context * half * sizeof(float2));
     if (e == cudaSuccess) e = cudaMalloc(&s->step_sync, words * sizeof(unsigned));
     if (e == cudaSuccess)
         e = cudaMemcpy(s->step_layers, host.data(), host.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(s->step_sync, 0, words * sizeof(unsigned));
-    if (e == cudaSuccess) e = launch_rope_table(m->inv_freq, c.context, half, s->rope_cs, s->st);
     if (e == cudaSuccess) e = step_prepare();
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
     if (e != cudaSuccess) return cuda_fail(x, e, "step kernel setup");
@@ -589,6 +691,17 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
                           ? attn_prefill_scores_bytes((int)k.max_tokens, (int)H, k.kv_heads, k.context)
                           : 0;
     if (e == cudaSuccess && sb) e = cudaMalloc(&s->scores, sb);
+    // f32 cos/sin of every position's RoPE angles (float64), for the decode
+    // attention's fused RoPE and the step kernel
+    const int half = k.rope_dims / 2;
+    if (e == cudaSuccess && half > 0) e = cudaMalloc(&s->rope_cs, (size_t)k.context * half * sizeof(float2));
+    if (e == cudaSuccess && half > 0) e = launch_rope_table(m->inv_freq, k.context, half, s->rope_cs, s->st);
+    if (e == cudaSuccess && k.cache_f16 && D == 128) {
+        s->kmap.resize(k.layers);
+        s->kmap_ok = true;
+        for (int l = 0; l < k.layers; l++)
+            s->kmap_ok = s->kmap_ok && attn_decode_kmap(s->kc[l], slots, k.kv_heads / N, k.context, &s->kmap[l]);
+    }
     if (e != cudaSuccess) {
         free_session(s);
         return cuda_fail(c, e, "key-value cache");
@@ -770,6 +883,25 @@ int mimgpu_session_set_step_kernel(mimgpu_session *s, int on) {
 }
 
 int mimgpu_session_uses_step_kernel(mimgpu_session *s) { return s && s->use_step ? 1 : 0; }
+
+int mimgpu_session_step_kernels(mimgpu_session *s) { return s ? s->step_kernels : 0; }
+
+int mimgpu_session_set_l2_prefetch(mimgpu_session *s, int64_t bytes_per_sm) {
+    if (!s || bytes_per_sm < 0 || bytes_per_sm > (1 << 24) || bytes_per_sm % 16) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    if ((uint32_t)bytes_per_sm == s->prefetch_bytes) return MIMGPU_OK;
+    int rc = use_device(c);
+    if (rc) return rc;
+    // the captured graphs carry the old setting
+    cudaStreamSynchronize(s->st);
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
+    if (s->g_batch) cudaGraphExecDestroy(s->g_batch);
+    s->g_step = s->g_greedy = s->g_batch = nullptr;
+    s->prefetch_bytes = (uint32_t)bytes_per_sm;
+    return MIMGPU_OK;
+}
 
 size_t mimgpu_session_trace_bytes(mimgpu_session *s) {
     if (!s || !s->step_ok) return 0;

@@ -1,6 +1,8 @@
 // model_kernels.h -- launchers of the device-resident llama step kernels.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (types only)
+
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -80,6 +82,26 @@ inline size_t attn_exact_smem(int H, int Hkv, int D, int C, int f16) {
     return 1024 + sizeof(float) * (256 + (size_t)(256 / D) * C) + (size_t)kAttnRing * chunk;
 }
 cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
+// The attention of a decode step with the token's RoPE and cache write fused
+// in (k_attn_decode.cu): same bits as launch_rope_scatter + launch_attn_exact.
+// Rows are single tokens of distinct sequences (T == 1, or one slot per row);
+// D == 128, an even group size, an f16 cache and C <= attn_decode_max_context().
+// It reads pos and the cache rows below pos before its grid dependency wait:
+// the caller's forward must start with a kernel that waits for the previous
+// forward before it lets its dependents launch (embedding_kernel does).
+struct AttnDecodeArgs {
+    CUtensorMap kmap;      // the layer's key cache [slots * Hkv][C][D] f16: box [64][256][1], 128-byte swizzle
+    AttnArgs2 at;          // qh unused
+    const float *qkv;      // [T, ldq]: q (H*D) | k (Hkv*D) | v (Hkv*D), before RoPE
+    long long ldq;
+    const float2 *rope_cs; // [C][rotary/2]: f32(cos), f32(sin) of pos * inv_freq[i] (float64)
+    int rotary, interleaved;
+};
+int attn_decode_max_context();
+// The key-cache map of one layer for launch_attn_decode (false: no driver encoder).
+bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap *out);
+bool attn_decode_ok(const AttnArgs2 &a);
+cudaError_t launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // wait / keys: tensor parallelism, the ranks' keys arrive in keys[0..N)
 cudaError_t launch_advance(unsigned long long *key, int32_t *tok, int64_t *pos, int32_t *ids, int *step,
                            cudaStream_t st, bool pdl, const P2P *wait = nullptr,

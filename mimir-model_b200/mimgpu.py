@@ -71,6 +71,8 @@ SIGNATURES = {
     "mimgpu_session_stream": (P, [P]),
     "mimgpu_session_set_step_kernel": (I32, [P, I32]),
     "mimgpu_session_uses_step_kernel": (I32, [P]),
+    "mimgpu_session_set_l2_prefetch": (I32, [P, I64]),
+    "mimgpu_session_step_kernels": (I32, [P]),
     "mimgpu_session_trace_bytes": (SZ, [P]),
     "mimgpu_session_set_trace": (I32, [P, P, SZ]),
     "mimgpu_tp_unique_id": (I32, [P, SZ]),
@@ -457,8 +459,8 @@ class Session:
         return ids
 
     def set_step_kernel(self, on: bool):
-        """One persistent kernel per decode step (the default where the model
-        qualifies) or the kernel-per-op path; both give the same bits."""
+        """One persistent kernel per decode step (opt-in, where the model
+        qualifies) or the kernel-per-op path (the default); same bits."""
         self.m.ctx._check(lib().mimgpu_session_set_step_kernel(self.h, int(on)))
 
     def trace_bytes(self) -> int:
@@ -467,6 +469,15 @@ class Session:
     def set_trace(self, dev_ptr: int | None, nbytes: int = 0):
         """Binds a device buffer for the step kernel's phase timeline (profiling)."""
         self.m.ctx._check(lib().mimgpu_session_set_trace(self.h, dev_ptr, nbytes))
+
+    @property
+    def step_kernels(self) -> int:
+        """Kernel launches per captured greedy decode step (0 before capture)."""
+        return int(lib().mimgpu_session_step_kernels(self.h))
+
+    def set_l2_prefetch(self, bytes_per_sm: int):
+        """L2 prefetch of the next decode GEMV's weights (0 = off)."""
+        self.m.ctx._check(lib().mimgpu_session_set_l2_prefetch(self.h, int(bytes_per_sm)))
 
     @property
     def uses_step_kernel(self) -> bool:

@@ -157,3 +157,33 @@ def test_8b_layer_shapes_token_identity(ctx):
     assert gen.tolist() == want_ids, (gen.tolist(), want_ids, margins)
     s.free()
     m.free()
+
+
+def test_refused_rows_same_in_step_and_prompt(ctx):
+    """Weight rows with a non-finite block scale take the f32 product
+    (linearA8, interp/fast.go:282-379) on every path: a one-token step, whose
+    GEMVs normalise their own activation row (fused rms_norm), gives the same
+    logits bit for bit as the same token as the last row of a prompt pass,
+    whose rms_norm is a kernel of its own."""
+    import mimgpu
+    cfg, w = _synthetic(2, 512, 4, 2, 1024, 700, seed=7)
+    rb = {O.Q4_K: 144, O.Q6_K: 210}
+    for name, row in (("blk.0.attn_q.weight", 5), ("blk.1.ffn_gate.weight", 100), ("output.weight", 17)):
+        dt, arr = w[name]
+        b = bytearray(arr.tobytes())
+        o = row * (512 // 256) * rb[dt] + (0 if dt == O.Q4_K else 208)
+        b[o:o + 2] = bytes([0x00, 0x7C])  # d = +inf in the row's first block
+        w[name] = (dt, np.frombuffer(bytes(b), np.uint8))
+    C = 64
+    ids = np.array([3, 9, 27, 81, 243, 5, 15, 45], np.int32)
+    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=8), w)
+    s = m.session()
+    whole = s.run(ids, np.arange(8), all_rows=True)
+    s.reset()
+    s.run(ids[:7], np.arange(7))
+    step = s.run(ids[7:], np.array([7]))
+    assert np.array_equal(np.isnan(step[0]), np.isnan(whole[7]))
+    fin = ~np.isnan(whole[7])
+    assert np.array_equal(step[0][fin].view(np.uint32), whole[7][fin].view(np.uint32))
+    s.free()
+    m.free()

@@ -188,6 +188,35 @@ def test_a8_batch_invariance(ctx):
         t.free()
 
 
+@pytest.mark.parametrize("block", [256, 32])
+def test_a8_quantizer_rounds_near_half_integers(ctx, block):
+    """TestQuantQ8 (internal/kernels/q8_test.go:116-160): activations on
+    half-integer steps of amax/127, nudged by a few ulps, where the rounding
+    of 127 x / amax decides the quant; every quant shows in the product bits
+    (exact integer block sums), compared with the oracle's float64 rounding."""
+    rng = np.random.default_rng(13)
+    k, n = 4096, 24
+    x = np.empty((4, k), np.float32)
+    for r in range(4):
+        amax = np.float32(rng.exponential(10.0) + 1e-3)
+        h = (rng.integers(0, 255, k) - 127) / 2.0
+        v = (h * np.float64(amax) / 127).astype(np.float32)
+        for _ in range(2):
+            nudge = rng.integers(0, 3, k)
+            v = np.where(nudge == 1, np.nextafter(v, np.float32(np.inf)), v)
+            v = np.where(nudge == 2, np.nextafter(v, np.float32(-np.inf)), v)
+        v = np.clip(v, -amax, amax)
+        v[::32] = amax  # every run of 32 (so every block) reaches amax exactly
+        x[r] = v
+    for dt in (O.Q4_K, O.Q6_K):
+        w = _weights(dt, n, k, 91)
+        t = ctx.upload(dt, (n, k), w)
+        want = O.dequant_matmul_a8(x, dt, w, n, block=block)
+        got = ctx.dequant_matmul(x, t, a8_block=block)
+        assert np.array_equal(bits(got), bits(want))
+        t.free()
+
+
 def test_a8_block_attribute(ctx):
     import mimgpu
     w = _weights(O.Q4_K, 4, 256, 1)
