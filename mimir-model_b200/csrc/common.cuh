@@ -149,6 +149,20 @@ __device__ __forceinline__ int q8_round(float v, double a, double inv_a) {
     return (int)q;
 }
 
+// q8_round in float32 where that is provably the same: with r = fl(127/amax)
+// and y = fl(v r), |y - 127 v / amax| <= 127 * 2^-23 (< 1.6e-5, plus 2^-149
+// when y is subnormal), so when y is farther than 4e-5 from a half-integer
+// its nearest integer is the exact quotient's.  Otherwise (about one element
+// in 10^4), or for amax below 2^-100 (r could overflow), the exact routine.
+// r = __fdiv_rn(127.f, amax), computed once per block.
+__device__ __forceinline__ int q8_round_f(float v, float amax, float r) {
+    const float y = __fmul_rn(v, r);
+    const float f = rintf(y);
+    if (fabsf(__fsub_rn(y, f)) < 0.49996f && amax >= 0x1p-100f) return (int)f;
+    const double a = (double)amax;
+    return q8_round(v, a, __ddiv_rn(1.0, a));
+}
+
 // ------------------------------------------------------------- argmax
 // argmax (cmd/mim-run/main.go:184-193): best = 0; x > v[best] moves best.
 // The result is the first index of the largest non-NaN value (NaNs never

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(256) quantize_a8_b32_kernel(const float *__res
         const float amax = warp_max(b ? 0.f : a);
         bad = __any_sync(0xffffffffu, b);
         int q = 0;
-        if (amax != 0.f && !bad) q = q8_round(v, (double)amax, __ddiv_rn(1.0, (double)amax));
+        if (amax != 0.f && !bad) q = q8_round_f(v, amax, __fdiv_rn(127.f, amax));
         act.q[i] = (int8_t)q;
         int s = q;
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);

@@ -148,12 +148,12 @@ __device__ __forceinline__ void stage_norm(const RowParams &p, uint8_t *smem, in
         am = warp_max(am);
         bad = __any_sync(FULL, bad);
         const bool quant = am != 0.f && !bad;
-        const double ad = (double)am, inv_a = quant ? __ddiv_rn(1.0, ad) : 0.0;
+        const float r127 = quant ? __fdiv_rn(127.f, am) : 0.f;
         uint32_t qw[2] = {0u, 0u};
         int s8 = 0;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const int q = quant ? q8_round(v[j], ad, inv_a) : 0;
+            const int q = quant ? q8_round_f(v[j], am, r127) : 0;
             s8 += q;
             qw[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
         }

@@ -15,7 +15,7 @@ struct QuantScratch {
 };
 
 // Quantizes the block whose element threadIdx.x is v: amax over the block,
-// q = RoundToEven(127*x/amax) as float64 gives it (q8_round), dx = amax/127, the sums of each
+// q = RoundToEven(127*x/amax) as float64 gives it (q8_round_f), dx = amax/127, the sums of each
 // run of 32 and of 16 quants, and the block's flag (0 when it holds NaN,
 // Inf or |x| > 2^60, which the reference refuses).
 __device__ __forceinline__ void quant_block_256(float v, long long row, long long K, int blk, ActQ8 act,
@@ -38,7 +38,7 @@ __device__ __forceinline__ void quant_block_256(float v, long long row, long lon
         anybad |= qs.bad[i];
     }
     int q = 0;
-    if (amax != 0.f && !anybad) q = q8_round(v, (double)amax, __ddiv_rn(1.0, (double)amax));
+    if (amax != 0.f && !anybad) q = q8_round_f(v, amax, __fdiv_rn(127.f, amax));
     act.q[row * K + (long long)blk * 256 + t] = (int8_t)q;
     int s16 = q;
     for (int o = 8; o; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
