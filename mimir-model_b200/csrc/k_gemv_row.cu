@@ -33,6 +33,7 @@
 //    its chain warp is done with it; the data stream never waits for a chain.
 // The activation row sits in shared memory in a layout that puts the lanes
 // of a quarter-warp on distinct banks for both block orders.
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -527,7 +528,18 @@ bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
     if (rps < 1) return false;
     pl.sb = rps * nb;
     auto al = [](int v, int a) { return (v + a - 1) / a * a; };
-    pl.slot_bytes = pl.sb * maxbb;
+    // a slot holds the largest stage the launch has: rows per stage, or a
+    // whole slab when that is smaller (a q|k|v launch's Q6_K v slab of a
+    // few rows needs no full Q6_K stage), so small launches get more slots
+    // and every copy is in flight from the start
+    const int G = num_sms();
+    long long stage_max = 16;
+    for (int i = 0; i < nseg; i++) {
+        const long long units = segs[i].n / pl.unit;
+        const long long slab_rows = (units + G - 1) / G * pl.unit;
+        stage_max = std::max(stage_max, std::min((long long)rps, slab_rows) * nb * block_bytes(segs[i].dt));
+    }
+    pl.slot_bytes = al((int)std::min(stage_max, (long long)pl.sb * maxbb), 128);
     int o = 512;  // barriers and flags
     pl.off_act = o;
     o = al(o + act_bytes(nb), 16);
