@@ -363,6 +363,32 @@ def tp_rows(n: int, nranks: int, rank: int) -> tuple:
     return r0, min(n, r0 + per)
 
 
+def load_llama(ctx: "Context", path: str, *, a8: bool = True, cache_f16: bool = True, max_tokens: int = 1,
+               context: int | None = None) -> "Model":
+    """A Llama mim file written by the reference's importer (importer/llama.go:
+    tensors under their GGUF names, the dimensions in the metadata) as a
+    device-resident model.  The file's graph section is not interpreted:
+    the model runs the same Llama step as Model(ctx, cfg, weights), with
+    8-bit activations (a8, dequant_matmul_a8.v2) or exact f32 products and an
+    f16 or f32 key-value cache as asked.  Weight bytes go from the mapped
+    file to HBM byte for byte."""
+    try:
+        from . import mimfile  # type: ignore
+    except ImportError:
+        import mimfile  # type: ignore
+    with mimfile.MimFile(path) as f:
+        cfg = mimfile.llama_config(f)
+        if context:
+            cfg["context"] = int(context)
+        cfg.update(a8=int(a8), cache_f16=int(cache_f16), interleaved=1, max_tokens=int(max_tokens))
+        names = [n for n in f.tensors if n in ("token_embd.weight", "output.weight", "output_norm.weight")
+                 or (n.startswith("blk.") and n.endswith(".weight"))]
+        # each tensor with the file's own shape (the model checks it against the dimensions)
+        weights = {n: (f.tensors[n].dtype, ctx.upload(f.tensors[n].dtype, f.tensors[n].shape,
+                                                      np.frombuffer(f.data(n), np.uint8))) for n in names}
+        return Model(ctx, cfg, weights)
+
+
 class Model:
     """The llama graph (importer/llama.go:317-547) as a device-resident decoder."""
 

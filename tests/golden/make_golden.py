@@ -11,10 +11,15 @@ It reads, and never modifies:
     179-267): the 2-layer tiny Llama whose prompt and greedy logits the
     float64 oracle wrote.
 
+  * testdata/compat/0.2-0.1/tiny-llama.mim: the same tiny Llama as the
+    reference's importer writes it (container 0.2: weights, metadata and
+    graph sections), for the mim-file loader.
+
 It writes quant_golden.json, tiny_llama.bin (the raw tensor bytes, byte for
-byte as File.TensorData returns them) and tiny_llama.json (tensor index,
-hyperparameters and the expected logits/ids).  The gguf package (0.19)
-parses the GGUF container only; no arithmetic of it is used.
+byte as File.TensorData returns them), tiny_llama.json (tensor index,
+hyperparameters and the expected logits/ids) and tiny_llama.mim (a byte
+copy).  The gguf package (0.19) parses the GGUF container only; no
+arithmetic of it is used.
 """
 from __future__ import annotations
 
@@ -83,10 +88,17 @@ def tiny_llama(ref: str, name: str = "llama"):
         json.dump(out, f)
 
 
+def mim_fixture(ref: str):
+    src = os.path.join(ref, "testdata", "compat", "0.2-0.1", "tiny-llama.mim")
+    with open(src, "rb") as f, open(os.path.join(OUT, "tiny_llama.mim"), "wb") as g:
+        g.write(f.read())
+
+
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MIM_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
         sys.exit("usage: make_golden.py <path to the mimir-model checkout>")
     quant(ref)
     tiny_llama(ref, "llama")
+    mim_fixture(ref)
     print("wrote", sorted(os.listdir(OUT)))

@@ -187,3 +187,34 @@ def test_refused_rows_same_in_step_and_prompt(ctx):
     assert np.array_equal(step[0][fin].view(np.uint32), whole[7][fin].view(np.uint32))
     s.free()
     m.free()
+
+
+def test_tiny_llama_from_the_importers_mim_file(ctx, tiny):
+    """The reference importer's own file of the tiny Llama (container 0.2,
+    tests/golden/tiny_llama.mim) through mimgpu.load_llama: its prompt and
+    greedy logits stay within llama.cpp's distance from the float64 oracle
+    (cmd/mim-run/main_test.go:218-267), and equal bit for bit those of the
+    same weights bound from the GGUF bytes."""
+    import os
+    import mimgpu
+    e, w = tiny
+    V = e["config"]["vocab"]
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tiny_llama.mim")
+    ids = e["prompt_ids"]
+    m = mimgpu.load_llama(ctx, path, a8=True, cache_f16=True, max_tokens=len(ids))
+    s = m.session()
+    got = s.run(ids, np.arange(len(ids)), all_rows=True)
+    worst = np.abs(got - f32b64(e["prompt_logits"]).reshape(len(ids), V)).max()
+    logits, pos = got[-1], len(ids)
+    for i, nxt in enumerate(e["greedy"]):
+        worst = max(worst, np.abs(logits - f32b64(e["greedy_logits"][i])).max())
+        logits = s.run([nxt], [pos])[0]
+        pos += 1
+    assert worst <= e["llama_cpp_max_diff"] * 1.1
+    m2 = _model(ctx, e, w, a8=1, cache_f16=1)
+    s2 = m2.session()
+    assert np.array_equal(s2.run(ids, np.arange(len(ids)), all_rows=True).view(np.uint32), got.view(np.uint32))
+    s.free()
+    m.free()
+    s2.free()
+    m2.free()
