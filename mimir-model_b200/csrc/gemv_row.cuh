@@ -58,6 +58,27 @@ __device__ __forceinline__ void slab(int n, int b, int G, int u, int &r0, int &n
     nr = (int)(e - a) * u;
 }
 
+// The first pf.bytes of slab `sl` of a one-row GEMV launch into L2 (the
+// bytes that launch's CTA sl streams first): the launch before it issues this
+// for its own CTA's slab once its copies are out.
+__device__ __forceinline__ void slab_prefetch(const GemvPrefetch &pf, int sl) {
+    uint32_t left = pf.bytes;
+    for (int s = 0; s < pf.nseg && left; s++) {
+        int r0, nr;
+        slab(pf.n[s], sl, pf.G, pf.unit, r0, nr);
+        const long long rbn = row_bytes(pf.dt[s], pf.K);
+        const uint8_t *src = pf.w[s] + (long long)r0 * rbn;
+        long long avail = (long long)nr * rbn;  // a multiple of 16: slabs come in whole units
+        while (left && avail > 0) {
+            const uint32_t take = (uint32_t)min((long long)min(left, 32768u), avail);
+            prefetch_l2(src, take);
+            src += take;
+            avail -= take;
+            left -= take;
+        }
+    }
+}
+
 // The bytes a Q6_K lane needs from one block, read with aligned 16-byte
 // loads: WO is the block start's word offset within its 16-byte line
 // (warp-uniform), the remaining 0/16-bit shift comes from the address.

@@ -242,23 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         }
         // the next launch's first bytes of this CTA's slabs into L2, while
         // this launch's last stages are in flight
-        if (ok && p.pf.nseg > 0) {
-            uint32_t left = p.pf.bytes;
-            for (int s = 0; s < p.pf.nseg && left; s++) {
-                int r0, nr;
-                slab(p.pf.n[s], cta, G, p.pf.unit, r0, nr);
-                const long long rbn = row_bytes(p.pf.dt[s], p.pf.K);
-                const uint8_t *src = p.pf.w[s] + (long long)r0 * rbn;
-                long long avail = (long long)nr * rbn;  // a multiple of 16: slabs come in whole units
-                while (left && avail > 0) {
-                    const uint32_t take = (uint32_t)min((long long)min(left, 32768u), avail);
-                    prefetch_l2(src, take);
-                    src += take;
-                    avail -= take;
-                    left -= take;
-                }
-            }
-        }
+        if (ok && p.pf.nseg > 0) slab_prefetch(p.pf, cta);
         // copies still in flight land before the block exits
         for (int u = max(0, n - p.slots); u < n; u++)
             mbar_wait_bounded(&full[u % p.slots], (u / p.slots) & 1, p.status);
@@ -608,6 +592,7 @@ bool gemv_prefetch_plan(const GemvSeg *segs, int nseg, long long K, uint32_t byt
     }
     pf.nseg = nseg;
     pf.unit = pl.unit;
+    pf.G = num_sms();
     pf.K = K;
     pf.bytes = bytes;
     return true;

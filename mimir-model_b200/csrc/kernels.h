@@ -96,8 +96,9 @@ struct GemvPrefetch {
     const uint8_t *w[kMaxSegs];
     int n[kMaxSegs], dt[kMaxSegs];
     int nseg, unit;
+    int G;           // slabs (the launch's CTAs: one per SM)
     long long K;
-    uint32_t bytes;  // per CTA, a multiple of 16
+    uint32_t bytes;  // per slab, a multiple of 16
 };
 // Fills pf for a launch of segs over K; false when that launch would not be
 // a one-row (slab) GEMV.
