@@ -298,6 +298,20 @@ int mimgpu_session_uses_step_kernel(mimgpu_session *s);
  * starts from L2 while HBM would otherwise idle through the launch boundary
  * and the small kernels between.  Results are unchanged. */
 int mimgpu_session_set_l2_prefetch(mimgpu_session *s, int64_t bytes_per_sm);
+/* The same per GEMV kind and distance: `kind` is the GEMV prefetched (0 the
+ * q|k|v GEMV, 1 o, 2 gate|up, 3 down, 4 the head), `distance` 1 when the
+ * GEMV just before it issues the prefetch, 2 when the one before that does
+ * (for instance the q|k|v GEMV prefetching gate|up bytes that stream while
+ * the attention runs).  mimgpu_session_set_l2_prefetch sets every kind at
+ * distance 1 and clears distance 2.  Results are unchanged. */
+int mimgpu_session_set_l2_prefetch_for(mimgpu_session *s, int kind, int distance, int64_t bytes_per_sm);
+
+/* Which small ops a one-token step on one GPU runs inside a GEMV instead of
+ * as kernels of their own (default: all): MIMGPU_FUSE_NORM, each rms_norm in
+ * the prologue of the GEMV that reads it.  Results are unchanged, bit for
+ * bit; the flag exists to compare the forms. */
+#define MIMGPU_FUSE_NORM 1u
+int mimgpu_session_set_fusions(mimgpu_session *s, unsigned mask);
 
 /* Kernel launches in one replay of the session's captured one-token greedy
  * step (mimgpu_session_generate), counted from the CUDA graph; 0 before the

@@ -58,23 +58,26 @@ __device__ __forceinline__ void slab(int n, int b, int G, int u, int &r0, int &n
     nr = (int)(e - a) * u;
 }
 
-// The first pf.bytes of slab `sl` of a one-row GEMV launch into L2 (the
+// The first bytes of slab `sl` of each target launch of pf into L2 (the
 // bytes that launch's CTA sl streams first): the launch before it issues this
 // for its own CTA's slab once its copies are out.
 __device__ __forceinline__ void slab_prefetch(const GemvPrefetch &pf, int sl) {
-    uint32_t left = pf.bytes;
-    for (int s = 0; s < pf.nseg && left; s++) {
-        int r0, nr;
-        slab(pf.n[s], sl, pf.G, pf.unit, r0, nr);
-        const long long rbn = row_bytes(pf.dt[s], pf.K);
-        const uint8_t *src = pf.w[s] + (long long)r0 * rbn;
-        long long avail = (long long)nr * rbn;  // a multiple of 16: slabs come in whole units
-        while (left && avail > 0) {
-            const uint32_t take = (uint32_t)min((long long)min(left, 32768u), avail);
-            prefetch_l2(src, take);
-            src += take;
-            avail -= take;
-            left -= take;
+    for (int t = 0; t < pf.nt; t++) {
+        const GemvPrefetchTarget &g = pf.t[t];
+        uint32_t left = g.bytes;
+        for (int s = 0; s < g.nseg && left; s++) {
+            int r0, nr;
+            slab(g.n[s], sl, pf.G, g.unit, r0, nr);
+            const long long rbn = row_bytes(g.dt[s], g.K);
+            const uint8_t *src = g.w[s] + (long long)r0 * rbn;
+            long long avail = (long long)nr * rbn;  // a multiple of 16: slabs come in whole units
+            while (left && avail > 0) {
+                const uint32_t take = (uint32_t)min((long long)min(left, 32768u), avail);
+                prefetch_l2(src, take);
+                src += take;
+                avail -= take;
+                left -= take;
+            }
         }
     }
 }

@@ -707,9 +707,11 @@ cudaError_t gemv_a8_prepare() {
 }
 
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put, const GemvPrefetch *pf, const GemvNorm *nrm) {
+                           unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put,
+                           const GemvPrefetch *pf, const GemvNorm *nrm) {
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
     if (put && put->N > 1 && (rows != 1 || nseg != 1)) return cudaErrorInvalidValue;  // exchanges carry one row
+    if (nrm && rows != 1) return cudaErrorInvalidValue;  // the fused norm makes one row
     if (rows == 0 || K == 0) return cudaSuccess;
     // many activation rows: the tensor-core GEMM (same results bit for bit)
     if ((!put || put->N <= 1) && gemm_a8_tc_ok(segs, nseg, act, rows, K))

@@ -70,8 +70,10 @@ struct RowParams {
     int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
     P2P put;
     unsigned *status;
-    GemvPrefetch pf;    // the next launch's weights into L2 (pf.nseg 0: none)
+    GemvPrefetch pf;    // the next launches' weights into L2 (pf.nt 0: none)
     GemvNorm nrm;       // nrm.x set: the activation row is rms_norm(nrm.x), made here
+    int off_aux;        // floats: the slab's residual values (pre_res)
+    int pre_res;        // one segment with a residual: its slab's values read at the start
 };
 
 // rms_norm.v1 of the residual row and its 8-bit blocks, made by the 16
@@ -88,7 +90,6 @@ __device__ __forceinline__ void stage_norm(const RowParams &p, uint8_t *smem, in
                                            const float (&nsc)[kNormRounds][8]) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, K = (int)p.K;
     const float *x = p.nrm.x;
-    // the row once, in the quantization's layout: warp w holds blocks w, w + 16, ...
     float xv[kNormRounds][8];
     double ss = 0.0;
 #pragma unroll
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         }
         // the next launch's first bytes of this CTA's slabs into L2, while
         // this launch's last stages are in flight
-        if (ok && p.pf.nseg > 0) slab_prefetch(p.pf, cta);
+        if (ok) slab_prefetch(p.pf, cta);
         // copies still in flight land before the block exits
         for (int u = max(0, n - p.slots); u < n; u++)
             mbar_wait_bounded(&full[u % p.slots], (u / p.slots) & 1, p.status);
@@ -268,9 +269,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
         }
     }
     pdl_wait();
+    float *aux = (float *)(smem + p.off_aux);
     if (warp < kCW && p.nrm.x) {
         stage_norm(p, smem, misc, (double *)(smem + 4 * kMaxSlots * 8 + 16), nsc);
         for (int i = tid; i < RS * rps; i += kCT) smem[p.off_bad + i] = 0;
+    } else if (warp > kCW) {
+        // the residual of this CTA's rows, written by an earlier kernel and
+        // final once the wait above returned: read now, beside the
+        // activation staging, rather than by each row chain at its end
+        if (p.pre_res) {
+            int r0, nr;
+            slab(p.seg[0].n, cta, G, p.unit, r0, nr);
+            for (int i = threadIdx.x - (kCT + 32); i < nr; i += 32 * kNC) aux[i] = __ldcg(p.seg[0].res + r0 + i);
+        }
     } else if (warp < kCW) {
         // the activation row into shared memory (act_off layout), the
         // per-half headers (xs of the 4 runs of 32, dx, ok), the sums of 16
@@ -333,6 +344,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
             slab(sg.n, cta, G, p.unit, r0, nr);
             const int dt = sg.dt;
             const long long rb = row_bytes(dt, p.K);
+            // the finished row `rel` of the slab (output row r0 + rel): bias,
+            // residual, stores
+            auto emit = [&](int rel, float r) {
+                const int orow = r0 + rel;
+                if (sg.bias) r = __fadd_rn(r, sg.bias[orow]);
+                if (sg.res) r = __fadd_rn(p.pre_res ? aux[rel] : sg.res[orow], r);
+                sg.y[orow] = r;
+                for (int k = 0; k < (p.put.N > 1 ? p.put.N : 0); k++)
+                    peer_ptr<float>(p.put, k, p.put.off)[p.put.col0 + orow] = r;
+            };
             for (int lo = 0; lo < nr; lo += rps, m++) {
                 if (m % kNC != c) continue;
                 const int rs = m % RS;
@@ -363,15 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                     }
                     const bool refused = valid && (bad[idx] != 0 || !act_ok);
                     if (valid) bad[idx] = 0;
-                    const int orow = r0 + row;
-                    if (valid && !refused && !failed) {
-                        float r = __fsub_rn(tot, off);
-                        if (sg.bias) r = __fadd_rn(r, sg.bias[orow]);
-                        if (sg.res) r = __fadd_rn(sg.res[orow], r);
-                        sg.y[orow] = r;
-                        for (int k = 0; k < (p.put.N > 1 ? p.put.N : 0); k++)
-                            peer_ptr<float>(p.put, k, p.put.off)[p.put.col0 + orow] = r;
-                    }
+                    if (valid && !refused && !failed) emit(row, __fsub_rn(tot, off));
                     // rows whose weights or activations the 8-bit kernel refuses: f32 product
                     unsigned rm = __ballot_sync(FULL, refused && !failed);
                     while (rm) {
@@ -389,13 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_row_kernel(const __grid_cons
                         } else {
                             r = row_dot_f32(dt, sg.w + (long long)frow * rb, p.x, nb);
                         }
-                        if (sg.bias) r = __fadd_rn(r, sg.bias[frow]);
-                        if (sg.res) r = __fadd_rn(sg.res[frow], r);
-                        if (lane == 0) {
-                            sg.y[frow] = r;
-                            for (int k = 0; k < (p.put.N > 1 ? p.put.N : 0); k++)
-                                peer_ptr<float>(p.put, k, p.put.off)[p.put.col0 + frow] = r;
-                        }
+                        if (lane == 0) emit(t0 + i, r);
                     }
                 }
                 __syncwarp();
@@ -495,7 +502,8 @@ int row_unit(int dt, long long K) {
 
 struct RowPlan {
     int unit, sb, rstages, slots, slot_bytes, smem;
-    int off_act, off_hdr, off_ys, off_rec, off_bad, off_ring;
+    int off_act, off_hdr, off_ys, off_aux, off_rec, off_bad, off_ring;
+    int pre_res;
 };
 
 bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
@@ -531,6 +539,16 @@ bool plan_row(const GemvSeg *segs, int nseg, long long K, RowPlan &pl) {
     o += hdr_bytes(nb);
     pl.off_ys = o;
     o += hdr_bytes(nb);
+    // aux: the slab's residual values, read at the start (one matrix with a
+    // residual, a few KB at most)
+    long long slab_max = 0;
+    for (int i = 0; i < nseg; i++) {
+        const long long units = segs[i].n / pl.unit;
+        slab_max = std::max(slab_max, (units + G - 1) / G * pl.unit);
+    }
+    pl.pre_res = nseg == 1 && segs[0].res && slab_max <= 1024;
+    pl.off_aux = o;
+    if (pl.pre_res) o += al((int)slab_max * 4, 16);
     pl.off_rec = o;
     const int fixed = o, rec_stage = rps * (nb + 1) * 16;
     // the most data slots first (3 at least), then the most record stages (2 at least)
@@ -578,23 +596,25 @@ bool gemv_row_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, long long K) {
 
 cudaError_t gemv_row_prepare() { return prepare_row(); }
 
-bool gemv_prefetch_plan(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf) {
+bool gemv_prefetch_add(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf) {
     RowPlan pl;
-    pf = GemvPrefetch{};
+    if (pf.nt >= kMaxPrefetchTargets || bytes == 0) return false;
     if (nseg <= 0 || nseg > kMaxSegs || bytes % 16 || !plan_row(segs, nseg, K, pl)) return false;
+    GemvPrefetchTarget t{};
     for (int i = 0; i < nseg; i++) {
         if ((segs[i].dt != Q4_K && segs[i].dt != Q6_K) || ((uintptr_t)segs[i].w & 15) || segs[i].n % pl.unit ||
             (unsigned long long)segs[i].n * (unsigned long long)num_sms() >= (1ULL << 32))
             return false;
-        pf.w[i] = segs[i].w;
-        pf.n[i] = segs[i].n;
-        pf.dt[i] = segs[i].dt;
+        t.w[i] = segs[i].w;
+        t.n[i] = segs[i].n;
+        t.dt[i] = segs[i].dt;
     }
-    pf.nseg = nseg;
-    pf.unit = pl.unit;
+    t.nseg = nseg;
+    t.unit = pl.unit;
+    t.K = K;
+    t.bytes = bytes;
+    pf.t[pf.nt++] = t;
     pf.G = num_sms();
-    pf.K = K;
-    pf.bytes = bytes;
     return true;
 }
 
@@ -619,6 +639,8 @@ cudaError_t launch_gemv_row(const GemvSeg *segs, int nseg, const float *x, ActQ8
     p.off_act = pl.off_act;
     p.off_hdr = pl.off_hdr;
     p.off_ys = pl.off_ys;
+    p.off_aux = pl.off_aux;
+    p.pre_res = pl.pre_res;
     p.off_rec = pl.off_rec;
     p.off_bad = pl.off_bad;
     p.off_ring = pl.off_ring;

@@ -87,22 +87,30 @@ cudaError_t gemv_a8_prepare();
 // encode it on the stack every launch, allocating nothing).
 // put: the (one-segment, one-row) outputs also go to every rank's copy of
 // the exchanged buffer, then the launch publishes (producer side)
-// The next one-row GEMV of a decode step, whose weights a launch prefetches
-// into L2 once its own copies are all issued: each CTA takes the first
-// `bytes` of its slabs of those matrices, the bytes the next launch's CTA of
-// the same index streams first, so the next launch starts from L2 while HBM
-// is otherwise idle (its predecessor's tail, the small kernels between).
-struct GemvPrefetch {
+// The next one-row GEMVs of a decode step, whose weights a launch prefetches
+// into L2 once its own copies are all issued: for each target launch, each
+// CTA takes the first `bytes` of its slabs of that launch's matrices, the
+// bytes the target's CTA of the same index streams first, so the target
+// starts from L2 while HBM would otherwise idle (its predecessor's tail, the
+// small kernels between).  Targets are the next launch and, optionally, the
+// one after it (the o GEMV prefetches little of its own successor's bytes
+// while the attention runs unless the q|k|v GEMV before it starts early).
+struct GemvPrefetchTarget {
     const uint8_t *w[kMaxSegs];
     int n[kMaxSegs], dt[kMaxSegs];
     int nseg, unit;
-    int G;           // slabs (the launch's CTAs: one per SM)
     long long K;
     uint32_t bytes;  // per slab, a multiple of 16
 };
-// Fills pf for a launch of segs over K; false when that launch would not be
-// a one-row (slab) GEMV.
-bool gemv_prefetch_plan(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf);
+constexpr int kMaxPrefetchTargets = 2;
+struct GemvPrefetch {
+    GemvPrefetchTarget t[kMaxPrefetchTargets];
+    int nt;
+    int G;  // slabs (the launches' CTAs: one per SM)
+};
+// Adds the launch of segs over K as a target of pf (bytes per slab); false,
+// leaving pf unchanged, when that launch would not be a one-row (slab) GEMV.
+bool gemv_prefetch_add(const GemvSeg *segs, int nseg, long long K, uint32_t bytes, GemvPrefetch &pf);
 // rms_norm of the row nrm.x fused into a one-row GEMV: every CTA makes its
 // own 8-bit activations instead of reading act (CTA 0 also writes the
 // normalised row to nrm.h, which must be the launch's x); same bits as

@@ -79,9 +79,12 @@ struct mimgpu_session {
     int g_batch_rows = 0;
     // the one-kernel decode step (k_step.cu), when the model qualifies
     bool step_ok = false, use_step = false;
-    // one-row decode GEMVs prefetch the next GEMV's first bytes of each SM's
-    // slab into L2 (mimgpu_session_set_l2_prefetch; 0 = off)
-    uint32_t prefetch_bytes = 160 * 1024;
+    // one-row decode GEMVs prefetch the first bytes of each SM's slab of the
+    // next GEMV (prefetch_next) and of the one after it (prefetch_skip) into
+    // L2, by the kind of that GEMV: 0 q|k|v, 1 o, 2 gate|up, 3 down, 4 head
+    // (mimgpu_session_set_l2_prefetch / _for; 0 = off)
+    uint32_t prefetch_next[5] = {160 * 1024, 160 * 1024, 160 * 1024, 160 * 1024, 160 * 1024};
+    uint32_t prefetch_skip[5] = {0, 0, 0, 0, 0};
     // one-token steps on one GPU: each rms_norm runs inside the GEMV that
     // reads it (GemvNorm) instead of as a kernel of its own
     bool fuse_norm = true;
@@ -248,21 +251,32 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         default: g[0] = slice(w.down, F, E, (long long)k * El, El, nullptr, 0, nullptr); return 1;
         }
     };
+    // the launch after (l, which): q|k|v, o, gate|up, down per layer, then
+    // the head, then the next step's first q|k|v
+    auto after = [&](int &l, int &which) {
+        if (which == 3) {
+            l++;
+            which = l < c.layers ? 0 : 4;
+        } else if (which == 4) {
+            l = 0;
+            which = 0;
+        } else {
+            which++;
+        }
+    };
     GemvPrefetch pfbuf;
     auto next_pf = [&](int l, int which) -> const GemvPrefetch * {
-        if (T != 1 || !a8 || s->prefetch_bytes == 0) return nullptr;
-        int nl = l, nw = which + 1;
-        if (which == 3) {
-            nl = l + 1;
-            nw = nl < c.layers ? 0 : 4;
-        } else if (which == 4) {
-            nl = 0;
-            nw = 0;
+        if (T != 1 || !a8) return nullptr;
+        pfbuf = GemvPrefetch{};
+        int nl = l, nw = which;
+        for (int d = 0; d < 2; d++) {
+            after(nl, nw);
+            const uint32_t bytes = d == 0 ? s->prefetch_next[nw] : s->prefetch_skip[nw];
+            GemvSeg g[kMaxSegs];
+            const int ns = bytes ? segs_of(nl, nw, g) : 0;
+            if (ns > 0) gemv_prefetch_add(g, ns, nw == 3 ? F : E, bytes, pfbuf);
         }
-        GemvSeg g[kMaxSegs];
-        const int ns = segs_of(nl, nw, g);
-        if (ns == 0 || !gemv_prefetch_plan(g, ns, nw == 3 ? F : E, s->prefetch_bytes, pfbuf)) return nullptr;
-        return &pfbuf;
+        return pfbuf.nt ? &pfbuf : nullptr;
     };
     auto fuse_norm = [&](const GemvSeg *g, int n) {
         return s->fuse_norm && T == 1 && N == 1 && a8 && E <= 8192 && gemv_row_ok(g, n, s->actE, E);
@@ -886,20 +900,52 @@ int mimgpu_session_uses_step_kernel(mimgpu_session *s) { return s && s->use_step
 
 int mimgpu_session_step_kernels(mimgpu_session *s) { return s ? s->step_kernels : 0; }
 
-int mimgpu_session_set_l2_prefetch(mimgpu_session *s, int64_t bytes_per_sm) {
-    if (!s || bytes_per_sm < 0 || bytes_per_sm > (1 << 24) || bytes_per_sm % 16) return MIMGPU_EINVAL;
-    mimgpu_ctx *c = s->m->ctx;
-    std::lock_guard<std::recursive_mutex> lk(c->mu);
-    if ((uint32_t)bytes_per_sm == s->prefetch_bytes) return MIMGPU_OK;
-    int rc = use_device(c);
+namespace {
+// the captured graphs carry the old prefetch setting
+int drop_graphs(mimgpu_session *s) {
+    int rc = use_device(s->m->ctx);
     if (rc) return rc;
-    // the captured graphs carry the old setting
     cudaStreamSynchronize(s->st);
     if (s->g_step) cudaGraphExecDestroy(s->g_step);
     if (s->g_greedy) cudaGraphExecDestroy(s->g_greedy);
     if (s->g_batch) cudaGraphExecDestroy(s->g_batch);
     s->g_step = s->g_greedy = s->g_batch = nullptr;
-    s->prefetch_bytes = (uint32_t)bytes_per_sm;
+    return MIMGPU_OK;
+}
+}  // namespace
+
+int mimgpu_session_set_l2_prefetch(mimgpu_session *s, int64_t bytes_per_sm) {
+    if (!s || bytes_per_sm < 0 || bytes_per_sm > (1 << 24) || bytes_per_sm % 16) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = drop_graphs(s);
+    if (rc) return rc;
+    for (int i = 0; i < 5; i++) {
+        s->prefetch_next[i] = (uint32_t)bytes_per_sm;
+        s->prefetch_skip[i] = 0;
+    }
+    return MIMGPU_OK;
+}
+
+int mimgpu_session_set_fusions(mimgpu_session *s, unsigned mask) {
+    if (!s || (mask & ~MIMGPU_FUSE_NORM)) return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = drop_graphs(s);
+    if (rc) return rc;
+    s->fuse_norm = (mask & MIMGPU_FUSE_NORM) != 0;
+    return MIMGPU_OK;
+}
+
+int mimgpu_session_set_l2_prefetch_for(mimgpu_session *s, int kind, int distance, int64_t bytes_per_sm) {
+    if (!s || kind < 0 || kind > 4 || distance < 1 || distance > 2 || bytes_per_sm < 0 ||
+        bytes_per_sm > (1 << 24) || bytes_per_sm % 16)
+        return MIMGPU_EINVAL;
+    mimgpu_ctx *c = s->m->ctx;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    int rc = drop_graphs(s);
+    if (rc) return rc;
+    (distance == 1 ? s->prefetch_next : s->prefetch_skip)[kind] = (uint32_t)bytes_per_sm;
     return MIMGPU_OK;
 }
 

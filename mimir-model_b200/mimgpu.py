@@ -72,6 +72,8 @@ SIGNATURES = {
     "mimgpu_session_set_step_kernel": (I32, [P, I32]),
     "mimgpu_session_uses_step_kernel": (I32, [P]),
     "mimgpu_session_set_l2_prefetch": (I32, [P, I64]),
+    "mimgpu_session_set_l2_prefetch_for": (I32, [P, I32, I32, I64]),
+    "mimgpu_session_set_fusions": (I32, [P, C.c_uint]),
     "mimgpu_session_step_kernels": (I32, [P]),
     "mimgpu_session_trace_bytes": (SZ, [P]),
     "mimgpu_session_set_trace": (I32, [P, P, SZ]),
@@ -504,6 +506,17 @@ class Session:
     def set_l2_prefetch(self, bytes_per_sm: int):
         """L2 prefetch of the next decode GEMV's weights (0 = off)."""
         self.m.ctx._check(lib().mimgpu_session_set_l2_prefetch(self.h, int(bytes_per_sm)))
+
+    def set_fusions(self, norm: bool = True):
+        """rms_norm of one-token steps inside the GEMVs that read it, or as a
+        kernel of its own; the results are the same bits either way."""
+        self.m.ctx._check(lib().mimgpu_session_set_fusions(self.h, 1 if norm else 0))
+
+    def set_l2_prefetch_for(self, kind: int, distance: int, bytes_per_sm: int):
+        """L2 prefetch of decode GEMV `kind` (0 q|k|v, 1 o, 2 gate|up, 3 down,
+        4 head) by the GEMV `distance` (1 or 2) launches before it."""
+        self.m.ctx._check(lib().mimgpu_session_set_l2_prefetch_for(self.h, int(kind), int(distance),
+                                                                   int(bytes_per_sm)))
 
     @property
     def uses_step_kernel(self) -> bool:

@@ -11,6 +11,9 @@ Bars (gsoultan/mimir-model):
       reference (the a8 products are bit-exact; attention is the only
       tolerance-level step) over 64 steps at 8B layer shapes.
 """
+import os
+import sys
+
 import numpy as np
 import pytest
 
@@ -162,16 +165,19 @@ def test_8b_layer_shapes_token_identity(ctx):
 def test_refused_rows_same_in_step_and_prompt(ctx):
     """Weight rows with a non-finite block scale take the f32 product
     (linearA8, interp/fast.go:282-379) on every path: a one-token step, whose
-    GEMVs normalise their own activation row (fused rms_norm), gives the same
-    logits bit for bit as the same token as the last row of a prompt pass,
-    whose rms_norm is a kernel of its own."""
+    GEMVs normalise their own activation row (fused rms_norm) and add the
+    residual read at their start, gives the same logits bit for bit as the
+    same token as the last row of a prompt pass, whose rms_norm is a kernel
+    of its own."""
     import mimgpu
     cfg, w = _synthetic(2, 512, 4, 2, 1024, 700, seed=7)
     rb = {O.Q4_K: 144, O.Q6_K: 210}
-    for name, row in (("blk.0.attn_q.weight", 5), ("blk.1.ffn_gate.weight", 100), ("output.weight", 17)):
+    for name, row in (("blk.0.attn_q.weight", 5), ("blk.1.ffn_gate.weight", 100), ("blk.0.ffn_up.weight", 513),
+                      ("blk.1.ffn_down.weight", 33), ("output.weight", 17)):
         dt, arr = w[name]
         b = bytearray(arr.tobytes())
-        o = row * (512 // 256) * rb[dt] + (0 if dt == O.Q4_K else 208)
+        k = 1024 if "ffn_down" in name else 512
+        o = row * (k // 256) * rb[dt] + (0 if dt == O.Q4_K else 208)
         b[o:o + 2] = bytes([0x00, 0x7C])  # d = +inf in the row's first block
         w[name] = (dt, np.frombuffer(bytes(b), np.uint8))
     C = 64
@@ -218,3 +224,34 @@ def test_tiny_llama_from_the_importers_mim_file(ctx, tiny):
     m.free()
     s2.free()
     m2.free()
+
+
+@pytest.mark.parametrize("shape,layers", [("8b", 2), ("70b", 1)])
+def test_fused_norm_bit_identical(ctx, shape, layers):
+    """One-token steps with each rms_norm inside the GEMV that reads it (the
+    default) and as a kernel of its own: logits bit for bit and greedy ids
+    identical, at the 8B and 70B layer dimensions."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    cfg = dict(bench.SHAPES[shape], layers=layers, vocab=4096)
+    C, P = 64, 12
+    m, weights = bench.build_model(ctx, cfg, C, P)
+    ids = bench.prompt_ids(cfg["vocab"], P, seed=9)
+    sess = []
+    for norm in (True, False):
+        s = m.session()
+        s.set_fusions(norm=norm)
+        s.run(ids, np.arange(P))
+        sess.append(s)
+    tok = 5
+    for i in range(3):
+        a, b = (s.run([tok], [P + i])[0] for s in sess)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), P + i
+        tok = int(np.argmax(a))
+    ga, gb = (s.generate(tok, P + 3, 16).tolist() for s in sess)
+    assert ga == gb
+    for s in sess:
+        s.free()
+    m.free()
+    for _, t in weights.values():
+        t.free()
