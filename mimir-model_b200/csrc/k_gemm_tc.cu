@@ -8,28 +8,29 @@
 // block-ordered f32 chain tot = fma(float(S), d*dx, tot),
 // off = fma(float(M), dmin*dx, off), result tot - off.
 //
-// A CTA owns 128 weight rows (TMEM lanes) x 64 activation rows.  For every
-// 256-element block the rows' quants become int8 "digit planes" whose
-// products with the int8 activations are exact MMA operands, and
-// tcgen05.mma kind::i8 (M 128, N 64, K 32) sums each plane over the block
-// into TMEM:
+// A CTA owns 128 weight rows (TMEM lanes) x NT activation rows (NT = 64, or
+// 32 for launches of 16-32 rows).  For every 256-element block the rows'
+// quants become int8 "digit planes" whose products with the int8
+// activations are exact MMA operands, and tcgen05.mma kind::i8 (M 128,
+// N NT, K 32) sums each plane over the block into TMEM:
 //   Q4_K  sc = lo + 8 hi (3-bit digits): planes q*lo, q*hi in [0, 105] and
 //         the sub-block mins m in [0, 63]:  S = P0 + 8 P1,  M = P2;
 //   Q6_K  sc = d0 + 8 d1 + 64 d2 (digits in [-3, 4]): planes (q-32)*d in
 //         [-128, 124]:  S = P0 + 8 P1 + 64 P2.
-// Data flow per block: one control thread (warp 0) fetches the tile's raw
-// weight blocks and the activation tile of the block by TMA into a 4-slot
-// input ring (refilled a quarter block after a slot's MMAs are done);
-// warps 1-4 (one weight row per thread, the thread's TMEM lane) unpack
-// their rows a quarter block at a time into the planes, written straight
-// into TMEM with tcgen05.st (two stages of 3 x 16 columns), so the MMA reads
-// A from TMEM and only the activation tile from shared memory; once every
-// decoder has filled a stage, the control thread issues its 6 MMAs into one
-// of two TMEM accumulator sets and commits them to the barriers that free
-// the stage, the input slot and hand the set on; warps 5-12 (one row and 32
+// Data flow per block: the tile's raw weight blocks and the block's
+// activation tile arrive by TMA in a 4-slot input ring; warps 1-4 (one
+// weight row per thread, the thread's TMEM lane) unpack their rows a
+// quarter block at a time into the planes, written straight into TMEM with
+// tcgen05.st (two plane stages of one quarter, or of half a block when
+// NT = 32), so the MMA reads A from TMEM and only the activation tile from
+// shared memory; once every decoder has filled a stage, the MMA thread
+// (warp 0) issues its MMAs into one of two TMEM accumulator sets and
+// commits them to the barriers that free the stage and hand the set on; it
+// never waits on the tensor pipe itself.  Warps 5-12 (one row and NT/2
 // activation rows per thread) read the sums back with tcgen05.ld, convert
 // them exactly and continue the block-ordered chain in registers, and
-// write the outputs at the end (bias, residual, refused pairs).
+// write the outputs at the end (bias, residual, refused pairs); one of them
+// refills each input slot as soon as its block's MMAs are complete.
 // Every wait is bounded (2 s, or sooner once another role has given up):
 // the kernel then sets DEV_TIMEOUT, drains the MMAs it issued, frees TMEM
 // and returns.
@@ -48,33 +49,54 @@ void *tmap_encode_fn();  // cuTensorMapEncodeTiled from the driver (k_gemv_a8.cu
 namespace {
 
 constexpr int TM = 128;                          // weight rows per CTA = MMA M = TMEM lanes
-constexpr int NT = 64;                           // activation rows per CTA = MMA N
+constexpr int kNTMax = 64;                       // activation rows per CTA = MMA N: 64, or 32 for 16-32 rows
 constexpr int kPlanes = 3;
 constexpr int kQuarter = 64;                     // K elements per plane stage
-constexpr int kStages = 2;                       // plane stages in TMEM
+constexpr int kMaxStages = 4;                    // plane stages in TMEM (TcCfg::kStages)
 constexpr int kNin = 4;                          // input ring slots
 constexpr int kRawPitch = 240;                   // Q6_K box width: a 210-byte block from its 16-byte boundary
-constexpr int kBBlock = NT * 256;                // activation tile of one block: two 128-byte-swizzled boxes
-constexpr int kInQ4 = TM * 144 + kBBlock;        // input slot: raw rows, then the activation tile
-constexpr int kInQ6 = TM * kRawPitch + kBBlock;
 constexpr int kMeta = 4;                         // per-block scale ring between decoders and epilogue
 constexpr int kDec = 128, kEpi = 256;
 constexpr int kThreads = 32 + kDec + kEpi;
-constexpr int kEpiTok = NT / 2;                  // activation rows per epilogue thread
-constexpr uint32_t kAccCols = kPlanes * NT;      // one accumulator set
-constexpr uint32_t kACol0 = 2 * kAccCols;        // plane stages after the two accumulator sets
 constexpr uint32_t kAStageCols = kPlanes * kQuarter / 4;  // 4 int8 per 32-bit column
 constexpr uint32_t kTmemCols = 512;
-static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "TMEM columns");
+constexpr int kOffMeta = 256;
+constexpr int kOffIn = 7168;
+
+// The shapes that depend on the activation tile NT.  With NT = 32 the two
+// accumulator sets take 192 TMEM columns, which leaves room for plane
+// stages of half a block.
+template <int NT>
+struct TcCfg {
+    // kStages plane stages of kGroup quarters each: with NT = 32 a stage is
+    // half a block, so the MMA thread waits and commits once per 12 MMAs
+    static constexpr int kStages = 2;
+    static constexpr int kGroup = NT == 32 ? 2 : 1;
+    static constexpr int kBBlock = NT * 256;     // activation tile of one block: two 128-byte-swizzled boxes
+    static constexpr int kInQ4 = TM * 144 + kBBlock;  // input slot: raw rows, then the activation tile
+    static constexpr int kInQ6 = TM * kRawPitch + kBBlock;
+    static constexpr int kEpiTok = NT / 2;       // activation rows per epilogue thread
+    static constexpr uint32_t kAccCols = kPlanes * NT;  // one accumulator set
+    static constexpr uint32_t kACol0 = 2 * kAccCols;    // plane stages after the two accumulator sets
+    static constexpr int kSmem = kOffIn + kNin * kInQ6;
+    // kind::i8 instruction descriptor: D s32, A and B signed 8-bit, K-major, N = NT, M = TM
+    static constexpr uint32_t kIdesc =
+        (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+    static_assert(NT == 32 || NT == 64, "activation tile");
+    static_assert(kStages <= kMaxStages, "plane stages");
+    static_assert(kACol0 + kStages * kGroup * kAStageCols <= kTmemCols, "TMEM columns");
+    static_assert(kOffIn % 1024 == 0 && kInQ4 % 1024 == 0 && kInQ6 % 1024 == 0, "alignment");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
 
 struct Meta {
     float d[TM], dmin[TM];
-    float dx[NT];
-    int ok[NT];
+    float dx[kNTMax];
+    int ok[kNTMax];
 };
 
 struct Bars {
-    uint64_t full[kStages], empty[kStages];
+    uint64_t full[kMaxStages], empty[kMaxStages];
     uint64_t accfull[2], accempty[2];
     uint64_t infull[kNin], inempty[kNin];
     uint64_t metafull[kMeta], metaempty[kMeta];
@@ -83,13 +105,8 @@ struct Bars {
     int abort;
 };
 
-constexpr int kOffMeta = 256;
-constexpr int kOffIn = 7168;
-constexpr int kSmemTc = kOffIn + kNin * kInQ6;
 static_assert(sizeof(Bars) <= kOffMeta, "barrier block");
 static_assert(kOffMeta + kMeta * (int)sizeof(Meta) <= kOffIn, "meta ring");
-static_assert(kOffIn % 1024 == 0 && kInQ4 % 1024 == 0 && kInQ6 % 1024 == 0, "alignment");
-static_assert(kSmemTc <= 227 * 1024, "shared memory");
 
 struct TcParams {
     CUtensorMap tmap[kMaxSegs];  // raw weights [n, row bytes] u8, box [box width, 128]
@@ -125,10 +142,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
            (2ull << 61);
 }
 
-// kind::i8 instruction descriptor: D s32, A and B signed 8-bit, K-major, N = NT, M = TM
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
-
-// D (TMEM) += A (TMEM: lane = row, 4 int8 of K per column) x B (shared memory)
+// D (TMEM) += A (TMEM: lane = row, 4 int8 of K per column) x B (shared memory);
+// kIdesc: the kind::i8 instruction descriptor (TcCfg)
+template <uint32_t kIdesc>
 __device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -290,10 +306,10 @@ __device__ __forceinline__ void decode_q6k_quarter(const uint8_t *win, int sh, i
     tmem_st16(ta + 2 * kQuarter / 4, w[2]);
 }
 
-// One block of the chain for the thread's row and its 32 activation rows:
+// One block of the chain for the thread's row and its NT/2 activation rows:
 // the block sums from TMEM (accumulator columns from `col`, this warp's
 // lanes), converted exactly and folded in block order.
-template <bool Q4>
+template <int NT, bool Q4, int kEpiTok = TcCfg<NT>::kEpiTok>
 __device__ __forceinline__ void epi_block(uint32_t col, const float *dxs, float d, float dmin,
                                           float (&tot)[kEpiTok], float (&off)[kEpiTok]) {
 #pragma unroll
@@ -341,14 +357,21 @@ __device__ __forceinline__ void tma_2d(const CUtensorMap *map, uint8_t *dst, int
         : "memory");
 }
 
+template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_constant__ TcParams p) {
+    using Cf = TcCfg<NT>;
+    constexpr int kStages = Cf::kStages, kGroup = Cf::kGroup, kBBlock = Cf::kBBlock, kInQ4 = Cf::kInQ4,
+                  kInQ6 = Cf::kInQ6;
+    constexpr int kGroups = 4 / kGroup;  // plane stages per block
+    constexpr int kEpiTok = Cf::kEpiTok;
+    constexpr uint32_t kAccCols = Cf::kAccCols, kACol0 = Cf::kACol0;
     extern __shared__ __align__(1024) uint8_t sm[];
     Bars &B = *(Bars *)sm;
     Meta *meta = (Meta *)(sm + kOffMeta);
     uint8_t *inring = sm + kOffIn;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    // the tile: segment, its 128 rows, the 64 activation rows
+    // the tile: segment, its 128 rows, the NT activation rows
     const int tile = blockIdx.y;
     int si = 0;
     while (si + 1 < p.nseg && tile >= p.seg_t0[si + 1]) si++;
@@ -402,20 +425,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
     const uint32_t tmem = B.tmem;
     pdl_launch_dependents();
 
+    // block kb's inputs into slot kb % nin: raw weights, then the activation tile
+    auto fetch_raw = [&](int kb) {
+        uint8_t *slot = inring + (kb % nin) * inbytes;
+        mbar_arrive_expect_tx(&B.infull[kb % nin], rawbox + (uint32_t)kBBlock);
+        tma_2d(map, slot, (kb * bb) & ~15, r0, &B.infull[kb % nin]);
+    };
+    auto fetch_act = [&](int kb) {  // two boxes of NT rows x 128 bytes
+        uint8_t *slot = inring + (kb % nin) * inbytes + TM * pitch;
+        tma_2d(&p.amap, slot, kb * 256, n0, &B.infull[kb % nin]);
+        tma_2d(&p.amap, slot + NT * 128, kb * 256 + 128, n0, &B.infull[kb % nin]);
+    };
     if (warp == 0) {
-        // ------------------------------------------- control: TMA and MMA issue
+        // ------------------------------------------------------- MMA issue
+        // (the input slots are refilled by the epilogue, which sees each
+        // block's MMAs complete: this thread never waits on the tensor pipe)
         if (lane == 0) {
-            // block kb's inputs into slot kb % nin: raw weights, then the activation tile
-            auto fetch_raw = [&](int kb) {
-                uint8_t *slot = inring + (kb % nin) * inbytes;
-                mbar_arrive_expect_tx(&B.infull[kb % nin], rawbox + (uint32_t)kBBlock);
-                tma_2d(map, slot, (kb * bb) & ~15, r0, &B.infull[kb % nin]);
-            };
-            auto fetch_act = [&](int kb) {  // two boxes of 64 rows x 128 bytes
-                uint8_t *slot = inring + (kb % nin) * inbytes + TM * pitch;
-                tma_2d(&p.amap, slot, kb * 256, n0, &B.infull[kb % nin]);
-                tma_2d(&p.amap, slot + NT * 128, kb * 256 + 128, n0, &B.infull[kb % nin]);
-            };
             for (int kb = 0; kb < min(nin, nb); kb++) fetch_raw(kb);  // weights are read-only
             pdl_wait();
             for (int kb = 0; kb < min(nin, nb); kb++) fetch_act(kb);
@@ -424,37 +449,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
             for (int kb = 0; kb < nb && ok; kb++) {
                 const int j = kb % nin, b = kb & 1;
                 if (!wait_bar(&B.accempty[b], ((kb >> 1) & 1) ^ 1, B, p.status)) break;
-                for (int qi = 0; qi < 4; qi++) {
-                    const int i = 4 * kb + qi, s = i % kStages;
+                const uint32_t dcol = tmem + (uint32_t)(b * kAccCols);
+                for (int g = 0; g < kGroups; g++) {
+                    const int i = kGroups * kb + g, s = i % kStages;
                     if (!wait_bar(&B.full[s], (i / kStages) & 1, B, p.status)) {
                         ok = false;
                         break;
                     }
                     fence_after_sync();
-                    // quarter qi: box qi/2, bytes 64 (qi&1) + 32 ks of each 128-byte row
-                    const uint64_t bd = smem_desc_sw128(in0 + (uint32_t)(j * inbytes + (qi >> 1) * NT * 128 + (qi & 1) * 64));
-                    const uint32_t dcol = tmem + (uint32_t)(b * kAccCols), acol = tmem + kACol0 + (uint32_t)(s * kAStageCols);
 #pragma unroll
-                    for (int pl = 0; pl < kPlanes; pl++) {
-                        mma_i8_ts(dcol + pl * NT, acol + pl * (kQuarter / 4), bd, qi ? 1u : 0u);
-                        mma_i8_ts(dcol + pl * NT, acol + pl * (kQuarter / 4) + 8, bd + 2, 1u);  // + 32 bytes
+                    for (int u = 0; u < kGroup; u++) {
+                        const int qi = g * kGroup + u;
+                        // quarter qi: box qi/2, bytes 64 (qi&1) + 32 ks of each 128-byte row
+                        const uint64_t bd =
+                            smem_desc_sw128(in0 + (uint32_t)(j * inbytes + (qi >> 1) * NT * 128 + (qi & 1) * 64));
+                        const uint32_t acol = tmem + kACol0 + (uint32_t)((s * kGroup + u) * kAStageCols);
+#pragma unroll
+                        for (int pl = 0; pl < kPlanes; pl++) {
+                            mma_i8_ts<Cf::kIdesc>(dcol + pl * NT, acol + pl * (kQuarter / 4), bd, qi ? 1u : 0u);
+                            mma_i8_ts<Cf::kIdesc>(dcol + pl * NT, acol + pl * (kQuarter / 4) + 8, bd + 2,
+                                                  1u);  // + 32 bytes
+                        }
                     }
                     mma_commit(&B.empty[s]);
-                    if (qi == 3) {
-                        mma_commit(&B.accfull[b]);
-                    } else if (qi == 1 && kb >= 1 && kb - 1 + nin < nb) {
-                        // refill the previous block's slot once the decoders are done with
-                        // it and its MMAs have completed (the block's accumulator commit;
-                        // one commit fewer per block: each costs a pipeline drain)
-                        if (!wait_bar(&B.inempty[(kb - 1) % nin], ((kb - 1) / nin) & 1, B, p.status) ||
-                            !wait_bar(&B.accfull[(kb - 1) & 1], ((kb - 1) >> 1) & 1, B, p.status)) {
-                            ok = false;
-                            break;
-                        }
-                        fetch_raw(kb - 1 + nin);
-                        fetch_act(kb - 1 + nin);
-                    }
                 }
+                if (ok) mma_commit(&B.accfull[b]);
             }
             // every MMA issued has completed before TMEM is released
             mma_commit(&B.drain);
@@ -503,13 +522,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
             mbar_arrive(&B.metafull[ms]);
             bool ok = true;
             for (int qi = 0; qi < 4; qi++) {
-                const int i = 4 * kb + qi, s = i % kStages;
-                if (!__all_sync(0xFFFFFFFFu, wait_bar(&B.empty[s], ((i / kStages) & 1) ^ 1, B, p.status))) {
+                const int i = kGroups * kb + qi / kGroup, s = i % kStages, u = qi % kGroup;
+                if (u == 0 &&
+                    !__all_sync(0xFFFFFFFFu, wait_bar(&B.empty[s], ((i / kStages) & 1) ^ 1, B, p.status))) {
                     ok = false;
                     break;
                 }
-                fence_after_sync();
-                const uint32_t ta = ta0 + (uint32_t)(s * kAStageCols);
+                if (u == 0) fence_after_sync();
+                const uint32_t ta = ta0 + (uint32_t)((s * kGroup + u) * kAStageCols);
                 if (q4) {
                     decode_q4k_quarter(win, qi, ta);
                 } else {
@@ -521,9 +541,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                     default: decode_q6k_quarter<3>(win, sh, qi, ta); break;
                     }
                 }
-                tmem_wait_st();
-                fence_before_sync();
-                mbar_arrive(&B.full[s]);
+                if (u == kGroup - 1) {  // the stage is written: its MMAs may go
+                    tmem_wait_st();
+                    fence_before_sync();
+                    mbar_arrive(&B.full[s]);
+                }
             }
             if (!ok) break;
             mbar_arrive(&B.inempty[j]);  // this thread is done with the slot's raw rows
@@ -550,14 +572,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                 break;
             }
             fence_after_sync();
+            if (warp == 5 && kb + nin < nb) {
+                // block kb's MMAs are complete, so its slot's activation tile is
+                // free; once the decoders are done with its raw rows (long
+                // before), the slot takes block kb + nin
+                if (lane == 0 && wait_bar(&B.inempty[kb % nin], (kb / nin) & 1, B, p.status)) {
+                    fetch_raw(kb + nin);
+                    fetch_act(kb + nin);
+                }
+                __syncwarp();
+            }
             const Meta &m = meta[ms];
             const float d = m.d[r], dmin = m.dmin[r];
             rowbad |= !isfinite(d) || !isfinite(dmin);
             const uint32_t col = lane_base + (uint32_t)(b * kAccCols);
             if (dt == Q4_K)
-                epi_block<true>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
+                epi_block<NT, true>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
             else
-                epi_block<false>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
+                epi_block<NT, false>(col, m.dx + th * kEpiTok, d, dmin, tot, off);
             fence_before_sync();
             mbar_arrive(&B.accempty[b]);
 #pragma unroll
@@ -622,9 +654,9 @@ bool raw_tmap(const GemvSeg &sg, long long K, CUtensorMap *out) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// [rows, K] u8 map of the activation quants, box [128 bytes, 64 rows] in the
+// [rows, K] u8 map of the activation quants, box [128 bytes, NT rows] in the
 // 128-byte swizzle: one box is the MMA's B operand for half a block
-bool act_tmap(const int8_t *q, int rows, long long K, CUtensorMap *out) {
+bool act_tmap(const int8_t *q, int rows, long long K, int NT, CUtensorMap *out) {
     const EncodeTiledFn fn = (EncodeTiledFn)tmap_encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
@@ -652,7 +684,12 @@ bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, lo
 cudaError_t gemm_a8_tc_prepare() {
     static std::atomic<unsigned long long> done{0};
     return once_per_device(done, [] {
-        return cudaFuncSetAttribute(gemm_a8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+        cudaError_t e = cudaFuncSetAttribute(gemm_a8_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             TcCfg<64>::kSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_a8_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     TcCfg<32>::kSmem);
+        return e;
     });
 }
 
@@ -670,7 +707,10 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
     }
     p.seg_t0[nseg] = t;
     if (t == 0) return cudaSuccess;
-    if (!act_tmap(act.q, rows, K, &p.amap)) return cudaErrorInvalidValue;
+    // 16-32 activation rows: one tile of 32 (half the MMA work of 64, and
+    // deeper plane staging); more: tiles of 64
+    const int NT = rows <= 32 ? 32 : 64;
+    if (!act_tmap(act.q, rows, K, NT, &p.amap)) return cudaErrorInvalidValue;
     p.act = act;
     p.x = x;
     p.rows = rows;
@@ -683,13 +723,13 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
     cudaLaunchAttribute at[1];
     cfg.gridDim = dim3((rows + NT - 1) / NT, t);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemTc;
+    cfg.dynamicSmemBytes = NT == 32 ? TcCfg<32>::kSmem : TcCfg<64>::kSmem;
     cfg.stream = st;
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel, p);
+    return NT == 32 ? cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<32>, p) : cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<64>, p);
 }
 
 }  // namespace mimgpu
