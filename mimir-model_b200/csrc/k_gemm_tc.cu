@@ -36,6 +36,7 @@
 // and returns.
 #include <cuda.h>  // CUtensorMap (types only)
 
+#include <algorithm>
 #include <cstdint>
 
 #include "a8_refused.cuh"
@@ -120,6 +121,12 @@ struct TcParams {
     long long K;
     int nb;
     unsigned *status;
+    // split launches (REC): each CTA's exact block sums (S, M) go to
+    // rec[seg_rec0[s] + (kb * rows + t) * n_s + row] and the row's block
+    // scales (d, dmin) to dd[seg_dd0[s] + kb * n_s + row], for the chain kernel
+    int2 *rec;
+    float2 *dd;
+    long long seg_rec0[kMaxSegs], seg_dd0[kMaxSegs];
 };
 
 // byte offset of (row, 16-byte K chunk c) in a K-major no-swizzle operand of
@@ -357,7 +364,10 @@ __device__ __forceinline__ void tma_2d(const CUtensorMap *map, uint8_t *dst, int
         : "memory");
 }
 
-template <int NT>
+// REC: a split launch (gridDim.z parts of the K axis): the epilogue stores
+// each block's exact sums to p.rec instead of folding them; the chain
+// kernel then runs the block-ordered fused multiply-adds.
+template <int NT, bool REC>
 __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_constant__ TcParams p) {
     using Cf = TcCfg<NT>;
     constexpr int kStages = Cf::kStages, kGroup = Cf::kGroup, kBBlock = Cf::kBBlock, kInQ4 = Cf::kInQ4,
@@ -385,7 +395,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
         }
     const int r0 = (tile - p.seg_t0[si]) * TM, nrow = min(TM, sg.n - r0);
     const int n0 = blockIdx.x * NT, ntok = min(NT, p.rows - n0);
-    const int dt = sg.dt, bb = block_bytes(dt), nb = p.nb;
+    const int dt = sg.dt, bb = block_bytes(dt);
+    // this CTA's blocks [kb0, kb0 + nb) of the K axis: all of them, or its
+    // part of a split launch (REC); loops run over the local index kb
+    const int kb0 = REC ? (int)((long long)p.nb * blockIdx.z / gridDim.z) : 0;
+    const int nb = REC ? (int)((long long)p.nb * (blockIdx.z + 1) / gridDim.z) - kb0 : p.nb;
     const bool q4 = dt == Q4_K;
     const int pitch = q4 ? 144 : kRawPitch;      // raw box width = row pitch in the slot
     const int nin = kNin;
@@ -429,12 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
     auto fetch_raw = [&](int kb) {
         uint8_t *slot = inring + (kb % nin) * inbytes;
         mbar_arrive_expect_tx(&B.infull[kb % nin], rawbox + (uint32_t)kBBlock);
-        tma_2d(map, slot, (kb * bb) & ~15, r0, &B.infull[kb % nin]);
+        tma_2d(map, slot, ((kb0 + kb) * bb) & ~15, r0, &B.infull[kb % nin]);
     };
     auto fetch_act = [&](int kb) {  // two boxes of NT rows x 128 bytes
         uint8_t *slot = inring + (kb % nin) * inbytes + TM * pitch;
-        tma_2d(&p.amap, slot, kb * 256, n0, &B.infull[kb % nin]);
-        tma_2d(&p.amap, slot + NT * 128, kb * 256 + 128, n0, &B.infull[kb % nin]);
+        tma_2d(&p.amap, slot, (kb0 + kb) * 256, n0, &B.infull[kb % nin]);
+        tma_2d(&p.amap, slot + NT * 128, (kb0 + kb) * 256 + 128, n0, &B.infull[kb % nin]);
     };
     if (warp == 0) {
         // ------------------------------------------------------- MMA issue
@@ -489,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
         float dx_next = 0.f;
         int ok_next = 1;
         if (r < ntok) {
-            dx_next = p.act.dx[(long long)(n0 + r) * nb];
-            ok_next = p.act.ok[(long long)(n0 + r) * nb];
+            dx_next = p.act.dx[(long long)(n0 + r) * p.nb + kb0];
+            ok_next = p.act.ok[(long long)(n0 + r) * p.nb + kb0];
         }
         for (int kb = 0; kb < nb; kb++) {
             const int j = kb % nin, ms = kb % kMeta;
@@ -498,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
             const bool got = wait_bar(&B.infull[j], (kb / nin) & 1, B, p.status) &&
                              wait_bar(&B.metaempty[ms], ((kb / kMeta) & 1) ^ 1, B, p.status);
             if (!__all_sync(0xFFFFFFFFu, got)) break;
-            const int ph = (kb * bb) & 15;
+            const int ph = ((kb0 + kb) * bb) & 15;
             const uint8_t *win = inring + j * inbytes + r * pitch;
             // per-block scales of the row and of the activation rows
             Meta &m = meta[ms];
@@ -515,8 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                 m.dx[r] = dx_next;
                 m.ok[r] = ok_next;
                 if (r < ntok && kb + 1 < nb) {
-                    dx_next = p.act.dx[(long long)(n0 + r) * nb + kb + 1];
-                    ok_next = p.act.ok[(long long)(n0 + r) * nb + kb + 1];
+                    dx_next = p.act.dx[(long long)(n0 + r) * p.nb + kb0 + kb + 1];
+                    ok_next = p.act.ok[(long long)(n0 + r) * p.nb + kb0 + kb + 1];
                 }
             }
             mbar_arrive(&B.metafull[ms]);
@@ -582,6 +596,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                 }
                 __syncwarp();
             }
+            if (REC) {
+                // the block's exact sums of the row and its NT/2 activation rows
+                static_assert(!REC || kEpiTok == 16, "records from one 16-column load per plane");
+                const uint32_t col = lane_base + (uint32_t)(b * kAccCols);
+                uint32_t a0[16], a1[16], a2[16];
+                tmem_ld16(col, a0);
+                tmem_ld16(col + NT, a1);
+                tmem_ld16(col + 2 * NT, a2);
+                tmem_wait_ld();
+                fence_before_sync();
+                mbar_arrive(&B.accempty[b]);
+                if (r < nrow) {
+                    if (th == 0) {
+                        const Meta &m = meta[ms];
+                        p.dd[p.seg_dd0[si] + (long long)(kb0 + kb) * sg.n + r0 + r] = make_float2(m.d[r], m.dmin[r]);
+                    }
+                    int2 *rc = p.rec + p.seg_rec0[si] + ((long long)(kb0 + kb) * p.rows + n0 + th * kEpiTok) * sg.n + r0 + r;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (th * kEpiTok + j >= ntok) break;
+                        const int S = q4 ? (int)(a0[j] + 8u * a1[j]) : (int)(a0[j] + 8u * a1[j] + 64u * a2[j]);
+                        rc[(long long)j * sg.n] = make_int2(S, q4 ? (int)a2[j] : 0);
+                    }
+                }
+                mbar_arrive(&B.metaempty[ms]);
+                continue;
+            }
             const Meta &m = meta[ms];
             const float d = m.d[r], dmin = m.dmin[r];
             rowbad |= !isfinite(d) || !isfinite(dmin);
@@ -597,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                 if (!m.ok[th * kEpiTok + n]) tokbad |= 1u << n;
             mbar_arrive(&B.metaempty[ms]);
         }
-        if (__all_sync(0xFFFFFFFFu, done)) {
+        if (!REC && __all_sync(0xFFFFFFFFu, done)) {
             // outputs: tot - off (+ bias, + residual) ...
             const int grow = r0 + r, t0 = n0 + th * kEpiTok, nt = min(kEpiTok, ntok - th * kEpiTok);
             if (r < nrow && !rowbad) {
@@ -620,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_a8_tc_kernel(const __grid_co
                     for (int n = 0; n < nt; n++) {
                         if (!(badr >> rr & 1u) && !(tokbad >> n & 1u)) continue;
                         float v = row_dot_f32(dt, sg.w + (long long)gr * row_bytes(dt, p.K),
-                                              p.x + (long long)(t0 + n) * p.K, nb);
+                                              p.x + (long long)(t0 + n) * p.K, p.nb);
                         if (sg.bias) v = __fadd_rn(v, sg.bias[gr]);
                         if (sg.res) v = __fadd_rn(sg.res[(long long)(t0 + n) * sg.ldy + gr], v);
                         if (lane == 0) sg.y[(long long)(t0 + n) * sg.ldy + gr] = v;
@@ -668,7 +709,107 @@ bool act_tmap(const int8_t *q, int rows, long long K, int NT, CUtensorMap *out) 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The second half of a split launch: for every (weight row, activation
+// row) pair, the block-ordered chain of dotQ8KRef over the records of the
+// split CTAs -- tot = fma(float(S), d*dx, tot), off = fma(float(M),
+// dmin*dx, off) -- then bias and residual, exactly as the unsplit
+// epilogue; pairs either side refuses take the f32 product.  A CTA is 32
+// consecutive weight rows (the lanes) x 8 activation rows (the warps).
+struct ChainParams {
+    GemvSeg seg[kMaxSegs];
+    int seg_n0[kMaxSegs + 1];      // first row of each segment in the launch's row order
+    long long seg_rec0[kMaxSegs];  // its records in rec
+    long long seg_dd0[kMaxSegs];   // its block scales in dd
+    int nseg;
+    const int2 *rec;
+    const float2 *dd;
+    ActQ8 act;
+    const float *x;
+    int rows;
+    long long K;
+    int nb;
+};
+
+__global__ void __launch_bounds__(256) gemm_a8_chain_kernel(const __grid_constant__ ChainParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.y * 8 + (threadIdx.x >> 5);  // warp-uniform
+    const int gn = blockIdx.x * 32 + lane;
+    const int total = p.seg_n0[p.nseg];
+    auto seg_of = [&](int g) {
+        int si = 0;
+        while (si + 1 < p.nseg && g >= p.seg_n0[si + 1]) si++;
+        return si;
+    };
+    const bool valid = gn < total && t < p.rows;
+    const int si = valid ? seg_of(gn) : 0;
+    const GemvSeg &sg = p.seg[si];
+    const int n = gn - p.seg_n0[si];
+    float tot = 0.f, off = 0.f;
+    bool bad = false;
+    if (valid) {
+        const bool q4 = sg.dt == Q4_K;
+        const int2 *rc = p.rec + p.seg_rec0[si] + (long long)t * sg.n + n;
+        const float2 *ddp = p.dd + p.seg_dd0[si] + n;
+        const long long kstride = (long long)p.rows * sg.n;
+        const float *dxs = p.act.dx + (long long)t * p.nb;
+        const int *oks = p.act.ok + (long long)t * p.nb;
+#pragma unroll 8
+        for (int kb = 0; kb < p.nb; kb++) {
+            const int2 v = __ldcg(rc + kb * kstride);
+            const float2 sc = __ldcg(ddp + (long long)kb * sg.n);
+            const float dx = dxs[kb];
+            const float d = sc.x, dmin = sc.y;
+            bad |= !isfinite(d) || !isfinite(dmin) || !oks[kb];
+            tot = __fmaf_rn(__int2float_rn(v.x), __fmul_rn(d, dx), tot);
+            if (q4) off = __fmaf_rn(__int2float_rn(v.y), __fmul_rn(dmin, dx), off);
+        }
+        if (!bad) {
+            float r = __fsub_rn(tot, off);
+            if (sg.bias) r = __fadd_rn(r, sg.bias[n]);
+            if (sg.res) r = __fadd_rn(sg.res[(long long)t * sg.ldy + n], r);
+            sg.y[(long long)t * sg.ldy + n] = r;
+        }
+    }
+    // refused pairs: the warp-collective f32 product of the GEMV and the GEMM
+    unsigned rm = __ballot_sync(0xFFFFFFFFu, valid && bad);
+    while (rm) {
+        const int i = __ffs(rm) - 1;
+        rm &= rm - 1;
+        const int gi = blockIdx.x * 32 + i, sj = seg_of(gi);
+        const GemvSeg &sgi = p.seg[sj];
+        const int ni = gi - p.seg_n0[sj];
+        float r = row_dot_f32(sgi.dt, sgi.w + (long long)ni * row_bytes(sgi.dt, p.K), p.x + (long long)t * p.K, p.nb);
+        if (sgi.bias) r = __fadd_rn(r, sgi.bias[ni]);
+        if (sgi.res) r = __fadd_rn(sgi.res[(long long)t * sgi.ldy + ni], r);
+        if (lane == 0) sgi.y[(long long)t * sgi.ldy + ni] = r;
+    }
+}
+
+// The K split of a launch of `tiles` row tiles and nb blocks: parts of at
+// least 4 blocks that fill the SMs, when one part per tile leaves more
+// than half of them idle; 1 = no split.
+int split_parts(int tiles, int nb) {
+    const int sms = num_sms();
+    if (tiles <= 0 || 2 * tiles > sms) return 1;
+    return std::max(1, std::min({sms / tiles, nb / 4, 8}));
+}
+
 }  // namespace
+
+size_t gemm_a8_split_bytes(const GemvSeg *segs, int nseg, int rows, long long K) {
+    if (rows < kTcMinRows || rows > 32 || K <= 0 || K % 256 || nseg <= 0 || nseg > kMaxSegs) return 0;
+    int tiles = 0;
+    long long n = 0;
+    for (int i = 0; i < nseg; i++) {
+        tiles += (segs[i].n + TM - 1) / TM;
+        n += segs[i].n;
+    }
+    if (split_parts(tiles, (int)(K / 256)) < 2) return 0;
+    // records, then the block scales
+    return (size_t)n * (size_t)(K / 256) * ((size_t)rows * sizeof(int2) + sizeof(float2));
+}
 
 bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, long long K) {
     if (rows < kTcMinRows || K <= 0 || K % 256 || nseg <= 0 || nseg > kMaxSegs) return false;
@@ -684,17 +825,20 @@ bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, lo
 cudaError_t gemm_a8_tc_prepare() {
     static std::atomic<unsigned long long> done{0};
     return once_per_device(done, [] {
-        cudaError_t e = cudaFuncSetAttribute(gemm_a8_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             TcCfg<64>::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_a8_tc_kernel<64, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<64>::kSmem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_a8_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            e = cudaFuncSetAttribute(gemm_a8_tc_kernel<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     TcCfg<32>::kSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_a8_tc_kernel<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      TcCfg<32>::kSmem);
         return e;
     });
 }
 
 cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                              unsigned *status, cudaStream_t st, bool pdl) {
+                              unsigned *status, cudaStream_t st, bool pdl, const GemmSplit *split) {
     if (!gemm_a8_tc_ok(segs, nseg, act, rows, K)) return cudaErrorInvalidValue;
     TcParams p = {};
     p.nseg = nseg;
@@ -719,9 +863,13 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
     p.status = status;
     cudaError_t e = gemm_a8_tc_prepare();
     if (e != cudaSuccess) return e;
+    // few row tiles: split K over more CTAs when the caller gave room for
+    // their records (records of n x rows x nb block sums)
+    const size_t need = gemm_a8_split_bytes(segs, nseg, rows, K);
+    const int parts = (need && split && split->rec && split->bytes >= need) ? split_parts(t, p.nb) : 1;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
-    cfg.gridDim = dim3((rows + NT - 1) / NT, t);
+    cfg.gridDim = dim3((rows + NT - 1) / NT, t, parts);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = NT == 32 ? TcCfg<32>::kSmem : TcCfg<64>::kSmem;
     cfg.stream = st;
@@ -729,7 +877,48 @@ cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, Act
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    return NT == 32 ? cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<32>, p) : cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<64>, p);
+    if (parts < 2)
+        return NT == 32 ? cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<32, false>, p)
+                        : cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<64, false>, p);
+    ChainParams c = {};
+    long long r0 = 0;
+    int n0 = 0;
+    for (int i = 0; i < nseg; i++) {
+        p.seg_rec0[i] = c.seg_rec0[i] = r0;
+        r0 += (long long)segs[i].n * rows * p.nb;
+        c.seg[i] = segs[i];
+        c.seg_n0[i] = n0;
+        n0 += segs[i].n;
+    }
+    c.seg_n0[nseg] = n0;
+    long long d0 = 0;
+    for (int i = 0; i < nseg; i++) {
+        p.seg_dd0[i] = c.seg_dd0[i] = d0;
+        d0 += (long long)segs[i].n * p.nb;
+    }
+    c.nseg = nseg;
+    p.rec = split->rec;
+    c.rec = split->rec;
+    // the scales after the records (8-byte aligned: records are 8 bytes each)
+    p.dd = (float2 *)(split->rec + r0);
+    c.dd = p.dd;
+    c.act = act;
+    c.x = x;
+    c.rows = rows;
+    c.K = K;
+    c.nb = p.nb;
+    cudaError_t e2 = cudaLaunchKernelEx(&cfg, gemm_a8_tc_kernel<32, true>, p);
+    if (e2 != cudaSuccess) return e2;
+    cudaLaunchConfig_t cc = {};
+    cudaLaunchAttribute ca[1];
+    cc.gridDim = dim3((n0 + 31) / 32, (rows + 7) / 8);
+    cc.blockDim = dim3(256);
+    cc.stream = st;
+    ca[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    ca[0].val.programmaticStreamSerializationAllowed = 1;
+    cc.attrs = ca;
+    cc.numAttrs = 1;  // the records come from the launch just before, which it waits for
+    return cudaLaunchKernelEx(&cc, gemm_a8_chain_kernel, c);
 }
 
 }  // namespace mimgpu

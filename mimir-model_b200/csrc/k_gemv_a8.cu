@@ -708,14 +708,14 @@ cudaError_t gemv_a8_prepare() {
 
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
                            unsigned *status, cudaStream_t st, bool pdl, bool cache_maps, const P2P *put,
-                           const GemvPrefetch *pf, const GemvNorm *nrm) {
+                           const GemvPrefetch *pf, const GemvNorm *nrm, const GemmSplit *split) {
     if (nseg <= 0 || nseg > kMaxSegs || K % 256 != 0 || rows < 0) return cudaErrorInvalidValue;
     if (put && put->N > 1 && (rows != 1 || nseg != 1)) return cudaErrorInvalidValue;  // exchanges carry one row
     if (nrm && rows != 1) return cudaErrorInvalidValue;  // the fused norm makes one row
     if (rows == 0 || K == 0) return cudaSuccess;
     // many activation rows: the tensor-core GEMM (same results bit for bit)
     if ((!put || put->N <= 1) && gemm_a8_tc_ok(segs, nseg, act, rows, K))
-        return launch_gemm_a8_tc(segs, nseg, x, act, rows, K, status, st, pdl);
+        return launch_gemm_a8_tc(segs, nseg, x, act, rows, K, status, st, pdl, split);
     // one activation row: the slab-streaming kernel (same results bit for bit)
     if (rows == 1 && gemv_row_ok(segs, nseg, act, K))
         return launch_gemv_row(segs, nseg, x, act, K, status, st, pdl, put, pf, nrm);

@@ -53,6 +53,17 @@ struct GemvSeg {
 
 constexpr int kMaxSegs = 4;
 
+// Room for the records of a split launch: a launch of 16-32 activation rows
+// whose matrices have too few 128-row tiles to fill the SMs splits K over
+// several CTAs, which store their exact block sums (8 bytes per weight row,
+// activation row and block) for a second kernel that runs each pair's
+// block-ordered chain.  Without it (or when it is too small) the launch is
+// not split.  Same results bit for bit either way.
+struct GemmSplit {
+    int2 *rec;
+    size_t bytes;
+};
+
 // One exchange of a tensor-parallel step through peer memory (p2p.cuh):
 // N = 0 or 1 means none.  The producer stores into every rank's copy of a
 // buffer at arena offset `off` (+ column `col0`); the consumer publishes
@@ -125,14 +136,16 @@ struct GemvNorm {
 cudaError_t launch_gemv_a8(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
                            unsigned *status, cudaStream_t st, bool pdl, bool cache_maps = true,
                            const P2P *put = nullptr, const GemvPrefetch *pf = nullptr,
-                           const GemvNorm *nrm = nullptr);
+                           const GemvNorm *nrm = nullptr, const GemmSplit *split = nullptr);
 // The same product on the tensor cores (tcgen05 kind::i8) for launches of
 // at least kTcMinRows activation rows; launch_gemv_a8 dispatches to it.
 constexpr int kTcMinRows = 16;
 bool gemm_a8_tc_ok(const GemvSeg *segs, int nseg, const ActQ8 &act, int rows, long long K);
 cudaError_t gemm_a8_tc_prepare();
+// Bytes of records a launch of these matrices would split into (0: it would not split).
+size_t gemm_a8_split_bytes(const GemvSeg *segs, int nseg, int rows, long long K);
 cudaError_t launch_gemm_a8_tc(const GemvSeg *segs, int nseg, const float *x, ActQ8 act, int rows, long long K,
-                              unsigned *status, cudaStream_t st, bool pdl);
+                              unsigned *status, cudaStream_t st, bool pdl, const GemmSplit *split = nullptr);
 // The one-activation-row product (decode steps): one slab of consecutive
 // rows per SM, streamed with bulk copies; launch_gemv_a8 dispatches to it
 // when every matrix is a whole number of row units (the fewest rows whose

@@ -48,6 +48,7 @@ struct mimgpu_session {
     std::vector<void *> kc, vc;
     size_t cache_bytes = 0;
     float *scores = nullptr;  // score scratch of the many-row attention (prompt passes), or null
+    GemmSplit split{};        // records of split tensor-core GEMMs (16-32-row runs), or none
     void *arena = nullptr;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *qh = nullptr, *att = nullptr, *gu = nullptr, *a = nullptr;
     float *logits = nullptr;
@@ -297,7 +298,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
                                     a8 ? s->actE : none, st, pdl, (p2p && l > 0) ? &xin : nullptr));
         if (a8)
             CK(launch_gemv_a8(qkv, 3, s->h, s->actE, T, E, status, st, pdl, true, nullptr, next_pf(l, 0),
-                              f_attn ? &n_attn : nullptr));
+                              f_attn ? &n_attn : nullptr, &s->split));
         else CK(launch_gemv_f32(qkv, 3, s->h, T, E, st, pdl));
         AttnArgs2 aa{s->qh, s->kc[l], s->vc[l], s->pos, T, Hl, Hkvl, D, c.context, c.cache_f16,
                      (float)(1.0 / std::sqrt((double)D)), N > 1 ? s->attl : s->att, none, status, s->scores,
@@ -341,7 +342,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         const P2P oput = xch(4 * l + 1, s->x, (long long)k * El);
         if (a8)
             CK(launch_gemv_a8(&o, 1, s->att, s->actE, T, E, status, st, pdl, true, p2p ? &oput : nullptr,
-                              next_pf(l, 1)));
+                              next_pf(l, 1), nullptr, &s->split));
         else CK(launch_gemv_f32(&o, 1, s->att, T, E, st, pdl));
         if (N > 1 && !p2p) CK(gather_x());
         GemvSeg gu[2] = {slice(w.gate, E, F, (long long)k * Fl, Fl, s->gu, 2LL * Fl, nullptr),
@@ -353,7 +354,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
                                     a8 ? s->actE : none, st, pdl, p2p ? &oput : nullptr));
         if (a8)
             CK(launch_gemv_a8(gu, 2, s->h, s->actE, T, E, status, st, pdl, true, nullptr, next_pf(l, 2),
-                              f_ffn ? &n_ffn : nullptr));
+                              f_ffn ? &n_ffn : nullptr, &s->split));
         else CK(launch_gemv_f32(gu, 2, s->h, T, E, st, pdl));
         const P2P aput = xch(4 * l + 2, s->a, (long long)k * Fl);
         CK(launch_swiglu_quant(s->gu, s->gu + Fl, 2LL * Fl, T, Fl, N > 1 ? s->al : s->a,
@@ -366,7 +367,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         const P2P xput = xch(4 * l + 3, s->x, (long long)k * El);
         if (a8)
             CK(launch_gemv_a8(&dn, 1, s->a, s->actF, T, F, status, st, pdl, true, p2p ? &xput : nullptr,
-                              next_pf(l, 3)));
+                              next_pf(l, 3), nullptr, &s->split));
         else CK(launch_gemv_f32(&dn, 1, s->a, T, F, st, pdl));
         if (N > 1 && !p2p) CK(gather_x());
     }
@@ -386,7 +387,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
     if (vn > 0) {
         if (a8)
             CK(launch_gemv_a8(&hs, 1, s->h, s->actE, rows, E, status, st, pdl, true, nullptr, next_pf(0, 4),
-                              f_out ? &n_out : nullptr));
+                              f_out ? &n_out : nullptr, &s->split));
         else CK(launch_gemv_f32(&hs, 1, s->h, rows, E, st, pdl));
     }
     if (greedy) {
@@ -545,6 +546,7 @@ void free_session(mimgpu_session *s) {
     for (void *p : s->opened) cudaIpcCloseMemHandle(p);
     if (s->arena) cudaFree(s->arena);
     if (s->scores) cudaFree(s->scores);
+    if (s->split.rec) cudaFree(s->split.rec);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
 }
@@ -705,6 +707,23 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
                           ? attn_prefill_scores_bytes((int)k.max_tokens, (int)H, k.kv_heads, k.context)
                           : 0;
     if (e == cudaSuccess && sb) e = cudaMalloc(&s->scores, sb);
+    // runs of 16-32 rows (batched steps, short prompts): the records of the
+    // tensor-core GEMMs that split K because their matrices have few row
+    // tiles (this rank's rows of q|k|v, o, gate|up, down and the head)
+    if (e == cudaSuccess && T >= kTcMinRows && k.a8) {
+        const int rows = (int)std::min<long long>(T, 32);
+        const long long KVl = KV / N;
+        auto seg = [](int n) { GemvSeg g{}; g.n = n; return g; };
+        const GemvSeg qkv[3] = {seg((int)El), seg((int)KVl), seg((int)KVl)}, o[1] = {seg((int)El)},
+                      gu[2] = {seg((int)Fl), seg((int)Fl)}, hd[1] = {seg((int)Vl)};
+        size_t need = std::max({gemm_a8_split_bytes(qkv, 3, rows, E), gemm_a8_split_bytes(o, 1, rows, E),
+                                gemm_a8_split_bytes(gu, 2, rows, E), gemm_a8_split_bytes(o, 1, rows, F),
+                                gemm_a8_split_bytes(hd, 1, rows, E)});
+        if (need) {
+            e = cudaMalloc(&s->split.rec, need);
+            s->split.bytes = need;
+        }
+    }
     // f32 cos/sin of every position's RoPE angles (float64), for the decode
     // attention's fused RoPE and the step kernel
     const int half = k.rope_dims / 2;

@@ -3,7 +3,8 @@ each with its own key-value cache.  Every sequence's logits and greedy ids
 are the bits a single-sequence session gives for it -- the batch invariance
 of interp/transformer_test.go:297-354 carried to whole decode steps (rows of
 the batched step go through the GEMV below 16 rows and the tensor-core GEMM
-from 16 rows, the same bits either way)."""
+from 16 rows -- with K split over several CTAs when a matrix has few row
+tiles -- the same bits either way)."""
 import numpy as np
 import pytest
 
@@ -32,7 +33,7 @@ def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
 
-@pytest.mark.parametrize("B", [4, 20])
+@pytest.mark.parametrize("B", [4, 20, 32])
 def test_slots_match_single_sequences(model, B):
     rng = np.random.default_rng(B)
     lens = [int(rng.integers(3, 36)) for _ in range(B)]
