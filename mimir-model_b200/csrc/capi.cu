@@ -42,18 +42,26 @@ int cuda_fail(mimgpu_ctx *c, cudaError_t e, const char *what) {
 int use_device(mimgpu_ctx *c) { return cuda_fail(c, cudaSetDevice(c->device), "cudaSetDevice"); }
 
 int sync_bounded(mimgpu_ctx *c, cudaStream_t st) {
-    auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->timeout_ms);
-    for (int spin = 0;; spin++) {
-        cudaError_t e = cudaStreamQuery(st);
+    // the status word comes back with the stream's own work (pinned host
+    // memory): no synchronous copy after the wait
+    cudaError_t e = cudaMemcpyAsync(c->status_host, c->status, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "status");
+    // the wait: polled without sleeping for the first 20 ms (a decode step
+    // or a per-op product ends well within that, and a sleep would add its
+    // timer slack to every call), then with 20 us sleeps up to the deadline
+    const auto t0 = std::chrono::steady_clock::now();
+    const auto deadline = t0 + std::chrono::milliseconds(c->timeout_ms);
+    const auto spin_until = t0 + std::chrono::milliseconds(20);
+    for (;;) {
+        e = cudaStreamQuery(st);
         if (e == cudaSuccess) break;
         if (e != cudaErrorNotReady) return cuda_fail(c, e, "stream");
-        if (std::chrono::steady_clock::now() > deadline)
+        const auto now = std::chrono::steady_clock::now();
+        if (now > deadline)
             return fail(c, MIMGPU_ETIMEOUT, "device work did not finish within %lld ms", (long long)c->timeout_ms);
-        if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (now > spin_until) std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
-    unsigned status = 0;
-    cudaError_t e = cudaMemcpy(&status, c->status, sizeof status, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(c, e, "status");
+    const unsigned status = *(volatile unsigned *)c->status_host;
     if (status) {
         cudaMemset(c->status, 0, sizeof(unsigned));
         if (status & DEV_TIMEOUT) return fail(c, MIMGPU_ETIMEOUT, "a kernel gave up a bounded wait");
@@ -215,11 +223,14 @@ int mimgpu_open(int device, mimgpu_ctx **out) {
     const unsigned long long limit = kDefaultWaitNs;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->status, 256) != cudaSuccess || cudaMemset(c->status, 0, 256) != cudaSuccess ||
-        cudaMemcpy(c->status + 2, &limit, sizeof limit, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(c->status + 2, &limit, sizeof limit, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaHostAlloc((void **)&c->status_host, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess) {
+        if (c->status) cudaFree(c->status);
         if (c->stream) cudaStreamDestroy(c->stream);
         delete c;
         return MIMGPU_ECUDA;
     }
+    *c->status_host = 0;
     *out = c;
     return MIMGPU_OK;
 }
@@ -230,6 +241,7 @@ void mimgpu_close(mimgpu_ctx *c) {
     cudaStreamSynchronize(c->stream);
     if (c->ws) cudaFree(c->ws);
     if (c->status) cudaFree(c->status);
+    if (c->status_host) cudaFreeHost(c->status_host);
     cudaStreamDestroy(c->stream);
     delete c;
 }

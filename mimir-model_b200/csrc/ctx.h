@@ -16,6 +16,7 @@ struct mimgpu_ctx {
     void *ws = nullptr;        // grow-only workspace of the host-buffer calls
     size_t ws_size = 0;
     unsigned *status = nullptr;  // device word: DevStatus bits set by kernels
+    unsigned *status_host = nullptr;  // pinned copy of status[0], written on the waited stream
     int64_t timeout_ms = 60000;
     std::recursive_mutex mu;
     std::string err;
