@@ -262,9 +262,9 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=3):
     return total_b / launches, total_t / launches, launches
 
 
-PORT_NOTE = ("oracle/ C restatement of the reference's a8 decode path (portable C, gcc -O3 -march=x86-64-v3; "
-             "no hand-written AVX2/AMX kernels like the reference's internal/kernels/*_amd64.s, so slower per core "
-             "than the reference's published 6.1-6.7 tok/s on 4 cores)")
+PORT_NOTE = ("oracle/ C restatement of the reference's a8 decode path (gcc -O3 -march=x86-64-v3; the block sums of "
+             "dotQ8KRef in AVX2 as the reference's dotQ4KQ8KAVX2/dotQ6KQ8KAVX2 compute them, bit-identical to the scalar "
+             "checker; quantizer, attention and the f32 steps scalar C, threads created per product)")
 
 
 def cpu_baseline_sample(ctx, cfg, weights, prompt, budget_s=20.0):

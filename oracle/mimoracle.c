@@ -401,6 +401,84 @@ int mo_q8_quantize(const float *x, int64_t k, int block, int8_t *q, float *d32, 
 
 static inline int f16_finite(const uint8_t *p) { return (le16(p) & 0x7C00) != 0x7C00; }
 
+/* The block sums of dotQ8KRef are exact integers, so any summation order
+ * gives the same S: besides the scalar loops below (the checker) the block
+ * sums have an AVX2 form, as the reference computes them on amd64
+ * (dotQ4KQ8KAVX2 / dotQ6KQ8KAVX2, internal/kernels/kernels_amd64.s:
+ * 1045-1510): VPMADDUBSW of the unsigned quants with the int8 activations
+ * (no saturation for these ranges: |pair| <= 15*127*2 for Q4_K, 63*127*2
+ * for Q6_K), VPMADDWD with the sub-block scales, int32 lanes summed at the
+ * end.  mo_set_simd(0) selects the scalar loops. */
+static int g_simd = 1;
+
+void mo_set_simd(int on) { g_simd = on != 0; }
+
+int mo_simd_active(void) {
+#if defined(__AVX2__)
+    return g_simd;
+#else
+    return 0;
+#endif
+}
+
+#if defined(__AVX2__)
+#include <immintrin.h>
+
+static inline int32_t hsum_i32x8(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4E));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xB1));
+    return _mm_cvtsi128_si32(s);
+}
+
+/* S = sum_c sc[2c] * sum(lo nibbles of qs[32c..] * y[64c..]) + sc[2c+1] * sum(hi * y[64c+32..]) */
+static int32_t q4k_block_s_avx2(const uint8_t *qs, const int8_t *y, const int32_t sc[8]) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F);
+    __m256i acc = _mm256_setzero_si256();
+    for (int c = 0; c < 4; c++) {
+        const __m256i v = _mm256_loadu_si256((const __m256i *)(qs + 32 * c));
+        const __m256i lo = _mm256_and_si256(v, m4);
+        const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(v, 4), m4);
+        const __m256i p0 = _mm256_maddubs_epi16(lo, _mm256_loadu_si256((const __m256i *)(y + 64 * c)));
+        const __m256i p1 = _mm256_maddubs_epi16(hi, _mm256_loadu_si256((const __m256i *)(y + 64 * c + 32)));
+        acc = _mm256_add_epi32(acc, _mm256_madd_epi16(p0, _mm256_set1_epi16((short)sc[2 * c])));
+        acc = _mm256_add_epi32(acc, _mm256_madd_epi16(p1, _mm256_set1_epi16((short)sc[2 * c + 1])));
+    }
+    return hsum_i32x8(acc);
+}
+
+/* S of a Q6_K block: per half h, per quarter k of 32 elements, the 6-bit
+ * quants r (q = r - 32) times y, scales sc[8h + 2k + (l >= 16)]. */
+static int32_t q6k_block_s_avx2(const uint8_t *blk, const int8_t *y) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F), m2 = _mm256_set1_epi8(0x03), c32 = _mm256_set1_epi8(32);
+    __m256i acc = _mm256_setzero_si256();
+    for (int h = 0; h < 2; h++) {
+        const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+        const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);
+        const int8_t *yh = y + 128 * h;
+        const __m256i la = _mm256_loadu_si256((const __m256i *)ql);
+        const __m256i lb = _mm256_loadu_si256((const __m256i *)(ql + 32));
+        const __m256i hv = _mm256_loadu_si256((const __m256i *)qh);
+        __m256i r[4];
+        r[0] = _mm256_or_si256(_mm256_and_si256(la, m4), _mm256_slli_epi16(_mm256_and_si256(hv, m2), 4));
+        r[1] = _mm256_or_si256(_mm256_and_si256(lb, m4),
+                               _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hv, 2), m2), 4));
+        r[2] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(la, 4), m4),
+                               _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hv, 4), m2), 4));
+        r[3] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(lb, 4), m4),
+                               _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hv, 6), m2), 4));
+        for (int k = 0; k < 4; k++) {
+            const __m256i yk = _mm256_loadu_si256((const __m256i *)(yh + 32 * k));
+            /* (r - 32) y in pairs: r y - 32 y, each term within int16 */
+            const __m256i pk = _mm256_sub_epi16(_mm256_maddubs_epi16(r[k], yk), _mm256_maddubs_epi16(c32, yk));
+            const __m256i s16 = _mm256_set_m128i(_mm_set1_epi16(sc[2 * k + 1]), _mm_set1_epi16(sc[2 * k]));
+            acc = _mm256_add_epi32(acc, _mm256_madd_epi16(pk, s16));
+        }
+    }
+    return hsum_i32x8(acc);
+}
+#endif
+
 int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k,
                    float *out) {
     float tot = 0, off = 0;
@@ -420,6 +498,11 @@ int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32
                 m[4 + j] = (s[j + 8] >> 4) | ((s[j + 4] >> 6) << 4);
             }
             int32_t S = 0, M = 0;
+#if defined(__AVX2__)
+            if (g_simd) {
+                S = q4k_block_s_avx2(blk + 16, y, sc);
+            } else
+#endif
             for (int c = 0; c < 4; c++) {
                 int32_t lo = 0, hi = 0;
                 for (int i = 0; i < 32; i++) {
@@ -438,6 +521,12 @@ int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32
         if (!f16_finite(blk + 208)) return 0;
         float d = mo_f16_to_f32(le16(blk + 208));
         int32_t S = 0;
+#if defined(__AVX2__)
+        if (g_simd) {
+            tot = fmaf((float)q6k_block_s_avx2(blk, y), d * dx, tot);
+            continue;
+        }
+#endif
         for (int h = 0; h < 2; h++) {
             const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
             const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);

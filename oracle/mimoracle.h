@@ -73,6 +73,11 @@ int mo_q8_quantize(const float *x, int64_t k, int block, int8_t *q, float *d32, 
  * then one fused multiply-add per block in block order.  Returns 1 and sets
  * *out, or 0 when a block scale of the row is not finite. */
 int mo_dot_q8k_ref(int dt, const uint8_t *row, const int8_t *q, const float *d32, const int16_t *xs, int64_t k, float *out);
+/* Its exact integer block sums as the reference computes them on amd64, in
+ * AVX2 (default when compiled for AVX2), or by the scalar loops (0): the
+ * same bits either way.  mo_simd_active() says which runs. */
+void mo_set_simd(int on);
+int mo_simd_active(void);
 
 /* RowDot.DotQ8 with blocks of 32 (q8.go:143-151): the AVX2 kernels
  * dotQ4KQ8AVX2, dotQ6KQ8AVX2 and dotQ8_0Q8AVX2 (internal/kernels/

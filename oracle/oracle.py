@@ -62,6 +62,8 @@ def lib():
             "mo_gen_normal": (None, [C.c_uint64, I64, F, F, P]),
             "mo_q8_quantize": (I32, [P, I64, I32, P, P, P, P]),
             "mo_dot_q8k_ref": (I32, [I32, P, P, P, P, I64, P]),
+            "mo_set_simd": (None, [I32]),
+            "mo_simd_active": (I32, []),
             "mo_dot_q8_b32": (I32, [I32, P, P, P, P, I64, P]),
             "mo_dot_f32": (F, [P, P, I64]),
             "mo_dequant_matmul": (I32, [P, I64, I64, I32, P, I64, P, P, I32]),
@@ -88,6 +90,16 @@ def lib():
 
 def _p(a: np.ndarray | None):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def set_simd(on: bool) -> None:
+    """dotQ8KRef's exact block sums in AVX2 (default) or by the scalar loops:
+    the same bits either way (tests/test_oracle.py checks)."""
+    lib().mo_set_simd(1 if on else 0)
+
+
+def simd_active() -> bool:
+    return bool(lib().mo_simd_active())
 
 
 def threads() -> int:

@@ -223,6 +223,52 @@ def test_dot_q8k_ref_edge_cases(dt):
 
 
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+def test_dot_q8k_simd_equals_scalar(dt):
+    """The AVX2 block sums (the timed CPU baseline) and the scalar loops (the
+    checker) give the same bits: random rows, rows of all-ones quants with
+    the largest scales (the int16 pair sums at their extremes), activations
+    saturated at +-127 and alternating signs."""
+    if not O.simd_active():
+        pytest.skip("oracle built without AVX2")
+    k = 4096
+    rng = np.random.default_rng(5)
+    acts = [O.q8_quantize(O.gen_normal(300 + i, k), 256) for i in range(3)]
+    x = np.where(np.arange(k) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    acts.append(O.q8_quantize(x, 256))                      # quants +-127
+    acts.append(O.q8_quantize(np.ones(k, np.float32), 256))  # quants 127
+    bb = 144 if dt == O.Q4_K else 210
+    rows = [O.gen_weight(dt, 40 + i, 1, k) for i in range(4)]
+    w = bytearray(rows[0].tobytes())
+    for o in range(0, len(w), bb):
+        if dt == O.Q4_K:
+            w[o + 4:o + 144] = b"\xff" * 140
+        else:
+            w[o:o + 192] = b"\xff" * 192
+            w[o + 192:o + 208] = bytes(rng.choice([0x80, 0x7F], 16).astype(np.uint8))
+    rows.append(np.frombuffer(bytes(w), np.uint8))
+    try:
+        for row in rows:
+            for ok, q, d32, xs, _ in acts:
+                assert ok
+                O.set_simd(True)
+                a = O.dot_q8k_ref(dt, row, q, d32, xs, k)
+                O.set_simd(False)
+                b = O.dot_q8k_ref(dt, row, q, d32, xs, k)
+                assert a[0] == b[0]
+                assert np.float32(a[1]).view(np.uint32) == np.float32(b[1]).view(np.uint32)
+        # and a whole product
+        wm = O.gen_weight(dt, 77, 64, k)
+        xm = O.gen_normal(78, 3 * k).reshape(3, k)
+        O.set_simd(True)
+        ya = O.dequant_matmul_a8(xm, dt, wm, 64)
+        O.set_simd(False)
+        yb = O.dequant_matmul_a8(xm, dt, wm, 64)
+        assert np.array_equal(ya.view(np.uint32), yb.view(np.uint32))
+    finally:
+        O.set_simd(True)
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
 def test_dot_q8k_refuses_nonfinite_scale(dt):
     k = 512
     w = bytearray(O.gen_weight(dt, 9, 1, k).tobytes())
