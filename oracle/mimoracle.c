@@ -11,6 +11,7 @@
 #include "mimoracle.h"
 
 #include <math.h>
+#include <stdint.h>
 #include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -28,33 +29,95 @@ static inline void put16(uint8_t *p, uint16_t v) { p[0] = (uint8_t)v; p[1] = (ui
 typedef void (*range_fn)(void *ctx, int64_t lo, int64_t hi);
 typedef struct { range_fn fn; void *ctx; int64_t lo, hi; } range_job;
 
-static void *range_thread(void *p) {
-    range_job *j = (range_job *)p;
-    j->fn(j->ctx, j->lo, j->hi);
+/* A persistent pool of worker threads, like the reference's worker pool
+ * (interp/pool.go): created on first use, each product wakes them with a
+ * new generation of jobs instead of creating threads.  One product uses the
+ * pool at a time (pool_mu); no job calls parallel_for itself. */
+#define POOL_MAX 256
+static pthread_mutex_t pool_mu = PTHREAD_MUTEX_INITIALIZER;
+static pthread_mutex_t pool_lk = PTHREAD_MUTEX_INITIALIZER;
+static pthread_cond_t pool_go = PTHREAD_COND_INITIALIZER, pool_done = PTHREAD_COND_INITIALIZER;
+static int pool_n = 0;              /* workers created (ids 1..pool_n) */
+static unsigned long pool_gen = 0;  /* generation of the jobs in pool_jobs */
+static int pool_active = 0;         /* jobs of this generation (job 0 is the caller's) */
+static int pool_pending = 0;        /* worker jobs of this generation not finished */
+static range_job pool_jobs[POOL_MAX];
+
+static void *pool_worker(void *arg) {
+    const int id = (int)(intptr_t)arg;
+    unsigned long seen = 0;
+    pthread_mutex_lock(&pool_lk);
+    for (;;) {
+        while (pool_gen == seen) pthread_cond_wait(&pool_go, &pool_lk);
+        seen = pool_gen;
+        /* a generation's workers all finish it before the next one starts */
+        if (id < pool_active) {
+            const range_job j = pool_jobs[id];
+            pthread_mutex_unlock(&pool_lk);
+            if (j.lo < j.hi) j.fn(j.ctx, j.lo, j.hi);
+            pthread_mutex_lock(&pool_lk);
+            if (--pool_pending == 0) pthread_cond_signal(&pool_done);
+        }
+    }
     return NULL;
 }
+
+/* A forked child has none of the workers: it starts with an empty pool (the
+ * locks are held across the fork, so none is left locked by a thread the
+ * child does not have). */
+static void pool_prefork(void) {
+    pthread_mutex_lock(&pool_mu);
+    pthread_mutex_lock(&pool_lk);
+}
+static void pool_postfork_parent(void) {
+    pthread_mutex_unlock(&pool_lk);
+    pthread_mutex_unlock(&pool_mu);
+}
+static void pool_postfork_child(void) {
+    pool_n = 0;
+    pool_active = pool_pending = 0;
+    pthread_cond_init(&pool_go, NULL);
+    pthread_cond_init(&pool_done, NULL);
+    pthread_mutex_unlock(&pool_lk);
+    pthread_mutex_unlock(&pool_mu);
+}
+static pthread_once_t pool_once = PTHREAD_ONCE_INIT;
+static void pool_register(void) { pthread_atfork(pool_prefork, pool_postfork_parent, pool_postfork_child); }
 
 /* Runs fn over [0, n) split into nthreads contiguous pieces, like the
  * reference's parallel() over output rows (interp/pool.go:33-66). */
 static void parallel_for(int64_t n, int nthreads, range_fn fn, void *ctx) {
-    if (nthreads > 256) nthreads = 256;
+    if (nthreads > POOL_MAX) nthreads = POOL_MAX;
     if (nthreads > n) nthreads = (int)n;
     if (nthreads <= 1) { fn(ctx, 0, n); return; }
-    pthread_t th[256];
-    range_job jobs[256];
-    int ok[256];
-    int64_t per = (n + nthreads - 1) / nthreads;
-    for (int t = 0; t < nthreads; t++) {
-        int64_t lo = t * per, hi = lo + per < n ? lo + per : n;
-        jobs[t] = (range_job){fn, ctx, lo < n ? lo : n, hi};
-        ok[t] = 0;
-        if (t > 0 && jobs[t].lo < jobs[t].hi) ok[t] = pthread_create(&th[t], NULL, range_thread, &jobs[t]) == 0;
+    pthread_once(&pool_once, pool_register);
+    pthread_mutex_lock(&pool_mu);
+    pthread_mutex_lock(&pool_lk);
+    while (pool_n < nthreads - 1) {
+        pthread_t th;
+        if (pthread_create(&th, NULL, pool_worker, (void *)(intptr_t)(pool_n + 1)) != 0) break;
+        pthread_detach(th);
+        pool_n++;
     }
-    fn(ctx, jobs[0].lo, jobs[0].hi);
-    for (int t = 1; t < nthreads; t++) {
-        if (ok[t]) pthread_join(th[t], NULL);
-        else if (jobs[t].lo < jobs[t].hi) fn(ctx, jobs[t].lo, jobs[t].hi);
+    const int use = pool_n + 1 < nthreads ? pool_n + 1 : nthreads;
+    const int64_t per = (n + use - 1) / use;
+    for (int t = 0; t < use; t++) {
+        const int64_t lo = t * per < n ? t * per : n, hi = lo + per < n ? lo + per : n;
+        pool_jobs[t] = (range_job){fn, ctx, lo, hi};
     }
+    const range_job mine = pool_jobs[0];
+    pool_active = use;
+    pool_pending = use - 1;
+    if (pool_pending > 0) {
+        pool_gen++;
+        pthread_cond_broadcast(&pool_go);
+    }
+    pthread_mutex_unlock(&pool_lk);
+    if (mine.lo < mine.hi) fn(ctx, mine.lo, mine.hi);
+    pthread_mutex_lock(&pool_lk);
+    while (pool_pending > 0) pthread_cond_wait(&pool_done, &pool_lk);
+    pthread_mutex_unlock(&pool_lk);
+    pthread_mutex_unlock(&pool_mu);
 }
 
 /* ------------------------------------------------------------------ */

@@ -353,3 +353,26 @@ def test_argmax_first_max_and_nan():
     assert O.argmax(v) == 0
     v = np.float32([1, np.nan, 6, 6])
     assert O.argmax(v) == 2
+
+
+def test_thread_pool_products_and_fork():
+    """The oracle's persistent worker pool: repeated products give the same
+    bits as one thread, and a process forked after the pool exists still
+    runs products (its pool starts empty)."""
+    import os
+    import warnings
+    w = O.gen_weight(O.Q4_K, 11, 300, 2048)
+    x = O.gen_normal(12, 2 * 2048).reshape(2, 2048)
+    one = O.dequant_matmul_a8(x, O.Q4_K, w, 300, nthreads=1)
+    for _ in range(3):
+        assert np.array_equal(O.dequant_matmul_a8(x, O.Q4_K, w, 300, nthreads=8).view(np.uint32), one.view(np.uint32))
+    if not hasattr(os, "fork"):
+        return
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", DeprecationWarning)
+        pid = os.fork()
+    if pid == 0:
+        ok = np.array_equal(O.dequant_matmul_a8(x, O.Q4_K, w, 300, nthreads=8).view(np.uint32), one.view(np.uint32))
+        os._exit(0 if ok else 3)
+    _, status = os.waitpid(pid, 0)
+    assert os.WIFEXITED(status) and os.WEXITSTATUS(status) == 0
