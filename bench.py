@@ -264,7 +264,7 @@ def gemv_roofline(ctx, cfg, weights, torch, reps=3):
 
 PORT_NOTE = ("oracle/ C restatement of the reference's a8 decode path (gcc -O3 -march=x86-64-v3; the block sums of "
              "dotQ8KRef in AVX2 as the reference's dotQ4KQ8KAVX2/dotQ6KQ8KAVX2 compute them, bit-identical to the scalar "
-             "checker; quantizer, attention and the f32 steps scalar C, threads created per product)")
+             "checker; quantizer, attention and the f32 steps scalar C; a persistent worker pool over output rows)")
 
 
 def cpu_baseline_sample(ctx, cfg, weights, prompt, budget_s=20.0):
