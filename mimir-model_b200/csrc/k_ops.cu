@@ -306,8 +306,10 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnArgs a) {
     }
 }
 
-
-__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ v, long long n, long long i0,
+// The logits v come from the kernel just before, which may still run when
+// this one starts (programmatic dependent launch): v is not __restrict__, so
+// its loads stay after the dependency wait and off the read-only cache.
+__global__ void __launch_bounds__(256) argmax_kernel(const float *v, long long n, long long i0,
                                                      int holds_first, unsigned long long *__restrict__ key,
                                                      long long ldv) {
     __shared__ unsigned long long red[8];
