@@ -156,72 +156,118 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *gate, co
 }
 
 // The same rms_norm + quantization for many rows (prompt passes): one
-// 256-thread block per row reads the row once into registers (R elements
-// per thread, n <= 256 R), sums its squares once, and normalises and
-// quantizes its 256-element blocks one after another (two scratch sets, so
-// one barrier per block).  Same bits as rmsnorm_quant_kernel: the mean is
-// decided by the same certainty bound (or the in-order sum), whatever the
-// tree.
-template <int R>
+// 256-thread block per row reads the row once, sums its squares once, and
+// each warp normalises and quantizes whole 256-element blocks (warp w takes
+// blocks w, w + 8, ...; lane l elements 8l..8l+7), with shuffles instead of
+// block barriers.  Same bits as rmsnorm_quant_kernel: the mean is decided by
+// the same certainty bound (or the in-order sum), whatever the tree, and the
+// block's amax, refusal, rounding and run sums are those of quant_block_256.
+template <int BW>  // blocks per warp: n <= 8 * 256 * BW, n % 256 == 0
 __global__ void __launch_bounds__(256) rmsnorm_quant_rows_kernel(const float *x, int n,
                                                                  const float *__restrict__ scale, float eps,
                                                                  float *__restrict__ y, ActQ8 act) {
-    __shared__ QuantScratch qs[2];
     __shared__ double dred[8];
     __shared__ float ms_seq;
     pdl_launch_dependents();
     const long long row = blockIdx.x;
-    const int t = threadIdx.x;
-    float sc[R];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nb = n / 256;
+    float sc[BW][8];
     const uint64_t keep = l2_policy_evict_last();
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = u * 256 + t;
-        sc[u] = (scale && i < n) ? ldg_keep(scale + i, keep) : 1.f;  // read-only: before the wait
+    for (int u = 0; u < BW; u++) {  // the norm weights are read-only: before the wait
+        const int kb = w + 8 * u, e0 = kb * 256 + lane * 8;
+        float4 sa = make_float4(1.f, 1.f, 1.f, 1.f), sb = sa;
+        if (kb < nb && scale) {
+            sa = ldg_keep4((const float4 *)(scale + e0), keep);
+            sb = ldg_keep4((const float4 *)(scale + e0 + 4), keep);
+        }
+        sc[u][0] = sa.x; sc[u][1] = sa.y; sc[u][2] = sa.z; sc[u][3] = sa.w;
+        sc[u][4] = sb.x; sc[u][5] = sb.y; sc[u][6] = sb.z; sc[u][7] = sb.w;
     }
     pdl_wait();
     // the row was written by the kernel before this one, which may still
     // have been running when this block started (programmatic dependent
     // launch): read through L2, never a possibly stale read-only-cache line
     const float *xr = x + row * n;
-    float xv[R];
+    float xv[BW][8];
     double ss = 0.0;
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = u * 256 + t;
-        xv[u] = i < n ? __ldcg(xr + i) : 0.f;
+    for (int u = 0; u < BW; u++) {
+        const int kb = w + 8 * u, e0 = kb * 256 + lane * 8;
+        float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
+        if (kb < nb) {
+            xa = __ldcg((const float4 *)(xr + e0));
+            xb = __ldcg((const float4 *)(xr + e0 + 4));
+        }
+        xv[u][0] = xa.x; xv[u][1] = xa.y; xv[u][2] = xa.z; xv[u][3] = xa.w;
+        xv[u][4] = xb.x; xv[u][5] = xb.y; xv[u][6] = xb.z; xv[u][7] = xb.w;
     }
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const double e = (double)xv[u];
-        ss = __fma_rn(e, e, ss);  // e*e is exact in float64 (0 past n)
-    }
+    for (int u = 0; u < BW; u++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const double e = (double)xv[u][j];
+            ss = __fma_rn(e, e, ss);  // e*e is exact in float64 (0 past n)
+        }
     ss = warp_sum_d(ss);
-    if ((t & 31) == 0) dred[t >> 5] = ss;
+    if (lane == 0) dred[w] = ss;
     __syncthreads();
     double tot = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) tot += dred[i];
     float ms;
-    // a term goes through R products-and-sums in its thread, 5 shuffle levels
-    // and 8 partials: within rms_inv's depth bound n/256 + 16 for n > 256(R-1)
-    if (!rms_mean_certain(tot, n, R + 16, ms)) {
-        if (t == 0) ms_seq = (float)__ddiv_rn(rms_seq_sum_cg(xr, n), (double)n);
+    // a term goes through 8 BW products-and-sums in its lane, 5 shuffle
+    // levels and 8 partials
+    if (!rms_mean_certain(tot, n, 8 * BW + 16, ms)) {
+        if (threadIdx.x == 0) ms_seq = (float)__ddiv_rn(rms_seq_sum_cg(xr, n), (double)n);
         __syncthreads();
         ms = ms_seq;
     }
     const float inv = rms_inv_of_mean(ms, eps);
+    const long long K = n, nbr = (long long)row * nb;
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = u * 256 + t;
-        if (u * 256 >= n) break;  // uniform: whole blocks (n % 256 == 0 when quantizing)
-        float v = 0.f;
-        if (i < n) {
-            v = __fmul_rn(xv[u], inv);
-            if (scale) v = __fmul_rn(v, sc[u]);
-            y[row * n + i] = v;
+    for (int u = 0; u < BW; u++) {
+        const int kb = w + 8 * u, e0 = kb * 256 + lane * 8;
+        if (kb >= nb) break;  // warp-uniform
+        float v[8];
+        float am = 0.f;
+        int bad = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            v[j] = __fmul_rn(xv[u][j], inv);
+            if (scale) v[j] = __fmul_rn(v[j], sc[u][j]);
+            const float a = fabsf(v[j]);
+            const bool b = !(a <= 0x1p60f);
+            bad |= b;
+            am = fmaxf(am, b ? 0.f : a);
         }
-        if (act.q) quant_block_256(v, row, n, u, act, qs[u & 1]);
+        *(float4 *)(y + row * K + e0) = make_float4(v[0], v[1], v[2], v[3]);
+        *(float4 *)(y + row * K + e0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        if (!act.q) continue;
+        // QuantizeBlocks of the block (quant_block_256's arithmetic)
+        am = warp_max(am);
+        bad = __any_sync(0xffffffffu, bad);
+        const bool quant = am != 0.f && !bad;
+        const float r127 = quant ? __fdiv_rn(127.f, am) : 0.f;
+        uint32_t qw[2] = {0u, 0u};
+        int s8 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int q = quant ? q8_round_f(v[j], am, r127) : 0;
+            s8 += q;
+            qw[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+        }
+        *(uint2 *)(act.q + row * K + e0) = make_uint2(qw[0], qw[1]);
+        // lane pairs hold runs of 16, quads runs of 32
+        const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+        const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+        const long long bk = nbr + kb;
+        if ((lane & 1) == 0) act.ys[bk * 16 + (lane >> 1)] = (int16_t)s16;
+        if ((lane & 3) == 0) act.xs[bk * 8 + (lane >> 2)] = (int16_t)s32;
+        if (lane == 0) {
+            act.dx[bk] = __fdiv_rn(am, 127.f);
+            act.ok[bk] = bad ? 0 : 1;
+        }
     }
 }
 
@@ -251,12 +297,14 @@ cudaError_t launch_rmsnorm_quant(const float *x, int rows, int n, const float *s
                                  ActQ8 act, cudaStream_t st, bool pdl, const P2P *wait) {
     if (rows <= 0 || n <= 0) return cudaSuccess;
     if (act.q && n % 256) return cudaErrorInvalidValue;
-    if (rows >= 16 && !(wait && wait->N > 1) && n <= 8192) {
-        // many rows: one block per row, the row read once
+    if (rows >= num_sms() && !(wait && wait->N > 1) && n % 256 == 0 && n <= 8192) {
+        // a row per SM at least (prompt passes): one block per row, the row
+        // read once (fewer rows keep the block-per-256-elements kernel,
+        // whose rows spread over more SMs)
         cudaLaunchAttribute attr[1];
         cudaLaunchConfig_t cfg = blocks_cfg(rows, 1, st, pdl, attr);
-        if (n <= 4096) return cudaLaunchKernelEx(&cfg, rmsnorm_quant_rows_kernel<16>, x, n, scale, eps, y, act);
-        return cudaLaunchKernelEx(&cfg, rmsnorm_quant_rows_kernel<32>, x, n, scale, eps, y, act);
+        if (n <= 4096) return cudaLaunchKernelEx(&cfg, rmsnorm_quant_rows_kernel<2>, x, n, scale, eps, y, act);
+        return cudaLaunchKernelEx(&cfg, rmsnorm_quant_rows_kernel<4>, x, n, scale, eps, y, act);
     }
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (n + 255) / 256, st, pdl, attr);

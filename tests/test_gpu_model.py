@@ -162,7 +162,8 @@ def test_8b_layer_shapes_token_identity(ctx):
     m.free()
 
 
-def test_refused_rows_same_in_step_and_prompt(ctx):
+@pytest.mark.parametrize("T", [8, 160])
+def test_refused_rows_same_in_step_and_prompt(ctx, T):
     """Weight rows with a non-finite block scale take the f32 product
     (linearA8, interp/fast.go:282-379) on every path: a one-token step, whose
     GEMVs normalise their own activation row (fused rms_norm) and add the
@@ -180,17 +181,18 @@ def test_refused_rows_same_in_step_and_prompt(ctx):
         o = row * (k // 256) * rb[dt] + (0 if dt == O.Q4_K else 208)
         b[o:o + 2] = bytes([0x00, 0x7C])  # d = +inf in the row's first block
         w[name] = (dt, np.frombuffer(bytes(b), np.uint8))
-    C = 64
-    ids = np.array([3, 9, 27, 81, 243, 5, 15, 45], np.int32)
-    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=8), w)
+    C = 192
+    # 160 tokens: the prompt pass takes the one-block-per-row rms_norm
+    ids = ((np.arange(T) * 37 + 3) % 700).astype(np.int32)
+    m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=T), w)
     s = m.session()
-    whole = s.run(ids, np.arange(8), all_rows=True)
+    whole = s.run(ids, np.arange(T), all_rows=True)
     s.reset()
-    s.run(ids[:7], np.arange(7))
-    step = s.run(ids[7:], np.array([7]))
-    assert np.array_equal(np.isnan(step[0]), np.isnan(whole[7]))
-    fin = ~np.isnan(whole[7])
-    assert np.array_equal(step[0][fin].view(np.uint32), whole[7][fin].view(np.uint32))
+    s.run(ids[:T - 1], np.arange(T - 1))
+    step = s.run(ids[T - 1:], np.array([T - 1]))
+    assert np.array_equal(np.isnan(step[0]), np.isnan(whole[T - 1]))
+    fin = ~np.isnan(whole[T - 1])
+    assert np.array_equal(step[0][fin].view(np.uint32), whole[T - 1][fin].view(np.uint32))
     s.free()
     m.free()
 
