@@ -224,50 +224,61 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_rows_kernel(const float *x,
         ms = ms_seq;
     }
     const float inv = rms_inv_of_mean(ms, eps);
-    const long long K = n, nbr = (long long)row * nb;
+    const long long K = n;
 #pragma unroll
     for (int u = 0; u < BW; u++) {
         const int kb = w + 8 * u, e0 = kb * 256 + lane * 8;
         if (kb >= nb) break;  // warp-uniform
         float v[8];
-        float am = 0.f;
-        int bad = 0;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             v[j] = __fmul_rn(xv[u][j], inv);
             if (scale) v[j] = __fmul_rn(v[j], sc[u][j]);
-            const float a = fabsf(v[j]);
-            const bool b = !(a <= 0x1p60f);
-            bad |= b;
-            am = fmaxf(am, b ? 0.f : a);
         }
         *(float4 *)(y + row * K + e0) = make_float4(v[0], v[1], v[2], v[3]);
         *(float4 *)(y + row * K + e0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
-        if (!act.q) continue;
-        // QuantizeBlocks of the block (quant_block_256's arithmetic)
-        am = warp_max(am);
-        bad = __any_sync(0xffffffffu, bad);
-        const bool quant = am != 0.f && !bad;
-        const float r127 = quant ? __fdiv_rn(127.f, am) : 0.f;
-        uint32_t qw[2] = {0u, 0u};
-        int s8 = 0;
+        if (act.q) quant_block_warp(v, row, K, kb, act);
+    }
+}
+
+// swiglu.v1 + quantization and plain quantization for many rows (prompt
+// passes): one 256-thread block per row, each warp taking whole 256-element
+// blocks (w, w + 8, ...; lane l elements 8l..8l+7) through
+// quant_block_warp.  Same bits as swiglu_quant_kernel / quantize_a8_kernel.
+__global__ void __launch_bounds__(256) swiglu_quant_rows_kernel(const float *gate, const float *up, long long ldg,
+                                                                int n, float *__restrict__ y, ActQ8 act) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long row = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nb = n / 256, n8 = n & ~7;
+    const float *g = gate + row * ldg, *u = up + row * ldg;
+    for (int kb = w; kb < nb; kb += 8) {
+        const int e0 = kb * 256 + lane * 8;
+        // written by the kernel before this one: through L2
+        const float4 ga = __ldcg((const float4 *)(g + e0)), gb = __ldcg((const float4 *)(g + e0 + 4));
+        const float4 ua = __ldcg((const float4 *)(u + e0)), ub = __ldcg((const float4 *)(u + e0 + 4));
+        const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        const float uv[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+        float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int q = quant ? q8_round_f(v[j], am, r127) : 0;
-            s8 += q;
-            qw[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
-        }
-        *(uint2 *)(act.q + row * K + e0) = make_uint2(qw[0], qw[1]);
-        // lane pairs hold runs of 16, quads runs of 32
-        const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
-        const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
-        const long long bk = nbr + kb;
-        if ((lane & 1) == 0) act.ys[bk * 16 + (lane >> 1)] = (int16_t)s16;
-        if ((lane & 3) == 0) act.xs[bk * 8 + (lane >> 2)] = (int16_t)s32;
-        if (lane == 0) {
-            act.dx[bk] = __fdiv_rn(am, 127.f);
-            act.ok[bk] = bad ? 0 : 1;
-        }
+        for (int j = 0; j < 8; j++) v[j] = e0 + j < n8 ? silu_mul_amd64(gv[j], uv[j]) : silu_mul_f64(gv[j], uv[j]);
+        *(float4 *)(y + row * n + e0) = make_float4(v[0], v[1], v[2], v[3]);
+        *(float4 *)(y + row * n + e0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        if (act.q) quant_block_warp(v, row, n, kb, act);
+    }
+}
+
+__global__ void __launch_bounds__(256) quantize_a8_rows_kernel(const float *x, long long K, ActQ8 act) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long row = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nb = (int)(K / 256);
+    const float *xr = x + row * K;
+    for (int kb = w; kb < nb; kb += 8) {
+        const int e0 = kb * 256 + lane * 8;
+        const float4 a = __ldcg((const float4 *)(xr + e0)), b = __ldcg((const float4 *)(xr + e0 + 4));
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        quant_block_warp(v, row, K, kb, act);
     }
 }
 
@@ -288,6 +299,10 @@ cudaError_t launch_quantize_a8(const float *x, int rows, long long K, ActQ8 act,
     if (rows <= 0 || K <= 0) return cudaSuccess;
     if (K % 256) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
+    if (rows >= num_sms() && !(wait && wait->N > 1) && ((uintptr_t)x & 15) == 0) {  // a row per SM at least
+        cudaLaunchConfig_t cfg = blocks_cfg(rows, 1, st, pdl, attr);
+        return cudaLaunchKernelEx(&cfg, quantize_a8_rows_kernel, x, K, act);
+    }
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (int)(K / 256), st, pdl, attr);
     const P2P w = wait ? *wait : P2P{};
     return cudaLaunchKernelEx(&cfg, quantize_a8_kernel, x, K, act, w);
@@ -318,6 +333,11 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, long long ld
     if (act.q && n % 256) return cudaErrorInvalidValue;
     if (put && put->N > 1 && rows != 1) return cudaErrorInvalidValue;  // exchanges carry one row
     cudaLaunchAttribute attr[1];
+    if (rows >= num_sms() && !(put && put->N > 1) && n % 256 == 0 && ldg % 4 == 0 &&
+        (((uintptr_t)gate | (uintptr_t)up | (uintptr_t)y) & 15) == 0) {  // a row per SM at least
+        cudaLaunchConfig_t cfg = blocks_cfg(rows, 1, st, pdl, attr);
+        return cudaLaunchKernelEx(&cfg, swiglu_quant_rows_kernel, gate, up, ldg, n, y, act);
+    }
     cudaLaunchConfig_t cfg = blocks_cfg(rows, (n + 255) / 256, st, pdl, attr);
     const P2P p = put ? *put : P2P{};
     return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, ldg, n, y, act, p);

@@ -52,4 +52,45 @@ __device__ __forceinline__ void quant_block_256(float v, long long row, long lon
     }
 }
 
+// The same quantization by one warp: lane l holds elements 8l..8l+7 of
+// block kb of the row in v (v is the value the block would pass to
+// quant_block_256 element by element); amax, refusal, rounding, the sums of
+// runs of 16 (lane pairs) and 32 (quads), dx and the flag are
+// quant_block_256's, bit for bit.
+__device__ __forceinline__ void quant_block_warp(const float (&v)[8], long long row, long long K, int kb,
+                                                 ActQ8 act) {
+    const int lane = threadIdx.x & 31;
+    float am = 0.f;
+    int bad = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float a = fabsf(v[j]);
+        const bool b = !(a <= 0x1p60f);
+        bad |= b;
+        am = fmaxf(am, b ? 0.f : a);
+    }
+    am = warp_max(am);
+    bad = __any_sync(0xffffffffu, bad);
+    const bool quant = am != 0.f && !bad;
+    const float r127 = quant ? __fdiv_rn(127.f, am) : 0.f;
+    uint32_t qw[2] = {0u, 0u};
+    int s8 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int q = quant ? q8_round_f(v[j], am, r127) : 0;
+        s8 += q;
+        qw[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    *(uint2 *)(act.q + row * K + (long long)kb * 256 + lane * 8) = make_uint2(qw[0], qw[1]);
+    const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+    const long long bk = row * (K / 256) + kb;
+    if ((lane & 1) == 0) act.ys[bk * 16 + (lane >> 1)] = (int16_t)s16;
+    if ((lane & 3) == 0) act.xs[bk * 8 + (lane >> 2)] = (int16_t)s32;
+    if (lane == 0) {
+        act.dx[bk] = __fdiv_rn(am, 127.f);
+        act.ok[bk] = bad ? 0 : 1;
+    }
+}
+
 }  // namespace mimgpu
