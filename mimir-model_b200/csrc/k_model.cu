@@ -62,9 +62,18 @@ __global__ void rope_scatter_kernel(RopeScatterArgs a) {
         if (a.interleaved) { i = e >> 1; first = !(e & 1); }
         else { i = e < h2 ? e : e - h2; first = e < h2; }
         const int i1 = a.interleaved ? 2 * i : i, i2 = a.interleaved ? 2 * i + 1 : i + h2;
-        double sd, cd;
-        sincos(__dmul_rn((double)pos, a.inv_freq[i]), &sd, &cd);
-        const float c = (float)cd, s = (float)sd, x1 = src[i1], x2 = src[i2];
+        float c, s;
+        if (a.rope_cs) {  // the session's table: the same float64 sincos, rounded
+            const float2 cs = a.rope_cs[pos * h2 + i];
+            c = cs.x;
+            s = cs.y;
+        } else {
+            double sd, cd;
+            sincos(__dmul_rn((double)pos, a.inv_freq[i]), &sd, &cd);
+            c = (float)cd;
+            s = (float)sd;
+        }
+        const float x1 = src[i1], x2 = src[i2];
         out = first ? __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)) : __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     }
     if (isq) {

@@ -321,7 +321,7 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         if (!fused) {
             RopeScatterArgs ra{s->qkv, ldq, s->pos, m->inv_freq, T, Hl, Hkvl, D, c.context, c.rope_dims,
                                c.interleaved, c.cache_f16, s->qh, s->kc[l], s->vc[l],
-                               s->batched ? s->slot : nullptr, s->slot0};
+                               s->batched ? s->slot : nullptr, s->slot0, s->rope_cs};
             CK(launch_rope_scatter(ra, st, pdl));
         }
         const P2P attx = xch(4 * l, s->att, (long long)k * El);

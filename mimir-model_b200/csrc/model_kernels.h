@@ -35,6 +35,9 @@ struct RopeScatterArgs {
     void *kc, *vc;         // [slots][Hkv, C, D]
     const int32_t *slot;   // [T] sequence (cache) of each row, or null: every row in sequence slot0
     int slot0;
+    // the session's (f32(cos), f32(sin)) of pos * inv_freq[i] computed in
+    // float64, [C][rotary/2] (the same values sincos gives here), or null
+    const float2 *rope_cs;
 };
 // elements of one sequence's cache of one layer
 __host__ __device__ inline long long cache_slot_elems(int Hkv, int C, int D) { return (long long)Hkv * C * D; }
