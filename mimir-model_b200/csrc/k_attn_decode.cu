@@ -15,17 +15,24 @@
 // A block takes two query heads of one token (one kv head: the group size
 // must be even) and 256 threads.  Decode attention is latency-bound (a few
 // blocks per token), so the layout minimises serial steps:
-//  * The keys and values of earlier tokens stream through two 256-key chunk
+//  * The keys and values of earlier tokens stream through a ring of chunk
 //    buffers, requested BEFORE the grid dependency wait: they were written by
 //    earlier steps, all complete once this step's first kernel (the
 //    embedding) has passed its own wait, and nothing in this step writes them.
 //    The token's own key and value rows are made here (RoPE, f16) and read
 //    from shared memory, never from the cache.
-//  * A key chunk is two 3-D tensor copies (TMA) of [256 keys][64 elements]
-//    in the 128-byte swizzle, so the 16-byte loads of eight consecutive keys
-//    at one column hit eight distinct bank groups; a value chunk is one bulk
-//    copy of dense rows.  A thread scores one key for both heads with the
-//    whole row unrolled.
+//  * The chunk size is chosen at launch.  A grid of at most one block per
+//    SM (one token) takes 256-key chunks: few serial steps.  A larger grid
+//    (batched decode), or a context whose scores leave no room for two 64 KB
+//    buffers, takes 128-key chunks, so that three blocks share an SM and one
+//    block's serial phases (softmax, the key-ordered weighted sum) overlap
+//    the others' copies.
+//  * A key chunk is two 3-D tensor copies (TMA) of [CH keys][64 elements] in
+//    the 128-byte swizzle (one map per chunk size), so the 16-byte loads of
+//    eight consecutive keys at one column hit eight distinct bank groups; a
+//    value chunk is one bulk copy of dense rows.  A thread scores one key
+//    with the whole row unrolled: for both heads in a 256-key chunk, for one
+//    head (threads 0-127 the first) in a 128-key one.
 //  * The weighted sum: 128 threads, two output elements each, with the
 //    exponentials and value pairs of eight keys loaded ahead of the fused
 //    multiply-adds.
@@ -42,18 +49,19 @@ namespace mimgpu {
 namespace {
 
 constexpr int kD = 128;               // head elements
-constexpr int kCh = 256;              // keys per chunk
-constexpr int kRing = 2;              // chunk buffers
-constexpr int kSlot = kCh * kD * 2;   // 64 KB: a key chunk (two swizzled halves) or a value chunk
-constexpr int kHalf = kCh * 128;      // bytes of one 64-element half of a key chunk
+constexpr int kRing = 2;              // chunk buffers (one mbarrier each, below kOffQ)
+// CH keys per chunk: a buffer holds a key chunk (two swizzled 64-element
+// halves of CH rows) or a value chunk (CH dense rows)
+template <int CH> constexpr int slot_bytes() { return CH * kD * 2; }
 constexpr int kOffQ = 64, kOffNew = kOffQ + 2 * kD * 4, kOffRed = kOffNew + 2 * kD * 2, kOffQs = 1792, kOffRing = 2048;
 static_assert(kOffRed + 20 * 4 <= kOffQs && kOffQs + (int)sizeof(QuantScratch) <= kOffRing, "shared layout");
+static_assert(kRing * 8 <= kOffQ, "mbarriers below the query");
 constexpr int kSmemCap = 226 * 1024;  // + the static quantization scratch
 constexpr unsigned FULLM = 0xffffffffu;
 
 __host__ __device__ inline int sc_stride(int C) { return (C + 3) & ~3; }
-__host__ __device__ inline size_t dec_smem(int C) {
-    return (size_t)kOffRing + (size_t)kRing * kSlot + (size_t)2 * sc_stride(C) * 4;
+__host__ __device__ inline size_t dec_smem(int C, int ch) {
+    return (size_t)kOffRing + (size_t)kRing * ch * kD * 2 + (size_t)2 * sc_stride(C) * 4;
 }
 
 // Element e of one RoPE'd head (rope.v1, fast.go:507-557): pairs (i, i + r/2)
@@ -98,7 +106,12 @@ __device__ __forceinline__ void tma_3d(const CUtensorMap *map, uint8_t *dst, int
         : "memory");
 }
 
+// Three 128-key blocks share an SM when a thread holds at most 80 registers
+// (the 128-key instance uses fewer; -Xptxas -v shows it).
+template <int CH>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant__ AttnDecodeArgs p) {
+    static_assert(CH == 128 || CH == 256, "chunk of one key per thread and head, or per thread");
+    constexpr int kSlot = slot_bytes<CH>(), kHalf = CH * 128, kCh = CH;
     // No static shared memory: the dynamic block starts at the CTA's shared
     // base, so the swizzled key chunks at kOffRing are 1024-byte aligned.
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -111,7 +124,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     float *hmax = red + 16, *hsum = red + 18;
     uint8_t *ring = sm + kOffRing;
     const int ldsc = sc_stride(a.C);
-    float *sc = (float *)(sm + kOffRing + kRing * kSlot);  // [2][ldsc]
+    constexpr int R = kRing;
+    float *sc = (float *)(sm + kOffRing + R * kSlot);  // [2][ldsc]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t = blockIdx.y, h0 = 2 * blockIdx.x, G = a.H / a.Hkv, kvh = h0 / G;
     // the 128-byte swizzle needs a 1024-byte aligned destination: a block
@@ -122,7 +136,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
         return;
     }
     if (tid == 0) {
-        for (int b = 0; b < kRing; b++) mbar_init(&bar[b], 1);
+        for (int b = 0; b < R; b++) mbar_init(&bar[b], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -136,16 +150,16 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     const long long slot_elems = (long long)seq * cache_slot_elems(a.Hkv, a.C, kD);
     const long long head_off = slot_elems + (long long)kvh * a.C * kD;
     const uint16_t *vbase = (const uint16_t *)a.vc + head_off;
-    // item i into buffer i % kRing (lane 0 of warp 0): key chunk i (two
+    // item i into buffer i % R (lane 0 of warp 0): key chunk i (two
     // swizzled halves; rows past the context come as zeros) or value chunk
     // i - nch (rows [j0, n - 1): the token's own row is made here)
     auto issue = [&](int i) {
-        const int b = i % kRing;
+        const int b = i % R;
         uint8_t *dst = ring + (size_t)b * kSlot;
         if (i < nch) {
             mbar_arrive_expect_tx(&bar[b], (uint32_t)kSlot);
-            tma_3d(&p.kmap, dst, 0, i * kCh, seq * a.Hkv + kvh, &bar[b]);
-            tma_3d(&p.kmap, dst + kHalf, 64, i * kCh, seq * a.Hkv + kvh, &bar[b]);
+            tma_3d(&p.kmap[CH == 256 ? 0 : 1], dst, 0, i * kCh, seq * a.Hkv + kvh, &bar[b]);
+            tma_3d(&p.kmap[CH == 256 ? 0 : 1], dst + kHalf, 64, i * kCh, seq * a.Hkv + kvh, &bar[b]);
             return;
         }
         const int j0 = (i - nch) * kCh, len = min(kCh, n - 1 - j0);
@@ -157,7 +171,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
         bulk_g2s(dst, vbase + (long long)j0 * kD, (uint32_t)len * (kD * 2), &bar[b]);
     };
     if (tid == 0)
-        for (int i = 0; i < min(items, kRing); i++) issue(i);
+        for (int i = 0; i < min(items, R); i++) issue(i);
 
     // ---- after the wait: the token's q, k, v (the QKV product)
     pdl_wait();
@@ -182,15 +196,16 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    // ---- scores: thread = key tid of the chunk, both heads
+    // ---- scores: a 256-key chunk takes key tid for both heads, a 128-key
+    // chunk key tid % 128 for head tid / 128
     bool ok = true;
     const int n4 = n & ~3;
-    {
+    if constexpr (CH == 256) {
         const uint32_t knew_s = smem_u32(knew), ring_s = smem_u32(ring);
         const float *q0 = q, *q1 = q + kD;
         for (int c = 0; c < nch; c++) {
-            const int b = c % kRing, jj = tid, j = c * kCh + jj;
-            ok &= mbar_wait_bounded(&bar[b], (c / kRing) & 1, a.status);
+            const int b = c % R, jj = tid, j = c * kCh + jj;
+            ok &= mbar_wait_bounded(&bar[b], (c / R) & 1, a.status);
             if (j < n) {
                 // 16-byte unit c8 of key jj: half c8/8, row jj, swizzled unit (c8 % 8) ^ (jj % 8)
                 const bool own = j == n - 1;
@@ -217,9 +232,42 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
                 sc[ldsc + j] = __fmul_rn(vb, a.scale);
             }
             __syncthreads();  // every thread is done with buffer b
-            if (tid == 0 && c + kRing < items) {
+            if (tid == 0 && c + R < items) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue(c + kRing);
+                issue(c + R);
+            }
+        }
+    } else {
+        const uint32_t knew_s = smem_u32(knew), ring_s = smem_u32(ring);
+        const int hh = tid >> 7, jj = tid & (kCh - 1);
+        const float *qh = q + hh * kD;
+        float *sch = sc + hh * ldsc;
+        const uint32_t sw = (uint32_t)(jj & 7);
+        for (int c = 0; c < nch; c++) {
+            const int b = c % R, j = c * kCh + jj;
+            ok &= mbar_wait_bounded(&bar[b], (c / R) & 1, a.status);
+            if (j < n) {
+                const bool own = j == n - 1;
+                const uint32_t kb = ring_s + (uint32_t)(b * kSlot + jj * 128);
+                float la[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c8 = 0; c8 < kD / 8; c8++) {
+                    const uint32_t addr = own ? knew_s + 16 * c8
+                                              : kb + (uint32_t)((c8 >> 3) * kHalf) + ((((uint32_t)c8 & 7) ^ sw) << 4);
+                    uint4 w;
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w) : "r"(addr));
+                    fma8(la, *(const float4 *)(qh + 8 * c8), *(const float4 *)(qh + 8 * c8 + 4), w);
+                }
+                const float va = j < n4 ? __fadd_rn(__fadd_rn(__fadd_rn(la[0], la[1]), __fadd_rn(la[2], la[3])),
+                                                    __fadd_rn(__fadd_rn(la[4], la[5]), __fadd_rn(la[6], la[7])))
+                                        : __fadd_rn(__fadd_rn(__fadd_rn(la[0], la[4]), __fadd_rn(la[1], la[5])),
+                                                    __fadd_rn(__fadd_rn(la[2], la[6]), __fadd_rn(la[3], la[7])));
+                sch[j] = __fmul_rn(va, a.scale);
+            }
+            __syncthreads();  // every thread is done with buffer b
+            if (tid == 0 && c + R < items) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(c + R);
             }
         }
     }
@@ -264,8 +312,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     const float *e = sc + hw * ldsc;
     float acc0 = 0.f, acc1 = 0.f;
     for (int c = 0; c < nch; c++) {
-        const int i = nch + c, b = i % kRing, j0 = c * kCh;
-        ok &= mbar_wait_bounded(&bar[b], (i / kRing) & 1, a.status);
+        const int i = nch + c, b = i % R, j0 = c * kCh;
+        ok &= mbar_wait_bounded(&bar[b], (i / R) & 1, a.status);
         if (tid < 128) {
             const uint8_t *vb = ring + (size_t)b * kSlot + d0 * 2;
             const int lc = min(kCh, n - 1 - j0);  // rows from the ring (the token's own row after them)
@@ -293,9 +341,9 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
             }
         }
         __syncthreads();
-        if (tid == 0 && i + kRing < items) {
+        if (tid == 0 && i + R < items) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(i + kRing);
+            issue(i + R);
         }
     }
     (void)ok;  // a wait that ran out has set DEV_TIMEOUT in *status: the host reports it
@@ -326,19 +374,31 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap *out) {
+bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap out[2]) {
     const EncodeTiledFn fn = (EncodeTiledFn)tmap_encode_fn();
     if (!fn || !kc || ((uintptr_t)kc & 15) || slots <= 0 || Hkv <= 0 || C <= 0) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)C, (cuuint64_t)slots * Hkv};
     const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)C * kD * 2};
-    const cuuint32_t box[3] = {64, (cuuint32_t)kCh, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(kc), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    for (int m = 0; m < 2; m++) {  // box rows: 256, then 128
+        const cuuint32_t box[3] = {64, (cuuint32_t)(256 >> m), 1};
+        if (fn(&out[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(kc), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
 }
 
-int attn_decode_max_context() { return (int)((kSmemCap - kOffRing - (size_t)kRing * kSlot) / 8) & ~3; }
+int attn_decode_max_context() { return (int)((kSmemCap - kOffRing - (size_t)kRing * slot_bytes<128>()) / 8) & ~3; }
+
+// Keys per chunk for a launch: 256 for a grid of at most one block per SM
+// whose scores leave room for two 256-key buffers, else 128, so that several
+// blocks share an SM.
+static int decode_chunk(const AttnArgs2 &a) {
+    const bool room = dec_smem(a.C, 256) <= kSmemCap;
+    return (a.H / 2) * a.T <= num_sms() && room ? 256 : 128;
+}
 
 bool attn_decode_ok(const AttnArgs2 &a) {
     return a.cache_f16 && a.D == kD && a.Hkv > 0 && a.H % a.Hkv == 0 && (a.H / a.Hkv) % 2 == 0 && a.T >= 1 &&
@@ -349,8 +409,10 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs &p, cudaStream_t st, bool pd
     const AttnArgs2 &a = p.at;
     if (!attn_decode_ok(a) || !p.qkv || !p.rope_cs || p.rotary <= 0 || p.rotary > kD || p.rotary % 2)
         return cudaErrorInvalidValue;
-    const size_t smem = dec_smem(a.C);
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int ch = decode_chunk(a);
+    const size_t smem = dec_smem(a.C, ch);
+    void (*kern)(AttnDecodeArgs) = ch == 256 ? attn_decode_kernel<256> : attn_decode_kernel<128>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.H / 2, a.T);
@@ -362,7 +424,7 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs &p, cudaStream_t st, bool pd
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, p);
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace mimgpu

@@ -309,7 +309,8 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         auto attend = [&](const AttnArgs2 &x) -> cudaError_t {
             if (!fused) return launch_attn_exact(x, st, pdl);
             AttnDecodeArgs da{};
-            da.kmap = s->kmap[l];
+            da.kmap[0] = s->kmap[2 * l];
+            da.kmap[1] = s->kmap[2 * l + 1];
             da.at = x;
             da.qkv = s->qkv;
             da.ldq = ldq;
@@ -730,10 +731,10 @@ int mimgpu_session_new_slots(mimgpu_model *m, int slots, mimgpu_session **out) {
     if (e == cudaSuccess && half > 0) e = cudaMalloc(&s->rope_cs, (size_t)k.context * half * sizeof(float2));
     if (e == cudaSuccess && half > 0) e = launch_rope_table(m->inv_freq, k.context, half, s->rope_cs, s->st);
     if (e == cudaSuccess && k.cache_f16 && D == 128) {
-        s->kmap.resize(k.layers);
+        s->kmap.resize(2 * (size_t)k.layers);  // two per layer: 256- and 128-key boxes
         s->kmap_ok = true;
         for (int l = 0; l < k.layers; l++)
-            s->kmap_ok = s->kmap_ok && attn_decode_kmap(s->kc[l], slots, k.kv_heads / N, k.context, &s->kmap[l]);
+            s->kmap_ok = s->kmap_ok && attn_decode_kmap(s->kc[l], slots, k.kv_heads / N, k.context, &s->kmap[2 * l]);
     }
     if (e != cudaSuccess) {
         free_session(s);

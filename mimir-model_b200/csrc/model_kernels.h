@@ -93,7 +93,7 @@ cudaError_t launch_attn_exact(const AttnArgs2 &a, cudaStream_t st, bool pdl);
 // the caller's forward must start with a kernel that waits for the previous
 // forward before it lets its dependents launch (embedding_kernel does).
 struct AttnDecodeArgs {
-    CUtensorMap kmap;      // the layer's key cache [slots * Hkv][C][D] f16: box [64][256][1], 128-byte swizzle
+    CUtensorMap kmap[2];   // the layer's key cache [slots * Hkv][C][D] f16: boxes [64][256][1], [64][128][1], 128-byte swizzle
     AttnArgs2 at;          // qh unused
     const float *qkv;      // [T, ldq]: q (H*D) | k (Hkv*D) | v (Hkv*D), before RoPE
     long long ldq;
@@ -101,8 +101,9 @@ struct AttnDecodeArgs {
     int rotary, interleaved;
 };
 int attn_decode_max_context();
-// The key-cache map of one layer for launch_attn_decode (false: no driver encoder).
-bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap *out);
+// The key-cache maps of one layer for launch_attn_decode, one per chunk size
+// (false: no driver encoder).
+bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap out[2]);
 bool attn_decode_ok(const AttnArgs2 &a);
 cudaError_t launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t st, bool pdl);
 // wait / keys: tensor parallelism, the ranks' keys arrive in keys[0..N)
