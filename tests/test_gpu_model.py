@@ -162,7 +162,7 @@ def test_8b_layer_shapes_token_identity(ctx):
     m.free()
 
 
-@pytest.mark.parametrize("T", [8, 160])
+@pytest.mark.parametrize("T", [8, 24, 160])
 def test_refused_rows_same_in_step_and_prompt(ctx, T):
     """Weight rows with a non-finite block scale take the f32 product
     (linearA8, interp/fast.go:282-379) on every path: a one-token step, whose
@@ -182,7 +182,9 @@ def test_refused_rows_same_in_step_and_prompt(ctx, T):
         b[o:o + 2] = bytes([0x00, 0x7C])  # d = +inf in the row's first block
         w[name] = (dt, np.frombuffer(bytes(b), np.uint8))
     C = 192
-    # 160 tokens: the prompt pass takes the one-block-per-row rms_norm
+    # 24 tokens: the prompt pass's products split K over several CTAs (few
+    # row tiles), refused pairs included in the chain kernel; 160 tokens:
+    # the prompt pass takes the one-block-per-row rms_norm
     ids = ((np.arange(T) * 37 + 3) % 700).astype(np.int32)
     m = mimgpu.Model(ctx, dict(cfg, context=C, a8=1, cache_f16=1, interleaved=1, max_tokens=T), w)
     s = m.session()
