@@ -287,9 +287,11 @@ class MimFile:
             if s.hash_alg == 1 and hashlib.sha256(self._b[s.offset:s.offset + s.length]).digest() != s.hash:
                 raise MimError("hash-mismatch", f"section kind {s.kind}")
 
-    def metadata(self) -> dict:
+    def metadata(self, typed: bool = False) -> dict:
         """The metadata section as {key: value} (spec/metadata.md); ints,
-        uints, floats, bools, strings, bytes and arrays decoded."""
+        uints, floats, bools, strings, bytes and arrays decoded.  typed:
+        {key: (type, value)}, the entry's type kept (1 int64, 2 uint64, ...),
+        as the writer takes them back."""
         m = self.section_bytes(METADATA)
         if m is None:
             return {}
@@ -332,7 +334,7 @@ class MimFile:
                 v = [pool_bytes(tab[2 * j], tab[2 * j + 1]).decode("utf-8") for j in range(cnt)]
             else:
                 raise MimError("bad-metadata", f"{key}: type {typ}")
-            out[key] = v
+            out[key] = (typ, v) if typed else v
         return out
 
 
