@@ -194,6 +194,21 @@ def build_model(ctx, cfg, context, max_tokens, tp=None):
     return mimgpu.Model(ctx, full, weights), weights
 
 
+def write_mim(ctx, cfg, weights, path, context):
+    """The benchmark model as a mim file: every tensor under its GGUF name,
+    the Llama hyperparameters as a GGUF carries them, and the reference
+    importer's forward graph with dequant_matmul_a8.v2 products and an f16
+    cache (mimwriter.write_llama), so the reference's interpreter and
+    mimgpu.load_llama both run it.  Each tensor is read back from the device
+    when the file is written.  Returns the file's size in bytes."""
+    import mimwriter
+    tensors = {name: (dt, t.shape, (lambda t=t: ctx.download(t).tobytes())) for name, (dt, t) in weights.items()}
+    md = mimwriter.llama_metadata(dict(cfg, context=context), name=f"synthetic {cfg['layers']}-layer Q4_K_M "
+                                  f"(seeded N(0,0.02) weights)")
+    mimwriter.write_llama(path, cfg, tensors, a8=True, cache_f16=True, context=context, metadata=md)
+    return os.path.getsize(path)
+
+
 def gemv_roofline(ctx, cfg, weights, torch, reps=3):
     """The one-row GEMV alone over the decode step's own launch list -- per
     layer q|k|v (one fused launch), o, gate|up (one fused launch), down, then
@@ -309,7 +324,14 @@ def run_gpu(args):
     # or with --tp; otherwise N independent replicas, one sequence per GPU
     use_tp = world > 1 and (args.tp or args.shape == "70b")
     # a tensor-parallel rank makes and holds only its own rows of every split matrix
-    model, weights = build_model(ctx, cfg, context, prompt, (world, rank) if use_tp else None)
+    if args.mim:
+        if use_tp:
+            raise SystemExit("--mim runs one GPU or replicas, not tensor parallelism")
+        # the model from a mim file (written by --write-mim, or by the reference's importer)
+        model = mimgpu.load_llama(ctx, args.mim, max_tokens=prompt, context=context)
+        weights = {n: (t.dtype, t) for n, t in model.weights.items()}
+    else:
+        model, weights = build_model(ctx, cfg, context, prompt, (world, rank) if use_tp else None)
     tp = None
     if use_tp:
         # each rank computes its output rows of every matrix, bit-identical to one GPU
@@ -399,7 +421,8 @@ def run_gpu(args):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if use_tp else "weak",
         "vs_baseline": round(value / PUBLISHED_8B, 2) if args.shape == "8b" else None, "dtype": "int8",
-        "data": "synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)",
+        "data": ("synthetic (seeded N(0,0.02) weights quantized Q4_K_M on the device; seeded random prompt ids)"
+                 if not args.mim else f"weights from the mim file {os.path.basename(args.mim)}; seeded random prompt ids"),
         "config": {"workload": ("8B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 3)" if args.shape == "8b"
                                 else "70B-shape Q4_K_M greedy decode, batch 1 (BASELINE config 5)"),
                    "layers": cfg["layers"], "d_model": cfg["embed"], "heads": cfg["heads"],
@@ -753,6 +776,23 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_write_mim(args):
+    """--write-mim: the benchmark model of --shape / --layers, made on the
+    device as the bench makes it, written as a mim file."""
+    import mimgpu
+    cfg = dict(SHAPES[args.shape], layers=args.layers)
+    ctx = mimgpu.Context(int(os.environ.get("LOCAL_RANK", "0")))
+    model, weights = build_model(ctx, cfg, args.context, 1)
+    t0 = time.time()
+    n = write_mim(ctx, cfg, weights, args.write_mim, args.context)
+    print(json.dumps({"wrote": args.write_mim, "bytes": n, "shape": args.shape, "layers": args.layers,
+                      "context": args.context, "seconds": round(time.time() - t0, 1)}), flush=True)
+    model.free()
+    for _, t in weights.values():
+        t.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -775,13 +815,21 @@ def main():
     ap.add_argument("--gemv-hot", action="store_true", help="GEMV-only mode with one weight copy (L2-hot)")
     ap.add_argument("--prefill", default="", help="prefill mode (config 4): prompt lengths, e.g. 512,2048")
     ap.add_argument("--batch", type=int, default=0, help="batched decode mode (config 4): sequences, e.g. 32")
-    ap.add_argument("--context", type=int, default=1024, help="key-value cache per sequence in --batch mode")
+    ap.add_argument("--context", type=int, default=1024,
+                    help="key-value cache per sequence in --batch mode, and the cache --write-mim records")
+    ap.add_argument("--write-mim", default="", metavar="PATH",
+                    help="write the --shape / --layers benchmark model as a mim file and exit")
+    ap.add_argument("--mim", default="", metavar="PATH",
+                    help="decode bench from a mim file (the --shape / --layers of the file) instead of weights "
+                         "made on the device")
     args = ap.parse_args()
     if not args.layers:
         args.layers = SHAPES[args.shape]["layers"]
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    if args.gemv:
+    if args.write_mim:
+        run_write_mim(args)
+    elif args.gemv:
         run_gemv(args)
     elif args.prefill:
         run_prefill(args)

@@ -135,8 +135,18 @@ class _WTensor:
     name: str
     dtype: int
     shape: tuple
-    data: bytes
+    data: object   # bytes, or a callable returning them (read twice: hash, then write)
+    length: int
     offset: int = 0
+
+    def bytes(self) -> bytes:
+        if not callable(self.data):
+            return self.data
+        b = self.data()
+        b = b if isinstance(b, bytes) else bytes(b)
+        if len(b) != self.length:
+            raise MimError("size-mismatch", f"tensor {self.name!r} gave {len(b)} bytes, needs {self.length}")
+        return b
 
 
 class MimWriter:
@@ -151,6 +161,10 @@ class MimWriter:
         self._names: set[str] = set()
 
     def add_tensor(self, name: str, dtype: int, shape, data) -> None:
+        """data: the tensor's bytes, or a callable that returns them when the
+        file is written (called twice with hashes on: once for the weights
+        section's SHA-256, once to write), so large models need not sit in
+        host memory whole."""
         nb = name.encode("utf-8")
         if not nb or len(nb) > MAX_NAME:
             raise MimError("bad-name", repr(name))
@@ -161,12 +175,13 @@ class MimWriter:
             raise MimError("bad-shape", f"tensor {name!r} rank {len(shape)}")
         if dtype not in DTYPES:
             raise MimError("unsupported-dtype", f"tensor {name!r} dtype {dtype}")
-        data = data if isinstance(data, bytes) else bytes(data)
         need = _nbytes(dtype, shape)
-        if need != len(data):
-            raise MimError("size-mismatch", f"tensor {name!r} needs {need} bytes, got {len(data)}")
+        if not callable(data):
+            data = data if isinstance(data, bytes) else bytes(data)
+            if need != len(data):
+                raise MimError("size-mismatch", f"tensor {name!r} needs {need} bytes, got {len(data)}")
         self._names.add(name)
-        self.tensors.append(_WTensor(name, dtype, shape, data))
+        self.tensors.append(_WTensor(name, dtype, shape, data, need))
 
     def add_section(self, kind: int, data: bytes, required: bool = False) -> None:
         if kind == WEIGHTS or any(k == kind for k, _, _ in self.sections):
@@ -177,8 +192,8 @@ class MimWriter:
         """Offsets of the canonical packing, in insertion order; the length."""
         end = 0
         for t in self.tensors:
-            t.offset = _up(end, LARGE_ALIGN if len(t.data) >= LARGE else TENSOR_ALIGN)
-            end = t.offset + len(t.data)
+            t.offset = _up(end, LARGE_ALIGN if t.length >= LARGE else TENSOR_ALIGN)
+            end = t.offset + t.length
         return end
 
     def _weight_chunks(self):
@@ -186,8 +201,8 @@ class MimWriter:
         for t in self.tensors:
             if t.offset > at:
                 yield bytes(t.offset - at)
-            yield t.data
-            at = t.offset + len(t.data)
+            yield t.bytes()
+            at = t.offset + t.length
 
     def chunks(self):
         """The file as a sequence of byte strings (the weights are not
@@ -225,7 +240,7 @@ class MimWriter:
         for t in order:
             dims = list(t.shape) + [0] * (MAX_RANK - len(t.shape))
             head += struct.pack("<IIIB3x8QQQ", name_off[t.name], len(t.name.encode("utf-8")), t.dtype,
-                                len(t.shape), *dims, t.offset, len(t.data))
+                                len(t.shape), *dims, t.offset, t.length)
         head += pool
         yield bytes(head)
         at = len(head)
@@ -571,7 +586,8 @@ def write_llama(path: str | None, cfg: dict, tensors: dict, *, a8: bool = True, 
 
     cfg: layers, embed, ffn, heads, kv_heads, rope_dims, rope_theta, norm_eps
     (head_dim = embed / heads, the vocabulary from token_embd.weight).
-    tensors: {GGUF name: (dtype, shape, bytes)}, every tensor of the file.
+    tensors: {GGUF name: (dtype, shape, bytes or a callable returning them)},
+    every tensor of the file.
     metadata: the entries to keep (llama_metadata(cfg) when None); the
     builder adds mim.context_length (and mim.slots), the importer
     import.source_format.  a8 writes the quantized products as
