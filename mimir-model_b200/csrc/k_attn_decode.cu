@@ -53,15 +53,27 @@ constexpr int kRing = 2;              // chunk buffers (one mbarrier each, below
 // CH keys per chunk: a buffer holds a key chunk (two swizzled 64-element
 // halves of CH rows) or a value chunk (CH dense rows)
 template <int CH> constexpr int slot_bytes() { return CH * kD * 2; }
-constexpr int kOffQ = 64, kOffNew = kOffQ + 2 * kD * 4, kOffRed = kOffNew + 2 * kD * 2, kOffQs = 1792, kOffRing = 2048;
-static_assert(kOffRed + 20 * 4 <= kOffQs && kOffQs + (int)sizeof(QuantScratch) <= kOffRing, "shared layout");
+// Shared layout of a block of HPB query heads: mbarriers, the queries (then
+// the outputs) [HPB][kD] f32, the token's key and value rows f16, the
+// softmax's lane sums [HPB][8], maxima [HPB] and sums [HPB], the
+// quantization scratch, then the chunk ring (1024-byte aligned for the
+// swizzle) and the scores [HPB][C].
+constexpr int kOffQ = 64;
+template <int HPB> struct Lay {
+    static constexpr int kOffNew = kOffQ + HPB * kD * 4, kOffRed = kOffNew + 2 * kD * 2;
+    static constexpr int kOffQs = HPB == 2 ? 1792 : 2816, kOffRing = HPB == 2 ? 2048 : 3072;
+    static_assert(kOffRed + 10 * HPB * 4 <= kOffQs && kOffQs + (int)sizeof(QuantScratch) <= kOffRing,
+                  "shared layout");
+    static_assert(kOffRing % 1024 == 0, "swizzled ring alignment");
+};
 static_assert(kRing * 8 <= kOffQ, "mbarriers below the query");
 constexpr int kSmemCap = 226 * 1024;  // + the static quantization scratch
 constexpr unsigned FULLM = 0xffffffffu;
 
 __host__ __device__ inline int sc_stride(int C) { return (C + 3) & ~3; }
-__host__ __device__ inline size_t dec_smem(int C, int ch) {
-    return (size_t)kOffRing + (size_t)kRing * ch * kD * 2 + (size_t)2 * sc_stride(C) * 4;
+__host__ __device__ inline size_t dec_smem(int C, int ch, int hpb) {
+    return (size_t)(hpb == 2 ? Lay<2>::kOffRing : Lay<4>::kOffRing) + (size_t)kRing * ch * kD * 2 +
+           (size_t)hpb * sc_stride(C) * 4;
 }
 
 // Element e of one RoPE'd head (rope.v1, fast.go:507-557): pairs (i, i + r/2)
@@ -106,28 +118,32 @@ __device__ __forceinline__ void tma_3d(const CUtensorMap *map, uint8_t *dst, int
         : "memory");
 }
 
-// Three 128-key blocks share an SM when a thread holds at most 80 registers
-// (the 128-key instance uses fewer; -Xptxas -v shows it).
-template <int CH>
+// Three 128-key blocks of two heads share an SM when a thread holds at most
+// 80 registers (that instance uses fewer; -Xptxas -v shows it); blocks of
+// four heads take twice the scores and fit two to an SM.
+template <int CH, int HPB>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant__ AttnDecodeArgs p) {
     static_assert(CH == 128 || CH == 256, "chunk of one key per thread and head, or per thread");
+    static_assert(HPB == 2 || (HPB == 4 && CH == 128), "two heads a block, or four with 128-key chunks");
     constexpr int kSlot = slot_bytes<CH>(), kHalf = CH * 128, kCh = CH;
+    constexpr int kOffNew = Lay<HPB>::kOffNew, kOffRed = Lay<HPB>::kOffRed, kOffQs = Lay<HPB>::kOffQs,
+                  kOffRing = Lay<HPB>::kOffRing;
     // No static shared memory: the dynamic block starts at the CTA's shared
     // base, so the swizzled key chunks at kOffRing are 1024-byte aligned.
     extern __shared__ __align__(1024) uint8_t sm[];
     QuantScratch &qs = *(QuantScratch *)(sm + kOffQs);
     const AttnArgs2 &a = p.at;
     uint64_t *bar = (uint64_t *)sm;
-    float *q = (float *)(sm + kOffQ);                  // [2][kD]; the outputs at the end
+    float *q = (float *)(sm + kOffQ);                  // [HPB][kD]; the outputs at the end
     uint16_t *knew = (uint16_t *)(sm + kOffNew), *vnew = knew + kD;
-    float *red = (float *)(sm + kOffRed);              // [2][8] lane sums, then max[2], sum[2]
-    float *hmax = red + 16, *hsum = red + 18;
+    float *red = (float *)(sm + kOffRed);              // [HPB][8] lane sums, then max[HPB], sum[HPB]
+    float *hmax = red + 8 * HPB, *hsum = hmax + HPB;
     uint8_t *ring = sm + kOffRing;
     const int ldsc = sc_stride(a.C);
     constexpr int R = kRing;
-    float *sc = (float *)(sm + kOffRing + R * kSlot);  // [2][ldsc]
+    float *sc = (float *)(sm + kOffRing + R * kSlot);  // [HPB][ldsc]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t = blockIdx.y, h0 = 2 * blockIdx.x, G = a.H / a.Hkv, kvh = h0 / G;
+    const int t = blockIdx.y, h0 = HPB * blockIdx.x, G = a.H / a.Hkv, kvh = h0 / G;
     // the 128-byte swizzle needs a 1024-byte aligned destination: a block
     // placed otherwise reports DEV_BADARG and copies nothing
     if (smem_u32(ring) & 1023u) {
@@ -178,9 +194,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     const float *row = p.qkv + (long long)t * p.ldq;
     const float2 *cs = p.rope_cs + pos * (p.rotary / 2);
     const uint64_t keep = l2_policy_evict_last();
-    {
+    if constexpr (HPB == 2) {
         const int hh = tid >> 7, e = tid & (kD - 1);
         q[hh * kD + e] = rope_elem(row + (long long)(h0 + hh) * kD, e, p.rotary, p.interleaved, cs, keep);
+    } else {
+#pragma unroll
+        for (int u = 0; u < HPB / 2; u++) {
+            const int hh = 2 * u + (tid >> 7), e = tid & (kD - 1);
+            q[hh * kD + e] = rope_elem(row + (long long)(h0 + hh) * kD, e, p.rotary, p.interleaved, cs, keep);
+        }
     }
     const bool writer = h0 % G == 0;  // one block of each kv group writes the cache rows
     const long long at = head_off + pos * kD;
@@ -196,15 +218,18 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    // ---- scores: a 256-key chunk takes key tid for both heads, a 128-key
-    // chunk key tid % 128 for head tid / 128
+    // ---- scores: a 256-key chunk takes key tid for both heads; a 128-key
+    // chunk of two heads key tid % 128 for head tid / 128, of four heads key
+    // tid % 128 for heads 2 (tid / 128) and 2 (tid / 128) + 1
     bool ok = true;
     const int n4 = n & ~3;
-    if constexpr (CH == 256) {
+    if constexpr (CH == 256 || HPB == 4) {
         const uint32_t knew_s = smem_u32(knew), ring_s = smem_u32(ring);
-        const float *q0 = q, *q1 = q + kD;
+        const int hb = CH == 256 ? 0 : 2 * (tid >> 7);  // the thread's first head
+        const float *q0 = q + hb * kD, *q1 = q0 + kD;
+        float *sc0 = sc + hb * ldsc;
         for (int c = 0; c < nch; c++) {
-            const int b = c % R, jj = tid, j = c * kCh + jj;
+            const int b = c % R, jj = CH == 256 ? tid : tid & (kCh - 1), j = c * kCh + jj;
             ok &= mbar_wait_bounded(&bar[b], (c / R) & 1, a.status);
             if (j < n) {
                 // 16-byte unit c8 of key jj: half c8/8, row jj, swizzled unit (c8 % 8) ^ (jj % 8)
@@ -228,8 +253,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
                                                     __fadd_rn(__fadd_rn(lb[4], lb[5]), __fadd_rn(lb[6], lb[7])))
                                         : __fadd_rn(__fadd_rn(__fadd_rn(lb[0], lb[4]), __fadd_rn(lb[1], lb[5])),
                                                     __fadd_rn(__fadd_rn(lb[2], lb[6]), __fadd_rn(lb[3], lb[7])));
-                sc[j] = __fmul_rn(va, a.scale);
-                sc[ldsc + j] = __fmul_rn(vb, a.scale);
+                sc0[j] = __fmul_rn(va, a.scale);
+                sc0[ldsc + j] = __fmul_rn(vb, a.scale);
             }
             __syncthreads();  // every thread is done with buffer b
             if (tid == 0 && c + R < items) {
@@ -272,7 +297,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
         }
     }
     // ---- softmax: max per head (exact in any order)
-    if (warp < 2) {
+    if (warp < HPB) {
         float m = -INFINITY;
         for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[warp * ldsc + j]);
         m = warp_max(m);
@@ -282,14 +307,14 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     // exponentials: Cephes on the first n&~7 keys (none when n < 8), float64 on the rest
     const int n8 = n >= 8 ? (n & ~7) : 0;
 #pragma unroll
-    for (int hh = 0; hh < 2; hh++)
+    for (int hh = 0; hh < HPB; hh++)
         for (int j = tid; j < n; j += 256) {
             const float x = __fsub_rn(sc[hh * ldsc + j], hmax[hh]);
             sc[hh * ldsc + j] = j < n8 ? expf_amd64(x) : (float)exp((double)x);
         }
     __syncthreads();
     // ExpSumF32's sum: eight lane sums in key order, combined, then the tail in order
-    if (tid < 16) {
+    if (tid < 8 * HPB) {
         const int hh = tid >> 3, ll = tid & 7;
         const float *e = sc + hh * ldsc;
         float sl = 0.f;
@@ -298,7 +323,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
         red[hh * 8 + ll] = sl;
     }
     __syncthreads();
-    if (tid < 2) {
+    if (tid < HPB) {
         const float *r = red + tid * 8;
         float sum = 0.f;
         if (n8) sum = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[4]), __fadd_rn(r[1], r[5])),
@@ -307,14 +332,14 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
         hsum[tid] = sum;
     }
     // ---- weighted sum of the values, one fused multiply-add per key in key
-    // order: thread tid < 128 takes elements d0, d0 + 1 of head tid / 64
+    // order: thread tid < 64 HPB takes elements d0, d0 + 1 of head tid / 64
     const int hw = tid >> 6, d0 = (tid & 63) * 2;
     const float *e = sc + hw * ldsc;
     float acc0 = 0.f, acc1 = 0.f;
     for (int c = 0; c < nch; c++) {
         const int i = nch + c, b = i % R, j0 = c * kCh;
         ok &= mbar_wait_bounded(&bar[b], (i / R) & 1, a.status);
-        if (tid < 128) {
+        if (tid < 64 * HPB) {
             const uint8_t *vb = ring + (size_t)b * kSlot + d0 * 2;
             const int lc = min(kCh, n - 1 - j0);  // rows from the ring (the token's own row after them)
             int jj = 0;
@@ -348,23 +373,45 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     }
     (void)ok;  // a wait that ran out has set DEV_TIMEOUT in *status: the host reports it
     // ---- outputs: o = acc / sum, in element order through shared memory
-    if (tid < 128) {
+    if (tid < 64 * HPB) {
         q[hw * kD + d0] = __fdiv_rn(acc0, hsum[hw]);
         q[hw * kD + d0 + 1] = __fdiv_rn(acc1, hsum[hw]);
     }
     __syncthreads();
     const int E = a.H * kD;
-    const float o = q[tid];
-    a.out[(long long)t * E + (long long)h0 * kD + tid] = o;
-    // tensor parallelism: this rank's heads into every rank's full vector
-    for (int r = 0; r < (a.put.N > 1 ? a.put.N : 0); r++)
-        peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * kD + tid] = o;
-    if (a.put.N > 1) {
-        // visible system-wide before the kernel ends (the next kernel publishes the exchange)
-        __syncthreads();
-        if (tid == 0) __threadfence_system();
+    if constexpr (HPB == 2) {
+        const float o = q[tid];
+        a.out[(long long)t * E + (long long)h0 * kD + tid] = o;
+        // tensor parallelism: this rank's heads into every rank's full vector
+        for (int r = 0; r < (a.put.N > 1 ? a.put.N : 0); r++)
+            peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * kD + tid] = o;
+        if (a.put.N > 1) {
+            // visible system-wide before the kernel ends (the next kernel publishes the exchange)
+            __syncthreads();
+            if (tid == 0) __threadfence_system();
+        }
+        if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
+    } else {
+        // HPB / 2 quantization blocks of 256 outputs each
+#pragma unroll
+        for (int u = 0; u < HPB / 2; u++) {
+            const float o = q[256 * u + tid];
+            a.out[(long long)t * E + (long long)h0 * kD + 256 * u + tid] = o;
+            for (int r = 0; r < (a.put.N > 1 ? a.put.N : 0); r++)
+                peer_ptr<float>(a.put, r, a.put.off)[a.put.col0 + (long long)h0 * kD + 256 * u + tid] = o;
+        }
+        if (a.put.N > 1) {
+            __syncthreads();
+            if (tid == 0) __threadfence_system();
+        }
+        if (a.act.q) {
+#pragma unroll
+            for (int u = 0; u < HPB / 2; u++) {
+                if (u) __syncthreads();  // the scratch of the previous block is read
+                quant_block_256(q[256 * u + tid], t, E, (HPB / 2) * blockIdx.x + u, a.act, qs);
+            }
+        }
     }
-    if (a.act.q) quant_block_256(o, t, E, blockIdx.x, a.act, qs);
 }
 
 }  // namespace
@@ -390,14 +437,25 @@ bool attn_decode_kmap(const void *kc, int slots, int Hkv, int C, CUtensorMap out
     return true;
 }
 
-int attn_decode_max_context() { return (int)((kSmemCap - kOffRing - (size_t)kRing * slot_bytes<128>()) / 8) & ~3; }
+int attn_decode_max_context() {
+    return (int)((kSmemCap - Lay<2>::kOffRing - (size_t)kRing * slot_bytes<128>()) / 8) & ~3;
+}
 
-// Keys per chunk for a launch: 256 for a grid of at most one block per SM
-// whose scores leave room for two 256-key buffers, else 128, so that several
-// blocks share an SM.
-static int decode_chunk(const AttnArgs2 &a) {
-    const bool room = dec_smem(a.C, 256) <= kSmemCap;
-    return (a.H / 2) * a.T <= num_sms() && room ? 256 : 128;
+// The shape of a launch: 256-key chunks and two heads a block for a grid of
+// at most one block per SM whose scores leave room for two 256-key buffers;
+// else 128-key chunks, so that several blocks share an SM, with four heads
+// a block (each kv head's rows read into shared memory once per four query
+// heads) when the group size allows, the scores fit and the grid still has
+// a block for every SM.
+static void decode_shape(const AttnArgs2 &a, int *ch, int *hpb) {
+    const int G = a.H / a.Hkv;
+    if ((a.H / 2) * a.T <= num_sms() && dec_smem(a.C, 256, 2) <= kSmemCap) {
+        *ch = 256;
+        *hpb = 2;
+        return;
+    }
+    *ch = 128;
+    *hpb = G % 4 == 0 && dec_smem(a.C, 128, 4) <= kSmemCap && (a.H / 4) * a.T >= num_sms() ? 4 : 2;
 }
 
 bool attn_decode_ok(const AttnArgs2 &a) {
@@ -409,13 +467,15 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs &p, cudaStream_t st, bool pd
     const AttnArgs2 &a = p.at;
     if (!attn_decode_ok(a) || !p.qkv || !p.rope_cs || p.rotary <= 0 || p.rotary > kD || p.rotary % 2)
         return cudaErrorInvalidValue;
-    const int ch = decode_chunk(a);
-    const size_t smem = dec_smem(a.C, ch);
-    void (*kern)(AttnDecodeArgs) = ch == 256 ? attn_decode_kernel<256> : attn_decode_kernel<128>;
+    int ch = 0, hpb = 0;
+    decode_shape(a, &ch, &hpb);
+    const size_t smem = dec_smem(a.C, ch, hpb);
+    void (*kern)(AttnDecodeArgs) = ch == 256 ? attn_decode_kernel<256, 2>
+                                   : hpb == 4 ? attn_decode_kernel<128, 4> : attn_decode_kernel<128, 2>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.H / 2, a.T);
+    cfg.gridDim = dim3(a.H / hpb, a.T);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

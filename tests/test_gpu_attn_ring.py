@@ -5,8 +5,10 @@ ring of chunk buffers whose chunk size and depth are chosen at launch: a
 one-token grid takes 256-key chunks and as many buffers as fit beside the
 scores (three at a 1,100-token cache, two at 8,192); a batched grid of more
 blocks than SMs, or a cache whose scores leave no room for two 256-key
-buffers (14,000 tokens), takes two 128-key buffers, so that three blocks
-share an SM.  These cases wrap the ring many times, cross chunk boundaries
+buffers (14,000 tokens), takes two 128-key buffers, so that several blocks
+share an SM, and blocks of four query heads when the group size allows and
+there are still as many blocks as SMs (40 sequences here; 20 keep blocks
+of two).  These cases wrap the ring many times, cross chunk boundaries
 (a context of 128·k + 1 keys leaves the last value chunk with only the
 token's own row) and are checked bit for bit: one-token steps
 against the CPU restatement of the reference (attendRow with the amd64
@@ -67,15 +69,17 @@ def test_long_context_steps_bit_exact(ctx, C):
     m.free()
 
 
-def test_batched_long_contexts_match_single_sequences(ctx):
-    """20 sequences of 16 query heads (160 blocks per step: more than the
-    SMs, so the two-buffer ring), prompts of 129-600 tokens (including the
+@pytest.mark.parametrize("B", [20, 40])
+def test_batched_long_contexts_match_single_sequences(ctx, B):
+    """B sequences of 16 query heads in groups of four (more blocks of two
+    heads than SMs: 128-key chunks; at 40 sequences blocks of four heads),
+    prompts of 128-600 tokens (including the
     128·k + 1 and 128·k edges), 6 greedy steps: every sequence's ids and
     the logits of one more batched row equal a single-sequence session's."""
     import mimgpu
     from test_gpu_model import _synthetic
     cfg, w = _synthetic(2, 2048, 16, 4, 1024, 700, seed=12)
-    B, steps = 20, 6
+    steps = 6
     m = mimgpu.Model(ctx, dict(cfg, context=640, a8=1, cache_f16=1, interleaved=1, max_tokens=600), w)
     rng = np.random.default_rng(5)
     lens = [128, 129, 256, 257, 600] + [int(v) for v in rng.integers(130, 600, B - 5)]
