@@ -556,21 +556,21 @@ class _LlamaGraph:
         self.main[2].append(logits)
 
 
-def llama_metadata(cfg: dict, name: str = "") -> dict:
-    """The hyperparameter entries a Llama GGUF carries, as the reference's
-    GGUF importer keeps them (unsigned integers, float64): the keys
-    importer/llama.go:104-162 (LlamaConfigOf) reads back."""
+def llama_metadata(cfg: dict, name: str = "", arch: str = "llama") -> dict:
+    """The hyperparameter entries a Llama (or Qwen 2) GGUF carries, as the
+    reference's GGUF importer keeps them (unsigned integers, float64): the
+    keys importer/llama.go:104-162 (LlamaConfigOf) reads back."""
     md = {
-        "general.architecture": "llama",
-        "llama.block_count": Uint(cfg["layers"]),
-        "llama.embedding_length": Uint(cfg["embed"]),
-        "llama.feed_forward_length": Uint(cfg["ffn"]),
-        "llama.attention.head_count": Uint(cfg["heads"]),
-        "llama.attention.head_count_kv": Uint(cfg["kv_heads"]),
-        "llama.context_length": Uint(cfg.get("max_context", cfg.get("context", 4096))),
-        "llama.rope.dimension_count": Uint(cfg.get("rope_dims", cfg["embed"] // cfg["heads"])),
-        "llama.rope.freq_base": float(cfg.get("rope_theta", 10000.0)),
-        "llama.attention.layer_norm_rms_epsilon": float(cfg["norm_eps"]),
+        "general.architecture": arch,
+        f"{arch}.block_count": Uint(cfg["layers"]),
+        f"{arch}.embedding_length": Uint(cfg["embed"]),
+        f"{arch}.feed_forward_length": Uint(cfg["ffn"]),
+        f"{arch}.attention.head_count": Uint(cfg["heads"]),
+        f"{arch}.attention.head_count_kv": Uint(cfg["kv_heads"]),
+        f"{arch}.context_length": Uint(cfg.get("max_context", cfg.get("context", 4096))),
+        f"{arch}.rope.dimension_count": Uint(cfg.get("rope_dims", cfg["embed"] // cfg["heads"])),
+        f"{arch}.rope.freq_base": float(cfg.get("rope_theta", 10000.0)),
+        f"{arch}.attention.layer_norm_rms_epsilon": float(cfg["norm_eps"]),
     }
     if name:
         md["general.name"] = name

@@ -9,8 +9,10 @@ It reads, and never modifies:
     encoder's input bits;
   * testdata/llama/tiny-q4km.gguf + expected.json (cmd/mim-run/main_test.go:
     179-267): the 2-layer tiny Llama whose prompt and greedy logits the
-    float64 oracle wrote.
-
+    float64 oracle wrote;
+  * testdata/qwen2/tiny-q4km.gguf + expected.json: the tiny Qwen 2 of the
+    same test (query/key/value biases, rotation of head halves), written as
+    tiny_qwen2.bin / tiny_qwen2.json in the same way;
   * testdata/compat/0.2-0.1/tiny-llama.mim: the same tiny Llama as the
     reference's importer writes it (container 0.2: weights, metadata and
     graph sections), for the mim-file loader.
@@ -100,5 +102,6 @@ if __name__ == "__main__":
         sys.exit("usage: make_golden.py <path to the mimir-model checkout>")
     quant(ref)
     tiny_llama(ref, "llama")
+    tiny_llama(ref, "qwen2")
     mim_fixture(ref)
     print("wrote", sorted(os.listdir(OUT)))

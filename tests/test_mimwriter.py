@@ -11,6 +11,9 @@
     ones the reference's own Python package validated and executed when the
     fixture was made (tests/golden/make_mim_writer_golden.py); the logits
     it computed for them are checked against the CPU restatement here.
+  * The tiny Qwen 2's file (biases, rotation of head halves) was executed
+    by the same package and meets the reference's own 2e-5 bar against its
+    float64 logits, with the same greedy ids.
   * Round trips through this library's reader, every metadata type, and the
     writer's refusals.
 """
@@ -88,6 +91,31 @@ def test_reference_executor_logits_match_the_oracle():
     ref = O.Llama(dict(e["config"], a8=0, cache_f16=1, interleaved=1), w)
     want = ref.forward(ids, np.arange(T), all_rows=True)
     assert np.abs(single - want).max() <= 2e-5 * np.abs(want).max()
+
+
+def test_qwen2_file_meets_the_references_bar():
+    """The tiny Qwen 2 (query/key/value biases, rotation of head halves) as
+    this writer authors it is the file the reference's Python executor ran
+    when the fixture was made; what it computed meets the reference's own
+    bar (cmd/mim-run/main_test.go:179-216): every prompt logit within 2e-5
+    of the largest float64 logit of testdata/qwen2/expected.json, and the
+    same 8 greedy ids."""
+    g = _golden()["qwen2_v1"]
+    e, _ = load_tiny("qwen2")
+    with open(os.path.join(GOLDEN, "tiny_qwen2.bin"), "rb") as f:
+        blob = f.read()
+    tensors = {t["name"]: (t["dtype"], tuple(t["shape"]), blob[t["offset"]:t["offset"] + t["nbytes"]])
+               for t in e["tensors"]}
+    cfg = e["config"]
+    out = W.write_llama(None, cfg, tensors, a8=False, cache_f16=False, context=cfg["context"],
+                        metadata=W.llama_metadata(cfg, arch="qwen2"))
+    assert hashlib.sha256(out).hexdigest() == g["sha256"] and len(out) == g["bytes"]
+    got, want = f32b64(g["logits"]), f32b64(e["prompt_logits"])
+    assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
+    assert g["greedy"] == e["greedy"]
+    # the graph carries the biases as third inputs of the q, k, v products
+    # and rotates head halves
+    assert b"attn_q.bias" in out and b"interleaved" in out
 
 
 def test_round_trip_through_the_reader(tmp_path):
