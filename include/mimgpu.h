@@ -239,8 +239,11 @@ typedef struct {
 
 int mimgpu_model_new(mimgpu_ctx *ctx, const mimgpu_llama_config *cfg, mimgpu_model **out);
 /* Binds an uploaded weight by its GGUF name (token_embd.weight,
- * blk.N.attn_q.weight, ..., output_norm.weight, output.weight).  The
- * model keeps the handle; it must outlive the model. */
+ * blk.N.attn_q.weight, ..., output_norm.weight, output.weight, and for a
+ * Qwen 2 graph the f32 biases blk.N.attn_q.bias / attn_k.bias / attn_v.bias,
+ * all three or none: the optional third input of the q, k, v products,
+ * importer/llama.go:470-478).  The model keeps the handle; it must outlive
+ * the model. */
 int mimgpu_model_set_weight(mimgpu_model *m, const char *name, const mimgpu_tensor *w);
 void mimgpu_model_free(mimgpu_model *m);
 

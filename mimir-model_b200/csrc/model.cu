@@ -29,6 +29,9 @@ namespace {
 struct LayerW {
     const mimgpu_tensor *attn_norm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     const mimgpu_tensor *ffn_norm = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+    // the query/key/value biases of a Qwen 2 graph (importer/llama.go:470-478:
+    // the optional third input of the products), all three or none
+    const mimgpu_tensor *bq = nullptr, *bk = nullptr, *bv = nullptr;
 };
 
 }  // namespace
@@ -143,6 +146,18 @@ int validate(mimgpu_model *m) {
             if (e.d1 >= 0 && !matrix_dtype(e.t->dtype, c.a8))
                 return fail(x, MIMGPU_ENOTHANDLED, "%s: dtype %d is not served", n.c_str(), e.t->dtype);
         }
+        // biases: all three or none, f32 vectors of the matrix's rows (or this rank's)
+        const bool any = w.bq || w.bk || w.bv;
+        if (any && !(w.bq && w.bk && w.bv))
+            return fail(x, MIMGPU_EINVAL, "blk.%d: attn_q/k/v biases come together", l);
+        const struct { const char *n; const mimgpu_tensor *t; long long d0, shard; } bl[] = {
+            {"attn_q", w.bq, E, sE}, {"attn_k", w.bk, KV, sKV}, {"attn_v", w.bv, KV, sKV}};
+        for (auto &e : bl) {
+            if (!any) break;
+            const bool ok = e.t->dtype == F32 && e.t->ndim == 1 &&
+                            (e.t->shape[0] == e.d0 || (e.shard >= 0 && e.t->shape[0] == e.shard));
+            if (!ok) return fail(x, MIMGPU_EINVAL, "blk.%d.%s.bias must be f32 [%lld]", l, e.n, e.d0);
+        }
     }
     const mimgpu_tensor *head = m->out ? m->out : m->embd;
     if (!matrix_dtype(head->dtype, c.a8)) return fail(x, MIMGPU_ENOTHANDLED, "output head dtype %d", head->dtype);
@@ -153,9 +168,10 @@ int validate(mimgpu_model *m) {
 // a GEMV segment: `w` is the whole matrix, or exactly this rank's rows (a
 // tensor-parallel shard, which starts at row r0 of the whole).
 GemvSeg slice(const mimgpu_tensor *w, long long K, long long full, long long r0, int rows, float *y, long long ldy,
-              const float *res) {
+              const float *res, const mimgpu_tensor *bias = nullptr) {
     const uint8_t *base = w->shape[0] == full ? w->dev + r0 * row_bytes(w->dtype, K) : w->dev;
-    GemvSeg g{base, w->dtype, rows, y, ldy, nullptr, res};
+    const float *b = bias ? (const float *)bias->dev + (bias->shape[0] == full ? r0 : 0) : nullptr;
+    GemvSeg g{base, w->dtype, rows, y, ldy, b, res};
     return g;
 }
 
@@ -288,9 +304,9 @@ cudaError_t enqueue_forward(mimgpu_session *s, int T, bool all_rows, bool greedy
         // exchange slots of the layer: 4l attention output, 4l+1 residual after o,
         // 4l+2 SwiGLU output, 4l+3 residual after down
         const P2P xin = xch(4 * (l - 1) + 3, nullptr, 0);
-        GemvSeg qkv[3] = {slice(w.q, E, E, (long long)k * El, El, s->qkv, ldq, nullptr),
-                          slice(w.k, E, KV, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr),
-                          slice(w.v, E, KV, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr)};
+        GemvSeg qkv[3] = {slice(w.q, E, E, (long long)k * El, El, s->qkv, ldq, nullptr, w.bq),
+                          slice(w.k, E, KV, (long long)k * KVl, KVl, s->qkv + El, ldq, nullptr, w.bk),
+                          slice(w.v, E, KV, (long long)k * KVl, KVl, s->qkv + El + KVl, ldq, nullptr, w.bv)};
         const GemvNorm n_attn{s->x, (const float *)w.attn_norm->dev, (float)c.norm_eps, s->h};
         const bool f_attn = fuse_norm(qkv, 3);
         if (!f_attn)
@@ -498,6 +514,7 @@ int setup_step(mimgpu_session *s) {
         const LayerW &w = m->L[l];
         const mimgpu_tensor *mats[7] = {w.q, w.k, w.v, w.o, w.gate, w.up, w.down};
         for (auto *t : mats) ok &= t->dtype == Q4_K || t->dtype == Q6_K;
+        ok &= !w.bq;  // the step kernel has no bias inputs
         ok &= w.gate->dtype == w.up->dtype;
     }
     if (!ok) return MIMGPU_OK;
@@ -606,7 +623,8 @@ int mimgpu_model_set_weight(mimgpu_model *m, const char *name, const mimgpu_tens
     const struct { const char *n; const mimgpu_tensor **slot; } names[] = {
         {"attn_norm.weight", &L.attn_norm}, {"attn_q.weight", &L.q},       {"attn_k.weight", &L.k},
         {"attn_v.weight", &L.v},           {"attn_output.weight", &L.o},  {"ffn_norm.weight", &L.ffn_norm},
-        {"ffn_gate.weight", &L.gate},      {"ffn_up.weight", &L.up},      {"ffn_down.weight", &L.down}};
+        {"ffn_gate.weight", &L.gate},      {"ffn_up.weight", &L.up},      {"ffn_down.weight", &L.down},
+        {"attn_q.bias", &L.bq},            {"attn_k.bias", &L.bk},        {"attn_v.bias", &L.bv}};
     for (auto &e : names)
         if (!strcmp(rest, e.n)) {
             *e.slot = w;

@@ -339,20 +339,22 @@ class MimFile:
 
 
 def llama_config(f: MimFile) -> dict:
-    """The Llama dimensions of a file written by the reference's importer
-    (metadata keys of importer/llama.go; the vocabulary from token_embd)."""
+    """The dimensions of a llama- or qwen2-architecture file written by the
+    reference's importer (metadata keys of importer/llama.go:104-162; the
+    vocabulary from token_embd); "arch" names the architecture."""
     md = f.metadata()
-    if md.get("general.architecture") != "llama":
-        raise MimError("unsupported-dtype", f"architecture {md.get('general.architecture')!r} is not llama")
+    arch = md.get("general.architecture")
+    if arch not in ("llama", "qwen2"):
+        raise MimError("unsupported-dtype", f"architecture {arch!r} is not llama or qwen2")
     emb = f.tensors.get("token_embd.weight")
     if emb is None or len(emb.shape) != 2:
         raise MimError("not-found", "token_embd.weight")
-    E = int(md["llama.embedding_length"])
-    H = int(md["llama.attention.head_count"])
-    cfg = dict(layers=int(md["llama.block_count"]), embed=E, ffn=int(md["llama.feed_forward_length"]), heads=H,
-               kv_heads=int(md.get("llama.attention.head_count_kv", H)), head_dim=E // H,
-               rope_dims=int(md.get("llama.rope.dimension_count", E // H)),
-               rope_theta=float(md.get("llama.rope.freq_base", 10000.0)),
-               norm_eps=float(md["llama.attention.layer_norm_rms_epsilon"]), vocab=int(emb.shape[0]),
-               context=int(md.get("mim.context_length", md.get("llama.context_length", 4096))))
+    E = int(md[f"{arch}.embedding_length"])
+    H = int(md[f"{arch}.attention.head_count"])
+    cfg = dict(arch=arch, layers=int(md[f"{arch}.block_count"]), embed=E, ffn=int(md[f"{arch}.feed_forward_length"]),
+               heads=H, kv_heads=int(md.get(f"{arch}.attention.head_count_kv", H)), head_dim=E // H,
+               rope_dims=int(md.get(f"{arch}.rope.dimension_count", E // H)),
+               rope_theta=float(md.get(f"{arch}.rope.freq_base", 10000.0)),
+               norm_eps=float(md[f"{arch}.attention.layer_norm_rms_epsilon"]), vocab=int(emb.shape[0]),
+               context=int(md.get("mim.context_length", md.get(f"{arch}.context_length", 4096))))
     return cfg

@@ -382,9 +382,12 @@ def load_llama(ctx: "Context", path: str, *, a8: bool = True, cache_f16: bool = 
         cfg = mimfile.llama_config(f)
         if context:
             cfg["context"] = int(context)
-        cfg.update(a8=int(a8), cache_f16=int(cache_f16), interleaved=1, max_tokens=int(max_tokens))
+        # llama rotates adjacent pairs, qwen2 the two halves of each head
+        cfg.update(a8=int(a8), cache_f16=int(cache_f16), interleaved=int(cfg["arch"] == "llama"),
+                   max_tokens=int(max_tokens))
         names = [n for n in f.tensors if n in ("token_embd.weight", "output.weight", "output_norm.weight")
-                 or (n.startswith("blk.") and n.endswith(".weight"))]
+                 or (n.startswith("blk.") and (n.endswith(".weight") or n.endswith(("attn_q.bias", "attn_k.bias",
+                                                                                   "attn_v.bias"))))]
         # each tensor with the file's own shape (the model checks it against the dimensions)
         weights = {n: (f.tensors[n].dtype, ctx.upload(f.tensors[n].dtype, f.tensors[n].shape,
                                                       np.frombuffer(f.data(n), np.uint8))) for n in names}
@@ -435,6 +438,7 @@ def _shape_of(name: str, cfg: dict, dt: int, arr) -> tuple:
         "attn_norm.weight": (E,), "ffn_norm.weight": (E,), "attn_q.weight": (E, E), "attn_k.weight": (kv, E),
         "attn_v.weight": (kv, E), "attn_output.weight": (E, E), "ffn_gate.weight": (F, E),
         "ffn_up.weight": (F, E), "ffn_down.weight": (E, F),
+        "attn_q.bias": (E,), "attn_k.bias": (kv,), "attn_v.bias": (kv,),
     }[base]
 
 

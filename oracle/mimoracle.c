@@ -1104,7 +1104,8 @@ int32_t mo_argmax(const float *v, int64_t n) {
 /* ------------------------------------------------------------------ */
 
 typedef struct { int dt; const uint8_t *p; } wref;
-typedef struct { wref attn_norm, q, k, v, o, ffn_norm, gate, up, down; void *ck, *cv; } layer_w;
+/* bq, bk, bv: the query/key/value biases of a Qwen 2 graph (f32), or none */
+typedef struct { wref attn_norm, q, k, v, o, ffn_norm, gate, up, down, bq, bk, bv; void *ck, *cv; } layer_w;
 
 struct mo_llama {
     mo_llama_config c;
@@ -1153,15 +1154,26 @@ int mo_llama_set_weight(mo_llama *m, const char *name, int dt, const void *data)
     else if (!strcmp(rest, "ffn_gate.weight")) L->gate = w;
     else if (!strcmp(rest, "ffn_up.weight")) L->up = w;
     else if (!strcmp(rest, "ffn_down.weight")) L->down = w;
+    else if (!strcmp(rest, "attn_q.bias") && dt == MO_F32) L->bq = w;
+    else if (!strcmp(rest, "attn_k.bias") && dt == MO_F32) L->bk = w;
+    else if (!strcmp(rest, "attn_v.bias") && dt == MO_F32) L->bv = w;
     else return -1;
     return 0;
 }
 
-/* matmulBias, importer/llama.go:264-280: a8.v2 block 256 for K-quants when a8 */
-static int mm(mo_llama *m, const float *x, int64_t rows, int64_t k, wref w, int64_t n, float *y) {
+/* matmulBias, importer/llama.go:243-268: a8.v2 block 256 for K-quants when
+   a8; the bias (Qwen 2's query/key/value projections) as the optional third
+   input */
+static int mmb(mo_llama *m, const float *x, int64_t rows, int64_t k, wref w, int64_t n, wref b, float *y) {
     if (!w.p) return -1;
-    if (m->c.a8) return mo_dequant_matmul_a8(x, rows, k, w.dt, w.p, n, NULL, 256, y, m->c.nthreads);
-    return mo_dequant_matmul(x, rows, k, w.dt, w.p, n, NULL, y, m->c.nthreads);
+    const float *bias = (const float *)b.p;
+    if (m->c.a8) return mo_dequant_matmul_a8(x, rows, k, w.dt, w.p, n, bias, 256, y, m->c.nthreads);
+    return mo_dequant_matmul(x, rows, k, w.dt, w.p, n, bias, y, m->c.nthreads);
+}
+
+static int mm(mo_llama *m, const float *x, int64_t rows, int64_t k, wref w, int64_t n, float *y) {
+    const wref none = {0, NULL};
+    return mmb(m, x, rows, k, w, n, none, y);
 }
 
 int mo_llama_forward(mo_llama *m, const int32_t *tokens, const int64_t *positions, int T, float *logits, int all_rows) {
@@ -1193,9 +1205,9 @@ int mo_llama_forward(mo_llama *m, const int32_t *tokens, const int64_t *position
     for (int l = 0; l < c->layers && rc == 0; l++) {
         layer_w *L = &m->L[l];
         mo_rms_norm(x, T, E, (const float *)L->attn_norm.p, c->norm_eps, h);
-        rc |= mm(m, h, T, E, L->q, E, q);
-        rc |= mm(m, h, T, E, L->k, KV, kk);
-        rc |= mm(m, h, T, E, L->v, KV, vv);
+        rc |= mmb(m, h, T, E, L->q, E, L->bq, q);
+        rc |= mmb(m, h, T, E, L->k, KV, L->bk, kk);
+        rc |= mmb(m, h, T, E, L->v, KV, L->bv, vv);
         /* [1,T,n,D] -> [1,n,T,D] */
         for (int t = 0; t < T; t++)
             for (int hd = 0; hd < H; hd++)

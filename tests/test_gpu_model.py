@@ -1,5 +1,5 @@
 """The device-resident llama step (mimgpu_session_*) against the reference's
-tiny-Llama fixture and against the CPU oracle.  Needs a B200.
+tiny-Llama and tiny-Qwen 2 fixtures and against the CPU oracle.  Needs a B200.
 
 Bars (gsoultan/mimir-model):
   cmd/mim-run/main_test.go:179-216  v1 graph, f32 cache: prompt and step
@@ -18,7 +18,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from conftest import f32b64
+from conftest import f32b64, load_tiny
 
 pytestmark = pytest.mark.gpu
 
@@ -33,13 +33,15 @@ def ctx():
 
 def _model(ctx, e, w, **over):
     import mimgpu
-    cfg = dict(e["config"], interleaved=1, max_tokens=len(e["prompt_ids"]))
+    # llama rotates adjacent pairs, qwen2 the halves of each head
+    cfg = dict(e["config"], interleaved=int(e["config"]["arch"] == "llama"), max_tokens=len(e["prompt_ids"]))
     cfg.update(over)
     return mimgpu.Model(ctx, cfg, w)
 
 
-def test_tiny_llama_v1_matches_float64_oracle(ctx, tiny):
-    e, w = tiny
+@pytest.mark.parametrize("name", ["llama", "qwen2"])
+def test_tiny_llama_v1_matches_float64_oracle(ctx, name):
+    e, w = load_tiny(name)
     V = e["config"]["vocab"]
     m = _model(ctx, e, w, a8=0, cache_f16=0)
     s = m.session()
@@ -58,9 +60,10 @@ def test_tiny_llama_v1_matches_float64_oracle(ctx, tiny):
     m.free()
 
 
+@pytest.mark.parametrize("name", ["llama", "qwen2"])
 @pytest.mark.parametrize("cache_f16,bound", [(0, 1.0), (1, 1.1)])
-def test_tiny_llama_a8_within_llama_cpp(ctx, tiny, cache_f16, bound):
-    e, w = tiny
+def test_tiny_llama_a8_within_llama_cpp(ctx, name, cache_f16, bound):
+    e, w = load_tiny(name)
     V = e["config"]["vocab"]
     m = _model(ctx, e, w, a8=1, cache_f16=cache_f16)
     s = m.session()
@@ -77,12 +80,14 @@ def test_tiny_llama_a8_within_llama_cpp(ctx, tiny, cache_f16, bound):
     m.free()
 
 
-def test_tiny_llama_a8_matches_cpu_restatement(ctx, tiny):
-    """Prompt logits and 48 greedy ids against the oracle's a8 + f16 graph."""
-    e, w = tiny
+@pytest.mark.parametrize("name", ["llama", "qwen2"])
+def test_tiny_llama_a8_matches_cpu_restatement(ctx, name):
+    """Prompt logits and 48 greedy ids against the oracle's a8 + f16 graph
+    (the Qwen 2 with its query/key/value biases and rotation of halves)."""
+    e, w = load_tiny(name)
     m = _model(ctx, e, w, a8=1, cache_f16=1)
     s = m.session()
-    ref = O.Llama(dict(e["config"], a8=1, cache_f16=1, interleaved=1), w)
+    ref = O.Llama(dict(e["config"], a8=1, cache_f16=1, interleaved=int(name == "llama")), w)
     ids = e["prompt_ids"]
     got = s.run(ids, np.arange(len(ids)), all_rows=True)
     want = ref.forward(ids, np.arange(len(ids)), all_rows=True)

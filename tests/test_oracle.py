@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from conftest import f32b64, fma32 as _fma32
+from conftest import load_tiny, f32b64, fma32 as _fma32
 
 F16 = lambda f: int(O.lib().mo_f32_to_f16(f))  # noqa: E731
 
@@ -308,13 +308,15 @@ def test_a8_matmul_falls_back_on_refused_rows():
     assert not np.array_equal(y8[0, :2], y32[0, :2])
 
 
-def test_tiny_llama_v1_matches_float64_oracle(tiny):
-    """cmd/mim-run/main_test.go:179-216: prompt and 8 greedy steps of the
-    dequant_matmul.v1 graph (f32 cache) within 2e-5 of the largest logit,
-    and the same greedy ids."""
-    e, w = tiny
+@pytest.mark.parametrize("name", ["llama", "qwen2"])
+def test_tiny_llama_v1_matches_float64_oracle(name):
+    """cmd/mim-run/main_test.go:179-216, both fixtures of the reference: the
+    tiny Llama and the tiny Qwen 2 (query/key/value biases, rotation of head
+    halves).  Prompt and 8 greedy steps of the dequant_matmul.v1 graph (f32
+    cache) within 2e-5 of the largest logit, and the same greedy ids."""
+    e, w = load_tiny(name)
     V = e["config"]["vocab"]
-    m = O.Llama(dict(e["config"], a8=0, cache_f16=0, interleaved=1), w)
+    m = O.Llama(dict(e["config"], a8=0, cache_f16=0, interleaved=int(name == "llama")), w)
     ids = e["prompt_ids"]
     all_ = m.forward(ids, np.arange(len(ids)), all_rows=True)
     want = f32b64(e["prompt_logits"]).reshape(len(ids), V)
@@ -328,13 +330,14 @@ def test_tiny_llama_v1_matches_float64_oracle(tiny):
         pos += 1
 
 
+@pytest.mark.parametrize("name", ["llama", "qwen2"])
 @pytest.mark.parametrize("cache_f16,bound", [(0, 1.0), (1, 1.1)])
-def test_tiny_llama_a8_within_llama_cpp(tiny, cache_f16, bound):
+def test_tiny_llama_a8_within_llama_cpp(name, cache_f16, bound):
     """cmd/mim-run/main_test.go:218-267: the a8 graph stays within llama.cpp's
     own distance from the float64 oracle (x1.1 with the f16 cache)."""
-    e, w = tiny
+    e, w = load_tiny(name)
     V = e["config"]["vocab"]
-    m = O.Llama(dict(e["config"], a8=1, cache_f16=cache_f16, interleaved=1), w)
+    m = O.Llama(dict(e["config"], a8=1, cache_f16=cache_f16, interleaved=int(name == "llama")), w)
     ids = e["prompt_ids"]
     all_ = m.forward(ids, np.arange(len(ids)), all_rows=True)
     worst = np.abs(all_ - f32b64(e["prompt_logits"]).reshape(len(ids), V)).max()
