@@ -13,8 +13,10 @@
 // key-ordered fused weighted sum of wsumF16AVX2, o = acc/sum.
 //
 // A block takes two query heads of one token (one kv head: the group size
-// must be even) and 256 threads.  Decode attention is latency-bound (a few
-// blocks per token), so the layout minimises serial steps:
+// must be even), or four in a batched grid that still has a block for every
+// SM and a group size divisible by four, and 256 threads.  Decode attention
+// is latency-bound (a few blocks per token), so the layout minimises serial
+// steps:
 //  * The keys and values of earlier tokens stream through a ring of chunk
 //    buffers, requested BEFORE the grid dependency wait: they were written by
 //    earlier steps, all complete once this step's first kernel (the
@@ -32,10 +34,11 @@
 //    eight consecutive keys at one column hit eight distinct bank groups; a
 //    value chunk is one bulk copy of dense rows.  A thread scores one key
 //    with the whole row unrolled: for both heads in a 256-key chunk, for one
-//    head (threads 0-127 the first) in a 128-key one.
-//  * The weighted sum: 128 threads, two output elements each, with the
-//    exponentials and value pairs of eight keys loaded ahead of the fused
-//    multiply-adds.
+//    head (threads 0-127 the first) in a 128-key chunk of two heads, for two
+//    heads (threads 0-127 heads 0-1, 128-255 heads 2-3) in one of four.
+//  * The weighted sum: 64 threads per head, two output elements each, with
+//    the exponentials and value pairs of eight keys loaded ahead of the
+//    fused multiply-adds.
 // The scores of the block's heads over the whole context live in shared
 // memory (context <= attn_decode_max_context()).
 #include "common.cuh"
